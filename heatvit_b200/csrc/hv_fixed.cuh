@@ -1,0 +1,210 @@
+// hv_fixed.cuh — integer fixed-point primitives for the HeatViT-T engine.
+//
+// Device restatements of the golden model's numeric contract
+// (verification/heatvit_ref/fixed.py:15-80, nonlinear.py:60-186).  Rounding is
+// ties-away-from-zero everywhere; every helper documents the operand range it
+// is exact for.  No floating-point result is ever used without an exact integer
+// correction step.
+#pragma once
+#include <stdint.h>
+
+#define HV_DEV __device__ __forceinline__
+#define HV_HD __host__ __device__ __forceinline__
+
+namespace hv {
+
+// ---------------------------------------------------------------------------
+// Rounding shifts (fixed.py:15-25)
+// ---------------------------------------------------------------------------
+
+// Ties-away right shift of a 32-bit value by s in [1, 30], valid while
+// |v| + 2^(s-1) < 2^31.  For v >= 0 it is floor((v + 2^(s-1)) / 2^s); for v < 0
+// the ties-away value -floor((|v| + 2^(s-1)) / 2^s) equals
+// floor((v + 2^(s-1) - 1) / 2^s), hence the (v >> 31) correction term.
+HV_HD int32_t rsa32(int32_t v, int s) {
+    return (v + (1 << (s - 1)) + (v >> 31)) >> s;
+}
+
+// Same on 64-bit values, s in [1, 62], |v| + 2^(s-1) < 2^63.
+HV_HD int64_t rsa64(int64_t v, int s) {
+    return (v + ((int64_t)1 << (s - 1)) + (v >> 63)) >> s;
+}
+
+// round_shift_away with any signed shift on a 64-bit value (negative = left
+// shift); callers guarantee the left-shifted value fits in 64 bits.
+HV_HD int64_t rsa64_any(int64_t v, int s) {
+    if (s > 0) return s >= 63 ? 0 : rsa64(v, s);
+    return v << (-s);
+}
+
+HV_HD int32_t clamp_i32(int32_t v, int32_t lo, int32_t hi) { return v < lo ? lo : (v > hi ? hi : v); }
+HV_HD int64_t clamp_i64(int64_t v, int64_t lo, int64_t hi) { return v < lo ? lo : (v > hi ? hi : v); }
+
+HV_HD int32_t sat8(int32_t v) { return clamp_i32(v, -128, 127); }
+HV_HD int32_t sat24(int32_t v) { return clamp_i32(v, -(1 << 23), (1 << 23) - 1); }
+
+// requant (fixed.py:37-45) of a 64-bit value to `bits` in {8, 24, 32} with
+// shift = dst - src (any sign).  A left shift saturates by sign once the value
+// is out of range, matching the unbounded Python result after saturation.
+HV_HD int64_t requant64(int64_t v, int shift, int bits) {
+    const int64_t hi = ((int64_t)1 << (bits - 1)) - 1, lo = -hi - 1;
+    if (shift > 0) {
+        if (shift >= 63) return 0;  // |v| < 2^62 in every caller
+        return clamp_i64(rsa64(v, shift), lo, hi);
+    }
+    if (shift == 0) return clamp_i64(v, lo, hi);
+    const int ls = -shift;
+    if (v == 0) return 0;
+    if (ls >= 40) return v > 0 ? hi : lo;
+    const int64_t lim = (int64_t)1 << (62 - ls);
+    if (v >= lim) return hi;
+    if (v <= -lim) return lo;
+    return clamp_i64(v << ls, lo, hi);
+}
+
+// Fast int8 requant of a 32-bit value with a right shift s in [1, 30]
+// (|v| + 2^(s-1) < 2^31).
+HV_HD int32_t requant8_r(int32_t v, int s) { return sat8(rsa32(v, s)); }
+
+// ---------------------------------------------------------------------------
+// Division helpers (fixed.py:58-72 round_div, fixed.py:75-80 isqrt)
+// ---------------------------------------------------------------------------
+
+// round_div for a non-negative denominator: nearest, ties away from zero, sign
+// of the numerator.
+HV_HD int64_t round_div64(int64_t n, int64_t d) {
+    uint64_t an = n < 0 ? (uint64_t)(-n) : (uint64_t)n;
+    uint64_t q = an / (uint64_t)d, r = an - q * (uint64_t)d;
+    if (2 * r >= (uint64_t)d) q += 1;
+    return n < 0 ? -(int64_t)q : (int64_t)q;
+}
+
+// Exact floor(n / d) for n < 2^32 and d in [2^16, 2^24): a float estimate of
+// the quotient (relative error < 2^-21, so |estimate - q| <= 1 for q < 2^17)
+// followed by an exact integer remainder correction.
+HV_DEV uint32_t udiv_u32_small_q(uint32_t n, uint32_t d) {
+    float fq = __fdividef(__uint2float_rz(n), __uint2float_rn(d));
+    uint32_t q = __float2uint_rz(fq);
+    int32_t r = (int32_t)(n - q * d);          // |true remainder| < 2d < 2^25
+    if (r < 0) { q -= 1; r += (int32_t)d; }
+    if (r >= (int32_t)d) { q += 1; }
+    return q;
+}
+
+// Floor square root of v < 2^62 (fixed.py:75-80 isqrt): a double estimate
+// corrected by exact integer comparisons.
+HV_DEV uint64_t isqrt64(uint64_t v) {
+    uint64_t s = (uint64_t)sqrt((double)v);
+    while (s > 0 && s * s > v) --s;
+    while ((s + 1) * (s + 1) <= v) ++s;
+    return s;
+}
+
+// ---------------------------------------------------------------------------
+// ShiftGELU (nonlinear.py:60-80): Q8.16 in [-2^23, 2^23) -> Q8.16
+// ---------------------------------------------------------------------------
+// The division sig = floor(((e << 16) + (den >> 1)) / den) with den = 2^16 + e
+// is rewritten without 64-bit operands: e*2^16 + h = den*2^16 - (2^32 - h), so
+// sig = 2^16 - ceil((2^32 - h) / den) = 65535 - floor((2^32 - 1 - h) / den),
+// and 2^32 - 1 - h is ~h in 32 bits.  den lies in [2^16, 2^23 + 2^16), so the
+// quotient is below 2^17 and udiv_u32_small_q is exact.  |x * sig| < 2^39 and
+// |y| <= 2^23 - 128, so the final sat24 of the golden model never clips.
+HV_DEV int32_t shift_gelu(int32_t x) {
+    int32_t ip = x + (x >> 1) + (x >> 3) + (x >> 4);     // 1.702x
+    int32_t ip2 = ip + (ip >> 1) - (ip >> 4);            // * log2(e)
+    uint32_t a = (uint32_t)(ip2 < 0 ? -ip2 : ip2);
+    uint32_t q = a >> 16;
+    uint32_t frac = ((a & 0xFFFFu) * 11u + 15u) >> 4;    // slope 11/16
+    uint32_t e;
+    if (ip2 < 0) {
+        e = (65536u - frac) >> (q < 31u ? q : 31u);      // q > 16 gives 0 anyway
+    } else {
+        uint32_t t = (65536u + frac) << (q < 8u ? q : 8u);
+        e = t < 8388607u ? t : 8388607u;                  // q >= 8 saturates
+    }
+    uint32_t den = 65536u + e;
+    uint32_t sig = 65535u - udiv_u32_small_q(~(den >> 1), den);
+    int64_t p = (int64_t)x * (int64_t)sig;
+    return (int32_t)rsa64(p, 16);
+}
+
+// The FFN / selector GELU post-op chain
+// requant(gelu(requant(v, src, -16, 24)), -16, dst, 8)
+// (transformer.py:351-356, selector.py:89-99).  sh_in = -16 - src,
+// sh_out = dst + 16.
+HV_DEV int32_t gelu_chain(int64_t v, int sh_in, int sh_out) {
+    int32_t q16 = (int32_t)requant64(v, sh_in, 24);
+    return (int32_t)requant64(shift_gelu(q16), sh_out, 8);
+}
+
+// PLAN sigmoid (nonlinear.py:83-95), unsigned Q0.16.
+HV_HD int32_t plan_sigmoid(int32_t x) {
+    int32_t ax = x < 0 ? -x : x, y;
+    if (ax >= 327680) y = 65536;
+    else if (ax >= 155648) y = (ax >> 5) + 55296;
+    else if (ax >= 65536) y = (ax >> 3) + 40960;
+    else y = (ax >> 2) + 32768;
+    return x < 0 ? 65536 - y : y;
+}
+
+// ---------------------------------------------------------------------------
+// Shift-softmax pieces (nonlinear.py:98-133)
+// ---------------------------------------------------------------------------
+// exp of a non-positive Q8.16 argument xt = x - max, |xt| < 2^31.
+// z = floor(-xt / 45426) by a multiply-high estimate with M = floor(2^32/45426)
+// = 94548: n*M/2^32 = (n/45426)(1 - 6.95e-6), so the estimate is q or q-1 for
+// every n < 2^31, and one remainder correction makes it exact.  Then
+// p = xt + z*45426 = -r, where r is the remainder.
+HV_DEV uint32_t softmax_exp_q16(int32_t xt) {
+    uint32_t n = (uint32_t)(-xt);
+    uint32_t z = __umulhi(n, 94548u);
+    uint32_t r = n - z * 45426u;
+    if (r >= 45426u) { z += 1; r -= 45426u; }
+    uint32_t sh = 88670u - r;                                   // p + 88670, in (43244, 88670]
+    uint64_t sq = ((uint64_t)sh * sh + 32768u) >> 16;           // rsa(sh^2, 16), <= 119970
+    uint32_t e = ((uint32_t)(23495u * (uint32_t)sq + 32768u) >> 16) + 22544u;
+    return z >= 31u ? 0u : (e >> z);
+}
+
+// recip = round_div(2^32, S) for S >= 1.
+HV_DEV uint64_t softmax_recip(uint64_t s) {
+    uint64_t q = ((uint64_t)1 << 32) / s, r = ((uint64_t)1 << 32) - q * s;
+    if (2 * r >= s) q += 1;
+    return q;
+}
+
+// ratio = rsa(E * recip, 16); scaled = rsa(ratio * 65536, 16) == ratio.
+HV_DEV uint32_t softmax_ratio(uint32_t e, uint64_t recip) {
+    return (uint32_t)(((uint64_t)e * recip + 32768u) >> 16);
+}
+
+// Attention narrowing: min(rsa(scaled, 8), 255) (nonlinear.py:130-133).
+HV_DEV uint32_t softmax_attn_u8(uint32_t ratio) {
+    uint32_t v = (ratio + 128u) >> 8;
+    return v < 255u ? v : 255u;
+}
+
+// ---------------------------------------------------------------------------
+// Residual align-add (transformer.py:96-101)
+// ---------------------------------------------------------------------------
+// out = requant((a << (ea - c)) + (b << (eb - c)), c, eo, 8), c = min(ea, eb).
+struct AlignAdd {
+    int sa, sb, sh;   // left shifts of a and b, requant shift eo - c
+};
+
+HV_HD AlignAdd make_align_add(int ea, int eb, int eo) {
+    int c = ea < eb ? ea : eb;
+    AlignAdd r;
+    r.sa = ea - c;
+    r.sb = eb - c;
+    r.sh = eo - c;
+    return r;
+}
+
+// Exact for shifts up to 54 (int8 << 54 stays below 2^62).
+HV_HD int32_t align_add8(int32_t a, int32_t b, AlignAdd k) {
+    int64_t v = ((int64_t)a << k.sa) + ((int64_t)b << k.sb);
+    return (int32_t)requant64(v, k.sh, 8);
+}
+
+}  // namespace hv

@@ -1,0 +1,63 @@
+// hv_gemm.cuh — int8 GEMM with fused integer epilogues.
+//
+// C[M][N] = A[M][K] · Bt[N][K]ᵀ (+ bias), int32 accumulation, then one of the
+// golden writebacks (gemm.py:123-139) fused with what follows it in the model:
+//   EPI_I8       requant to int8                          (QKV, generic)
+//   EPI_I8_RES   requant to int8, then residual align-add  (proj + residual 1,
+//                FC2 + residual 2; transformer.py:415-425, 373-381)
+//   EPI_GELU     requant to Q16/24 bit, ShiftGELU, requant to int8 (FC1;
+//                transformer.py:351-356)
+//   EPI_PATCH    requant to int8, align-add the positional row, write into the
+//                197-row token layout (transformer.py:125-145)
+//   EPI_I32      requant to int32 (head logits, model.py:109-115; unit API)
+//   EPI_ACC64    raw int64 accumulator + bias (unit API, gemm_numpy)
+//
+// Weights are stored K-major (Bt[n][k], the transpose of the golden w[k][n]).
+// A may be int8 or uint8 (P·V in attention uses uint8 probabilities;
+// gemm.py:81-84).  The pre-bias accumulator fits int32 for K <= 131071.
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include "hv_fixed.cuh"
+
+namespace hv {
+
+enum Epi { EPI_I8 = 0, EPI_I8_RES = 1, EPI_GELU = 2, EPI_PATCH = 3, EPI_I32 = 4, EPI_ACC64 = 5 };
+
+// Per-launch epilogue constants (all derived on the host from the golden
+// scale exponents).
+struct EpiParams {
+    const int32_t *bias;      // [N] or nullptr
+    int shift;                // requant shift dst - src for the first writeback
+    int bits_wide;            // 1: acc + bias may leave int32 -> 64-bit path
+    // residual (EPI_I8_RES): out = align_add(res @ e_res, y @ e_y -> e_out)
+    const int8_t *res;        // [M][N]
+    AlignAdd add;             // a = residual value, b = requantised GEMM value
+    // GELU chain (EPI_GELU): sh_in = -16 - src, sh_out = dst + 16
+    int gelu_sh_in, gelu_sh_out;
+    // patch (EPI_PATCH): pos [197][192], add = (a = embed, b = pos)
+    const int8_t *pos;
+};
+
+// Where A comes from.
+struct ASrc {
+    const void *ptr;          // row-major [M][lda] int8/uint8, or NHWC images
+    int lda;
+    int patch_mode;           // 1: A row r = patch (r % 196) of image r / 196
+};
+
+struct GemmArgs {
+    ASrc a;
+    const int8_t *bt;         // [Npad][K] K-major weights (Npad multiple of 64)
+    int n, k;                 // logical N (stores guarded), K multiple of 64
+    int m_host;               // row count when m_dev == nullptr
+    const int32_t *m_dev;     // device row count (ragged batches), or nullptr
+    void *out;                // int8 / int32 / int64 [M][ldo]
+    int ldo;
+    EpiParams epi;
+};
+
+// Launch helpers (defined in hv_gemm.cu).
+cudaError_t launch_gemm(const GemmArgs &g, int epi, int a_unsigned, int m_max, cudaStream_t st);
+
+}  // namespace hv

@@ -1,0 +1,102 @@
+// hv_internal.cuh — launch interfaces shared by the library's .cu files.
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include "hv_fixed.cuh"
+#include "hv_gemm.cuh"
+#include "../../include/heatvit_b200.h"
+
+namespace hv {
+
+// LayerNorm constants of one LN layer (nonlinear.py:136-186), host-derived.
+struct LnParams {
+    const int8_t *gamma, *beta;    // [192]
+    int x_scale;                   // in [-32, 0]
+    int sh_sum;                    // x_scale + 32           (left shift of Σx)
+    int sq_shift;                  // 2*x_scale + 32         (>= 0: left shift of Σx², < 0: per-element rsa)
+    int sh_g, sh_b;                // gamma/beta alignment left shifts
+    int sh_out;                    // out_scale - common
+    int fast;                      // 1: sh_g <= 16 and sh_b <= 40 (int64 output stage)
+};
+
+LnParams make_ln(const int8_t *gamma, const int8_t *beta, int x_scale, int gamma_scale, int beta_scale,
+                 int out_scale);
+
+// LN over rows [0, rows) of x (row stride 192) -> out.  rows is *rows_dev when
+// non-null.  Negative-variance rows set *negvar_row (per row, may be null) and
+// OR bit 2 into warn[image] where image is found from offsets (may be null).
+cudaError_t launch_layernorm(const int8_t *x, int8_t *out, int rows_max, const int32_t *rows_dev,
+                             const LnParams &p, uint8_t *negvar_row, const int32_t *offsets,
+                             int images, uint8_t *warn, cudaStream_t st);
+
+// LN of each image's first row (the CLS token): row offsets[i] -> out[i].
+cudaError_t launch_layernorm_cls(const int8_t *x, const int32_t *offsets, int images, int8_t *out,
+                                 const LnParams &p, uint8_t *warn, cudaStream_t st);
+
+// Attention for every (image, head) of a ragged batch: qkv [T][576] -> ctx [T][192].
+struct AttnParams {
+    int score_shift;   // score_scale - 2*qkv_out           (int32 score writeback)
+    int q16_shift;     // -(score_scale + 13)               (Q8.16 conversion, sat 24)
+    int ctx_shift;     // context_out - (prob_scale + qkv_out)
+};
+cudaError_t launch_attention(const int8_t *qkv, const int32_t *offsets, int images, int8_t *ctx,
+                             const AttnParams &p, cudaStream_t st);
+
+// Device-resident selector weights and constants.
+struct SelParams {
+    const int8_t *local_wt;   // [3][32][64]  (transposed local_w)
+    const int32_t *local_b;   // [3][32]
+    const int8_t *w1t;        // [3][32][64]  (transposed score_w1: [h][j][k], k = 0..63)
+    const int32_t *b1;        // [3][32]
+    const int8_t *w2t;        // [3][16][32]
+    const int32_t *b2;        // [3][16]
+    const int8_t *w3t;        // [3][2][16]
+    const int32_t *b3;        // [3][2]
+    const int8_t *hw1;        // [3][3]  (golden [i][j])
+    const int32_t *hb1;       // [3]
+    const int8_t *hw2;        // [3][3]
+    const int32_t *hb2;       // [3]
+    int local_sh_in, local_sh_out;    // GELU chain of the local MLP
+    int h1_sh_in, h1_sh_out;          // score layer 1
+    int h2_sh_in, h2_sh_out;          // score layer 2
+    int logit_shift;                  // logits writeback (h2 + w3 -> logits)
+    int logit_q16_shift;              // logits -> Q16 (24 bit)
+    int hw_sh_in, hw_sh_out;          // head-weight hidden GELU chain
+    int hw_q16_shift;                 // head-weight acc -> Q16 (24 bit)
+};
+
+// Optional selector intermediates (token_selector API), image stride 196.
+struct SelDebug {
+    int32_t *fused;         // [B][196]
+    int32_t *head_scores;   // [B][3][196]
+    int32_t *head_weights;  // [B][196][3]
+    int8_t *local;          // [B][3][196][32]
+    int8_t *global_;        // [B][3][32]
+    int8_t *stats;          // [B][196][3]
+};
+
+// Selector over a ragged batch: x rows offsets[i]..offsets[i+1], pkg_in[i] ->
+// stage[i][0..n') (stride 197 rows), counts_out[i] = n', pkg_out[i],
+// summary[i*sum_stride], warn[i] |= bits, token_counts[i*tc_stride + tc_col] = n'.
+// warn is a uint8 array whose allocation is padded to a multiple of 4 bytes.
+cudaError_t launch_selector(const int8_t *x, const int32_t *offsets, const uint8_t *pkg_in, int images,
+                            const SelParams &p, int8_t *stage, int32_t *counts_out, uint8_t *pkg_out,
+                            hv_selector_summary *summary, int sum_stride, uint8_t *warn, int32_t *token_counts,
+                            int tc_stride, int tc_col, const SelDebug *dbg, cudaStream_t st);
+
+// Pack stage[i] (count counts[i], stride 197 rows) into x at prefix-summed
+// offsets; writes offsets_out[0..images].
+cudaError_t launch_pack(const int8_t *stage, const int32_t *counts, int images, int8_t *x,
+                        int32_t *offsets_out, cudaStream_t st);
+
+// Element-wise units (unit API).
+cudaError_t launch_gelu(const int32_t *x, int64_t n, int32_t *out, cudaStream_t st);
+cudaError_t launch_plan(const int32_t *x, int64_t n, int32_t *out, cudaStream_t st);
+cudaError_t launch_gelu_requant(const int32_t *acc, int64_t n, int sh_in, int sh_out, int8_t *out,
+                                cudaStream_t st);
+cudaError_t launch_softmax_rows(const int32_t *x, const int32_t *offsets, int rows, int mode, void *out,
+                                cudaStream_t st);
+cudaError_t launch_align_add(const int8_t *a, const int8_t *b, AlignAdd k, int64_t n, int8_t *out, cudaStream_t st);
+cudaError_t launch_writeback(const int64_t *acc, int64_t n, int shift, int bits, void *out, cudaStream_t st);
+
+}  // namespace hv

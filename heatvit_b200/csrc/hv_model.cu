@@ -1,0 +1,923 @@
+// hv_model.cu — the C ABI: model packing, the batched pipeline and per-op entry points.
+//
+// Pipeline of one batch (HeatViTModel.infer, model.py:73-123, for every image):
+//   patch GEMM (+pos, CLS rows) -> for block b in 1..12:
+//       [selector + pack when a selector precedes b]
+//       LN1 -> QKV GEMM -> attention -> proj GEMM + residual -> LN2
+//       -> FC1 GEMM + GELU -> FC2 GEMM + residual
+//   -> LN of each CLS row -> head GEMM (int32 logits at 2^-14).
+// Tokens live in one packed ragged buffer: image i owns rows offsets[i] ..
+// offsets[i+1].  Kernels take the live row count from device memory, so the
+// host never synchronises on data-dependent token counts.
+#include <cuda_runtime.h>
+#include <stdarg.h>
+#include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
+#include <vector>
+#include <algorithm>
+
+#include "hv_internal.cuh"
+
+using namespace hv;
+
+namespace {
+
+thread_local char g_err[512] = "";
+
+int fail(int code, const char *fmt, ...) {
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(g_err, sizeof(g_err), fmt, ap);
+    va_end(ap);
+    return code;
+}
+
+#define CUDA_TRY(expr)                                                                      \
+    do {                                                                                    \
+        cudaError_t _e = (expr);                                                            \
+        if (_e != cudaSuccess) return fail(HV_ERR_CUDA, "%s: %s", #expr, cudaGetErrorString(_e)); \
+    } while (0)
+
+constexpr int64_t kNarrowLimit = (int64_t)1 << 30;
+
+// Largest |bias| of a vector.
+int64_t max_abs(const int32_t *b, int n) {
+    int64_t m = 0;
+    for (int i = 0; i < n; ++i) m = std::max<int64_t>(m, b[i] < 0 ? -(int64_t)b[i] : b[i]);
+    return m;
+}
+
+// acc + bias fits the 32-bit epilogue path: |acc| <= K * 2^14.
+int needs_wide(const int32_t *bias, int n, int k) {
+    return max_abs(bias, n) + (int64_t)k * 16384 >= kNarrowLimit ? 1 : 0;
+}
+
+// Host copy of align-add for the CLS row (transformer.py:96-101).
+int8_t host_align_add(int a, int ea, int b, int eb, int eo) {
+    AlignAdd k = make_align_add(ea, eb, eo);
+    return (int8_t)requant64(((int64_t)a << k.sa) + ((int64_t)b << k.sb), k.sh, 8);
+}
+
+bool align_ok(int ea, int eb, int eo) {
+    AlignAdd k = make_align_add(ea, eb, eo);
+    return k.sa <= 54 && k.sb <= 54;
+}
+
+struct Arena {
+    std::vector<uint8_t> host;
+    size_t add(const void *src, size_t bytes) {
+        size_t off = (host.size() + 255) & ~(size_t)255;
+        host.resize(off + bytes);
+        if (src) memcpy(host.data() + off, src, bytes);
+        else memset(host.data() + off, 0, bytes);
+        return off;
+    }
+    // transposed copy of an int8 [rows][cols] matrix into [cols_pad][rows]
+    size_t add_t(const int8_t *src, int rows, int cols, int cols_pad) {
+        std::vector<int8_t> t((size_t)cols_pad * rows, 0);
+        for (int r = 0; r < rows; ++r)
+            for (int c = 0; c < cols; ++c) t[(size_t)c * rows + r] = src[(size_t)r * cols + c];
+        return add(t.data(), t.size());
+    }
+};
+
+struct BlockDev {
+    size_t ln1_g, ln1_b, wqkv, bqkv, wproj, bproj, ln2_g, ln2_b, w1, b1, w2, b2;
+    int ln1_xs, ln1_gs, ln1_bs, ln1_os, ln2_xs, ln2_gs, ln2_bs, ln2_os;
+    int qkv_shift, qkv_wide, proj_shift, proj_wide, fc2_shift, fc2_wide;
+    int fc1_sh_in, fc1_sh_out;
+    AlignAdd res1, res2;
+    AttnParams attn;
+};
+
+struct SelDev {
+    size_t lwt, lb, w1t, b1, w2t, b2, w3t, b3, hw1, hb1, hw2, hb2;
+    SelParams p;  // shifts only until bind()
+};
+
+}  // namespace
+
+struct hv_model {
+    int device = 0;
+    int has_patch = 0, has_head = 0, has_block[HV_BLOCKS] = {0};
+    int used_sel = 0;  // selectors that actually run (strides of token counts / summaries)
+    uint8_t *weights = nullptr;
+    size_t weights_bytes = 0;
+    // patch
+    size_t patch_wt = 0, patch_b = 0, pos = 0, cls_row = 0;
+    int patch_shift = 0, patch_wide = 0;
+    AlignAdd patch_add{};
+    BlockDev blocks[HV_BLOCKS];
+    int sel_before[HV_BLOCKS];
+    int num_sel = 0;
+    SelDev sels[HV_MAX_SELECTORS];
+    size_t fin_g = 0, fin_b = 0, head_wt = 0, head_b = 0;
+    int fin_xs = 0, fin_gs = 0, fin_bs = 0, fin_os = 0, head_shift = 0;
+    // scratch
+    int cap = 0;
+    uint8_t *scratch = nullptr;
+    int8_t *X = nullptr, *Y = nullptr, *LN = nullptr, *QKV = nullptr, *CTX = nullptr, *HID = nullptr, *STAGE = nullptr,
+           *CLSLN = nullptr;
+    int32_t *off[2] = {nullptr, nullptr}, *counts = nullptr;
+    uint8_t *pkg[2] = {nullptr, nullptr}, *warn = nullptr;
+    // host-pipeline staging
+    int host_cap = 0;
+    int8_t *himg[2] = {nullptr, nullptr};
+    int32_t *hlogits = nullptr, *htc = nullptr;
+    hv_selector_summary *hsum = nullptr;
+    uint8_t *hwarn = nullptr;
+    cudaStream_t copy_stream = nullptr, compute_stream = nullptr;
+    cudaEvent_t ev_in[2] = {nullptr, nullptr}, ev_done[2] = {nullptr, nullptr};
+
+    // kernel timing (hv_profile_*)
+    int prof_stage = 0, prof_max = 0, prof_n = 0;
+    std::vector<cudaEvent_t> prof_ev;
+    int32_t *prof_rows = nullptr;  // device [prof_max] live row counts
+
+    template <class T>
+    const T *w(size_t off_) const { return (const T *)(weights + off_); }
+};
+
+namespace {
+
+LnParams ln_of(const hv_model *m, size_t g, size_t b, int xs, int gs, int bs, int os) {
+    return make_ln(m->w<int8_t>(g), m->w<int8_t>(b), xs, gs, bs, os);
+}
+
+SelParams bind_sel(const hv_model *m, const SelDev &s) {
+    SelParams p = s.p;
+    p.local_wt = m->w<int8_t>(s.lwt);
+    p.local_b = m->w<int32_t>(s.lb);
+    p.w1t = m->w<int8_t>(s.w1t);
+    p.b1 = m->w<int32_t>(s.b1);
+    p.w2t = m->w<int8_t>(s.w2t);
+    p.b2 = m->w<int32_t>(s.b2);
+    p.w3t = m->w<int8_t>(s.w3t);
+    p.b3 = m->w<int32_t>(s.b3);
+    p.hw1 = m->w<int8_t>(s.hw1);
+    p.hb1 = m->w<int32_t>(s.hb1);
+    p.hw2 = m->w<int8_t>(s.hw2);
+    p.hb2 = m->w<int32_t>(s.hb2);
+    return p;
+}
+
+int ensure_capacity(hv_model *m, int images) {
+    if (images <= m->cap) return HV_OK;
+    if (m->scratch) {
+        cudaFree(m->scratch);
+        m->scratch = nullptr;
+        m->cap = 0;
+    }
+    const size_t rows = (size_t)images * HV_TOKENS;
+    size_t total = 0;
+    auto take = [&](size_t bytes) {
+        size_t o = total;
+        total += (bytes + 255) & ~(size_t)255;
+        return o;
+    };
+    const size_t oX = take(rows * 192), oY = take(rows * 192), oLN = take(rows * 192), oQKV = take(rows * 576),
+                 oCTX = take(rows * 192), oHID = take(rows * 768), oSTAGE = take(rows * 192),
+                 oCLS = take((size_t)images * 192), oOff0 = take((size_t)(images + 1) * 4),
+                 oOff1 = take((size_t)(images + 1) * 4), oCnt = take((size_t)images * 4), oPkg0 = take(images),
+                 oPkg1 = take(images), oWarn = take(((size_t)images + 3) & ~(size_t)3);
+    uint8_t *base = nullptr;
+    if (cudaMalloc(&base, total) != cudaSuccess) return fail(HV_ERR_NOMEM, "cannot allocate %zu bytes of scratch", total);
+    m->scratch = base;
+    m->X = (int8_t *)(base + oX);
+    m->Y = (int8_t *)(base + oY);
+    m->LN = (int8_t *)(base + oLN);
+    m->QKV = (int8_t *)(base + oQKV);
+    m->CTX = (int8_t *)(base + oCTX);
+    m->HID = (int8_t *)(base + oHID);
+    m->STAGE = (int8_t *)(base + oSTAGE);
+    m->CLSLN = (int8_t *)(base + oCLS);
+    m->off[0] = (int32_t *)(base + oOff0);
+    m->off[1] = (int32_t *)(base + oOff1);
+    m->counts = (int32_t *)(base + oCnt);
+    m->pkg[0] = base + oPkg0;
+    m->pkg[1] = base + oPkg1;
+    m->warn = base + oWarn;
+    m->cap = images;
+    return HV_OK;
+}
+
+// ---- small pipeline kernels ----------------------------------------------------
+__global__ void init_batch_kernel(int images, int32_t *off, uint8_t *pkg, uint8_t *warn, int32_t *tc, int tc_stride,
+                                  int8_t *x, const int8_t *cls_row) {
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i <= images; i += gridDim.x * blockDim.x) {
+        off[i] = i * HV_TOKENS;
+        if (i < images) {
+            pkg[i] = 0;
+            if (tc) tc[(size_t)i * tc_stride] = HV_TOKENS;
+        }
+        if (i < ((images + 3) & ~3)) warn[i] = 0;
+    }
+    // CLS rows (row 0 of every image): 12 x 16 bytes each.
+    for (int c = blockIdx.x * blockDim.x + threadIdx.x; c < images * 12; c += gridDim.x * blockDim.x) {
+        const int i = c / 12, ch = c - i * 12;
+        ((int4 *)(x + (size_t)i * HV_TOKENS * 192))[ch] = ((const int4 *)cls_row)[ch];
+    }
+}
+
+__global__ void ckpt_copy_kernel(const int8_t *x, const int32_t *off, int8_t *ckpt, int32_t *ckpt_rows, int slot) {
+    const int i = blockIdx.x;
+    const int a = off[i], n = off[i + 1] - a;
+    const int4 *src = (const int4 *)(x + (size_t)a * 192);
+    int4 *dst = (int4 *)(ckpt + ((size_t)i * HV_CKPT_SLOTS + slot) * HV_TOKENS * 192);
+    for (int c = threadIdx.x; c < n * 12; c += blockDim.x) dst[c] = src[c];
+    if (threadIdx.x == 0) ckpt_rows[(size_t)i * HV_CKPT_SLOTS + slot] = n;
+}
+
+GemmArgs gemm_args(const void *a, int lda, int patch_mode, const int8_t *bt, int n, int k, int m_host,
+                   const int32_t *m_dev, void *out, int ldo) {
+    GemmArgs g;
+    memset(&g, 0, sizeof(g));
+    g.a.ptr = a;
+    g.a.lda = lda;
+    g.a.patch_mode = patch_mode;
+    g.bt = bt;
+    g.n = n;
+    g.k = k;
+    g.m_host = m_host;
+    g.m_dev = m_dev;
+    g.out = out;
+    g.ldo = ldo;
+    return g;
+}
+
+__global__ void copy_rows_kernel(const int32_t *src, int32_t *dst) { *dst = *src; }
+
+// Profiling bracket: begin/end around one launch of `stage` when enabled.
+struct Prof {
+    hv_model *m;
+    int on;
+    Prof(hv_model *m_, int stage, cudaStream_t st) : m(m_), on(0) {
+        if (m->prof_stage == stage && m->prof_n < m->prof_max) {
+            on = 1;
+            cudaEventRecord(m->prof_ev[2 * m->prof_n], st);
+        }
+    }
+    void end(cudaStream_t st, const int32_t *rows_dev, int rows_host) {
+        if (!on) return;
+        cudaEventRecord(m->prof_ev[2 * m->prof_n + 1], st);
+        if (rows_dev) copy_rows_kernel<<<1, 1, 0, st>>>(rows_dev, m->prof_rows + m->prof_n);
+        else cudaMemcpyAsync(m->prof_rows + m->prof_n, &rows_host, 4, cudaMemcpyHostToDevice, st);
+        m->prof_n++;
+    }
+};
+
+// One transformer block over the ragged batch in m->X (in place).
+int run_block(hv_model *m, int b, int images, const int32_t *off, cudaStream_t st) {
+    const BlockDev &d = m->blocks[b];
+    const int rows_max = images * HV_TOKENS;
+    const int32_t *rows_dev = off + images;
+    LnParams ln1 = ln_of(m, d.ln1_g, d.ln1_b, d.ln1_xs, d.ln1_gs, d.ln1_bs, d.ln1_os);
+    LnParams ln2 = ln_of(m, d.ln2_g, d.ln2_b, d.ln2_xs, d.ln2_gs, d.ln2_bs, d.ln2_os);
+    {
+        Prof pr(m, HV_STAGE_LN1, st);
+        CUDA_TRY(launch_layernorm(m->X, m->LN, rows_max, rows_dev, ln1, nullptr, off, images, m->warn, st));
+        pr.end(st, rows_dev, 0);
+    }
+    {
+        Prof pr(m, HV_STAGE_QKV, st);
+        GemmArgs g = gemm_args(m->LN, 192, 0, m->w<int8_t>(d.wqkv), HV_QKV, 192, 0, rows_dev, m->QKV, HV_QKV);
+        g.epi.bias = m->w<int32_t>(d.bqkv);
+        g.epi.shift = d.qkv_shift;
+        g.epi.bits_wide = d.qkv_wide;
+        CUDA_TRY(launch_gemm(g, EPI_I8, 0, rows_max, st));
+        pr.end(st, rows_dev, 0);
+    }
+    {
+        Prof pr(m, HV_STAGE_ATTN, st);
+        CUDA_TRY(launch_attention(m->QKV, off, images, m->CTX, d.attn, st));
+        pr.end(st, rows_dev, 0);
+    }
+    {
+        Prof pr(m, HV_STAGE_PROJ, st);
+        GemmArgs g = gemm_args(m->CTX, 192, 0, m->w<int8_t>(d.wproj), HV_EMBED, 192, 0, rows_dev, m->Y, HV_EMBED);
+        g.epi.bias = m->w<int32_t>(d.bproj);
+        g.epi.shift = d.proj_shift;
+        g.epi.bits_wide = d.proj_wide;
+        g.epi.res = m->X;
+        g.epi.add = d.res1;
+        CUDA_TRY(launch_gemm(g, EPI_I8_RES, 0, rows_max, st));
+        pr.end(st, rows_dev, 0);
+    }
+    {
+        Prof pr(m, HV_STAGE_LN2, st);
+        CUDA_TRY(launch_layernorm(m->Y, m->LN, rows_max, rows_dev, ln2, nullptr, off, images, m->warn, st));
+        pr.end(st, rows_dev, 0);
+    }
+    {
+        Prof pr(m, HV_STAGE_FC1, st);
+        GemmArgs g = gemm_args(m->LN, 192, 0, m->w<int8_t>(d.w1), HV_FFN, 192, 0, rows_dev, m->HID, HV_FFN);
+        g.epi.bias = m->w<int32_t>(d.b1);
+        g.epi.bits_wide = 1;
+        g.epi.gelu_sh_in = d.fc1_sh_in;
+        g.epi.gelu_sh_out = d.fc1_sh_out;
+        CUDA_TRY(launch_gemm(g, EPI_GELU, 0, rows_max, st));
+        pr.end(st, rows_dev, 0);
+    }
+    {
+        Prof pr(m, HV_STAGE_FC2, st);
+        GemmArgs g = gemm_args(m->HID, HV_FFN, 0, m->w<int8_t>(d.w2), HV_EMBED, HV_FFN, 0, rows_dev, m->X, HV_EMBED);
+        g.epi.bias = m->w<int32_t>(d.b2);
+        g.epi.shift = d.fc2_shift;
+        g.epi.bits_wide = d.fc2_wide;
+        g.epi.res = m->Y;
+        g.epi.add = d.res2;
+        CUDA_TRY(launch_gemm(g, EPI_I8_RES, 0, rows_max, st));
+        pr.end(st, rows_dev, 0);
+    }
+    return HV_OK;
+}
+
+int run_patch(hv_model *m, const int8_t *images, int count, int8_t *out, cudaStream_t st) {
+    GemmArgs g = gemm_args(images, 0, 1, m->w<int8_t>(m->patch_wt), HV_EMBED, HV_PATCH_K, count * HV_PATCHES, nullptr,
+                           out, HV_EMBED);
+    g.epi.bias = m->w<int32_t>(m->patch_b);
+    g.epi.shift = m->patch_shift;
+    g.epi.bits_wide = m->patch_wide;
+    g.epi.pos = m->w<int8_t>(m->pos);
+    g.epi.add = m->patch_add;
+    CUDA_TRY(launch_gemm(g, EPI_PATCH, 0, count * HV_PATCHES, st));
+    return HV_OK;
+}
+
+int infer_impl(hv_model *m, const int8_t *d_images, int batch, int32_t *d_logits, int32_t *d_tc,
+               hv_selector_summary *d_summary, uint8_t *d_warnings, int8_t *d_ckpt, int32_t *d_ckpt_rows,
+               cudaStream_t st) {
+    if (batch <= 0) return fail(HV_ERR_VALUE, "batch must be positive");
+    if (!d_images || !d_logits) return fail(HV_ERR_VALUE, "images and logits are required");
+    if (!m->has_patch || !m->has_head) return fail(HV_ERR_STATE, "model has no patch embedding or head");
+    for (int b = 0; b < HV_BLOCKS; ++b)
+        if (!m->has_block[b]) return fail(HV_ERR_STATE, "model has no block %d", b + 1);
+    CUDA_TRY(cudaSetDevice(m->device));
+    int rc = ensure_capacity(m, batch);
+    if (rc) return rc;
+    const int ns = m->used_sel;
+    const int tc_stride = ns + 1;
+    if (d_ckpt_rows) CUDA_TRY(cudaMemsetAsync(d_ckpt_rows, 0, sizeof(int32_t) * (size_t)batch * HV_CKPT_SLOTS, st));
+    int cur = 0;
+    init_batch_kernel<<<std::min(148 * 4, (batch * 12 + 255) / 256 + 1), 256, 0, st>>>(
+        batch, m->off[0], m->pkg[0], m->warn, d_tc, tc_stride, m->X, m->w<int8_t>(m->cls_row));
+    CUDA_TRY(cudaGetLastError());
+    {
+        Prof pr(m, HV_STAGE_PATCH, st);
+        rc = run_patch(m, d_images, batch, m->X, st);
+        if (rc) return rc;
+        pr.end(st, nullptr, batch * HV_PATCHES);
+    }
+    if (d_ckpt) {
+        ckpt_copy_kernel<<<batch, 256, 0, st>>>(m->X, m->off[cur], d_ckpt, d_ckpt_rows, HV_CKPT_PATCH);
+        CUDA_TRY(cudaGetLastError());
+    }
+    int sel_no = 0;
+    for (int b = 0; b < HV_BLOCKS; ++b) {
+        const int si = m->sel_before[b];
+        if (si >= 0) {
+            SelParams sp = bind_sel(m, m->sels[si]);
+            Prof pr(m, HV_STAGE_SELECTOR, st);
+            CUDA_TRY(launch_selector(m->X, m->off[cur], m->pkg[cur], batch, sp, m->STAGE, m->counts, m->pkg[cur ^ 1],
+                                     d_summary ? d_summary + sel_no : nullptr, ns, m->warn, d_tc, tc_stride,
+                                     sel_no + 1, nullptr, st));
+            pr.end(st, m->off[cur] + batch, 0);
+            CUDA_TRY(launch_pack(m->STAGE, m->counts, batch, m->X, m->off[cur ^ 1], st));
+            cur ^= 1;
+            ++sel_no;
+            if (d_ckpt) {
+                ckpt_copy_kernel<<<batch, 256, 0, st>>>(m->X, m->off[cur], d_ckpt, d_ckpt_rows,
+                                                        HV_CKPT_SELECTOR(sel_no));
+                CUDA_TRY(cudaGetLastError());
+            }
+        }
+        rc = run_block(m, b, batch, m->off[cur], st);
+        if (rc) return rc;
+        if (d_ckpt) {
+            ckpt_copy_kernel<<<batch, 256, 0, st>>>(m->X, m->off[cur], d_ckpt, d_ckpt_rows, HV_CKPT_BLOCK(b + 1));
+            CUDA_TRY(cudaGetLastError());
+        }
+    }
+    LnParams fin = ln_of(m, m->fin_g, m->fin_b, m->fin_xs, m->fin_gs, m->fin_bs, m->fin_os);
+    if (d_ckpt) {
+        CUDA_TRY(launch_layernorm(m->X, m->LN, batch * HV_TOKENS, m->off[cur] + batch, fin, nullptr, nullptr, 0,
+                                  nullptr, st));
+        ckpt_copy_kernel<<<batch, 256, 0, st>>>(m->LN, m->off[cur], d_ckpt, d_ckpt_rows, HV_CKPT_FINAL_LN);
+        CUDA_TRY(cudaGetLastError());
+    }
+    CUDA_TRY(launch_layernorm_cls(m->X, m->off[cur], batch, m->CLSLN, fin, m->warn, st));
+    {
+        GemmArgs g = gemm_args(m->CLSLN, 192, 0, m->w<int8_t>(m->head_wt), HV_CLASSES, 192, batch, nullptr, d_logits,
+                               HV_CLASSES);
+        g.epi.bias = m->w<int32_t>(m->head_b);
+        g.epi.shift = m->head_shift;
+        g.epi.bits_wide = 1;
+        Prof pr(m, HV_STAGE_HEAD, st);
+        CUDA_TRY(launch_gemm(g, EPI_I32, 0, batch, st));
+        pr.end(st, nullptr, batch);
+    }
+    if (d_warnings) CUDA_TRY(cudaMemcpyAsync(d_warnings, m->warn, batch, cudaMemcpyDeviceToDevice, st));
+    return HV_OK;
+}
+
+// ---- parameter validation and packing -------------------------------------------
+bool ln_scale_ok(int xs) { return xs >= -32 && xs <= 0; }
+
+int pack_model(hv_model *m, const hv_params *P) {
+    Arena A;
+    const hv_patch_params &pp = P->patch;
+    m->has_patch = pp.weight != nullptr;
+    if (m->has_patch) {
+    if (!pp.bias || !pp.cls || !pp.pos) return fail(HV_ERR_VALUE, "patch parameters missing");
+    m->patch_wt = A.add_t(pp.weight, HV_PATCH_K, HV_EMBED, HV_EMBED);
+    m->patch_b = A.add(pp.bias, HV_EMBED * 4);
+    m->pos = A.add(pp.pos, HV_TOKENS * HV_EMBED);
+    const int src_patch = pp.image_scale_exp + pp.weight_scale_exp;
+    m->patch_shift = pp.activation_scale_exp - src_patch;
+    m->patch_wide = needs_wide(pp.bias, HV_EMBED, HV_PATCH_K);
+    if (!align_ok(pp.activation_scale_exp, pp.pos_scale_exp, pp.tokens_scale_exp) ||
+        !align_ok(pp.cls_scale_exp, pp.pos_scale_exp, pp.tokens_scale_exp))
+        return fail(HV_ERR_VALUE, "patch align-add exponent gap above 54 is not supported");
+    m->patch_add = make_align_add(pp.activation_scale_exp, pp.pos_scale_exp, pp.tokens_scale_exp);
+    int8_t cls_row[HV_EMBED];
+    for (int c = 0; c < HV_EMBED; ++c)
+        cls_row[c] = host_align_add(pp.cls[c], pp.cls_scale_exp, pp.pos[c], pp.pos_scale_exp, pp.tokens_scale_exp);
+    m->cls_row = A.add(cls_row, HV_EMBED);
+    }
+
+    for (int b = 0; b < HV_BLOCKS; ++b) {
+        const hv_block_params &q = P->blocks[b];
+        BlockDev &d = m->blocks[b];
+        m->has_block[b] = q.wqkv != nullptr;
+        if (!m->has_block[b]) continue;
+        if (!q.ln1_gamma || !q.ln1_beta || !q.wqkv || !q.bqkv || !q.wproj || !q.bproj || !q.ln2_gamma ||
+            !q.ln2_beta || !q.w1 || !q.b1 || !q.w2 || !q.b2)
+            return fail(HV_ERR_VALUE, "block %d parameters missing", b + 1);
+        if (!ln_scale_ok(q.x_scale_exp) || !ln_scale_ok(q.ffn_x_scale_exp))
+            return fail(HV_ERR_VALUE, "layernorm input scale must be in [-32, 0] (block %d)", b + 1);
+        d.ln1_g = A.add(q.ln1_gamma, 192);
+        d.ln1_b = A.add(q.ln1_beta, 192);
+        d.wqkv = A.add_t(q.wqkv, 192, HV_QKV, HV_QKV);
+        d.bqkv = A.add(q.bqkv, HV_QKV * 4);
+        d.wproj = A.add_t(q.wproj, 192, 192, 192);
+        d.bproj = A.add(q.bproj, 192 * 4);
+        d.ln2_g = A.add(q.ln2_gamma, 192);
+        d.ln2_b = A.add(q.ln2_beta, 192);
+        d.w1 = A.add_t(q.w1, 192, HV_FFN, HV_FFN);
+        d.b1 = A.add(q.b1, HV_FFN * 4);
+        d.w2 = A.add_t(q.w2, HV_FFN, 192, 192);
+        d.b2 = A.add(q.b2, 192 * 4);
+        d.ln1_xs = q.x_scale_exp;
+        d.ln1_gs = q.gamma1_scale_exp;
+        d.ln1_bs = q.beta1_scale_exp;
+        d.ln1_os = q.ln1_out_scale_exp;
+        d.ln2_xs = q.ffn_x_scale_exp;
+        d.ln2_gs = q.gamma2_scale_exp;
+        d.ln2_bs = q.beta2_scale_exp;
+        d.ln2_os = q.ln2_out_scale_exp;
+        d.qkv_shift = q.qkv_out_scale_exp - (q.ln1_out_scale_exp + q.wqkv_scale_exp);
+        d.qkv_wide = needs_wide(q.bqkv, HV_QKV, 192);
+        d.proj_shift = q.msa_out_scale_exp - (q.context_out_scale_exp + q.wproj_scale_exp);
+        d.proj_wide = needs_wide(q.bproj, 192, 192);
+        d.fc1_sh_in = -16 - (q.ln2_out_scale_exp + q.w1_scale_exp);
+        d.fc1_sh_out = q.hidden_out_scale_exp + 16;
+        d.fc2_shift = q.ffn_out_scale_exp - (q.hidden_out_scale_exp + q.w2_scale_exp);
+        d.fc2_wide = needs_wide(q.b2, 192, HV_FFN);
+        if (!align_ok(q.x_scale_exp, q.msa_out_scale_exp, q.ffn_x_scale_exp) ||
+            !align_ok(q.ffn_x_scale_exp, q.ffn_out_scale_exp, q.out_scale_exp))
+            return fail(HV_ERR_VALUE, "residual exponent gap above 54 is not supported (block %d)", b + 1);
+        d.res1 = make_align_add(q.x_scale_exp, q.msa_out_scale_exp, q.ffn_x_scale_exp);
+        d.res2 = make_align_add(q.ffn_x_scale_exp, q.ffn_out_scale_exp, q.out_scale_exp);
+        d.attn.score_shift = q.score_scale_exp - 2 * q.qkv_out_scale_exp;
+        d.attn.q16_shift = -(q.score_scale_exp + 13);
+        d.attn.ctx_shift = q.context_out_scale_exp - (q.prob_scale_exp + q.qkv_out_scale_exp);
+    }
+    m->has_head = P->head_w != nullptr;
+    if (m->has_head && !ln_scale_ok(P->blocks[HV_BLOCKS - 1].out_scale_exp))
+        return fail(HV_ERR_VALUE, "layernorm input scale must be in [-32, 0] (final LN)");
+
+    if (P->num_selectors < 0 || P->num_selectors > HV_MAX_SELECTORS)
+        return fail(HV_ERR_VALUE, "num_selectors out of range");
+    m->used_sel = 0;
+    for (int b = 0; b < HV_BLOCKS; ++b) {
+        m->sel_before[b] = P->selector_before[b];
+        if (m->sel_before[b] >= P->num_selectors) return fail(HV_ERR_VALUE, "selector index out of range");
+        if (m->sel_before[b] >= 0) m->used_sel++;
+    }
+    m->num_sel = P->num_selectors;
+    for (int s = 0; s < P->num_selectors; ++s) {
+        const hv_selector_params &q = P->selectors[s];
+        SelDev &d = m->sels[s];
+        if (!q.local_w || !q.local_b || !q.score_w1 || !q.score_b1 || !q.score_w2 || !q.score_b2 || !q.score_w3 ||
+            !q.score_b3 || !q.hw_w1 || !q.hw_b1 || !q.hw_w2 || !q.hw_b2)
+            return fail(HV_ERR_VALUE, "selector %d parameters missing", s + 1);
+        std::vector<int8_t> t(3 * 32 * 64);
+        for (int h = 0; h < 3; ++h)
+            for (int k = 0; k < 64; ++k)
+                for (int j = 0; j < 32; ++j) t[(h * 32 + j) * 64 + k] = q.local_w[(h * 64 + k) * 32 + j];
+        d.lwt = A.add(t.data(), t.size());
+        for (int h = 0; h < 3; ++h)
+            for (int k = 0; k < 64; ++k)
+                for (int j = 0; j < 32; ++j) t[(h * 32 + j) * 64 + k] = q.score_w1[(h * 64 + k) * 32 + j];
+        d.w1t = A.add(t.data(), t.size());
+        std::vector<int8_t> t2(3 * 16 * 32);
+        for (int h = 0; h < 3; ++h)
+            for (int j = 0; j < 32; ++j)
+                for (int mm = 0; mm < 16; ++mm) t2[(h * 16 + mm) * 32 + j] = q.score_w2[(h * 32 + j) * 16 + mm];
+        d.w2t = A.add(t2.data(), t2.size());
+        std::vector<int8_t> t3(3 * 2 * 16);
+        for (int h = 0; h < 3; ++h)
+            for (int mm = 0; mm < 16; ++mm)
+                for (int o = 0; o < 2; ++o) t3[(h * 2 + o) * 16 + mm] = q.score_w3[(h * 16 + mm) * 2 + o];
+        d.w3t = A.add(t3.data(), t3.size());
+        d.lb = A.add(q.local_b, 96 * 4);
+        d.b1 = A.add(q.score_b1, 96 * 4);
+        d.b2 = A.add(q.score_b2, 48 * 4);
+        d.b3 = A.add(q.score_b3, 6 * 4);
+        d.hw1 = A.add(q.hw_w1, 9);
+        d.hb1 = A.add(q.hw_b1, 12);
+        d.hw2 = A.add(q.hw_w2, 9);
+        d.hb2 = A.add(q.hw_b2, 12);
+        SelParams &p = d.p;
+        memset(&p, 0, sizeof(p));
+        p.local_sh_in = -16 - (q.in_scale_exp + q.local_w_scale_exp);
+        p.local_sh_out = q.local_out_scale_exp + 16;
+        p.h1_sh_in = -16 - (q.concat_out_scale_exp + q.score_w1_scale_exp);
+        p.h1_sh_out = q.h1_out_scale_exp + 16;
+        p.h2_sh_in = -16 - (q.h1_out_scale_exp + q.score_w2_scale_exp);
+        p.h2_sh_out = q.h2_out_scale_exp + 16;
+        p.logit_shift = q.logits_out_scale_exp - (q.h2_out_scale_exp + q.score_w3_scale_exp);
+        p.logit_q16_shift = -16 - q.logits_out_scale_exp;
+        p.hw_sh_in = -16 - (q.stats_out_scale_exp + q.hw_w1_scale_exp);
+        p.hw_sh_out = q.hw_hidden_out_scale_exp + 16;
+        p.hw_q16_shift = -16 - (q.hw_hidden_out_scale_exp + q.hw_w2_scale_exp);
+    }
+    if (m->has_head) {
+    if (!P->final_gamma || !P->final_beta || !P->head_b) return fail(HV_ERR_VALUE, "head parameters missing");
+    m->fin_g = A.add(P->final_gamma, 192);
+    m->fin_b = A.add(P->final_beta, 192);
+    m->fin_xs = P->blocks[HV_BLOCKS - 1].out_scale_exp;
+    m->fin_gs = P->final_gamma_scale_exp;
+    m->fin_bs = P->final_beta_scale_exp;
+    m->fin_os = P->final_ln_out_scale_exp;
+    m->head_wt = A.add_t(P->head_w, 192, HV_CLASSES, 1024);
+    m->head_b = A.add(P->head_b, HV_CLASSES * 4);
+    m->head_shift = HV_LOGIT_SCALE_EXP - (P->final_ln_out_scale_exp + P->head_w_scale_exp);
+    }
+    if (A.host.empty()) A.add(nullptr, 256);
+
+    CUDA_TRY(cudaMalloc(&m->weights, A.host.size()));
+    m->weights_bytes = A.host.size();
+    CUDA_TRY(cudaMemcpy(m->weights, A.host.data(), A.host.size(), cudaMemcpyHostToDevice));
+    return HV_OK;
+}
+
+}  // namespace
+
+// =============================================================================
+// C ABI
+// =============================================================================
+extern "C" {
+
+const char *hv_version(void) { return "heatvit_b200 0.1 (sm_100a)"; }
+
+const char *hv_last_error(void) { return g_err; }
+
+int hv_model_create(const hv_params *params, int device, hv_model **out) {
+    if (!params || !out) return fail(HV_ERR_VALUE, "null argument");
+    *out = nullptr;
+    CUDA_TRY(cudaSetDevice(device));
+    hv_model *m = new hv_model();
+    m->device = device;
+    int rc = pack_model(m, params);
+    if (rc) {
+        hv_model_destroy(m);
+        return rc;
+    }
+    *out = m;
+    return HV_OK;
+}
+
+int hv_model_destroy(hv_model *m) {
+    if (!m) return HV_OK;
+    cudaSetDevice(m->device);
+    if (m->weights) cudaFree(m->weights);
+    if (m->scratch) cudaFree(m->scratch);
+    for (int i = 0; i < 2; ++i) {
+        if (m->himg[i]) cudaFree(m->himg[i]);
+        if (m->ev_in[i]) cudaEventDestroy(m->ev_in[i]);
+        if (m->ev_done[i]) cudaEventDestroy(m->ev_done[i]);
+    }
+    if (m->hlogits) cudaFree(m->hlogits);
+    if (m->htc) cudaFree(m->htc);
+    if (m->hsum) cudaFree(m->hsum);
+    if (m->hwarn) cudaFree(m->hwarn);
+    for (auto e : m->prof_ev) cudaEventDestroy(e);
+    if (m->prof_rows) cudaFree(m->prof_rows);
+    if (m->copy_stream) cudaStreamDestroy(m->copy_stream);
+    if (m->compute_stream) cudaStreamDestroy(m->compute_stream);
+    delete m;
+    return HV_OK;
+}
+
+int hv_infer_batch(hv_model *m, const int8_t *d_images, int batch, int32_t *d_logits, int32_t *d_token_counts,
+                   hv_selector_summary *d_summary, uint8_t *d_warnings, void *stream) {
+    if (!m) return fail(HV_ERR_VALUE, "null model");
+    return infer_impl(m, d_images, batch, d_logits, d_token_counts, d_summary, d_warnings, nullptr, nullptr,
+                      (cudaStream_t)stream);
+}
+
+int hv_infer_batch_checkpoints(hv_model *m, const int8_t *d_images, int batch, int32_t *d_logits,
+                               int32_t *d_token_counts, hv_selector_summary *d_summary, uint8_t *d_warnings,
+                               int8_t *d_ckpt, int32_t *d_ckpt_rows, void *stream) {
+    if (!m) return fail(HV_ERR_VALUE, "null model");
+    if (!d_ckpt || !d_ckpt_rows) return fail(HV_ERR_VALUE, "checkpoint buffers are required");
+    return infer_impl(m, d_images, batch, d_logits, d_token_counts, d_summary, d_warnings, d_ckpt, d_ckpt_rows,
+                      (cudaStream_t)stream);
+}
+
+int hv_infer_host(hv_model *m, const int8_t *h_images, int batch, int32_t *h_logits, int32_t *h_token_counts,
+                  hv_selector_summary *h_summary, uint8_t *h_warnings) {
+    if (!m) return fail(HV_ERR_VALUE, "null model");
+    if (batch <= 0 || !h_images || !h_logits) return fail(HV_ERR_VALUE, "bad arguments");
+    CUDA_TRY(cudaSetDevice(m->device));
+    const int chunk = std::min(batch, 256);
+    const int ns = m->used_sel;
+    if (!m->copy_stream) {
+        CUDA_TRY(cudaStreamCreateWithFlags(&m->copy_stream, cudaStreamNonBlocking));
+        CUDA_TRY(cudaStreamCreateWithFlags(&m->compute_stream, cudaStreamNonBlocking));
+        for (int i = 0; i < 2; ++i) {
+            CUDA_TRY(cudaEventCreateWithFlags(&m->ev_in[i], cudaEventDisableTiming));
+            CUDA_TRY(cudaEventCreateWithFlags(&m->ev_done[i], cudaEventDisableTiming));
+        }
+    }
+    if (chunk > m->host_cap) {
+        for (int i = 0; i < 2; ++i)
+            if (m->himg[i]) cudaFree(m->himg[i]);
+        if (m->hlogits) cudaFree(m->hlogits);
+        if (m->htc) cudaFree(m->htc);
+        if (m->hsum) cudaFree(m->hsum);
+        if (m->hwarn) cudaFree(m->hwarn);
+        for (int i = 0; i < 2; ++i) CUDA_TRY(cudaMalloc(&m->himg[i], (size_t)chunk * HV_IMAGE_BYTES));
+        CUDA_TRY(cudaMalloc(&m->hlogits, (size_t)chunk * HV_CLASSES * 4 * 2));
+        CUDA_TRY(cudaMalloc(&m->htc, (size_t)chunk * (HV_MAX_SELECTORS + 1) * 4 * 2));
+        CUDA_TRY(cudaMalloc(&m->hsum, (size_t)chunk * HV_MAX_SELECTORS * sizeof(hv_selector_summary) * 2));
+        CUDA_TRY(cudaMalloc(&m->hwarn, (size_t)chunk * 2));
+        m->host_cap = chunk;
+    }
+    int rc = ensure_capacity(m, chunk);
+    if (rc) return rc;
+    const int nchunks = (batch + chunk - 1) / chunk;
+    for (int c = 0; c < nchunks; ++c) {
+        const int buf = c & 1;
+        const int first = c * chunk, cnt = std::min(chunk, batch - first);
+        // The copy into buffer `buf` must wait until the compute two chunks back released it.
+        if (c >= 2) CUDA_TRY(cudaStreamWaitEvent(m->copy_stream, m->ev_done[buf], 0));
+        CUDA_TRY(cudaMemcpyAsync(m->himg[buf], h_images + (size_t)first * HV_IMAGE_BYTES, (size_t)cnt * HV_IMAGE_BYTES,
+                                 cudaMemcpyHostToDevice, m->copy_stream));
+        CUDA_TRY(cudaEventRecord(m->ev_in[buf], m->copy_stream));
+        CUDA_TRY(cudaStreamWaitEvent(m->compute_stream, m->ev_in[buf], 0));
+        int32_t *dl = m->hlogits + (size_t)buf * m->host_cap * HV_CLASSES;
+        int32_t *dtc = m->htc + (size_t)buf * m->host_cap * (HV_MAX_SELECTORS + 1);
+        hv_selector_summary *dsum = m->hsum + (size_t)buf * m->host_cap * HV_MAX_SELECTORS;
+        uint8_t *dw = m->hwarn + (size_t)buf * m->host_cap;
+        rc = infer_impl(m, m->himg[buf], cnt, dl, h_token_counts ? dtc : nullptr, h_summary ? dsum : nullptr,
+                        h_warnings ? dw : nullptr, nullptr, nullptr, m->compute_stream);
+        if (rc) return rc;
+        CUDA_TRY(cudaEventRecord(m->ev_done[buf], m->compute_stream));
+        CUDA_TRY(cudaMemcpyAsync(h_logits + (size_t)first * HV_CLASSES, dl, (size_t)cnt * HV_CLASSES * 4,
+                                 cudaMemcpyDeviceToHost, m->compute_stream));
+        if (h_token_counts)
+            CUDA_TRY(cudaMemcpyAsync(h_token_counts + (size_t)first * (ns + 1), dtc, (size_t)cnt * (ns + 1) * 4,
+                                     cudaMemcpyDeviceToHost, m->compute_stream));
+        if (h_summary && ns)
+            CUDA_TRY(cudaMemcpyAsync(h_summary + (size_t)first * ns, dsum, (size_t)cnt * ns * sizeof(hv_selector_summary),
+                                     cudaMemcpyDeviceToHost, m->compute_stream));
+        if (h_warnings)
+            CUDA_TRY(cudaMemcpyAsync(h_warnings + first, dw, cnt, cudaMemcpyDeviceToHost, m->compute_stream));
+    }
+    CUDA_TRY(cudaStreamSynchronize(m->compute_stream));
+    return HV_OK;
+}
+
+int hv_profile_start(hv_model *m, int stage, int max_launches) {
+    if (!m) return fail(HV_ERR_VALUE, "null model");
+    if (max_launches < 0) return fail(HV_ERR_VALUE, "negative launch count");
+    CUDA_TRY(cudaSetDevice(m->device));
+    if ((int)m->prof_ev.size() < 2 * max_launches) {
+        while ((int)m->prof_ev.size() < 2 * max_launches) {
+            cudaEvent_t e;
+            CUDA_TRY(cudaEventCreate(&e));
+            m->prof_ev.push_back(e);
+        }
+        if (m->prof_rows) cudaFree(m->prof_rows);
+        m->prof_rows = nullptr;
+        CUDA_TRY(cudaMalloc(&m->prof_rows, sizeof(int32_t) * (size_t)std::max(1, max_launches)));
+    }
+    if (!m->prof_rows) CUDA_TRY(cudaMalloc(&m->prof_rows, sizeof(int32_t) * (size_t)std::max(1, max_launches)));
+    m->prof_stage = stage;
+    m->prof_max = max_launches;
+    m->prof_n = 0;
+    return HV_OK;
+}
+
+int hv_profile_stop(hv_model *m, int *launches, double *total_ms, long long *rows) {
+    if (!m) return fail(HV_ERR_VALUE, "null model");
+    CUDA_TRY(cudaSetDevice(m->device));
+    const int n = m->prof_n;
+    double tot = 0.0;
+    long long rsum = 0;
+    if (n > 0) {
+        CUDA_TRY(cudaEventSynchronize(m->prof_ev[2 * n - 1]));
+        for (int i = 0; i < n; ++i) {
+            float ms = 0.f;
+            CUDA_TRY(cudaEventElapsedTime(&ms, m->prof_ev[2 * i], m->prof_ev[2 * i + 1]));
+            tot += ms;
+        }
+        std::vector<int32_t> r(n);
+        CUDA_TRY(cudaMemcpy(r.data(), m->prof_rows, sizeof(int32_t) * n, cudaMemcpyDeviceToHost));
+        for (int i = 0; i < n; ++i) rsum += r[i];
+    }
+    m->prof_stage = 0;
+    m->prof_n = 0;
+    if (launches) *launches = n;
+    if (total_ms) *total_ms = tot;
+    if (rows) *rows = rsum;
+    return HV_OK;
+}
+
+// ---- per-operator entry points ------------------------------------------------------
+
+int hv_gemm_i8_acc(const void *d_a, const int8_t *d_b, const int32_t *d_bias, int m, int n, int k, int transpose_b,
+                   int a_unsigned, int64_t *d_acc, void *stream);
+
+namespace {
+__global__ void pad_a_kernel(const uint8_t *a, int m, int k, int kp, uint8_t *out) {
+    const int64_t total = (int64_t)m * kp;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+        const int r = (int)(i / kp), c = (int)(i - (int64_t)r * kp);
+        out[i] = c < k ? a[(size_t)r * k + c] : 0;
+    }
+}
+// Bt[np][kp]: from b [k][n] (transpose_b = 0) or [n][k] (transpose_b = 1).
+__global__ void pad_b_kernel(const int8_t *b, int n, int k, int transpose_b, int np, int kp, int8_t *out) {
+    const int64_t total = (int64_t)np * kp;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+        const int r = (int)(i / kp), c = (int)(i - (int64_t)r * kp);
+        int8_t v = 0;
+        if (r < n && c < k) v = transpose_b ? b[(size_t)r * k + c] : b[(size_t)c * n + r];
+        out[i] = v;
+    }
+}
+}  // namespace
+
+int hv_gemm_i8_acc(const void *d_a, const int8_t *d_b, const int32_t *d_bias, int m, int n, int k, int transpose_b,
+                   int a_unsigned, int64_t *d_acc, void *stream) {
+    if (m < 0 || n < 0 || k < 0) return fail(HV_ERR_VALUE, "negative dimension");
+    if (m == 0 || n == 0) return HV_OK;
+    if (!d_a || !d_b || !d_acc) return fail(HV_ERR_VALUE, "null buffer");
+    if (k > (a_unsigned ? 65793 : 131071))
+        return fail(HV_ERR_VALUE, "k=%d can overflow the int32 accumulator; not supported", k);
+    cudaStream_t st = (cudaStream_t)stream;
+    const int kp = std::max(64, (k + 63) / 64 * 64), np = (n + 63) / 64 * 64;
+    uint8_t *ap = nullptr;
+    int8_t *bp = nullptr;
+    CUDA_TRY(cudaMalloc(&ap, (size_t)m * kp + 16));
+    if (cudaMalloc(&bp, (size_t)np * kp) != cudaSuccess) {
+        cudaFree(ap);
+        return fail(HV_ERR_NOMEM, "cannot allocate padded B");
+    }
+    int rc = HV_OK;
+    pad_a_kernel<<<148 * 4, 256, 0, st>>>((const uint8_t *)d_a, m, k, kp, ap);
+    pad_b_kernel<<<148 * 4, 256, 0, st>>>(d_b, n, k, transpose_b, np, kp, bp);
+    GemmArgs g = gemm_args(ap, kp, 0, bp, n, kp, m, nullptr, d_acc, n);
+    g.epi.bias = d_bias;
+    g.epi.bits_wide = 1;
+    cudaError_t e = launch_gemm(g, EPI_ACC64, a_unsigned, m, st);
+    if (e != cudaSuccess) rc = fail(HV_ERR_CUDA, "gemm launch: %s", cudaGetErrorString(e));
+    cudaStreamSynchronize(st);
+    cudaFree(ap);
+    cudaFree(bp);
+    return rc;
+}
+
+int hv_gemm_i8(const void *d_a, const int8_t *d_b, const int32_t *d_bias, int m, int n, int k, int transpose_b,
+               int a_unsigned, int src_exp, int dst_exp, int out_bits, void *d_out, void *stream) {
+    if (out_bits != 8 && out_bits != 32) return fail(HV_ERR_VALUE, "output_bits must be 8 or 32");
+    if (m == 0 || n == 0) return HV_OK;
+    int64_t *acc = nullptr;
+    CUDA_TRY(cudaMalloc(&acc, (size_t)m * n * 8));
+    int rc = hv_gemm_i8_acc(d_a, d_b, d_bias, m, n, k, transpose_b, a_unsigned, acc, stream);
+    if (!rc) {
+        cudaError_t e = launch_writeback(acc, (int64_t)m * n, dst_exp - src_exp, out_bits, d_out, (cudaStream_t)stream);
+        if (e != cudaSuccess) rc = fail(HV_ERR_CUDA, "writeback: %s", cudaGetErrorString(e));
+        cudaStreamSynchronize((cudaStream_t)stream);
+    }
+    cudaFree(acc);
+    return rc;
+}
+
+int hv_writeback_i64(const int64_t *d_acc, int64_t count, int src_exp, int dst_exp, int out_bits, void *d_out,
+                     void *stream) {
+    if (out_bits != 8 && out_bits != 24 && out_bits != 32) return fail(HV_ERR_VALUE, "output_bits must be 8 or 32");
+    if (count < 0) return fail(HV_ERR_VALUE, "negative count");
+    CUDA_TRY(launch_writeback(d_acc, count, dst_exp - src_exp, out_bits, d_out, (cudaStream_t)stream));
+    return HV_OK;
+}
+
+int hv_align_add_i8(const int8_t *d_a, int a_exp, const int8_t *d_b, int b_exp, int out_exp, int64_t count,
+                    int8_t *d_out, void *stream) {
+    if (count < 0) return fail(HV_ERR_VALUE, "negative count");
+    if (!align_ok(a_exp, b_exp, out_exp)) return fail(HV_ERR_VALUE, "align-add exponent gap above 54 is not supported");
+    CUDA_TRY(launch_align_add(d_a, d_b, make_align_add(a_exp, b_exp, out_exp), count, d_out, (cudaStream_t)stream));
+    return HV_OK;
+}
+
+int hv_layernorm_i8(const int8_t *d_x, const int8_t *d_gamma, const int8_t *d_beta, int rows, int x_scale,
+                    int gamma_scale, int beta_scale, int out_scale, int8_t *d_out, uint8_t *d_negvar, void *stream) {
+    if (x_scale < -32 || x_scale > 0) return fail(HV_ERR_VALUE, "layernorm input scale must be in [-32, 0]");
+    if (rows < 0) return fail(HV_ERR_VALUE, "negative row count");
+    const int common = std::min(gamma_scale - 16, beta_scale);
+    if (gamma_scale - 16 - common > 100 || beta_scale - common > 100)
+        return fail(HV_ERR_VALUE, "gamma/beta exponent gap above 100 is not supported");
+    LnParams p = make_ln(d_gamma, d_beta, x_scale, gamma_scale, beta_scale, out_scale);
+    CUDA_TRY(launch_layernorm(d_x, d_out, rows, nullptr, p, d_negvar, nullptr, 0, nullptr, (cudaStream_t)stream));
+    return HV_OK;
+}
+
+int hv_softmax_rows(const int32_t *d_x, const int32_t *d_row_offsets, int rows, int mode, void *d_out, void *stream) {
+    if (mode != 0 && mode != 1) return fail(HV_ERR_VALUE, "mode must be 0 (attention) or 1 (selector)");
+    CUDA_TRY(launch_softmax_rows(d_x, d_row_offsets, rows, mode, d_out, (cudaStream_t)stream));
+    return HV_OK;
+}
+
+int hv_shiftgelu(const int32_t *d_x, int64_t count, int32_t *d_out, void *stream) {
+    CUDA_TRY(launch_gelu(d_x, count, d_out, (cudaStream_t)stream));
+    return HV_OK;
+}
+
+int hv_plan_sigmoid(const int32_t *d_x, int64_t count, int32_t *d_out, void *stream) {
+    CUDA_TRY(launch_plan(d_x, count, d_out, (cudaStream_t)stream));
+    return HV_OK;
+}
+
+int hv_gelu_requant(const int32_t *d_acc, int64_t count, int src_exp, int dst_exp, int8_t *d_out, void *stream) {
+    CUDA_TRY(launch_gelu_requant(d_acc, count, -16 - src_exp, dst_exp + 16, d_out, (cudaStream_t)stream));
+    return HV_OK;
+}
+
+int hv_transformer_block(hv_model *m, int block_index, const int8_t *d_x, const int32_t *d_offsets, int images,
+                         int total_rows, int8_t *d_z, void *stream) {
+    if (!m) return fail(HV_ERR_VALUE, "null model");
+    if (block_index < 0 || block_index >= HV_BLOCKS) return fail(HV_ERR_VALUE, "block index out of range");
+    if (!m->has_block[block_index]) return fail(HV_ERR_STATE, "model has no block %d", block_index + 1);
+    if (images <= 0 || total_rows < 0 || total_rows > images * HV_TOKENS)
+        return fail(HV_ERR_VALUE, "bad ragged batch (each image holds at most 197 tokens)");
+    CUDA_TRY(cudaSetDevice(m->device));
+    int rc = ensure_capacity(m, images);
+    if (rc) return rc;
+    cudaStream_t st = (cudaStream_t)stream;
+    CUDA_TRY(cudaMemcpyAsync(m->X, d_x, (size_t)total_rows * 192, cudaMemcpyDeviceToDevice, st));
+    CUDA_TRY(cudaMemsetAsync(m->warn, 0, ((size_t)images + 3) & ~(size_t)3, st));
+    rc = run_block(m, block_index, images, d_offsets, st);
+    if (rc) return rc;
+    CUDA_TRY(cudaMemcpyAsync(d_z, m->X, (size_t)total_rows * 192, cudaMemcpyDeviceToDevice, st));
+    return HV_OK;
+}
+
+int hv_patch_embedding(hv_model *m, const int8_t *d_images, int batch, int8_t *d_tokens, void *stream) {
+    if (!m) return fail(HV_ERR_VALUE, "null model");
+    if (batch <= 0) return fail(HV_ERR_VALUE, "batch must be positive");
+    if (!m->has_patch) return fail(HV_ERR_STATE, "model has no patch embedding");
+    CUDA_TRY(cudaSetDevice(m->device));
+    int rc = ensure_capacity(m, batch);
+    if (rc) return rc;
+    cudaStream_t st = (cudaStream_t)stream;
+    init_batch_kernel<<<std::min(148 * 4, (batch * 12 + 255) / 256 + 1), 256, 0, st>>>(
+        batch, m->off[0], m->pkg[0], m->warn, nullptr, 0, d_tokens, m->w<int8_t>(m->cls_row));
+    CUDA_TRY(cudaGetLastError());
+    return run_patch(m, d_images, batch, d_tokens, st);
+}
+
+int hv_token_selector(hv_model *m, int selector_index, const int8_t *d_x, const int32_t *d_offsets,
+                      const uint8_t *d_pkg_in, int images, int8_t *d_y, int32_t *d_offsets_out, uint8_t *d_pkg_out,
+                      hv_selector_summary *d_summary, int32_t *d_fused, int32_t *d_head_scores,
+                      int32_t *d_head_weights, int8_t *d_local, int8_t *d_global, int8_t *d_stats, void *stream) {
+    if (!m) return fail(HV_ERR_VALUE, "null model");
+    if (selector_index < 0 || selector_index >= m->num_sel) return fail(HV_ERR_VALUE, "selector index out of range");
+    if (images <= 0) return fail(HV_ERR_VALUE, "images must be positive");
+    CUDA_TRY(cudaSetDevice(m->device));
+    int rc = ensure_capacity(m, images);
+    if (rc) return rc;
+    cudaStream_t st = (cudaStream_t)stream;
+    CUDA_TRY(cudaMemsetAsync(m->warn, 0, ((size_t)images + 3) & ~(size_t)3, st));
+    SelDebug dbg{d_fused, d_head_scores, d_head_weights, d_local, d_global, d_stats};
+    SelParams sp = bind_sel(m, m->sels[selector_index]);
+    CUDA_TRY(launch_selector(d_x, d_offsets, d_pkg_in, images, sp, m->STAGE, m->counts, d_pkg_out, d_summary, 1,
+                             m->warn, nullptr, 0, 0, &dbg, st));
+    CUDA_TRY(launch_pack(m->STAGE, m->counts, images, d_y, d_offsets_out, st));
+    return HV_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,394 @@
+// hv_selector.cu — fused per-image token selector and ragged compaction.
+//
+// One CTA per image restates selector.py:503-563 end to end:
+//   local MLP (253-270) -> global mean (273-289) -> score MLP with the global
+//   half of layer 1 computed once per image (concat, 292-355) -> keep scores
+//   via the 2-way selector softmax -> head stats (358-367) -> head-weight MLP
+//   with PLAN (370-389) -> head fuse with its zero-denominator fallback
+//   (392-418) -> inclusive 0.5 threshold, stable compaction and the package
+//   token with its own zero-denominator fallback (421-500).
+// Splitting layer 1 as [local ‖ global]·W1 = local·W1[0:32] + global·W1[32:64]
+// is exact in integer arithmetic.
+//
+// The output goes to a per-image staging slot (stride 197 rows); the pack
+// kernel then prefix-sums the new counts and writes the packed ragged layout
+// that every later kernel consumes.
+#include "hv_internal.cuh"
+
+namespace hv {
+
+namespace {
+
+constexpr int THREADS = 256;
+constexpr int MAXC = 196;
+constexpr int LSTR = 36;   // local row stride (32 data bytes + 4 pad)
+constexpr int WSTR = 68;   // transposed 64-wide weight row stride
+constexpr int W2STR = 36;  // transposed 32-wide weight row stride
+
+constexpr int OFF_TOK = 0;
+constexpr int SZ_TOK = 197 * 192;
+constexpr int OFF_LOCAL = OFF_TOK + SZ_TOK;
+constexpr int SZ_LOCAL = 3 * MAXC * LSTR;
+constexpr int OFF_LWT = OFF_LOCAL + SZ_LOCAL;
+constexpr int SZ_LWT = 3 * 32 * WSTR;
+constexpr int OFF_W1T = OFF_LWT + SZ_LWT;
+constexpr int SZ_W1T = 3 * 32 * WSTR;
+constexpr int OFF_W2T = OFF_W1T + SZ_W1T;
+constexpr int SZ_W2T = 3 * 16 * W2STR;
+constexpr int OFF_W3T = OFF_W2T + SZ_W2T;
+constexpr int SZ_W3T = 3 * 2 * 16;
+constexpr int OFF_G1 = (OFF_W3T + SZ_W3T + 15) & ~15;
+constexpr int SZ_G1 = 3 * 32 * 8;
+constexpr int OFF_GLOB = OFF_G1 + SZ_G1;
+constexpr int SZ_GLOB = 3 * 32;
+constexpr int OFF_HS = OFF_GLOB + SZ_GLOB;
+constexpr int SZ_HS = 3 * MAXC * 4;
+constexpr int OFF_HW = OFF_HS + SZ_HS;
+constexpr int SZ_HW = 3 * MAXC * 4;
+constexpr int OFF_FUSED = OFF_HW + SZ_HW;
+constexpr int SZ_FUSED = MAXC * 4;
+constexpr int OFF_KIDX = OFF_FUSED + SZ_FUSED;
+constexpr int SZ_KIDX = MAXC * 4;
+constexpr int OFF_FLAGS = OFF_KIDX + SZ_KIDX;
+constexpr int SZ_FLAGS = MAXC;  // bit0 keep, bit1 participant
+constexpr int OFF_STATS = (OFF_FLAGS + SZ_FLAGS + 15) & ~15;
+constexpr int SZ_STATS = MAXC * 3;
+constexpr int OFF_MISC = (OFF_STATS + SZ_STATS + 15) & ~15;
+constexpr int SZ_MISC = 64;
+constexpr int SMEM_BYTES = OFF_MISC + SZ_MISC;
+
+__device__ __forceinline__ int32_t sat_q016(int64_t v) { return (int32_t)(v < 0 ? 0 : (v > 65536 ? 65536 : v)); }
+
+// Keep score of one candidate-head: softmax_selector([q0, q1])[1]
+// (selector.py:345-354, nonlinear.py:109-127).
+__device__ __forceinline__ int32_t keep_score(int32_t q0, int32_t q1) {
+    const int32_t mx = max(q0, q1);
+    const uint32_t e0 = softmax_exp_q16(q0 - mx), e1 = softmax_exp_q16(q1 - mx);
+    const uint64_t rc = softmax_recip((uint64_t)e0 + e1);
+    const uint32_t r1 = softmax_ratio(e1, rc);
+    return (int32_t)(r1 < 65536u ? r1 : 65536u);
+}
+
+__global__ void __launch_bounds__(THREADS) selector_kernel(
+    const int8_t *__restrict__ x, const int32_t *__restrict__ offsets, const uint8_t *__restrict__ pkg_in,
+    SelParams p, int8_t *__restrict__ stage, int32_t *__restrict__ counts_out, uint8_t *__restrict__ pkg_out,
+    hv_selector_summary *__restrict__ summary, int sum_stride, uint8_t *__restrict__ warn,
+    int32_t *__restrict__ token_counts, int tc_stride, int tc_col, SelDebug dbg) {
+    extern __shared__ __align__(16) uint8_t smem[];
+    int8_t *tok = (int8_t *)(smem + OFF_TOK);
+    int8_t *local = (int8_t *)(smem + OFF_LOCAL);
+    int8_t *lwt = (int8_t *)(smem + OFF_LWT);
+    int8_t *w1t = (int8_t *)(smem + OFF_W1T);
+    int8_t *w2t = (int8_t *)(smem + OFF_W2T);
+    int8_t *w3t = (int8_t *)(smem + OFF_W3T);
+    int64_t *g1 = (int64_t *)(smem + OFF_G1);
+    int8_t *glob = (int8_t *)(smem + OFF_GLOB);
+    int32_t *hs = (int32_t *)(smem + OFF_HS);
+    int32_t *hwt = (int32_t *)(smem + OFF_HW);
+    int32_t *fused = (int32_t *)(smem + OFF_FUSED);
+    int32_t *kidx = (int32_t *)(smem + OFF_KIDX);
+    uint8_t *flags = (uint8_t *)(smem + OFF_FLAGS);
+    int8_t *stats = (int8_t *)(smem + OFF_STATS);
+    int32_t *misc = (int32_t *)(smem + OFF_MISC);  // [0] warn, [1] kept, [2] participants, [4..] scan
+
+    const int img = blockIdx.x, tid = threadIdx.x;
+    const int row0 = offsets[img];
+    const int n = offsets[img + 1] - row0;
+    const int C = n - 1;
+    const int pkg = pkg_in ? (pkg_in[img] != 0) : 0;
+    int8_t *out = stage + (size_t)img * 197 * 192;
+
+    if (tid < 16) misc[tid] = 0;
+    if (C < 1) {  // selector.py:513-514 needs CLS plus a candidate; pass the row through
+        if (tid < 12) ((int4 *)out)[tid] = ((const int4 *)(x + (size_t)row0 * 192))[tid];
+        if (tid == 0) {
+            counts_out[img] = n;
+            if (pkg_out) pkg_out[img] = (uint8_t)pkg;
+        }
+        return;
+    }
+
+    // ---- load tokens and weights ------------------------------------------------
+    for (int c = tid; c < n * 12; c += THREADS) ((int4 *)tok)[c] = ((const int4 *)(x + (size_t)row0 * 192))[c];
+    for (int c = tid; c < 3 * 32 * 16; c += THREADS) {
+        const int row = c >> 4, w = c & 15;
+        *(int32_t *)(lwt + row * WSTR + 4 * w) = ((const int32_t *)p.local_wt)[c];
+        *(int32_t *)(w1t + row * WSTR + 4 * w) = ((const int32_t *)p.w1t)[c];
+    }
+    for (int c = tid; c < 3 * 16 * 8; c += THREADS) {
+        const int row = c >> 3, w = c & 7;
+        *(int32_t *)(w2t + row * W2STR + 4 * w) = ((const int32_t *)p.w2t)[c];
+    }
+    if (tid < 24) ((int32_t *)w3t)[tid] = ((const int32_t *)p.w3t)[tid];
+    __syncthreads();
+
+    // ---- local MLP: local[h][c][j] ------------------------------------------------
+    for (int idx = tid; idx < 3 * C * 32; idx += THREADS) {
+        const int j = idx & 31, hc = idx >> 5;
+        const int h = hc / C, c = hc - h * C;
+        const int32_t *trow = (const int32_t *)(tok + (1 + c) * 192 + 64 * h);
+        const int32_t *wrow = (const int32_t *)(lwt + (h * 32 + j) * WSTR);
+        int32_t acc = 0;
+#pragma unroll
+        for (int w = 0; w < 16; ++w) acc = __dp4a(trow[w], wrow[w], acc);
+        local[(h * MAXC + c) * LSTR + j] =
+            (int8_t)gelu_chain((int64_t)acc + p.local_b[h * 32 + j], p.local_sh_in, p.local_sh_out);
+    }
+    __syncthreads();
+
+    // ---- global mean (selector.py:273-289) -----------------------------------------
+    if (tid < 96) {
+        const int h = tid >> 5, j = tid & 31;
+        int32_t t = 0;
+        for (int c = 0; c < C; ++c) t += local[(h * MAXC + c) * LSTR + j];
+        glob[h * 32 + j] = (int8_t)sat8((int32_t)round_div64(t, C));
+    }
+    __syncthreads();
+    if (tid < 96) {
+        const int h = tid >> 5, j = tid & 31;
+        int32_t acc = 0;
+        const int8_t *wrow = w1t + (h * 32 + j) * WSTR + 32;
+        for (int k = 0; k < 32; ++k) acc += (int32_t)glob[h * 32 + k] * wrow[k];
+        g1[h * 32 + j] = (int64_t)acc + p.b1[h * 32 + j];
+    }
+    __syncthreads();
+
+    // ---- score MLP per (head, candidate) ------------------------------------------
+    for (int it = tid; it < 3 * C; it += THREADS) {
+        const int h = it / C, c = it - h * C;
+        int32_t lw[8];
+#pragma unroll
+        for (int w = 0; w < 8; ++w) lw[w] = *(const int32_t *)(local + (h * MAXC + c) * LSTR + 4 * w);
+        uint32_t h1w[8];
+#pragma unroll
+        for (int jw = 0; jw < 8; ++jw) {
+            uint32_t packed = 0;
+#pragma unroll
+            for (int b = 0; b < 4; ++b) {
+                const int j = jw * 4 + b;
+                const int32_t *wrow = (const int32_t *)(w1t + (h * 32 + j) * WSTR);
+                int32_t acc = 0;
+#pragma unroll
+                for (int w = 0; w < 8; ++w) acc = __dp4a(lw[w], wrow[w], acc);
+                packed |= ((uint32_t)gelu_chain(acc + g1[h * 32 + j], p.h1_sh_in, p.h1_sh_out) & 0xffu) << (8 * b);
+            }
+            h1w[jw] = packed;
+        }
+        uint32_t h2w[4];
+#pragma unroll
+        for (int mw = 0; mw < 4; ++mw) {
+            uint32_t packed = 0;
+#pragma unroll
+            for (int b = 0; b < 4; ++b) {
+                const int m = mw * 4 + b;
+                const int32_t *wrow = (const int32_t *)(w2t + (h * 16 + m) * W2STR);
+                int32_t acc = 0;
+#pragma unroll
+                for (int w = 0; w < 8; ++w) acc = __dp4a((int32_t)h1w[w], wrow[w], acc);
+                packed |= ((uint32_t)gelu_chain((int64_t)acc + p.b2[h * 16 + m], p.h2_sh_in, p.h2_sh_out) & 0xffu)
+                          << (8 * b);
+            }
+            h2w[mw] = packed;
+        }
+        int32_t q[2];
+#pragma unroll
+        for (int o = 0; o < 2; ++o) {
+            const int32_t *wrow = (const int32_t *)(w3t + (h * 2 + o) * 16);
+            int32_t acc = 0;
+#pragma unroll
+            for (int w = 0; w < 4; ++w) acc = __dp4a((int32_t)h2w[w], wrow[w], acc);
+            const int32_t logit = (int32_t)requant64((int64_t)acc + p.b3[h * 2 + o], p.logit_shift, 8);
+            q[o] = (int32_t)requant64(logit, p.logit_q16_shift, 24);
+        }
+        hs[h * MAXC + c] = keep_score(q[0], q[1]);
+    }
+
+    // ---- head stats + head-weight MLP per candidate --------------------------------
+    for (int c = tid; c < C; c += THREADS) {
+        int32_t st[3];
+#pragma unroll
+        for (int h = 0; h < 3; ++h) {
+            const int32_t *trow = (const int32_t *)(tok + (1 + c) * 192 + 64 * h);
+            int32_t t = 0;
+#pragma unroll
+            for (int w = 0; w < 16; ++w) t = __dp4a(trow[w], 0x01010101, t);
+            st[h] = sat8((int32_t)round_div64(t, 64));
+            stats[c * 3 + h] = (int8_t)st[h];
+        }
+        int32_t hid[3];
+#pragma unroll
+        for (int j = 0; j < 3; ++j) {
+            int64_t acc = p.hb1[j];
+#pragma unroll
+            for (int i = 0; i < 3; ++i) acc += st[i] * (int32_t)p.hw1[i * 3 + j];
+            hid[j] = gelu_chain(acc, p.hw_sh_in, p.hw_sh_out);
+        }
+#pragma unroll
+        for (int j = 0; j < 3; ++j) {
+            int64_t acc = p.hb2[j];
+#pragma unroll
+            for (int i = 0; i < 3; ++i) acc += hid[i] * (int32_t)p.hw2[i * 3 + j];
+            hwt[c * 3 + j] = sat_q016(plan_sigmoid((int32_t)requant64(acc, p.hw_q16_shift, 24)));
+        }
+    }
+    __syncthreads();
+
+    // ---- fuse (selector.py:392-418) and keep flags ----------------------------------
+    const int normals = C - pkg;
+    for (int c = tid; c < C; c += THREADS) {
+        int64_t num = 0, den = 0;
+#pragma unroll
+        for (int h = 0; h < 3; ++h) {
+            num += (int64_t)hs[h * MAXC + c] * hwt[c * 3 + h];
+            den += hwt[c * 3 + h];
+        }
+        if (den == 0) {
+            num = (int64_t)hs[c] + hs[MAXC + c] + hs[2 * MAXC + c];
+            den = 3;
+            atomicOr(&misc[0], (int)HV_WARN_HEAD_DEN_ZERO);
+        }
+        const int32_t f = sat_q016(round_div64(num, den));
+        fused[c] = f;
+        const int keep = (c < normals) && f >= 32768;
+        flags[c] = (uint8_t)(keep | ((keep ? 0 : 1) << 1));
+    }
+    __syncthreads();
+
+    // ---- stable compaction index: exclusive scan of keep flags (C <= 196 < 256) -----
+    {
+        const int lane = tid & 31, warp = tid >> 5;
+        const int kf = tid < C ? (flags[tid] & 1) : 0;
+        const unsigned bal = __ballot_sync(0xffffffffu, kf);
+        if (lane == 0) misc[4 + warp] = __popc(bal);
+        __syncthreads();
+        int base = 0;
+        for (int w = 0; w < warp; ++w) base += misc[4 + w];
+        if (tid < C) kidx[tid] = base + __popc(bal & ((1u << lane) - 1u));
+        if (tid == THREADS - 1) {
+            int tot = 0;
+            for (int w = 0; w < THREADS / 32; ++w) tot += misc[4 + w];
+            misc[1] = tot;
+        }
+    }
+    // participants: pruned normals plus the incoming package (always).
+    __shared__ long long den_sh;
+    if (tid == 0) den_sh = 0;
+    __syncthreads();
+    {
+        long long d = 0;
+        int cnt = 0;
+        for (int c = tid; c < C; c += THREADS)
+            if (flags[c] & 2) { d += fused[c]; ++cnt; }
+        if (d) atomicAdd((unsigned long long *)&den_sh, (unsigned long long)d);
+        if (cnt) atomicAdd(&misc[2], cnt);
+    }
+    __syncthreads();
+    const int kept = misc[1];
+    const int parts = misc[2];
+    const long long pden = den_sh;
+    const int nout = 1 + kept + (parts > 0 ? 1 : 0);
+
+    // ---- write rows: CLS, kept (stable), package --------------------------------------
+    if (tid < 12) ((int4 *)out)[tid] = ((const int4 *)tok)[tid];
+    for (int idx = tid; idx < C * 12; idx += THREADS) {
+        const int c = idx / 12, ch = idx - c * 12;
+        if (flags[c] & 1) ((int4 *)(out + (size_t)(1 + kidx[c]) * 192))[ch] = ((const int4 *)(tok + (1 + c) * 192))[ch];
+    }
+    if (parts > 0) {
+        int8_t *prow = out + (size_t)(1 + kept) * 192;
+        for (int d = tid; d < 192; d += THREADS) {
+            long long num = 0;
+            if (pden == 0) {
+                for (int c = 0; c < C; ++c)
+                    if (flags[c] & 2) num += tok[(1 + c) * 192 + d];
+            } else {
+                for (int c = 0; c < C; ++c)
+                    if (flags[c] & 2) num += (long long)fused[c] * tok[(1 + c) * 192 + d];
+            }
+            prow[d] = (int8_t)sat8((int32_t)round_div64(num, pden == 0 ? parts : pden));
+        }
+    }
+    if (tid == 0) {
+        const int w = misc[0] | (parts > 0 && pden == 0 ? (int)HV_WARN_PACKAGE_DEN_ZERO : 0);
+        counts_out[img] = nout;
+        if (pkg_out) pkg_out[img] = (uint8_t)(parts > 0);
+        if (summary) {
+            hv_selector_summary s;
+            s.input_tokens = n;
+            s.output_tokens = nout;
+            s.kept_normal = kept;
+            s.pruned_normal = parts - pkg;
+            s.package_present = parts > 0;
+            s.warnings = w;
+            summary[(size_t)img * sum_stride] = s;
+        }
+        if (warn && w) atomicOr((unsigned int *)(warn + (img & ~3)), (unsigned int)w << (8 * (img & 3)));
+        if (token_counts) token_counts[(size_t)img * tc_stride + tc_col] = nout;
+    }
+    // ---- optional intermediates (token_selector API) -------------------------------
+    if (dbg.fused)
+        for (int c = tid; c < C; c += THREADS) dbg.fused[(size_t)img * MAXC + c] = fused[c];
+    if (dbg.head_scores)
+        for (int i = tid; i < 3 * C; i += THREADS) {
+            const int h = i / C, c = i - h * C;
+            dbg.head_scores[((size_t)img * 3 + h) * MAXC + c] = hs[h * MAXC + c];
+        }
+    if (dbg.head_weights)
+        for (int i = tid; i < 3 * C; i += THREADS) dbg.head_weights[(size_t)img * MAXC * 3 + i] = hwt[i];
+    if (dbg.local)
+        for (int i = tid; i < 3 * C * 32; i += THREADS) {
+            const int j = i & 31, hc = i >> 5, h = hc / C, c = hc - h * C;
+            dbg.local[(((size_t)img * 3 + h) * MAXC + c) * 32 + j] = local[(h * MAXC + c) * LSTR + j];
+        }
+    if (dbg.global_ && tid < 96) dbg.global_[(size_t)img * 96 + tid] = glob[tid];
+    if (dbg.stats)
+        for (int i = tid; i < 3 * C; i += THREADS) dbg.stats[(size_t)img * MAXC * 3 + i] = stats[i];
+}
+
+__global__ void __launch_bounds__(256) pack_kernel(const int8_t *__restrict__ stage,
+                                                   const int32_t *__restrict__ counts, int images,
+                                                   int8_t *__restrict__ x, int32_t *__restrict__ offsets_out) {
+    __shared__ int part[8];
+    const int img = blockIdx.x, tid = threadIdx.x;
+    int s = 0;
+    for (int i = tid; i < img; i += 256) s += counts[i];
+#pragma unroll
+    for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    if ((tid & 31) == 0) part[tid >> 5] = s;
+    __syncthreads();
+    int off = 0;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) off += part[w];
+    const int cnt = counts[img];
+    if (tid == 0) {
+        offsets_out[img] = off;
+        if (img == images - 1) offsets_out[images] = off + cnt;
+    }
+    const int4 *src = (const int4 *)(stage + (size_t)img * 197 * 192);
+    int4 *dst = (int4 *)(x + (size_t)off * 192);
+    for (int c = tid; c < cnt * 12; c += 256) dst[c] = src[c];
+}
+
+}  // namespace
+
+cudaError_t launch_selector(const int8_t *x, const int32_t *offsets, const uint8_t *pkg_in, int images,
+                            const SelParams &p, int8_t *stage, int32_t *counts_out, uint8_t *pkg_out,
+                            hv_selector_summary *summary, int sum_stride, uint8_t *warn, int32_t *token_counts,
+                            int tc_stride, int tc_col, const SelDebug *dbg, cudaStream_t st) {
+    if (images <= 0) return cudaSuccess;
+    cudaError_t e = cudaFuncSetAttribute(selector_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    if (e != cudaSuccess) return e;
+    SelDebug d = dbg ? *dbg : SelDebug{nullptr, nullptr, nullptr, nullptr, nullptr, nullptr};
+    selector_kernel<<<images, THREADS, SMEM_BYTES, st>>>(x, offsets, pkg_in, p, stage, counts_out, pkg_out, summary,
+                                                        sum_stride, warn, token_counts, tc_stride, tc_col, d);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_pack(const int8_t *stage, const int32_t *counts, int images, int8_t *x, int32_t *offsets_out,
+                        cudaStream_t st) {
+    if (images <= 0) return cudaSuccess;
+    pack_kernel<<<images, 256, 0, st>>>(stage, counts, images, x, offsets_out);
+    return cudaGetLastError();
+}
+
+}  // namespace hv
