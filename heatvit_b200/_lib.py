@@ -41,6 +41,7 @@ _SIGNATURES = {
     "hv_token_selector": (I, [P, I, P, P, P, I, P, P, P, P, P, P, P, P, P, P, P]),
     "hv_writeback_i64": (I, [P, I64, I, I, I, P, P]),
     "hv_profile_start": (I, [P, I, I]),
+    "hv_device_error": (I, [P, C.POINTER(C.c_int)]),
     "hv_profile_stop": (I, [P, C.POINTER(C.c_int), C.POINTER(C.c_double), C.POINTER(C.c_longlong)]),
     "hv_align_add_i8": (I, [P, I, P, I, I, I64, P, P]),
 }

@@ -1,230 +1,252 @@
-// hv_attention.cu — fused per-(image, head) attention on the ragged token layout.
+// hv_attention.cu — per-(image, head) attention on tcgen05 tensor cores and TMEM.
 //
 // Restates transformer.py:233-268 for one image and head:
 //   score = requant(Q·Kᵀ, 2q, score_scale, 32)            (int32 writeback)
 //   q16   = sat24(rsa(score, -(score_scale + 13)))         (Q8.16)
-//   prob  = softmax_attention(q16 row)                     (UQ0.8, nonlinear.py:130-133)
+//   prob  = softmax_attention(q16 row)                     (UQ0.8, nonlinear.py:98-133)
 //   ctx   = requant(prob(uint8)·V, prob_scale + q, context_out, 8)
 // written straight into the head-concatenated layout (layout.py:132-155).
 //
-// One CTA per (image, head), 4 warps; each warp owns 16-query strips.  Q, K and
-// a permuted, transposed V live in shared memory; scores and probabilities
-// never leave registers.  The S accumulator fragment of mma.m16n8k32 gives a
-// thread columns {8j + 2t, 8j + 2t + 1}; P·V needs A fragments holding 4
-// consecutive k per thread, so the token order along P·V's k axis is permuted
-// (k = 32g + 16h + 4u + 2a + b  <->  token 32g + 16h + 8a + 2u + b) and V is
-// stored with the same permutation.  A dot product does not depend on the
-// order of its terms, so the result is exact.
+// One CTA (4 warps) per (image, head), query rows in tiles of 128:
+//   1. K and Vᵀ (and each Q tile) are staged in shared memory in the
+//      no-swizzle K-major canonical layout (hv_tc05.cuh).
+//   2. One thread issues S = Q·Kᵀ as tcgen05.mma kind::i8 (M=128, N=np, K=64)
+//      into TMEM columns [0, np); completion arrives on an mbarrier.
+//   3. Thread t owns query row t = TMEM lane t: it reads its score row with
+//      tcgen05.ld (32 columns at a time) for the row max, writes the exp terms
+//      back into TMEM, then forms the UQ0.8 probabilities and stores them to
+//      shared memory as the A operand of the next MMA.  No shuffles: the whole
+//      row belongs to one thread.
+//   4. ctx = P·V as tcgen05.mma kind::i8 with unsigned A (M=128, N=64, K=np)
+//      into TMEM columns [0, 64), then requantised and written out.
+// TMEM: 256 columns per CTA; shared memory is padded so two CTAs share an SM.
 #include "hv_internal.cuh"
+#include "hv_tc05.cuh"
 
 namespace hv {
 
 namespace {
 
-constexpr int MAXN = 197;
-constexpr int NPMAX = 224;          // MAXN rounded up to 32
-constexpr int QK_STRIDE = 80;       // 64 data bytes + 16 pad: conflict-free ldmatrix
-constexpr int V_STRIDE = NPMAX + 16;
-constexpr int WARPS = 4;
-constexpr int SMEM_Q = NPMAX * QK_STRIDE;
-constexpr int SMEM_K = NPMAX * QK_STRIDE;
-constexpr int SMEM_V = 64 * V_STRIDE;
-constexpr int SMEM_BYTES = SMEM_Q + SMEM_K + SMEM_V;
+constexpr int THREADS = 128;
+constexpr int NPMAX = 224;        // 197 rounded up to 32
+constexpr uint32_t TMEM_COLS = 256;
+constexpr uint32_t WAIT_ITERS = 1u << 24;
 
-__device__ __forceinline__ uint32_t smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
+constexpr int OFF_K = 0;                      // [NPMAX][64]
+constexpr int OFF_V = OFF_K + NPMAX * 64;     // Vᵀ: [64][NPMAX]
+constexpr int OFF_Q = OFF_V + 64 * NPMAX;     // [128][64]
+constexpr int OFF_P = OFF_Q + 128 * 64;       // [128][NPMAX] uint8
+constexpr int OFF_BAR = OFF_P + 128 * NPMAX;  // mbarrier, TMEM base, abort flag
+constexpr int SMEM_BYTES = 80 * 1024;         // > 227 KB / 3: at most two CTAs per SM
+static_assert(OFF_BAR + 64 <= SMEM_BYTES, "attention shared memory layout");
 
-__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], uint32_t addr) {
-    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];\n"
-                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
-                 : "r"(addr));
+__device__ __forceinline__ int32_t q16_of(uint32_t acc_bits, const AttnParams &p) {
+    const int32_t acc = (int32_t)acc_bits;
+    if (p.fast) return p.fast_shift ? rsa32(acc, p.fast_shift) : acc;  // host-checked: no clipping
+    const int32_t score = (int32_t)requant64(acc, p.score_shift, 32);
+    return (int32_t)requant64(score, p.q16_shift, 24);
 }
 
-__device__ __forceinline__ void mma_s8(int (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
-    asm volatile(
-        "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
-        : "+r"(c[0]), "+r"(c[1]), "+r"(c[2]), "+r"(c[3])
-        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
-
-__device__ __forceinline__ void mma_u8(int (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
-    asm volatile(
-        "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
-        : "+r"(c[0]), "+r"(c[1]), "+r"(c[2]), "+r"(c[3])
-        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
-
-// Position along P·V's k axis of token r (see file comment).
-__device__ __forceinline__ int perm_pos(int r) {
-    const int g = r & ~31, h = r & 16, a = (r >> 3) & 1, u = (r >> 1) & 3, b = r & 1;
-    return g + h + 4 * u + 2 * a + b;
-}
-
-__global__ void __launch_bounds__(WARPS * 32) attention_kernel(const int8_t *__restrict__ qkv,
+__global__ void __launch_bounds__(THREADS) attention_tc_kernel(const int8_t *__restrict__ qkv,
                                                                const int32_t *__restrict__ offsets,
-                                                               int8_t *__restrict__ ctx, AttnParams p) {
-    extern __shared__ __align__(128) uint8_t smem[];
-    uint8_t *sQ = smem;
-    uint8_t *sK = smem + SMEM_Q;
-    uint8_t *sV = smem + SMEM_Q + SMEM_K;
+                                                               int8_t *__restrict__ ctx, AttnParams p,
+                                                               int *__restrict__ err) {
+    extern __shared__ __align__(1024) uint8_t smem[];
+    uint8_t *sK = smem + OFF_K;
+    uint8_t *sV = smem + OFF_V;
+    uint8_t *sQ = smem + OFF_Q;
+    uint8_t *sP = smem + OFF_P;
+    uint64_t *bar = (uint64_t *)(smem + OFF_BAR);
+    uint32_t *tmem_slot = (uint32_t *)(smem + OFF_BAR + 8);
+    volatile int *abort_flag = (volatile int *)(smem + OFF_BAR + 12);
+
     const int img = blockIdx.x, head = blockIdx.y;
     const int row0 = offsets[img];
     const int n = offsets[img + 1] - row0;
     if (n <= 0) return;
     const int np = (n + 31) & ~31;
-    const int tid = threadIdx.x;
+    const int tid = threadIdx.x, warp = tid >> 5;
 
-    // Q and K rows: 4 x 16-byte chunks each; zero rows up to np.
-    for (int c = tid; c < np * 4; c += WARPS * 32) {
-        const int r = c >> 2, ch = c & 3;
-        int4 qv = make_int4(0, 0, 0, 0), kv = qv;
-        if (r < n) {
-            const int8_t *src = qkv + (size_t)(row0 + r) * 576 + head * 64 + ch * 16;
-            qv = *(const int4 *)src;
-            kv = *(const int4 *)(src + 192);
-        }
-        *(int4 *)(sQ + r * QK_STRIDE + ch * 16) = qv;
-        *(int4 *)(sK + r * QK_STRIDE + ch * 16) = kv;
+    if (warp == 0) {
+        tc05::tmem_alloc(tmem_slot, TMEM_COLS);
+        tc05::tmem_relinquish();
     }
-    // V transposed + permuted: sV[lane][perm_pos(token)].
-    for (int c = tid; c < np * 16; c += WARPS * 32) {
+    if (tid == 0) {
+        tc05::mbar_init(bar, 1);
+        *abort_flag = 0;
+        tc05::fence_mbar_init();
+    }
+    // K rows and Vᵀ (zero beyond n up to np).
+    for (int c = tid; c < np * 4; c += THREADS) {
+        const int r = c >> 2, ch = c & 3;
+        int4 kv = make_int4(0, 0, 0, 0);
+        if (r < n) kv = *(const int4 *)(qkv + (size_t)(row0 + r) * 576 + 192 + head * 64 + ch * 16);
+        *(int4 *)(sK + tc05::kmajor_offset(r, ch * 16, 64)) = kv;
+    }
+    for (int c = tid; c < np * 16; c += THREADS) {
         const int r = c >> 4, w = c & 15;
         uint32_t word = 0;
         if (r < n) word = *(const uint32_t *)(qkv + (size_t)(row0 + r) * 576 + 384 + head * 64 + w * 4);
-        const int pos = perm_pos(r);
 #pragma unroll
-        for (int b = 0; b < 4; ++b) sV[(w * 4 + b) * V_STRIDE + pos] = (uint8_t)(word >> (8 * b));
+        for (int b = 0; b < 4; ++b) sV[tc05::kmajor_offset(w * 4 + b, r, np)] = (uint8_t)(word >> (8 * b));
+    }
+    tc05::fence_before();
+    __syncthreads();
+    tc05::fence_after();
+    const uint32_t tbase = *tmem_slot;
+    const uint32_t lane_addr = tbase + ((uint32_t)(warp * 32) << 16);
+    const uint32_t sbo_np = (uint32_t)(np / 16) * 128;
+    uint32_t phase = 0;
+
+    for (int t = 0; t * 128 < n; ++t) {
+        // ---- Q tile ------------------------------------------------------------
+        for (int c = tid; c < 128 * 4; c += THREADS) {
+            const int r = c >> 2, ch = c & 3, gr = t * 128 + r;
+            int4 qv = make_int4(0, 0, 0, 0);
+            if (gr < n) qv = *(const int4 *)(qkv + (size_t)(row0 + gr) * 576 + head * 64 + ch * 16);
+            *(int4 *)(sQ + tc05::kmajor_offset(r, ch * 16, 64)) = qv;
+        }
+        tc05::fence_proxy_async();
+        tc05::fence_before();
+        __syncthreads();
+        if (tid == 0) {
+            tc05::fence_after();
+            const uint32_t idesc = tc05::idesc_i8(128, np, true, true);
+#pragma unroll
+            for (int s = 0; s < 2; ++s)
+                tc05::mma_i8_ss(tbase, tc05::smem_desc(tc05::smem_u32(sQ) + s * 256, 128, 512),
+                                tc05::smem_desc(tc05::smem_u32(sK) + s * 256, 128, 512), idesc, s);
+            tc05::commit(bar);
+        }
+        if (tc05::mbar_wait(bar, phase, WAIT_ITERS)) phase ^= 1;
+        else *abort_flag = 1;
+        __syncthreads();
+        if (*abort_flag) break;
+        tc05::fence_after();
+
+        // ---- thread-per-row softmax straight from TMEM ------------------------------
+        int32_t mx = INT32_MIN;
+        for (int c0 = 0; c0 < np; c0 += 32) {
+            uint32_t v[32];
+            tc05::ld32(lane_addr + c0, v);
+            tc05::wait_ld();
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+                if (c0 + j < n) mx = max(mx, q16_of(v[j], p));
+        }
+        uint32_t sum = 0;
+        for (int c0 = 0; c0 < np; c0 += 32) {
+            uint32_t v[32];
+            tc05::ld32(lane_addr + c0, v);
+            tc05::wait_ld();
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+                const uint32_t e = (c0 + j < n) ? softmax_exp_q16(q16_of(v[j], p) - mx) : 0u;
+                v[j] = e;
+                sum += e;
+            }
+            tc05::st32(lane_addr + c0, v);
+        }
+        tc05::wait_st();
+        const uint64_t rc = softmax_recip(sum ? sum : 1u);
+        for (int c0 = 0; c0 < np; c0 += 32) {
+            uint32_t v[32];
+            tc05::ld32(lane_addr + c0, v);
+            tc05::wait_ld();
+            uint32_t pk[8];
+#pragma unroll
+            for (int w = 0; w < 8; ++w) {
+                uint32_t word = 0;
+#pragma unroll
+                for (int b = 0; b < 4; ++b) {
+                    // min(rsa(rsa(E*rc, 16), 8), 255) in one rounding step (nested floors).
+                    const uint64_t tt = (uint64_t)v[w * 4 + b] * rc + (32768u + (1u << 23));
+                    const uint32_t pr = (uint32_t)(tt >> 24);
+                    word |= (pr < 255u ? pr : 255u) << (8 * b);
+                }
+                pk[w] = word;
+            }
+            *(uint4 *)(sP + tc05::kmajor_offset(tid, c0, np)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+            *(uint4 *)(sP + tc05::kmajor_offset(tid, c0 + 16, np)) = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+        }
+
+        // ---- ctx = P·V -------------------------------------------------------------
+        tc05::fence_proxy_async();
+        tc05::fence_before();
+        __syncthreads();
+        if (tid == 0) {
+            tc05::fence_after();
+            const uint32_t idesc = tc05::idesc_i8(128, 64, false, true);
+            for (int s = 0; s < np / 32; ++s)
+                tc05::mma_i8_ss(tbase, tc05::smem_desc(tc05::smem_u32(sP) + s * 256, 128, sbo_np),
+                                tc05::smem_desc(tc05::smem_u32(sV) + s * 256, 128, sbo_np), idesc, s);
+            tc05::commit(bar);
+        }
+        if (tc05::mbar_wait(bar, phase, WAIT_ITERS)) phase ^= 1;
+        else *abort_flag = 1;
+        __syncthreads();
+        if (*abort_flag) break;
+        tc05::fence_after();
+        const int r = t * 128 + tid;
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+            uint32_t o[32];
+            tc05::ld32(lane_addr + half * 32, o);
+            tc05::wait_ld();
+            uint32_t pk[8];
+#pragma unroll
+            for (int w = 0; w < 8; ++w) {
+                uint32_t word = 0;
+#pragma unroll
+                for (int b = 0; b < 4; ++b) {
+                    const int32_t a = (int32_t)o[w * 4 + b];
+                    const int32_t v = p.ctx_fast ? requant8_r(a, p.ctx_shift) : (int32_t)requant64(a, p.ctx_shift, 8);
+                    word |= ((uint32_t)v & 0xffu) << (8 * b);
+                }
+                pk[w] = word;
+            }
+            if (r < n) {
+                uint4 *dst = (uint4 *)(ctx + (size_t)(row0 + r) * 192 + head * 64 + half * 32);
+                dst[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+                dst[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+            }
+        }
+        tc05::fence_before();
+        __syncthreads();
+    }
+
+    if (*abort_flag) {
+        if (tid == 0) atomicExch(err, 1);
+        // let any MMA still in flight drain (bounded) before the TMEM is released
+        tc05::mbar_wait(bar, phase, WAIT_ITERS);
     }
     __syncthreads();
-
-    const int warp = tid >> 5, lane = tid & 31;
-    const int q4 = lane >> 3, r8 = lane & 7;
-    const int gid = lane >> 2, t4 = lane & 3;
-    const int nt = np >> 3;           // 8-column score tiles
-    const int strips = (n + 15) >> 4;
-
-    for (int s = warp; s < strips; s += WARPS) {
-        uint32_t qa[2][4];
-#pragma unroll
-        for (int ks = 0; ks < 2; ++ks)
-            ldsm_x4(qa[ks], smem_u32(sQ + (s * 16 + (q4 & 1) * 8 + r8) * QK_STRIDE + (ks * 2 + (q4 >> 1)) * 16));
-
-        int sc[NPMAX / 8][4];
-#pragma unroll
-        for (int j = 0; j < NPMAX / 8; ++j) {
-            sc[j][0] = sc[j][1] = sc[j][2] = sc[j][3] = 0;
-        }
-#pragma unroll
-        for (int jp = 0; jp < NPMAX / 16; ++jp) {
-            if (2 * jp < nt) {
-#pragma unroll
-                for (int ks = 0; ks < 2; ++ks) {
-                    uint32_t kb[4];
-                    // matrices: (tile 2jp, k lo), (2jp, k hi), (2jp+1, k lo), (2jp+1, k hi)
-                    ldsm_x4(kb, smem_u32(sK + ((2 * jp + (q4 >> 1)) * 8 + r8) * QK_STRIDE + (ks * 2 + (q4 & 1)) * 16));
-                    mma_s8(sc[2 * jp], qa[ks], kb[0], kb[1]);
-                    mma_s8(sc[2 * jp + 1], qa[ks], kb[2], kb[3]);
-                }
-            }
-        }
-
-        // Softmax on rows gid (e = 0,1) and gid + 8 (e = 2,3).
-        int32_t mx0 = INT32_MIN, mx1 = INT32_MIN;
-#pragma unroll
-        for (int j = 0; j < NPMAX / 8; ++j) {
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const int col = j * 8 + t4 * 2 + (e & 1);
-                int32_t v = INT32_MIN;
-                if (col < n) {
-                    const int32_t score = (int32_t)requant64(sc[j][e], p.score_shift, 32);
-                    v = (int32_t)requant64(score, p.q16_shift, 24);
-                }
-                sc[j][e] = v;
-                if (e < 2) mx0 = max(mx0, v);
-                else mx1 = max(mx1, v);
-            }
-        }
-        mx0 = max(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
-        mx0 = max(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
-        mx1 = max(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
-        mx1 = max(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
-        uint32_t s0 = 0, s1 = 0;
-#pragma unroll
-        for (int j = 0; j < NPMAX / 8; ++j) {
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const int32_t v = sc[j][e];
-                uint32_t ex = 0;
-                if (v != INT32_MIN) ex = softmax_exp_q16(v - (e < 2 ? mx0 : mx1));
-                sc[j][e] = (int32_t)ex;
-                if (e < 2) s0 += ex;
-                else s1 += ex;
-            }
-        }
-        s0 += __shfl_xor_sync(0xffffffffu, s0, 1);
-        s0 += __shfl_xor_sync(0xffffffffu, s0, 2);
-        s1 += __shfl_xor_sync(0xffffffffu, s1, 1);
-        s1 += __shfl_xor_sync(0xffffffffu, s1, 2);
-        const uint64_t rc0 = softmax_recip(s0 ? s0 : 1u), rc1 = softmax_recip(s1 ? s1 : 1u);
-#pragma unroll
-        for (int j = 0; j < NPMAX / 8; ++j) {
-#pragma unroll
-            for (int e = 0; e < 4; ++e)
-                sc[j][e] = (int32_t)softmax_attn_u8(softmax_ratio((uint32_t)sc[j][e], e < 2 ? rc0 : rc1));
-        }
-
-        // ctx = P·V with P (uint8) as the A operand.
-        int oc[8][4];
-#pragma unroll
-        for (int j = 0; j < 8; ++j) oc[j][0] = oc[j][1] = oc[j][2] = oc[j][3] = 0;
-#pragma unroll
-        for (int g = 0; g < NPMAX / 32; ++g) {
-            if (4 * g < nt) {
-                uint32_t pa[4];
-                pa[0] = (uint32_t)sc[4 * g][0] | ((uint32_t)sc[4 * g][1] << 8) | ((uint32_t)sc[4 * g + 1][0] << 16) |
-                        ((uint32_t)sc[4 * g + 1][1] << 24);
-                pa[1] = (uint32_t)sc[4 * g][2] | ((uint32_t)sc[4 * g][3] << 8) | ((uint32_t)sc[4 * g + 1][2] << 16) |
-                        ((uint32_t)sc[4 * g + 1][3] << 24);
-                pa[2] = (uint32_t)sc[4 * g + 2][0] | ((uint32_t)sc[4 * g + 2][1] << 8) |
-                        ((uint32_t)sc[4 * g + 3][0] << 16) | ((uint32_t)sc[4 * g + 3][1] << 24);
-                pa[3] = (uint32_t)sc[4 * g + 2][2] | ((uint32_t)sc[4 * g + 2][3] << 8) |
-                        ((uint32_t)sc[4 * g + 3][2] << 16) | ((uint32_t)sc[4 * g + 3][3] << 24);
-#pragma unroll
-                for (int pr = 0; pr < 4; ++pr) {
-                    uint32_t vb[4];
-                    // matrices: (lanes 16pr..+7, k lo), (same, k hi), (16pr+8.., k lo), (k hi)
-                    ldsm_x4(vb, smem_u32(sV + (pr * 16 + (q4 >> 1) * 8 + r8) * V_STRIDE + g * 32 + (q4 & 1) * 16));
-                    mma_u8(oc[2 * pr], pa, vb[0], vb[1]);
-                    mma_u8(oc[2 * pr + 1], pa, vb[2], vb[3]);
-                }
-            }
-        }
-        const int ra = s * 16 + gid, rb = ra + 8;
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            const int col = head * 64 + j * 8 + t4 * 2;
-            if (ra < n) {
-                const uint32_t lo = (uint32_t)requant64(oc[j][0], p.ctx_shift, 8) & 0xff;
-                const uint32_t hi = (uint32_t)requant64(oc[j][1], p.ctx_shift, 8) & 0xff;
-                *(uint16_t *)(ctx + (size_t)(row0 + ra) * 192 + col) = (uint16_t)(lo | (hi << 8));
-            }
-            if (rb < n) {
-                const uint32_t lo = (uint32_t)requant64(oc[j][2], p.ctx_shift, 8) & 0xff;
-                const uint32_t hi = (uint32_t)requant64(oc[j][3], p.ctx_shift, 8) & 0xff;
-                *(uint16_t *)(ctx + (size_t)(row0 + rb) * 192 + col) = (uint16_t)(lo | (hi << 8));
-            }
-        }
+    if (warp == 0) {
+        tc05::fence_after();
+        tc05::tmem_dealloc(tbase, TMEM_COLS);
     }
 }
 
 }  // namespace
 
+AttnParams make_attn(int qkv_out_scale, int score_scale, int prob_scale, int context_out_scale) {
+    AttnParams a;
+    a.score_shift = score_scale - 2 * qkv_out_scale;
+    a.q16_shift = -(score_scale + 13);
+    a.ctx_shift = context_out_scale - (prob_scale + qkv_out_scale);
+    const int k = -a.score_shift;
+    a.fast = (k >= 0 && k <= 10 && a.q16_shift >= k) ? 1 : 0;
+    a.fast_shift = a.fast ? a.q16_shift - k : 0;
+    a.ctx_fast = (a.ctx_shift >= 1 && a.ctx_shift <= 30) ? 1 : 0;
+    return a;
+}
+
 cudaError_t launch_attention(const int8_t *qkv, const int32_t *offsets, int images, int8_t *ctx,
-                             const AttnParams &p, cudaStream_t st) {
+                             const AttnParams &p, int *err, cudaStream_t st) {
     if (images <= 0) return cudaSuccess;
-    cudaError_t e = cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    cudaError_t e = cudaFuncSetAttribute(attention_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
     if (e != cudaSuccess) return e;
-    attention_kernel<<<dim3(images, 3), WARPS * 32, SMEM_BYTES, st>>>(qkv, offsets, ctx, p);
+    attention_tc_kernel<<<dim3(images, 3), THREADS, SMEM_BYTES, st>>>(qkv, offsets, ctx, p, err);
     return cudaGetLastError();
 }
 

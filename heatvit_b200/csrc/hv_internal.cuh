@@ -38,9 +38,15 @@ struct AttnParams {
     int score_shift;   // score_scale - 2*qkv_out           (int32 score writeback)
     int q16_shift;     // -(score_scale + 13)               (Q8.16 conversion, sat 24)
     int ctx_shift;     // context_out - (prob_scale + qkv_out)
+    // fast = 1 when score_shift = -k (0 <= k <= 10) and q16_shift >= k: |Q.K| <= 2^20,
+    // so acc << k fits int32 and q16 = rsa(acc, q16_shift - k) never saturates.
+    int fast, fast_shift;
+    int ctx_fast;      // ctx_shift in [1, 30]: |P.V| < 2^23, 32-bit rounding shift is exact
 };
+AttnParams make_attn(int qkv_out_scale, int score_scale, int prob_scale, int context_out_scale);
+// err: device word set to a non-zero code when a bounded wait gave up.
 cudaError_t launch_attention(const int8_t *qkv, const int32_t *offsets, int images, int8_t *ctx,
-                             const AttnParams &p, cudaStream_t st);
+                             const AttnParams &p, int *err, cudaStream_t st);
 
 // Device-resident selector weights and constants.
 struct SelParams {

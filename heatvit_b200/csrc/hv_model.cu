@@ -121,6 +121,7 @@ struct hv_model {
            *CLSLN = nullptr;
     int32_t *off[2] = {nullptr, nullptr}, *counts = nullptr;
     uint8_t *pkg[2] = {nullptr, nullptr}, *warn = nullptr;
+    int *err = nullptr;  // device error word (bounded waits that gave up)
     // host-pipeline staging
     int host_cap = 0;
     int8_t *himg[2] = {nullptr, nullptr};
@@ -180,7 +181,7 @@ int ensure_capacity(hv_model *m, int images) {
                  oCTX = take(rows * 192), oHID = take(rows * 768), oSTAGE = take(rows * 192),
                  oCLS = take((size_t)images * 192), oOff0 = take((size_t)(images + 1) * 4),
                  oOff1 = take((size_t)(images + 1) * 4), oCnt = take((size_t)images * 4), oPkg0 = take(images),
-                 oPkg1 = take(images), oWarn = take(((size_t)images + 3) & ~(size_t)3);
+                 oPkg1 = take(images), oWarn = take(((size_t)images + 3) & ~(size_t)3), oErr = take(16);
     uint8_t *base = nullptr;
     if (cudaMalloc(&base, total) != cudaSuccess) return fail(HV_ERR_NOMEM, "cannot allocate %zu bytes of scratch", total);
     m->scratch = base;
@@ -198,6 +199,8 @@ int ensure_capacity(hv_model *m, int images) {
     m->pkg[0] = base + oPkg0;
     m->pkg[1] = base + oPkg1;
     m->warn = base + oWarn;
+    m->err = (int *)(base + oErr);
+    if (cudaMemset(m->err, 0, 16) != cudaSuccess) return fail(HV_ERR_CUDA, "cannot clear the error word");
     m->cap = images;
     return HV_OK;
 }
@@ -290,7 +293,7 @@ int run_block(hv_model *m, int b, int images, const int32_t *off, cudaStream_t s
     }
     {
         Prof pr(m, HV_STAGE_ATTN, st);
-        CUDA_TRY(launch_attention(m->QKV, off, images, m->CTX, d.attn, st));
+        CUDA_TRY(launch_attention(m->QKV, off, images, m->CTX, d.attn, m->err, st));
         pr.end(st, rows_dev, 0);
     }
     {
@@ -489,9 +492,7 @@ int pack_model(hv_model *m, const hv_params *P) {
             return fail(HV_ERR_VALUE, "residual exponent gap above 54 is not supported (block %d)", b + 1);
         d.res1 = make_align_add(q.x_scale_exp, q.msa_out_scale_exp, q.ffn_x_scale_exp);
         d.res2 = make_align_add(q.ffn_x_scale_exp, q.ffn_out_scale_exp, q.out_scale_exp);
-        d.attn.score_shift = q.score_scale_exp - 2 * q.qkv_out_scale_exp;
-        d.attn.q16_shift = -(q.score_scale_exp + 13);
-        d.attn.ctx_shift = q.context_out_scale_exp - (q.prob_scale_exp + q.qkv_out_scale_exp);
+        d.attn = make_attn(q.qkv_out_scale_exp, q.score_scale_exp, q.prob_scale_exp, q.context_out_scale_exp);
     }
     m->has_head = P->head_w != nullptr;
     if (m->has_head && !ln_scale_ok(P->blocks[HV_BLOCKS - 1].out_scale_exp))
@@ -698,6 +699,19 @@ int hv_infer_host(hv_model *m, const int8_t *h_images, int batch, int32_t *h_log
             CUDA_TRY(cudaMemcpyAsync(h_warnings + first, dw, cnt, cudaMemcpyDeviceToHost, m->compute_stream));
     }
     CUDA_TRY(cudaStreamSynchronize(m->compute_stream));
+    int code = 0;
+    CUDA_TRY(cudaMemcpy(&code, m->err, sizeof(int), cudaMemcpyDeviceToHost));
+    if (code) return fail(HV_ERR_STATE, "a device-side bounded wait gave up (code %d)", code);
+    return HV_OK;
+}
+
+int hv_device_error(hv_model *m, int *code) {
+    if (!m || !code) return fail(HV_ERR_VALUE, "null argument");
+    *code = 0;
+    if (!m->err) return HV_OK;
+    CUDA_TRY(cudaSetDevice(m->device));
+    CUDA_TRY(cudaMemcpy(code, m->err, sizeof(int), cudaMemcpyDeviceToHost));
+    if (*code) CUDA_TRY(cudaMemset(m->err, 0, sizeof(int)));
     return HV_OK;
 }
 

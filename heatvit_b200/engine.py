@@ -111,6 +111,14 @@ class Engine:
             out.update(checkpoints=ck, checkpoint_rows=rows)
         return out
 
+    def device_error(self):
+        """Read and clear the device error word (0 = every bounded wait completed)."""
+        torch = _torch()
+        code = C.c_int()
+        with torch.cuda.device(self.device):
+            check(lib().hv_device_error(self.handle, C.byref(code)))
+        return code.value
+
     def infer_host(self, images, logits=None, token_counts=None, summary=None, warnings=None):
         """Host-buffer entry: numpy int8 [B, 150528] in, numpy logits out.
         Copies overlap compute chunk by chunk inside the library (pinned input

@@ -191,6 +191,12 @@ HV_API int hv_infer_host(hv_model *model, const int8_t *h_images, int batch,
                   int32_t *h_logits, int32_t *h_token_counts,
                   hv_selector_summary *h_summary, uint8_t *h_warnings);
 
+/* Read and clear the model's device error word (synchronises with the device).
+ * *code != 0 means a kernel's bounded wait on a tensor-core completion gave up
+ * and that launch's outputs are invalid.  No counterpart in the reference (its
+ * RTL reports a watchdog timeout as a fatal error code). */
+HV_API int hv_device_error(hv_model *model, int *code);
+
 /* ---- kernel timing (bench and tracing) ------------------------------------------
  * Stage ids for hv_profile_*: one id per kernel of the per-block pipeline. */
 #define HV_STAGE_LN1 1

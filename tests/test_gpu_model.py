@@ -115,7 +115,9 @@ def test_full_size_sample_vs_oracle(cuda, oracle):
     from heatvit_b200.engine import Engine
     params = synth.config_params(synth.SEED, pruned=True)
     imgs = synth.baseline_images(synth.SEED, 1024, first=9000)
-    out = Engine(params).infer(torch.from_numpy(imgs).cuda())
+    eng = Engine(params)
+    out = eng.infer(torch.from_numpy(imgs).cuda())
+    assert eng.device_error() == 0
     idx = np.random.default_rng(1).choice(1024, 64, replace=False)
     ref = oracle.infer_batch(params, imgs[idx])
     np.testing.assert_array_equal(out["logits"].cpu().numpy()[idx], ref["logits"])
