@@ -40,13 +40,31 @@ constexpr int OFF_BAR = OFF_P + 128 * NPMAX;  // mbarrier, TMEM base, abort flag
 constexpr int SMEM_BYTES = 80 * 1024;         // > 227 KB / 3: at most two CTAs per SM
 static_assert(OFF_BAR + 64 <= SMEM_BYTES, "attention shared memory layout");
 
-__device__ __forceinline__ int32_t q16_of(uint32_t acc_bits, const AttnParams &p) {
-    const int32_t acc = (int32_t)acc_bits;
-    if (p.fast) return p.fast_shift ? rsa32(acc, p.fast_shift) : acc;  // host-checked: no clipping
+// q16 of one score accumulator.  FAST: host-proven that the int32 score
+// writeback and the sat24 cannot clip, so q16 = rsa(acc, fast_shift), written
+// branch-free with precomputed rounding constants (fast_shift may be 0).
+template <bool FAST>
+__device__ __forceinline__ int32_t q16_of(int32_t acc, const AttnParams &p) {
+    if (FAST) return (acc + p.fast_half + ((acc >> 31) & p.fast_negmask)) >> p.fast_shift;
     const int32_t score = (int32_t)requant64(acc, p.score_shift, 32);
     return (int32_t)requant64(score, p.q16_shift, 24);
 }
 
+// exp terms of one 32-column chunk (columns >= valid are masked to 0); returns their sum.
+template <bool FAST, bool MASK>
+__device__ __forceinline__ uint32_t chunk_exp(uint32_t (&v)[32], int valid, int32_t mx, const AttnParams &p) {
+    uint32_t sum = 0;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+        uint32_t e = softmax_exp_q16(q16_of<FAST>((int32_t)v[j], p) - mx);
+        if (MASK && j >= valid) e = 0u;
+        v[j] = e;
+        sum += e;
+    }
+    return sum;
+}
+
+template <bool FAST>
 __global__ void __launch_bounds__(THREADS) attention_tc_kernel(const int8_t *__restrict__ qkv,
                                                                const int32_t *__restrict__ offsets,
                                                                int8_t *__restrict__ ctx, AttnParams p,
@@ -125,27 +143,38 @@ __global__ void __launch_bounds__(THREADS) attention_tc_kernel(const int8_t *__r
         tc05::fence_after();
 
         // ---- thread-per-row softmax straight from TMEM ------------------------------
-        int32_t mx = INT32_MIN;
+        // q16 is monotone in the accumulator, so the row max is taken on raw
+        // accumulators and converted once.
+        const int nfull = n & ~31;
+        int32_t mxa = INT32_MIN;
         for (int c0 = 0; c0 < np; c0 += 32) {
             uint32_t v[32];
             tc05::ld32(lane_addr + c0, v);
             tc05::wait_ld();
+            if (c0 < nfull) {
 #pragma unroll
-            for (int j = 0; j < 32; ++j)
-                if (c0 + j < n) mx = max(mx, q16_of(v[j], p));
-        }
-        uint32_t sum = 0;
-        for (int c0 = 0; c0 < np; c0 += 32) {
-            uint32_t v[32];
-            tc05::ld32(lane_addr + c0, v);
-            tc05::wait_ld();
+                for (int j = 0; j < 32; ++j) mxa = max(mxa, (int32_t)v[j]);
+            } else {
 #pragma unroll
-            for (int j = 0; j < 32; ++j) {
-                const uint32_t e = (c0 + j < n) ? softmax_exp_q16(q16_of(v[j], p) - mx) : 0u;
-                v[j] = e;
-                sum += e;
+                for (int j = 0; j < 32; ++j)
+                    if (c0 + j < n) mxa = max(mxa, (int32_t)v[j]);
             }
+        }
+        const int32_t mx = q16_of<FAST>(mxa, p);
+        uint32_t sum = 0;
+        for (int c0 = 0; c0 < nfull; c0 += 32) {
+            uint32_t v[32];
+            tc05::ld32(lane_addr + c0, v);
+            tc05::wait_ld();
+            sum += chunk_exp<FAST, false>(v, 32, mx, p);
             tc05::st32(lane_addr + c0, v);
+        }
+        if (nfull < np) {
+            uint32_t v[32];
+            tc05::ld32(lane_addr + nfull, v);
+            tc05::wait_ld();
+            sum += chunk_exp<FAST, true>(v, n - nfull, mx, p);
+            tc05::st32(lane_addr + nfull, v);
         }
         tc05::wait_st();
         const uint64_t rc = softmax_recip(sum ? sum : 1u);
@@ -237,6 +266,8 @@ AttnParams make_attn(int qkv_out_scale, int score_scale, int prob_scale, int con
     const int k = -a.score_shift;
     a.fast = (k >= 0 && k <= 10 && a.q16_shift >= k) ? 1 : 0;
     a.fast_shift = a.fast ? a.q16_shift - k : 0;
+    a.fast_half = a.fast_shift ? (1 << (a.fast_shift - 1)) : 0;
+    a.fast_negmask = a.fast_shift ? -1 : 0;
     a.ctx_fast = (a.ctx_shift >= 1 && a.ctx_shift <= 30) ? 1 : 0;
     return a;
 }
@@ -244,9 +275,10 @@ AttnParams make_attn(int qkv_out_scale, int score_scale, int prob_scale, int con
 cudaError_t launch_attention(const int8_t *qkv, const int32_t *offsets, int images, int8_t *ctx,
                              const AttnParams &p, int *err, cudaStream_t st) {
     if (images <= 0) return cudaSuccess;
-    cudaError_t e = cudaFuncSetAttribute(attention_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    auto kern = p.fast ? attention_tc_kernel<true> : attention_tc_kernel<false>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
     if (e != cudaSuccess) return e;
-    attention_tc_kernel<<<dim3(images, 3), THREADS, SMEM_BYTES, st>>>(qkv, offsets, ctx, p, err);
+    kern<<<dim3(images, 3), THREADS, SMEM_BYTES, st>>>(qkv, offsets, ctx, p, err);
     return cudaGetLastError();
 }
 

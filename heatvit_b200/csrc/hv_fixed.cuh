@@ -137,6 +137,15 @@ HV_DEV int32_t gelu_chain(int64_t v, int sh_in, int sh_out) {
     return (int32_t)requant64(shift_gelu(q16), sh_out, 8);
 }
 
+// 32-bit form of gelu_chain for host-checked ranges: |v| < 2^30, sh_in in
+// [1, 30] (q16 = sat24(rsa(v, sh_in))) and sh_out in [-7, 30] (|gelu| < 2^23,
+// so a left shift by at most 7 stays inside int32 before the int8 clamp).
+HV_DEV int32_t gelu_chain_fast(int32_t v, int sh_in, int sh_out) {
+    const int32_t q16 = sat24(rsa32(v, sh_in));
+    const int32_t g = shift_gelu(q16);
+    return sh_out >= 1 ? requant8_r(g, sh_out) : sat8(g * (1 << -sh_out));
+}
+
 // PLAN sigmoid (nonlinear.py:83-95), unsigned Q0.16.
 HV_HD int32_t plan_sigmoid(int32_t x) {
     int32_t ax = x < 0 ? -x : x, y;
@@ -190,6 +199,7 @@ HV_DEV uint32_t softmax_attn_u8(uint32_t ratio) {
 // out = requant((a << (ea - c)) + (b << (eb - c)), c, eo, 8), c = min(ea, eb).
 struct AlignAdd {
     int sa, sb, sh;   // left shifts of a and b, requant shift eo - c
+    int fast;         // sa, sb <= 22 and sh in [1, 30]: the sum fits int32
 };
 
 HV_HD AlignAdd make_align_add(int ea, int eb, int eo) {
@@ -198,11 +208,13 @@ HV_HD AlignAdd make_align_add(int ea, int eb, int eo) {
     r.sa = ea - c;
     r.sb = eb - c;
     r.sh = eo - c;
+    r.fast = (r.sa <= 22 && r.sb <= 22 && r.sh >= 1 && r.sh <= 30) ? 1 : 0;
     return r;
 }
 
 // Exact for shifts up to 54 (int8 << 54 stays below 2^62).
 HV_HD int32_t align_add8(int32_t a, int32_t b, AlignAdd k) {
+    if (k.fast) return requant8_r(a * (1 << k.sa) + b * (1 << k.sb), k.sh);
     int64_t v = ((int64_t)a << k.sa) + ((int64_t)b << k.sb);
     return (int32_t)requant64(v, k.sh, 8);
 }

@@ -65,10 +65,12 @@ __device__ __forceinline__ int32_t wb8(int32_t acc, int32_t bias, int shift) {
 template <int EPI, bool U8, bool WIDE>
 __global__ void __launch_bounds__(THREADS) gemm_kernel(GemmArgs g) {
     extern __shared__ __align__(128) uint8_t smem[];
+    // N tiles vary fastest so the CTAs that share an A tile run together and
+    // read it from L2 rather than DRAM.
     const int m_lim = g.m_dev ? *g.m_dev : g.m_host;
-    const int m0 = blockIdx.x * BM;
+    const int m0 = blockIdx.y * BM;
     if (m0 >= m_lim) return;
-    const int n0 = blockIdx.y * BN;
+    const int n0 = blockIdx.x * BN;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int wm = warp & 3, wn = warp >> 2;
     const int ktiles = g.k / BK;
@@ -213,7 +215,9 @@ __global__ void __launch_bounds__(THREADS) gemm_kernel(GemmArgs g) {
                     const int32_t b = (g.epi.bias && col < g.n) ? g.epi.bias[col] : 0;
                     int32_t o;
                     if (EPI == EPI_GELU) {
-                        o = gelu_chain((int64_t)a + b, g.epi.gelu_sh_in, g.epi.gelu_sh_out);
+                        o = (!WIDE && g.epi.gelu_fast)
+                                ? gelu_chain_fast(a + b, g.epi.gelu_sh_in, g.epi.gelu_sh_out)
+                                : gelu_chain((int64_t)a + b, g.epi.gelu_sh_in, g.epi.gelu_sh_out);
                     } else {
                         o = wb8<WIDE>(a, b, g.epi.shift);
                         if (EPI == EPI_I8_RES) {
@@ -252,7 +256,7 @@ __global__ void __launch_bounds__(THREADS) gemm_kernel(GemmArgs g) {
 template <int EPI, bool U8, bool WIDE>
 cudaError_t launch_t(const GemmArgs &g, int m_max, cudaStream_t st) {
     auto kern = gemm_kernel<EPI, U8, WIDE>;
-    dim3 grid((m_max + BM - 1) / BM, (g.n + BN - 1) / BN);
+    dim3 grid((g.n + BN - 1) / BN, (m_max + BM - 1) / BM);
     if (grid.x == 0) return cudaSuccess;
     kern<<<grid, THREADS, SMEM_BYTES, st>>>(g);
     return cudaGetLastError();
@@ -269,7 +273,7 @@ cudaError_t launch_gemm(const GemmArgs &g, int epi, int a_unsigned, int m_max, c
             return wide ? launch_t<EPI_I8_RES, false, true>(g, m_max, st)
                         : launch_t<EPI_I8_RES, false, false>(g, m_max, st);
         case EPI_GELU:
-            return launch_t<EPI_GELU, false, true>(g, m_max, st);
+            return wide ? launch_t<EPI_GELU, false, true>(g, m_max, st) : launch_t<EPI_GELU, false, false>(g, m_max, st);
         case EPI_PATCH:
             return wide ? launch_t<EPI_PATCH, false, true>(g, m_max, st)
                         : launch_t<EPI_PATCH, false, false>(g, m_max, st);

@@ -35,6 +35,7 @@ struct EpiParams {
     AlignAdd add;             // a = residual value, b = requantised GEMM value
     // GELU chain (EPI_GELU): sh_in = -16 - src, sh_out = dst + 16
     int gelu_sh_in, gelu_sh_out;
+    int gelu_fast;            // host-checked ranges of gelu_chain_fast hold
     // patch (EPI_PATCH): pos [197][192], add = (a = embed, b = pos)
     const int8_t *pos;
 };

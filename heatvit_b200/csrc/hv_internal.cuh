@@ -17,6 +17,8 @@ struct LnParams {
     int sh_g, sh_b;                // gamma/beta alignment left shifts
     int sh_out;                    // out_scale - common
     int fast;                      // 1: sh_g <= 16 and sh_b <= 40 (int64 output stage)
+    int split;                     // 1: x_scale <= -4, so |x_q32 - mean| <= 2^36 (64-bit split product)
+    int out32;                     // 1: sh_g == 0, sh_b <= 22, sh_out in [1, 30] (32-bit output stage)
 };
 
 LnParams make_ln(const int8_t *gamma, const int8_t *beta, int x_scale, int gamma_scale, int beta_scale,
@@ -40,7 +42,7 @@ struct AttnParams {
     int ctx_shift;     // context_out - (prob_scale + qkv_out)
     // fast = 1 when score_shift = -k (0 <= k <= 10) and q16_shift >= k: |Q.K| <= 2^20,
     // so acc << k fits int32 and q16 = rsa(acc, q16_shift - k) never saturates.
-    int fast, fast_shift;
+    int fast, fast_shift, fast_half, fast_negmask;
     int ctx_fast;      // ctx_shift in [1, 30]: |P.V| < 2^23, 32-bit rounding shift is exact
 };
 AttnParams make_attn(int qkv_out_scale, int score_scale, int prob_scale, int context_out_scale);

@@ -86,7 +86,7 @@ struct BlockDev {
     size_t ln1_g, ln1_b, wqkv, bqkv, wproj, bproj, ln2_g, ln2_b, w1, b1, w2, b2;
     int ln1_xs, ln1_gs, ln1_bs, ln1_os, ln2_xs, ln2_gs, ln2_bs, ln2_os;
     int qkv_shift, qkv_wide, proj_shift, proj_wide, fc2_shift, fc2_wide;
-    int fc1_sh_in, fc1_sh_out;
+    int fc1_sh_in, fc1_sh_out, fc1_wide, fc1_fast;
     AlignAdd res1, res2;
     AttnParams attn;
 };
@@ -316,9 +316,10 @@ int run_block(hv_model *m, int b, int images, const int32_t *off, cudaStream_t s
         Prof pr(m, HV_STAGE_FC1, st);
         GemmArgs g = gemm_args(m->LN, 192, 0, m->w<int8_t>(d.w1), HV_FFN, 192, 0, rows_dev, m->HID, HV_FFN);
         g.epi.bias = m->w<int32_t>(d.b1);
-        g.epi.bits_wide = 1;
+        g.epi.bits_wide = d.fc1_wide;
         g.epi.gelu_sh_in = d.fc1_sh_in;
         g.epi.gelu_sh_out = d.fc1_sh_out;
+        g.epi.gelu_fast = d.fc1_fast;
         CUDA_TRY(launch_gemm(g, EPI_GELU, 0, rows_max, st));
         pr.end(st, rows_dev, 0);
     }
@@ -485,6 +486,9 @@ int pack_model(hv_model *m, const hv_params *P) {
         d.proj_wide = needs_wide(q.bproj, 192, 192);
         d.fc1_sh_in = -16 - (q.ln2_out_scale_exp + q.w1_scale_exp);
         d.fc1_sh_out = q.hidden_out_scale_exp + 16;
+        d.fc1_wide = needs_wide(q.b1, HV_FFN, 192);
+        d.fc1_fast = (!d.fc1_wide && d.fc1_sh_in >= 1 && d.fc1_sh_in <= 30 && d.fc1_sh_out >= -7 &&
+                      d.fc1_sh_out <= 30) ? 1 : 0;
         d.fc2_shift = q.ffn_out_scale_exp - (q.hidden_out_scale_exp + q.w2_scale_exp);
         d.fc2_wide = needs_wide(q.b2, 192, HV_FFN);
         if (!align_ok(q.x_scale_exp, q.msa_out_scale_exp, q.ffn_x_scale_exp) ||

@@ -24,6 +24,8 @@ LnParams make_ln(const int8_t *gamma, const int8_t *beta, int x_scale, int gamma
     p.sh_b = beta_scale - common;
     p.sh_out = out_scale - common;
     p.fast = (p.sh_g <= 16 && p.sh_b <= 40) ? 1 : 0;
+    p.split = x_scale <= -4 ? 1 : 0;
+    p.out32 = (p.sh_g == 0 && p.sh_b <= 22 && p.sh_out >= 1 && p.sh_out <= 30) ? 1 : 0;
     return p;
 }
 
@@ -60,70 +62,125 @@ __device__ __forceinline__ int32_t requant128_8(i128 v, int shift) {
     return r > 127 ? 127 : (r < -128 ? -128 : (int32_t)r);
 }
 
-// One row; returns true on negative variance.  Whole warp participates.
-__device__ __forceinline__ bool ln_row(const int8_t *xr, int8_t *outr, const LnParams &p, int lane) {
-    const int w4 = *(const int32_t *)(xr + 4 * lane);
-    const int16_t w2 = *(const int16_t *)(xr + 128 + 2 * lane);
-    int32_t v[6];
-    v[0] = (int8_t)(w4 & 0xff);
-    v[1] = (int8_t)((w4 >> 8) & 0xff);
-    v[2] = (int8_t)((w4 >> 16) & 0xff);
-    v[3] = (int8_t)((w4 >> 24) & 0xff);
-    v[4] = (int8_t)(w2 & 0xff);
-    v[5] = (int8_t)((w2 >> 8) & 0xff);
+// Row statistics shared by the 8 lanes of a row group (nonlinear.py:159-172):
+// mean, inv_std_q32 and the negative-variance flag.
+struct LnStats {
+    int64_t mean;
+    uint64_t inv;
+    bool neg;
+};
+
+__device__ __forceinline__ LnStats ln_stats(int32_t s, int64_t s2, const LnParams &p) {
+    LnStats st;
+    const int64_t sum_x = (int64_t)s << p.sh_sum;
+    st.mean = round_div64(sum_x, 192);
+    const int64_t e2 = round_div64(s2, 192);
+    const uint64_t am = (uint64_t)(st.mean < 0 ? -st.mean : st.mean);
+    const int64_t mean_sq = (int64_t)(((u128)am * am + ((u128)1 << 31)) >> 32);
+    int64_t var = e2 - mean_sq;
+    st.neg = var < 0;
+    if (st.neg) var = 0;
+    const uint64_t sd = isqrt64((uint64_t)var + 4295u);
+    uint64_t inv = ((uint64_t)1 << 48) / sd;
+    if (2 * (((uint64_t)1 << 48) - inv * sd) >= sd) inv += 1;
+    st.inv = inv;
+    return st;
+}
+
+// norm = sat24(rsa((x_q32 - mean) * inv, 48)) (nonlinear.py:176-179).
+// Split path (|d| <= 2^36, inv < 2^42): with inv = hi*2^16 + lo, T = d*inv =
+// U*2^16 + B_lo where U = d*hi + floor(d*lo / 2^16) and B_lo = (d*lo) mod 2^16.
+// The ties-away rounding floor((T + 2^47 - [T<0]) / 2^48) then equals
+// floor((U + 2^31 - [T<0 and B_lo == 0]) / 2^32), because the dropped low part
+// is a fraction in [0, 1) of the 2^16 unit.
+__device__ __forceinline__ int32_t ln_norm(int32_t v, const LnStats &st, const LnParams &p) {
+    const int64_t d = ((int64_t)v << p.sh_sum) - st.mean;
+    int64_t nr;
+    if (p.split) {
+        const int64_t hi = (int64_t)(st.inv >> 16), lo = (int64_t)(st.inv & 0xFFFFu);
+        const int64_t a = d * hi;
+        const int64_t b = d * lo;
+        const int64_t u = a + (b >> 16);
+        const int64_t adj = (d < 0 && (b & 0xFFFF) == 0) ? 1 : 0;
+        nr = (u + ((int64_t)1 << 31) - adj) >> 32;
+    } else {
+        const i128 prod = (i128)d * (i128)st.inv;
+        const i128 r = (prod + ((i128)1 << 47) + (prod >> 127)) >> 48;
+        nr = r > 8388607 ? 8388607 : (r < -8388608 ? -8388608 : (int64_t)r);
+    }
+    return (int32_t)clamp_i64(nr, -8388608, 8388607);
+}
+
+// out = requant((norm*gamma << sh_g) + (beta << sh_b), common, out, 8) (nonlinear.py:181-186).
+__device__ __forceinline__ int32_t ln_out(int32_t norm, int32_t g, int32_t b, const LnParams &p) {
+    const int32_t prodg = norm * g;
+    if (p.out32) return requant8_r(prodg + (b << p.sh_b), p.sh_out);
+    if (p.fast) return (int32_t)requant64(((int64_t)prodg << p.sh_g) + ((int64_t)b << p.sh_b), p.sh_out, 8);
+    return requant128_8(((i128)prodg << p.sh_g) + ((i128)b << p.sh_b), p.sh_out);
+}
+
+// One row per 8-lane group; lane `sub` owns channels [24*sub, 24*sub + 24).
+// Returns true on negative variance.  All 32 lanes of the warp must call it.
+__device__ __forceinline__ bool ln_row8(const int8_t *xr, int8_t *outr, const LnParams &p, int sub, bool active) {
+    int32_t v[24];
+    uint2 w[3] = {make_uint2(0, 0), make_uint2(0, 0), make_uint2(0, 0)};
+    if (active) {
+        const uint2 *src = (const uint2 *)(xr + 24 * sub);
+        w[0] = src[0];
+        w[1] = src[1];
+        w[2] = src[2];
+    }
+#pragma unroll
+    for (int i = 0; i < 3; ++i) {
+#pragma unroll
+        for (int b = 0; b < 4; ++b) {
+            v[i * 8 + b] = (int8_t)((w[i].x >> (8 * b)) & 0xffu);
+            v[i * 8 + 4 + b] = (int8_t)((w[i].y >> (8 * b)) & 0xffu);
+        }
+    }
     int32_t s = 0;
 #pragma unroll
-    for (int i = 0; i < 6; ++i) s += v[i];
-    s = warp_sum_i32(s);
+    for (int i = 0; i < 24; ++i) s += v[i];
     int64_t s2;
     if (p.sq_shift >= 0) {
         int32_t q = 0;
 #pragma unroll
-        for (int i = 0; i < 6; ++i) q += v[i] * v[i];
-        s2 = (int64_t)warp_sum_i32(q) << p.sq_shift;
+        for (int i = 0; i < 24; ++i) q += v[i] * v[i];
+#pragma unroll
+        for (int o = 1; o < 8; o <<= 1) q += __shfl_xor_sync(0xffffffffu, q, o);
+        s2 = (int64_t)q << p.sq_shift;
     } else {
         const int k = -p.sq_shift;  // per-element ties-away right shift (x^2 >= 0)
         int64_t q = 0;
 #pragma unroll
-        for (int i = 0; i < 6; ++i) q += ((int64_t)(v[i] * v[i]) + ((int64_t)1 << (k - 1))) >> k;
-        s2 = warp_sum_i64(q);
+        for (int i = 0; i < 24; ++i) q += ((int64_t)(v[i] * v[i]) + ((int64_t)1 << (k - 1))) >> k;
+#pragma unroll
+        for (int o = 1; o < 8; o <<= 1) q += __shfl_xor_sync(0xffffffffu, q, o);
+        s2 = q;
     }
-    const int64_t sum_x = (int64_t)s << p.sh_sum;
-    const int64_t mean = round_div64(sum_x, 192);
-    const int64_t e2 = round_div64(s2, 192);
-    const uint64_t am = (uint64_t)(mean < 0 ? -mean : mean);
-    const int64_t mean_sq = (int64_t)(((u128)am * am + ((u128)1 << 31)) >> 32);
-    int64_t var = e2 - mean_sq;
-    const bool neg = var < 0;
-    if (neg) var = 0;
-    const uint64_t sd = isqrt64((uint64_t)var + 4295u);
-    uint64_t inv = ((uint64_t)1 << 48) / sd;
-    if (2 * (((uint64_t)1 << 48) - inv * sd) >= sd) inv += 1;
-
-    int32_t o[6];
+#pragma unroll
+    for (int o = 1; o < 8; o <<= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    const LnStats st = ln_stats(s, s2, p);
+    uint32_t ow[6];
 #pragma unroll
     for (int i = 0; i < 6; ++i) {
-        const int ch = i < 4 ? 4 * lane + i : 128 + 2 * lane + (i - 4);
-        const int64_t d = ((int64_t)v[i] << p.sh_sum) - mean;
-        const i128 prod = (i128)d * (i128)inv;
-        i128 nr = (prod + ((i128)1 << 47) + (prod >> 127)) >> 48;
-        const int32_t norm = nr > 8388607 ? 8388607 : (nr < -8388608 ? -8388608 : (int32_t)nr);
-        const int32_t prodg = norm * (int32_t)p.gamma[ch];
-        const int32_t b = p.beta[ch];
-        if (p.fast) {
-            const int64_t aligned = ((int64_t)prodg << p.sh_g) + ((int64_t)b << p.sh_b);
-            o[i] = (int32_t)requant64(aligned, p.sh_out, 8);
-        } else {
-            const i128 aligned = ((i128)prodg << p.sh_g) + ((i128)b << p.sh_b);
-            o[i] = requant128_8(aligned, p.sh_out);
+        uint32_t word = 0;
+#pragma unroll
+        for (int b = 0; b < 4; ++b) {
+            const int vi = i * 4 + b;  // byte vi of this lane's 24-byte slice
+            const int chan = 24 * sub + vi;
+            const int32_t o = ln_out(ln_norm(v[vi], st, p), p.gamma[chan], p.beta[chan], p);
+            word |= ((uint32_t)o & 0xffu) << (8 * b);
         }
+        ow[i] = word;
     }
-    const uint32_t ow = (uint32_t)(o[0] & 0xff) | ((uint32_t)(o[1] & 0xff) << 8) |
-                        ((uint32_t)(o[2] & 0xff) << 16) | ((uint32_t)(o[3] & 0xff) << 24);
-    const uint16_t oh = (uint16_t)((o[4] & 0xff) | ((o[5] & 0xff) << 8));
-    *(uint32_t *)(outr + 4 * lane) = ow;
-    *(uint16_t *)(outr + 128 + 2 * lane) = oh;
-    return neg;
+    if (active) {
+        uint2 *dst = (uint2 *)(outr + 24 * sub);
+        dst[0] = make_uint2(ow[0], ow[1]);
+        dst[1] = make_uint2(ow[2], ow[3]);
+        dst[2] = make_uint2(ow[4], ow[5]);
+    }
+    return st.neg;
 }
 
 __device__ __forceinline__ int image_of_row(const int32_t *offsets, int images, int row) {
@@ -140,11 +197,16 @@ __global__ void __launch_bounds__(256) ln_kernel(const int8_t *x, int8_t *out, i
                                                  LnParams p, uint8_t *negvar_row, const int32_t *offsets,
                                                  int images, uint8_t *warn) {
     const int rows = rows_dev ? *rows_dev : rows_max;
-    const int lane = threadIdx.x & 31;
+    const int lane = threadIdx.x & 31, sub = lane & 7, grp = lane >> 3;
     const int warps = (gridDim.x * blockDim.x) >> 5;
-    for (int r = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; r < rows; r += warps) {
-        const bool neg = ln_row(x + (size_t)r * 192, out + (size_t)r * 192, p, lane);
-        if (lane == 0) {
+    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    // each warp handles 4 rows per iteration (one per 8-lane group)
+    for (int base = warp * 4; base < rows; base += warps * 4) {
+        const int r = base + grp;
+        const bool active = r < rows;
+        const bool neg = ln_row8(x + (size_t)(active ? r : 0) * 192, out + (size_t)(active ? r : 0) * 192, p, sub,
+                                 active);
+        if (active && sub == 0) {
             if (negvar_row) negvar_row[r] = neg ? 1 : 0;
             if (neg && warn && offsets) {
                 const int img = image_of_row(offsets, images, r);
@@ -156,11 +218,12 @@ __global__ void __launch_bounds__(256) ln_kernel(const int8_t *x, int8_t *out, i
 
 __global__ void __launch_bounds__(256) ln_cls_kernel(const int8_t *x, const int32_t *offsets, int images, int8_t *out,
                                                      LnParams p, uint8_t *warn) {
-    const int lane = threadIdx.x & 31;
-    const int i = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-    if (i >= images) return;
-    const bool neg = ln_row(x + (size_t)offsets[i] * 192, out + (size_t)i * 192, p, lane);
-    if (neg && lane == 0 && warn)
+    const int lane = threadIdx.x & 31, sub = lane & 7, grp = lane >> 3;
+    const int i = ((blockIdx.x * blockDim.x + threadIdx.x) >> 5) * 4 + grp;
+    const bool active = i < images;
+    const bool neg = ln_row8(x + (size_t)(active ? offsets[i] : 0) * 192, out + (size_t)(active ? i : 0) * 192, p,
+                             sub, active);
+    if (neg && active && sub == 0 && warn)
         atomicOr((unsigned int *)(warn + (i & ~3)), (unsigned int)HV_WARN_LN_NEG_VARIANCE << (8 * (i & 3)));
 }
 
@@ -256,10 +319,10 @@ cudaError_t launch_layernorm(const int8_t *x, int8_t *out, int rows_max, const i
                              const LnParams &p, uint8_t *negvar_row, const int32_t *offsets, int images,
                              uint8_t *warn, cudaStream_t st) {
     if (rows_max <= 0) return cudaSuccess;
-    const int warps_per_block = 8;
-    int blocks = (rows_max + warps_per_block - 1) / warps_per_block;
-    if (blocks > 148 * 8) blocks = 148 * 8;
-    ln_kernel<<<blocks, 32 * warps_per_block, 0, st>>>(x, out, rows_max, rows_dev, p, negvar_row, offsets, images,
+    const int rows_per_block = 8 * 4;  // 8 warps x 4 rows
+    int blocks = (rows_max + rows_per_block - 1) / rows_per_block;
+    if (blocks > 148 * 16) blocks = 148 * 16;
+    ln_kernel<<<blocks, 256, 0, st>>>(x, out, rows_max, rows_dev, p, negvar_row, offsets, images,
                                                        warn);
     return cudaGetLastError();
 }
@@ -267,7 +330,7 @@ cudaError_t launch_layernorm(const int8_t *x, int8_t *out, int rows_max, const i
 cudaError_t launch_layernorm_cls(const int8_t *x, const int32_t *offsets, int images, int8_t *out,
                                  const LnParams &p, uint8_t *warn, cudaStream_t st) {
     if (images <= 0) return cudaSuccess;
-    ln_cls_kernel<<<(images + 7) / 8, 256, 0, st>>>(x, offsets, images, out, p, warn);
+    ln_cls_kernel<<<(images + 31) / 32, 256, 0, st>>>(x, offsets, images, out, p, warn);
     return cudaGetLastError();
 }
 

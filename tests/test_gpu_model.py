@@ -266,3 +266,20 @@ def test_model_parameter_errors(cuda):
                   + params.blocks[1:])
     with pytest.raises(ValueError):
         Engine(bad)
+
+
+@pytest.mark.parametrize("l2,w1,hid", [(-12, -8, -11), (-20, -20, -8), (-9, -8, -20), (-8, -8, -9), (-14, -2, -5),
+                                       (-7, -10, -13)])
+def test_ffn_gelu_epilogue_exponents(cuda, oracle, l2, w1, hid):
+    """FC1's fused GELU epilogue (32-bit fast form and 64-bit generic form)
+    across input/output exponents, through the fused block kernel."""
+    from dataclasses import replace
+    from heatvit_b200 import synth
+    from heatvit_b200.transformer import transformer_block_batch
+    blk = synth.config_params(synth.SEED, pruned=True).blocks[2]
+    blk = replace(blk, ffn=replace(blk.ffn, ln2_out_scale_exp=l2, w1_scale_exp=w1, hidden_out_scale_exp=hid))
+    rng = np.random.default_rng(abs(l2 * 31 + hid))
+    xs = [rng.integers(-128, 128, (n, 192)) for n in (197, 64, 5)]
+    for x, z in zip(xs, transformer_block_batch(xs, blk)):
+        want, _, _ = oracle.transformer_block(x, blk)
+        np.testing.assert_array_equal(z, want)
