@@ -1,59 +1,46 @@
-// hv_gemm.cu — int8 tensor-core GEMM (mma.sync m16n8k32) with fused epilogues.
+// hv_gemm.cu — int8 GEMM on tcgen05 tensor cores with fused integer epilogues.
 //
-// CTA tile 128 x 64 x 64, 8 warps (4 along M x 2 along N, warp tile 32 x 32),
-// 3-stage cp.async pipeline, XOR-swizzled shared tiles (16-byte chunk c of row r
-// is stored at chunk c ^ ((r >> 1) & 3), which makes every ldmatrix phase hit
-// 32 distinct banks).  Ragged batches pass the live row count through device
-// memory; CTAs past it exit before touching memory.
+// One CTA computes a 128 x BN output tile (BN = 64, 192 or 256 columns):
+//   * 256 threads stream A [128 x 64] and B [BN x 64] k-tiles with cp.async into
+//     a 4-stage ring, each stage in the no-swizzle K-major canonical layout
+//     (hv_tc05.cuh); 8 consecutive threads fill one 128-byte core matrix, so
+//     the shared-memory writes are conflict-free.
+//   * one thread issues tcgen05.mma kind::i8 (M = 128, N = BN, K = 32 per
+//     instruction) into a TMEM accumulator of BN columns; each stage's MMAs
+//     commit to that stage's mbarrier, which gates the refill of the stage.
+//   * the epilogue reads the accumulator straight from TMEM: thread t owns row
+//     t % 128 (its TMEM lane) and half of the columns, applies the golden
+//     writeback and what follows it, and stores 32 contiguous bytes at a time.
+// Ragged batches pass the live row count through device memory; CTAs past it
+// exit before allocating anything.  TMEM: 256 columns per CTA, two CTAs per SM.
 #include "hv_gemm.cuh"
+#include "hv_tc05.cuh"
 
 namespace hv {
 
 namespace {
 
-constexpr int BM = 128, BN = 64, BK = 64, STAGES = 3, THREADS = 256;
-constexpr int A_TILE = BM * BK;
-constexpr int B_TILE = BN * BK;
-constexpr int STAGE_BYTES = A_TILE + B_TILE;
-constexpr int SMEM_BYTES = STAGES * STAGE_BYTES;
+constexpr int THREADS = 256;
+constexpr int BM = 128, BK = 64, STAGES = 4;
+constexpr uint32_t TMEM_COLS = 256;
+constexpr uint32_t WAIT_ITERS = 1u << 24;
 
-__device__ __forceinline__ uint32_t smem_u32(const void *p) {
-    return (uint32_t)__cvta_generic_to_shared(p);
-}
-
-__device__ __forceinline__ int swz(int row, int chunk) {
-    return row * BK + ((chunk ^ ((row >> 1) & 3)) << 4);
-}
+template <int BN>
+struct Layout {
+    static constexpr int A_ST = BM * BK;
+    static constexpr int B_ST = BN * BK;
+    static constexpr int STAGE = A_ST + B_ST;
+    static constexpr int OFF_BIAS = STAGES * STAGE;
+    static constexpr int OFF_BAR = OFF_BIAS + BN * 4;
+    static constexpr int SMEM = OFF_BAR + 64;
+};
 
 __device__ __forceinline__ void cp_async16(uint32_t saddr, const void *g, int src_bytes) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(saddr), "l"(g), "r"(src_bytes));
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(saddr), "l"(g), "r"(src_bytes) : "memory");
 }
-__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;\n" ::); }
+__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
 template <int N>
-__device__ __forceinline__ void cp_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N)); }
-
-__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], uint32_t addr) {
-    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];\n"
-                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
-                 : "r"(addr));
-}
-
-template <bool U8>
-__device__ __forceinline__ void mma_i8(int (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
-    if (U8) {
-        asm volatile(
-            "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-            "{%0,%1,%2,%3};\n"
-            : "+r"(c[0]), "+r"(c[1]), "+r"(c[2]), "+r"(c[3])
-            : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-    } else {
-        asm volatile(
-            "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-            "{%0,%1,%2,%3};\n"
-            : "+r"(c[0]), "+r"(c[1]), "+r"(c[2]), "+r"(c[3])
-            : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-    }
-}
+__device__ __forceinline__ void cp_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory"); }
 
 // First writeback: requant(acc + bias, shift, 8).
 template <bool WIDE>
@@ -62,27 +49,47 @@ __device__ __forceinline__ int32_t wb8(int32_t acc, int32_t bias, int shift) {
     return (int32_t)requant64((int64_t)acc + bias, shift, 8);
 }
 
-template <int EPI, bool U8, bool WIDE>
-__global__ void __launch_bounds__(THREADS) gemm_kernel(GemmArgs g) {
-    extern __shared__ __align__(128) uint8_t smem[];
-    // N tiles vary fastest so the CTAs that share an A tile run together and
-    // read it from L2 rather than DRAM.
+__device__ __forceinline__ int32_t byte_of(const uint32_t (&w)[8], int j) {
+    return (int8_t)((w[j >> 2] >> (8 * (j & 3))) & 0xffu);
+}
+
+template <int EPI, bool U8, bool WIDE, int BN>
+__global__ void __launch_bounds__(THREADS) tc_gemm_kernel(GemmArgs g, int *err) {
+    using L = Layout<BN>;
+    extern __shared__ __align__(1024) uint8_t smem[];
+    int32_t *sbias = (int32_t *)(smem + L::OFF_BIAS);
+    uint64_t *bar = (uint64_t *)(smem + L::OFF_BAR);
+    uint32_t *tslot = (uint32_t *)(smem + L::OFF_BAR + 8 * STAGES);
+    volatile int *abortf = (volatile int *)(smem + L::OFF_BAR + 8 * STAGES + 4);
+
+    // N tiles vary fastest so the CTAs sharing an A tile run together (L2 reuse).
     const int m_lim = g.m_dev ? *g.m_dev : g.m_host;
     const int m0 = blockIdx.y * BM;
     if (m0 >= m_lim) return;
     const int n0 = blockIdx.x * BN;
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int wm = warp & 3, wn = warp >> 2;
-    const int ktiles = g.k / BK;
+    const int tid = threadIdx.x, warp = tid >> 5;
+    const int KT = g.k / BK;
     const uint8_t *abase = (const uint8_t *)g.a.ptr;
 
-    auto load_stage = [&](int stage, int kt) {
-        uint8_t *sA = smem + stage * STAGE_BYTES;
-        uint8_t *sB = sA + A_TILE;
+    if (warp == 0) {
+        tc05::tmem_alloc(tslot, TMEM_COLS);
+        tc05::tmem_relinquish();
+    }
+    if (tid < STAGES) tc05::mbar_init(&bar[tid], 1);
+    if (tid == 0) {
+        *abortf = 0;
+        tc05::fence_mbar_init();
+    }
+    for (int i = tid; i < BN; i += THREADS) sbias[i] = (g.epi.bias && n0 + i < g.n) ? g.epi.bias[n0 + i] : 0;
+
+    // Chunk c of a tile: core matrix (c >> 5, (c >> 3) & 3), row c & 7 inside it.
+    auto load_stage = [&](int s, int kt) {
+        uint8_t *sA = smem + s * L::STAGE;
+        uint8_t *sB = sA + L::A_ST;
 #pragma unroll
-        for (int i = 0; i < 2; ++i) {
+        for (int i = 0; i < (BM * 4) / THREADS; ++i) {
             const int c = tid + i * THREADS;
-            const int row = c >> 2, ch = c & 3;
+            const int row = (c >> 5) * 8 + (c & 7), kc = (c >> 3) & 3;
             const int grow = m0 + row;
             const uint8_t *src = abase;
             int bytes = 0;
@@ -93,195 +100,218 @@ __global__ void __launch_bounds__(THREADS) gemm_kernel(GemmArgs g) {
                     // so a 16-byte chunk never straddles an image row (48 = 3 * 16).
                     const int img = grow / 196, p = grow - img * 196;
                     const int pr = p / 14, pc = p - pr * 14;
-                    const int k = kt * BK + ch * 16;
+                    const int k = kt * BK + kc * 16;
                     const int ir = k / 48, w = k - ir * 48;
                     src = abase + (size_t)img * 150528 + ((pr * 16 + ir) * 224 + pc * 16) * 3 + w;
                 } else {
-                    src = abase + (size_t)grow * g.a.lda + kt * BK + ch * 16;
+                    src = abase + (size_t)grow * g.a.lda + kt * BK + kc * 16;
                 }
             }
-            cp_async16(smem_u32(sA + swz(row, ch)), src, bytes);
+            cp_async16(tc05::smem_u32(sA + (c >> 5) * (8 * BK) + kc * 128 + (c & 7) * 16), src, bytes);
         }
-        {
-            const int row = tid >> 2, ch = tid & 3;
-            const int8_t *src = g.bt + (size_t)(n0 + row) * g.k + kt * BK + ch * 16;
-            cp_async16(smem_u32(sB + swz(row, ch)), src, 16);
+#pragma unroll
+        for (int i = 0; i < (BN * 4) / THREADS; ++i) {
+            const int c = tid + i * THREADS;
+            const int row = (c >> 5) * 8 + (c & 7), kc = (c >> 3) & 3;
+            const int8_t *src = g.bt + (size_t)(n0 + row) * g.k + kt * BK + kc * 16;
+            cp_async16(tc05::smem_u32(sB + (c >> 5) * (8 * BK) + kc * 128 + (c & 7) * 16), src, 16);
         }
     };
 
-    int acc[2][4][4];
 #pragma unroll
-    for (int i = 0; i < 2; ++i)
-#pragma unroll
-        for (int j = 0; j < 4; ++j)
-#pragma unroll
-            for (int e = 0; e < 4; ++e) acc[i][j][e] = 0;
-
-#pragma unroll
-    for (int s = 0; s < STAGES - 1; ++s) {
-        if (s < ktiles) load_stage(s, s);
+    for (int s = 0; s < STAGES; ++s) {
+        if (s < KT) load_stage(s, s);
         cp_commit();
     }
+    tc05::fence_before();
+    __syncthreads();
+    tc05::fence_after();
+    const uint32_t tbase = *tslot;
+    const uint32_t idesc = tc05::idesc_i8(BM, BN, !U8, true);
+    uint32_t phases = 0;
 
-    const int q = lane >> 3, r8 = lane & 7;
-    for (int kt = 0; kt < ktiles; ++kt) {
+    for (int kt = 0; kt < KT; ++kt) {
+        const int s = kt % STAGES;
         cp_wait<STAGES - 2>();
+        tc05::fence_proxy_async();
         __syncthreads();
-        {
-            const int pf = kt + STAGES - 1;
-            if (pf < ktiles) load_stage(pf % STAGES, pf);
-            cp_commit();
+        if (*abortf) break;
+        if (tid == 0) {
+            tc05::fence_after();
+            const uint32_t a0 = tc05::smem_u32(smem + s * L::STAGE), b0 = a0 + L::A_ST;
+#pragma unroll
+            for (int ks = 0; ks < 2; ++ks)
+                tc05::mma_i8_ss(tbase, tc05::smem_desc(a0 + ks * 256, 128, 8 * BK),
+                                tc05::smem_desc(b0 + ks * 256, 128, 8 * BK), idesc, (kt | ks) != 0);
+            tc05::commit(&bar[s]);
         }
-        const uint8_t *sA = smem + (kt % STAGES) * STAGE_BYTES;
-        const uint8_t *sB = sA + A_TILE;
-#pragma unroll
-        for (int ks = 0; ks < 2; ++ks) {
-            uint32_t af[2][4], bf[2][4];
-#pragma unroll
-            for (int i = 0; i < 2; ++i) {
-                const int row = wm * 32 + i * 16 + (q & 1) * 8 + r8;
-                ldsm_x4(af[i], smem_u32(sA + swz(row, ks * 2 + (q >> 1))));
+        // Refill the stage the previous k-tile used once its MMAs completed.
+        if (kt >= 1 && kt - 1 + STAGES < KT) {
+            const int ps = (kt - 1) % STAGES;
+            if (tc05::mbar_wait(&bar[ps], (phases >> ps) & 1u, WAIT_ITERS)) {
+                phases ^= 1u << ps;
+                load_stage(ps, kt - 1 + STAGES);
+            } else {
+                *abortf = 1;
             }
-#pragma unroll
-            for (int p = 0; p < 2; ++p) {
-                const int row = wn * 32 + p * 16 + (q >> 1) * 8 + r8;
-                ldsm_x4(bf[p], smem_u32(sB + swz(row, ks * 2 + (q & 1))));
-            }
-#pragma unroll
-            for (int i = 0; i < 2; ++i)
-#pragma unroll
-                for (int j = 0; j < 4; ++j)
-                    mma_i8<U8>(acc[i][j], af[i], bf[j >> 1][(j & 1) * 2], bf[j >> 1][(j & 1) * 2 + 1]);
+        }
+        cp_commit();
+    }
+    // Every MMA has completed once the last stage's final phase has.
+    {
+        const int ls = (KT - 1) % STAGES;
+        if (!*abortf) {
+            if (tc05::mbar_wait(&bar[ls], (phases >> ls) & 1u, WAIT_ITERS)) phases ^= 1u << ls;
+            else *abortf = 1;
         }
     }
     cp_wait<0>();
     __syncthreads();
 
-    const int gid = lane >> 2, t4 = lane & 3;
-
-    if (EPI == EPI_I32 || EPI == EPI_ACC64) {
+    if (!*abortf) {
+        tc05::fence_after();
+        const int row = tid & 127, half = tid >> 7;
+        const int grow = m0 + row;
+        const bool valid = grow < m_lim;
+        const uint32_t lane_addr = tbase + ((uint32_t)((warp & 3) * 32) << 16);
+        size_t orow = (size_t)grow;
+        int pidx = 0;
+        if (EPI == EPI_PATCH) {
+            const int img = valid ? grow / 196 : 0;
+            pidx = valid ? grow - img * 196 : 0;
+            orow = (size_t)img * 197 + 1 + pidx;
+        }
+#pragma unroll 1
+        for (int c = 0; c < BN / 64; ++c) {
+            const int col0 = half * (BN / 2) + c * 32;  // tile-local column of v[0]
+            const int gcol0 = n0 + col0;
+            uint32_t v[32];
+            tc05::ld32(lane_addr + col0, v);
+            tc05::wait_ld();
+            if (EPI == EPI_I32 || EPI == EPI_ACC64) {
+                if (valid) {
 #pragma unroll
-        for (int i = 0; i < 2; ++i)
-#pragma unroll
-            for (int j = 0; j < 4; ++j)
-#pragma unroll
-                for (int hh = 0; hh < 2; ++hh) {
-                    const int grow = m0 + wm * 32 + i * 16 + gid + hh * 8;
-                    if (grow >= m_lim) continue;
-#pragma unroll
-                    for (int e = 0; e < 2; ++e) {
-                        const int col = n0 + wn * 32 + j * 8 + t4 * 2 + e;
-                        if (col >= g.n) continue;
-                        const int64_t v = (int64_t)acc[i][j][hh * 2 + e] + (g.epi.bias ? g.epi.bias[col] : 0);
+                    for (int j = 0; j < 32; ++j) {
+                        if (gcol0 + j >= g.n) break;
+                        const int64_t x = (int64_t)(int32_t)v[j] + sbias[col0 + j];
                         if (EPI == EPI_I32)
-                            ((int32_t *)g.out)[(size_t)grow * g.ldo + col] = (int32_t)requant64(v, g.epi.shift, 32);
+                            ((int32_t *)g.out)[orow * g.ldo + gcol0 + j] = (int32_t)requant64(x, g.epi.shift, 32);
                         else
-                            ((int64_t *)g.out)[(size_t)grow * g.ldo + col] = v;
+                            ((int64_t *)g.out)[orow * g.ldo + gcol0 + j] = x;
                     }
                 }
-        return;
-    }
-
-    // int8 epilogues go through a shared tile so the global stores are 16-byte.
-    int8_t *sC = (int8_t *)smem;                   // [128][64]
-    const int8_t *sR = (const int8_t *)(smem + A_TILE);  // residual [128][64]
-    if (EPI == EPI_I8_RES) {
-        int8_t *sRw = (int8_t *)(smem + A_TILE);
+                continue;
+            }
+            uint4 r0 = make_uint4(0, 0, 0, 0), r1 = r0;
+            if (EPI == EPI_I8_RES && valid) {
+                const uint4 *r = (const uint4 *)(g.epi.res + orow * g.ldo + gcol0);
+                r0 = r[0];
+                r1 = r[1];
+            }
+            if (EPI == EPI_PATCH) {
+                const uint4 *r = (const uint4 *)(g.epi.pos + (pidx + 1) * 192 + gcol0);
+                r0 = r[0];
+                r1 = r[1];
+            }
+            const uint32_t aux[8] = {r0.x, r0.y, r0.z, r0.w, r1.x, r1.y, r1.z, r1.w};
+            uint32_t pk[8];
 #pragma unroll
-        for (int i = 0; i < 2; ++i) {
-            const int c = tid + i * THREADS;
-            const int row = c >> 2, ch = c & 3;
-            const int grow = m0 + row;
-            int4 v = make_int4(0, 0, 0, 0);
-            if (grow < m_lim) v = *(const int4 *)(g.epi.res + (size_t)grow * g.ldo + n0 + ch * 16);
-            *(int4 *)(sRw + row * BN + ch * 16) = v;
-        }
-        __syncthreads();
-    }
-
+            for (int w = 0; w < 8; ++w) {
+                uint32_t word = 0;
 #pragma unroll
-    for (int i = 0; i < 2; ++i)
-#pragma unroll
-        for (int j = 0; j < 4; ++j)
-#pragma unroll
-            for (int hh = 0; hh < 2; ++hh) {
-                const int lrow = wm * 32 + i * 16 + gid + hh * 8;
-                const int grow = m0 + lrow;
-#pragma unroll
-                for (int e = 0; e < 2; ++e) {
-                    const int lcol = wn * 32 + j * 8 + t4 * 2 + e;
-                    const int col = n0 + lcol;
-                    const int32_t a = acc[i][j][hh * 2 + e];
-                    const int32_t b = (g.epi.bias && col < g.n) ? g.epi.bias[col] : 0;
+                for (int b = 0; b < 4; ++b) {
+                    const int j = w * 4 + b;
+                    const int32_t a = (int32_t)v[j];
+                    const int32_t bb = sbias[col0 + j];
                     int32_t o;
                     if (EPI == EPI_GELU) {
-                        o = (!WIDE && g.epi.gelu_fast)
-                                ? gelu_chain_fast(a + b, g.epi.gelu_sh_in, g.epi.gelu_sh_out)
-                                : gelu_chain((int64_t)a + b, g.epi.gelu_sh_in, g.epi.gelu_sh_out);
+                        o = (!WIDE && g.epi.gelu_fast) ? gelu_chain_fast(a + bb, g.epi.gelu_sh_in, g.epi.gelu_sh_out)
+                                                       : gelu_chain((int64_t)a + bb, g.epi.gelu_sh_in,
+                                                                    g.epi.gelu_sh_out);
                     } else {
-                        o = wb8<WIDE>(a, b, g.epi.shift);
-                        if (EPI == EPI_I8_RES) {
-                            o = align_add8(sR[lrow * BN + lcol], o, g.epi.add);
-                        } else if (EPI == EPI_PATCH) {
-                            const int p = grow < m_lim ? grow % 196 : 0;
-                            o = align_add8(o, g.epi.pos[(p + 1) * 192 + col], g.epi.add);
-                        }
+                        o = wb8<WIDE>(a, bb, g.epi.shift);
+                        if (EPI == EPI_I8_RES) o = align_add8(byte_of(aux, j), o, g.epi.add);
+                        else if (EPI == EPI_PATCH) o = align_add8(o, byte_of(aux, j), g.epi.add);
                     }
-                    sC[lrow * BN + lcol] = (int8_t)o;
+                    word |= ((uint32_t)o & 0xffu) << (8 * b);
+                }
+                pk[w] = word;
+            }
+            if (valid) {
+                int8_t *dst = (int8_t *)g.out + orow * g.ldo + gcol0;
+                if (gcol0 + 32 <= g.n) {
+                    ((uint4 *)dst)[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+                    ((uint4 *)dst)[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+                } else {
+#pragma unroll
+                    for (int w = 0; w < 8; ++w)
+#pragma unroll
+                        for (int b = 0; b < 4; ++b)
+                            if (gcol0 + w * 4 + b < g.n) dst[w * 4 + b] = (int8_t)(pk[w] >> (8 * b));
                 }
             }
+        }
+    } else {
+        if (tid == 0) atomicExch(err, 2);
+        // let MMAs still in flight drain (bounded) before the TMEM is released
+        for (int s = 0; s < STAGES; ++s) tc05::mbar_wait(&bar[s], (phases >> s) & 1u, WAIT_ITERS);
+    }
+    tc05::fence_before();
     __syncthreads();
-
-#pragma unroll
-    for (int i = 0; i < 2; ++i) {
-        const int c = tid + i * THREADS;
-        const int row = c >> 2, ch = c & 3;
-        const int grow = m0 + row;
-        if (grow >= m_lim) continue;
-        size_t orow = (size_t)grow;
-        if (EPI == EPI_PATCH) {
-            const int img = grow / 196;
-            orow = (size_t)img * 197 + 1 + (grow - img * 196);
-        }
-        int8_t *dst = (int8_t *)g.out + orow * g.ldo + n0 + ch * 16;
-        if (n0 + ch * 16 + 16 <= g.n) {
-            *(int4 *)dst = *(const int4 *)(sC + row * BN + ch * 16);
-        } else {
-            for (int e = 0; e < 16; ++e)
-                if (n0 + ch * 16 + e < g.n) dst[e] = sC[row * BN + ch * 16 + e];
-        }
+    if (warp == 0) {
+        tc05::fence_after();
+        tc05::tmem_dealloc(tbase, TMEM_COLS);
     }
 }
 
-template <int EPI, bool U8, bool WIDE>
-cudaError_t launch_t(const GemmArgs &g, int m_max, cudaStream_t st) {
-    auto kern = gemm_kernel<EPI, U8, WIDE>;
+template <int EPI, bool U8, bool WIDE, int BN>
+cudaError_t launch_t(const GemmArgs &g, int m_max, int *err, cudaStream_t st) {
+    auto kern = tc_gemm_kernel<EPI, U8, WIDE, BN>;
+    const int smem = Layout<BN>::SMEM;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
     dim3 grid((g.n + BN - 1) / BN, (m_max + BM - 1) / BM);
-    if (grid.x == 0) return cudaSuccess;
-    kern<<<grid, THREADS, SMEM_BYTES, st>>>(g);
+    if (grid.x == 0 || grid.y == 0) return cudaSuccess;
+    kern<<<grid, THREADS, smem, st>>>(g, err);
     return cudaGetLastError();
+}
+
+template <int EPI, bool U8, bool WIDE>
+cudaError_t launch_bn(const GemmArgs &g, int m_max, int *err, cudaStream_t st) {
+    if (g.n % 192 == 0) return launch_t<EPI, U8, WIDE, 192>(g, m_max, err, st);
+    if (g.n > 256 || g.n % 64 != 0) return launch_t<EPI, U8, WIDE, 256>(g, m_max, err, st);
+    return launch_t<EPI, U8, WIDE, 64>(g, m_max, err, st);
 }
 
 }  // namespace
 
-cudaError_t launch_gemm(const GemmArgs &g, int epi, int a_unsigned, int m_max, cudaStream_t st) {
+int gemm_tile_n(int n) {
+    if (n % 192 == 0) return 192;
+    if (n > 256 || n % 64 != 0) return 256;
+    return 64;
+}
+
+cudaError_t launch_gemm(const GemmArgs &g, int epi, int a_unsigned, int m_max, int *err, cudaStream_t st) {
     const bool wide = g.epi.bits_wide != 0;
     switch (epi) {
         case EPI_I8:
-            return wide ? launch_t<EPI_I8, false, true>(g, m_max, st) : launch_t<EPI_I8, false, false>(g, m_max, st);
+            return wide ? launch_bn<EPI_I8, false, true>(g, m_max, err, st)
+                        : launch_bn<EPI_I8, false, false>(g, m_max, err, st);
         case EPI_I8_RES:
-            return wide ? launch_t<EPI_I8_RES, false, true>(g, m_max, st)
-                        : launch_t<EPI_I8_RES, false, false>(g, m_max, st);
+            return wide ? launch_bn<EPI_I8_RES, false, true>(g, m_max, err, st)
+                        : launch_bn<EPI_I8_RES, false, false>(g, m_max, err, st);
         case EPI_GELU:
-            return wide ? launch_t<EPI_GELU, false, true>(g, m_max, st) : launch_t<EPI_GELU, false, false>(g, m_max, st);
+            return wide ? launch_bn<EPI_GELU, false, true>(g, m_max, err, st)
+                        : launch_bn<EPI_GELU, false, false>(g, m_max, err, st);
         case EPI_PATCH:
-            return wide ? launch_t<EPI_PATCH, false, true>(g, m_max, st)
-                        : launch_t<EPI_PATCH, false, false>(g, m_max, st);
+            return wide ? launch_bn<EPI_PATCH, false, true>(g, m_max, err, st)
+                        : launch_bn<EPI_PATCH, false, false>(g, m_max, err, st);
         case EPI_I32:
-            return a_unsigned ? launch_t<EPI_I32, true, true>(g, m_max, st) : launch_t<EPI_I32, false, true>(g, m_max, st);
+            return a_unsigned ? launch_bn<EPI_I32, true, true>(g, m_max, err, st)
+                              : launch_bn<EPI_I32, false, true>(g, m_max, err, st);
         case EPI_ACC64:
-            return a_unsigned ? launch_t<EPI_ACC64, true, true>(g, m_max, st)
-                              : launch_t<EPI_ACC64, false, true>(g, m_max, st);
+            return a_unsigned ? launch_bn<EPI_ACC64, true, true>(g, m_max, err, st)
+                              : launch_bn<EPI_ACC64, false, true>(g, m_max, err, st);
         default:
             return cudaErrorInvalidValue;
     }

@@ -1,6 +1,7 @@
 // hv_gemm.cuh — int8 GEMM with fused integer epilogues.
 //
-// C[M][N] = A[M][K] · Bt[N][K]ᵀ (+ bias), int32 accumulation, then one of the
+// C[M][N] = A[M][K] · Bt[N][K]ᵀ (+ bias), int32 accumulation on tcgen05 tensor
+// cores (accumulator in TMEM), then one of the
 // golden writebacks (gemm.py:123-139) fused with what follows it in the model:
 //   EPI_I8       requant to int8                          (QKV, generic)
 //   EPI_I8_RES   requant to int8, then residual align-add  (proj + residual 1,
@@ -49,7 +50,7 @@ struct ASrc {
 
 struct GemmArgs {
     ASrc a;
-    const int8_t *bt;         // [Npad][K] K-major weights (Npad multiple of 64)
+    const int8_t *bt;         // [Npad][K] K-major weights (Npad: see launch_gemm)
     int n, k;                 // logical N (stores guarded), K multiple of 64
     int m_host;               // row count when m_dev == nullptr
     const int32_t *m_dev;     // device row count (ragged batches), or nullptr
@@ -58,7 +59,10 @@ struct GemmArgs {
     EpiParams epi;
 };
 
-// Launch helpers (defined in hv_gemm.cu).
-cudaError_t launch_gemm(const GemmArgs &g, int epi, int a_unsigned, int m_max, cudaStream_t st);
+// Launch helpers (defined in hv_gemm.cu).  `bt` must hold
+// ceil(n / gemm_tile_n(n)) * gemm_tile_n(n) rows; k must be a multiple of 64.
+// err: device word set non-zero when a bounded wait gave up.
+int gemm_tile_n(int n);
+cudaError_t launch_gemm(const GemmArgs &g, int epi, int a_unsigned, int m_max, int *err, cudaStream_t st);
 
 }  // namespace hv

@@ -71,6 +71,8 @@ struct SelParams {
     int logit_q16_shift;              // logits -> Q16 (24 bit)
     int hw_sh_in, hw_sh_out;          // head-weight hidden GELU chain
     int hw_q16_shift;                 // head-weight acc -> Q16 (24 bit)
+    // 1 when gelu_chain_fast's ranges hold for that layer (host-checked)
+    int local_fast, h1_fast, h2_fast, hw_fast;
 };
 
 // Optional selector intermediates (token_selector API), image stride 196.

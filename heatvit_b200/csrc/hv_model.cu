@@ -288,7 +288,7 @@ int run_block(hv_model *m, int b, int images, const int32_t *off, cudaStream_t s
         g.epi.bias = m->w<int32_t>(d.bqkv);
         g.epi.shift = d.qkv_shift;
         g.epi.bits_wide = d.qkv_wide;
-        CUDA_TRY(launch_gemm(g, EPI_I8, 0, rows_max, st));
+        CUDA_TRY(launch_gemm(g, EPI_I8, 0, rows_max, m->err, st));
         pr.end(st, rows_dev, 0);
     }
     {
@@ -304,7 +304,7 @@ int run_block(hv_model *m, int b, int images, const int32_t *off, cudaStream_t s
         g.epi.bits_wide = d.proj_wide;
         g.epi.res = m->X;
         g.epi.add = d.res1;
-        CUDA_TRY(launch_gemm(g, EPI_I8_RES, 0, rows_max, st));
+        CUDA_TRY(launch_gemm(g, EPI_I8_RES, 0, rows_max, m->err, st));
         pr.end(st, rows_dev, 0);
     }
     {
@@ -320,7 +320,7 @@ int run_block(hv_model *m, int b, int images, const int32_t *off, cudaStream_t s
         g.epi.gelu_sh_in = d.fc1_sh_in;
         g.epi.gelu_sh_out = d.fc1_sh_out;
         g.epi.gelu_fast = d.fc1_fast;
-        CUDA_TRY(launch_gemm(g, EPI_GELU, 0, rows_max, st));
+        CUDA_TRY(launch_gemm(g, EPI_GELU, 0, rows_max, m->err, st));
         pr.end(st, rows_dev, 0);
     }
     {
@@ -331,7 +331,7 @@ int run_block(hv_model *m, int b, int images, const int32_t *off, cudaStream_t s
         g.epi.bits_wide = d.fc2_wide;
         g.epi.res = m->Y;
         g.epi.add = d.res2;
-        CUDA_TRY(launch_gemm(g, EPI_I8_RES, 0, rows_max, st));
+        CUDA_TRY(launch_gemm(g, EPI_I8_RES, 0, rows_max, m->err, st));
         pr.end(st, rows_dev, 0);
     }
     return HV_OK;
@@ -345,7 +345,7 @@ int run_patch(hv_model *m, const int8_t *images, int count, int8_t *out, cudaStr
     g.epi.bits_wide = m->patch_wide;
     g.epi.pos = m->w<int8_t>(m->pos);
     g.epi.add = m->patch_add;
-    CUDA_TRY(launch_gemm(g, EPI_PATCH, 0, count * HV_PATCHES, st));
+    CUDA_TRY(launch_gemm(g, EPI_PATCH, 0, count * HV_PATCHES, m->err, st));
     return HV_OK;
 }
 
@@ -418,7 +418,7 @@ int infer_impl(hv_model *m, const int8_t *d_images, int batch, int32_t *d_logits
         g.epi.shift = m->head_shift;
         g.epi.bits_wide = 1;
         Prof pr(m, HV_STAGE_HEAD, st);
-        CUDA_TRY(launch_gemm(g, EPI_I32, 0, batch, st));
+        CUDA_TRY(launch_gemm(g, EPI_I32, 0, batch, m->err, st));
         pr.end(st, nullptr, batch);
     }
     if (d_warnings) CUDA_TRY(cudaMemcpyAsync(d_warnings, m->warn, batch, cudaMemcpyDeviceToDevice, st));
@@ -557,6 +557,13 @@ int pack_model(hv_model *m, const hv_params *P) {
         p.hw_sh_in = -16 - (q.stats_out_scale_exp + q.hw_w1_scale_exp);
         p.hw_sh_out = q.hw_hidden_out_scale_exp + 16;
         p.hw_q16_shift = -16 - (q.hw_hidden_out_scale_exp + q.hw_w2_scale_exp);
+        auto fast = [](int sh_in, int sh_out, int64_t bound) {
+            return (sh_in >= 1 && sh_in <= 30 && sh_out >= -7 && sh_out <= 30 && bound < kNarrowLimit) ? 1 : 0;
+        };
+        p.local_fast = fast(p.local_sh_in, p.local_sh_out, max_abs(q.local_b, 96) + 64 * 16384);
+        p.h1_fast = fast(p.h1_sh_in, p.h1_sh_out, max_abs(q.score_b1, 96) + 64 * 16384);
+        p.h2_fast = fast(p.h2_sh_in, p.h2_sh_out, max_abs(q.score_b2, 48) + 32 * 16384);
+        p.hw_fast = fast(p.hw_sh_in, p.hw_sh_out, max_abs(q.hw_b1, 3) + 3 * 16384);
     }
     if (m->has_head) {
     if (!P->final_gamma || !P->final_beta || !P->head_b) return fail(HV_ERR_VALUE, "head parameters missing");
@@ -798,25 +805,33 @@ int hv_gemm_i8_acc(const void *d_a, const int8_t *d_b, const int32_t *d_bias, in
     if (k > (a_unsigned ? 65793 : 131071))
         return fail(HV_ERR_VALUE, "k=%d can overflow the int32 accumulator; not supported", k);
     cudaStream_t st = (cudaStream_t)stream;
-    const int kp = std::max(64, (k + 63) / 64 * 64), np = (n + 63) / 64 * 64;
+    const int tn = gemm_tile_n(n);
+    const int kp = std::max(64, (k + 63) / 64 * 64), np = (n + tn - 1) / tn * tn;
     uint8_t *ap = nullptr;
     int8_t *bp = nullptr;
+    int *err = nullptr;
     CUDA_TRY(cudaMalloc(&ap, (size_t)m * kp + 16));
-    if (cudaMalloc(&bp, (size_t)np * kp) != cudaSuccess) {
+    if (cudaMalloc(&bp, (size_t)np * kp) != cudaSuccess || cudaMalloc(&err, 16) != cudaSuccess) {
         cudaFree(ap);
-        return fail(HV_ERR_NOMEM, "cannot allocate padded B");
+        cudaFree(bp);
+        return fail(HV_ERR_NOMEM, "cannot allocate padded operands");
     }
     int rc = HV_OK;
+    cudaMemsetAsync(err, 0, 16, st);
     pad_a_kernel<<<148 * 4, 256, 0, st>>>((const uint8_t *)d_a, m, k, kp, ap);
     pad_b_kernel<<<148 * 4, 256, 0, st>>>(d_b, n, k, transpose_b, np, kp, bp);
     GemmArgs g = gemm_args(ap, kp, 0, bp, n, kp, m, nullptr, d_acc, n);
     g.epi.bias = d_bias;
     g.epi.bits_wide = 1;
-    cudaError_t e = launch_gemm(g, EPI_ACC64, a_unsigned, m, st);
+    cudaError_t e = launch_gemm(g, EPI_ACC64, a_unsigned, m, err, st);
     if (e != cudaSuccess) rc = fail(HV_ERR_CUDA, "gemm launch: %s", cudaGetErrorString(e));
     cudaStreamSynchronize(st);
+    int code = 0;
+    cudaMemcpy(&code, err, sizeof(int), cudaMemcpyDeviceToHost);
+    if (!rc && code) rc = fail(HV_ERR_STATE, "a device-side bounded wait gave up (code %d)", code);
     cudaFree(ap);
     cudaFree(bp);
+    cudaFree(err);
     return rc;
 }
 

@@ -132,7 +132,8 @@ __global__ void __launch_bounds__(THREADS) selector_kernel(
 #pragma unroll
         for (int w = 0; w < 16; ++w) acc = __dp4a(trow[w], wrow[w], acc);
         local[(h * MAXC + c) * LSTR + j] =
-            (int8_t)gelu_chain((int64_t)acc + p.local_b[h * 32 + j], p.local_sh_in, p.local_sh_out);
+            (int8_t)(p.local_fast ? gelu_chain_fast(acc + p.local_b[h * 32 + j], p.local_sh_in, p.local_sh_out)
+                                  : gelu_chain((int64_t)acc + p.local_b[h * 32 + j], p.local_sh_in, p.local_sh_out));
     }
     __syncthreads();
 
@@ -170,7 +171,10 @@ __global__ void __launch_bounds__(THREADS) selector_kernel(
                 int32_t acc = 0;
 #pragma unroll
                 for (int w = 0; w < 8; ++w) acc = __dp4a(lw[w], wrow[w], acc);
-                packed |= ((uint32_t)gelu_chain(acc + g1[h * 32 + j], p.h1_sh_in, p.h1_sh_out) & 0xffu) << (8 * b);
+                const int64_t x = acc + g1[h * 32 + j];
+                const int32_t o = p.h1_fast ? gelu_chain_fast((int32_t)x, p.h1_sh_in, p.h1_sh_out)
+                                            : gelu_chain(x, p.h1_sh_in, p.h1_sh_out);
+                packed |= ((uint32_t)o & 0xffu) << (8 * b);
             }
             h1w[jw] = packed;
         }
@@ -185,8 +189,10 @@ __global__ void __launch_bounds__(THREADS) selector_kernel(
                 int32_t acc = 0;
 #pragma unroll
                 for (int w = 0; w < 8; ++w) acc = __dp4a((int32_t)h1w[w], wrow[w], acc);
-                packed |= ((uint32_t)gelu_chain((int64_t)acc + p.b2[h * 16 + m], p.h2_sh_in, p.h2_sh_out) & 0xffu)
-                          << (8 * b);
+                const int64_t x = (int64_t)acc + p.b2[h * 16 + m];
+                const int32_t o = p.h2_fast ? gelu_chain_fast((int32_t)x, p.h2_sh_in, p.h2_sh_out)
+                                            : gelu_chain(x, p.h2_sh_in, p.h2_sh_out);
+                packed |= ((uint32_t)o & 0xffu) << (8 * b);
             }
             h2w[mw] = packed;
         }
@@ -221,7 +227,8 @@ __global__ void __launch_bounds__(THREADS) selector_kernel(
             int64_t acc = p.hb1[j];
 #pragma unroll
             for (int i = 0; i < 3; ++i) acc += st[i] * (int32_t)p.hw1[i * 3 + j];
-            hid[j] = gelu_chain(acc, p.hw_sh_in, p.hw_sh_out);
+            hid[j] = p.hw_fast ? gelu_chain_fast((int32_t)acc, p.hw_sh_in, p.hw_sh_out)
+                               : gelu_chain(acc, p.hw_sh_in, p.hw_sh_out);
         }
 #pragma unroll
         for (int j = 0; j < 3; ++j) {
