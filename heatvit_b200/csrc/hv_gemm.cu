@@ -267,7 +267,8 @@ __global__ void __launch_bounds__(THREADS) tc_gemm_kernel(GemmArgs g, int *err) 
 template <int EPI, bool U8, bool WIDE, int BN>
 cudaError_t launch_t(const GemmArgs &g, int m_max, int *err, cudaStream_t st) {
     auto kern = tc_gemm_kernel<EPI, U8, WIDE, BN>;
-    const int smem = Layout<BN>::SMEM;
+    // At least 76 KB so no more than two CTAs (2 x 256 TMEM columns) share an SM.
+    const int smem = Layout<BN>::SMEM > 76 * 1024 ? Layout<BN>::SMEM : 76 * 1024;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
     dim3 grid((g.n + BN - 1) / BN, (m_max + BM - 1) / BM);
