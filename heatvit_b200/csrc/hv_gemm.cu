@@ -22,8 +22,13 @@ namespace {
 
 constexpr int THREADS = 256;
 constexpr int BM = 128, BK = 64, STAGES = 4;
-constexpr uint32_t TMEM_COLS = 256;
 constexpr uint32_t WAIT_ITERS = 1u << 24;
+
+// TMEM columns of a BN-wide accumulator (a power of two >= 32).
+template <int BN>
+struct TmemCols {
+    static constexpr uint32_t value = BN <= 32 ? 32 : (BN <= 64 ? 64 : (BN <= 128 ? 128 : 256));
+};
 
 template <int BN>
 struct Layout {
@@ -42,18 +47,26 @@ __device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_grou
 template <int N>
 __device__ __forceinline__ void cp_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory"); }
 
-// First writeback: requant(acc + bias, shift, 8).
-template <bool WIDE>
+// First writeback: requant(acc + bias, shift, 8).  FAST: host-proven that
+// acc + bias fits in 30 bits and shift is in [1, 30].
+template <bool FAST>
 __device__ __forceinline__ int32_t wb8(int32_t acc, int32_t bias, int shift) {
-    if (!WIDE && shift >= 1 && shift <= 30) return requant8_r(acc + bias, shift);
+    if (FAST) return requant8_r(acc + bias, shift);
     return (int32_t)requant64((int64_t)acc + bias, shift, 8);
+}
+
+// Residual / positional align-add; FAST: host-proven 32-bit form applies.
+template <bool FAST>
+__device__ __forceinline__ int32_t add8(int32_t a, int32_t b, AlignAdd k) {
+    if (FAST) return requant8_r(a * (1 << k.sa) + b * (1 << k.sb), k.sh);
+    return (int32_t)requant64(((int64_t)a << k.sa) + ((int64_t)b << k.sb), k.sh, 8);
 }
 
 __device__ __forceinline__ int32_t byte_of(const uint32_t (&w)[8], int j) {
     return (int8_t)((w[j >> 2] >> (8 * (j & 3))) & 0xffu);
 }
 
-template <int EPI, bool U8, bool WIDE, int BN>
+template <int EPI, bool U8, bool FAST, int BN>
 __global__ void __launch_bounds__(THREADS) tc_gemm_kernel(GemmArgs g, int *err) {
     using L = Layout<BN>;
     extern __shared__ __align__(1024) uint8_t smem[];
@@ -71,6 +84,7 @@ __global__ void __launch_bounds__(THREADS) tc_gemm_kernel(GemmArgs g, int *err) 
     const int KT = g.k / BK;
     const uint8_t *abase = (const uint8_t *)g.a.ptr;
 
+    constexpr uint32_t TMEM_COLS = TmemCols<BN>::value;
     if (warp == 0) {
         tc05::tmem_alloc(tslot, TMEM_COLS);
         tc05::tmem_relinquish();
@@ -225,13 +239,12 @@ __global__ void __launch_bounds__(THREADS) tc_gemm_kernel(GemmArgs g, int *err) 
                     const int32_t bb = sbias[col0 + j];
                     int32_t o;
                     if (EPI == EPI_GELU) {
-                        o = (!WIDE && g.epi.gelu_fast) ? gelu_chain_fast(a + bb, g.epi.gelu_sh_in, g.epi.gelu_sh_out)
-                                                       : gelu_chain((int64_t)a + bb, g.epi.gelu_sh_in,
-                                                                    g.epi.gelu_sh_out);
+                        o = FAST ? gelu_chain_fast(a + bb, g.epi.gelu_sh_in, g.epi.gelu_sh_out)
+                                 : gelu_chain((int64_t)a + bb, g.epi.gelu_sh_in, g.epi.gelu_sh_out);
                     } else {
-                        o = wb8<WIDE>(a, bb, g.epi.shift);
-                        if (EPI == EPI_I8_RES) o = align_add8(byte_of(aux, j), o, g.epi.add);
-                        else if (EPI == EPI_PATCH) o = align_add8(o, byte_of(aux, j), g.epi.add);
+                        o = wb8<FAST>(a, bb, g.epi.shift);
+                        if (EPI == EPI_I8_RES) o = add8<FAST>(byte_of(aux, j), o, g.epi.add);
+                        else if (EPI == EPI_PATCH) o = add8<FAST>(o, byte_of(aux, j), g.epi.add);
                     }
                     word |= ((uint32_t)o & 0xffu) << (8 * b);
                 }
@@ -264,11 +277,13 @@ __global__ void __launch_bounds__(THREADS) tc_gemm_kernel(GemmArgs g, int *err) 
     }
 }
 
-template <int EPI, bool U8, bool WIDE, int BN>
+template <int EPI, bool U8, bool FAST, int BN>
 cudaError_t launch_t(const GemmArgs &g, int m_max, int *err, cudaStream_t st) {
-    auto kern = tc_gemm_kernel<EPI, U8, WIDE, BN>;
-    // At least 76 KB so no more than two CTAs (2 x 256 TMEM columns) share an SM.
-    const int smem = Layout<BN>::SMEM > 76 * 1024 ? Layout<BN>::SMEM : 76 * 1024;
+    auto kern = tc_gemm_kernel<EPI, U8, FAST, BN>;
+    // Enough shared memory that the co-resident CTAs never ask for more than the
+    // SM's 512 TMEM columns (TMEM allocation then never waits).
+    constexpr int min_smem = (228 * 1024) / (512 / (int)TmemCols<BN>::value) + 1024;
+    const int smem = Layout<BN>::SMEM > min_smem ? Layout<BN>::SMEM : min_smem;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
     dim3 grid((g.n + BN - 1) / BN, (m_max + BM - 1) / BM);
@@ -277,42 +292,37 @@ cudaError_t launch_t(const GemmArgs &g, int m_max, int *err, cudaStream_t st) {
     return cudaGetLastError();
 }
 
-template <int EPI, bool U8, bool WIDE>
+template <int EPI, bool U8, bool FAST>
 cudaError_t launch_bn(const GemmArgs &g, int m_max, int *err, cudaStream_t st) {
-    if (g.n % 192 == 0) return launch_t<EPI, U8, WIDE, 192>(g, m_max, err, st);
-    if (g.n > 256 || g.n % 64 != 0) return launch_t<EPI, U8, WIDE, 256>(g, m_max, err, st);
-    return launch_t<EPI, U8, WIDE, 64>(g, m_max, err, st);
+    if (g.n % 64 == 0) return launch_t<EPI, U8, FAST, 64>(g, m_max, err, st);
+    return launch_t<EPI, U8, FAST, 256>(g, m_max, err, st);
 }
 
 }  // namespace
 
-int gemm_tile_n(int n) {
-    if (n % 192 == 0) return 192;
-    if (n > 256 || n % 64 != 0) return 256;
-    return 64;
-}
+int gemm_tile_n(int n) { return n % 64 == 0 ? 64 : 256; }
 
 cudaError_t launch_gemm(const GemmArgs &g, int epi, int a_unsigned, int m_max, int *err, cudaStream_t st) {
-    const bool wide = g.epi.bits_wide != 0;
+    const bool fast = g.epi.fast != 0;
     switch (epi) {
         case EPI_I8:
-            return wide ? launch_bn<EPI_I8, false, true>(g, m_max, err, st)
+            return fast ? launch_bn<EPI_I8, false, true>(g, m_max, err, st)
                         : launch_bn<EPI_I8, false, false>(g, m_max, err, st);
         case EPI_I8_RES:
-            return wide ? launch_bn<EPI_I8_RES, false, true>(g, m_max, err, st)
+            return fast ? launch_bn<EPI_I8_RES, false, true>(g, m_max, err, st)
                         : launch_bn<EPI_I8_RES, false, false>(g, m_max, err, st);
         case EPI_GELU:
-            return wide ? launch_bn<EPI_GELU, false, true>(g, m_max, err, st)
+            return fast ? launch_bn<EPI_GELU, false, true>(g, m_max, err, st)
                         : launch_bn<EPI_GELU, false, false>(g, m_max, err, st);
         case EPI_PATCH:
-            return wide ? launch_bn<EPI_PATCH, false, true>(g, m_max, err, st)
+            return fast ? launch_bn<EPI_PATCH, false, true>(g, m_max, err, st)
                         : launch_bn<EPI_PATCH, false, false>(g, m_max, err, st);
         case EPI_I32:
-            return a_unsigned ? launch_bn<EPI_I32, true, true>(g, m_max, err, st)
-                              : launch_bn<EPI_I32, false, true>(g, m_max, err, st);
+            return a_unsigned ? launch_bn<EPI_I32, true, false>(g, m_max, err, st)
+                              : launch_bn<EPI_I32, false, false>(g, m_max, err, st);
         case EPI_ACC64:
-            return a_unsigned ? launch_bn<EPI_ACC64, true, true>(g, m_max, err, st)
-                              : launch_bn<EPI_ACC64, false, true>(g, m_max, err, st);
+            return a_unsigned ? launch_bn<EPI_ACC64, true, false>(g, m_max, err, st)
+                              : launch_bn<EPI_ACC64, false, false>(g, m_max, err, st);
         default:
             return cudaErrorInvalidValue;
     }

@@ -30,7 +30,8 @@ enum Epi { EPI_I8 = 0, EPI_I8_RES = 1, EPI_GELU = 2, EPI_PATCH = 3, EPI_I32 = 4,
 struct EpiParams {
     const int32_t *bias;      // [N] or nullptr
     int shift;                // requant shift dst - src for the first writeback
-    int bits_wide;            // 1: acc + bias may leave int32 -> 64-bit path
+    int bits_wide;            // 1: acc + bias may leave 30 bits (64-bit arithmetic needed)
+    int fast;                 // 1: the 32-bit epilogue forms are exact (see gemm_epi_fast)
     // residual (EPI_I8_RES): out = align_add(res @ e_res, y @ e_y -> e_out)
     const int8_t *res;        // [M][N]
     AlignAdd add;             // a = residual value, b = requantised GEMM value
@@ -63,6 +64,18 @@ struct GemmArgs {
 // ceil(n / gemm_tile_n(n)) * gemm_tile_n(n) rows; k must be a multiple of 64.
 // err: device word set non-zero when a bounded wait gave up.
 int gemm_tile_n(int n);
+
+// Whether the 32-bit epilogue forms are exact for these constants: acc + bias
+// fits 30 bits, the first writeback shifts right by 1..30, and the align-add
+// (EPI_I8_RES / EPI_PATCH) or GELU chain (EPI_GELU) fast conditions hold.
+inline int gemm_epi_fast(int epi, const EpiParams &e) {
+    if (e.bits_wide) return 0;
+    if (epi == EPI_GELU) return e.gelu_fast;
+    const int wb_ok = e.shift >= 1 && e.shift <= 30;
+    if (epi == EPI_I8_RES || epi == EPI_PATCH) return wb_ok && e.add.fast;
+    if (epi == EPI_I8) return wb_ok;
+    return 0;
+}
 cudaError_t launch_gemm(const GemmArgs &g, int epi, int a_unsigned, int m_max, int *err, cudaStream_t st);
 
 }  // namespace hv

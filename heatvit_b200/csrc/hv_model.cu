@@ -288,6 +288,7 @@ int run_block(hv_model *m, int b, int images, const int32_t *off, cudaStream_t s
         g.epi.bias = m->w<int32_t>(d.bqkv);
         g.epi.shift = d.qkv_shift;
         g.epi.bits_wide = d.qkv_wide;
+        g.epi.fast = gemm_epi_fast(EPI_I8, g.epi);
         CUDA_TRY(launch_gemm(g, EPI_I8, 0, rows_max, m->err, st));
         pr.end(st, rows_dev, 0);
     }
@@ -304,6 +305,7 @@ int run_block(hv_model *m, int b, int images, const int32_t *off, cudaStream_t s
         g.epi.bits_wide = d.proj_wide;
         g.epi.res = m->X;
         g.epi.add = d.res1;
+        g.epi.fast = gemm_epi_fast(EPI_I8_RES, g.epi);
         CUDA_TRY(launch_gemm(g, EPI_I8_RES, 0, rows_max, m->err, st));
         pr.end(st, rows_dev, 0);
     }
@@ -320,6 +322,7 @@ int run_block(hv_model *m, int b, int images, const int32_t *off, cudaStream_t s
         g.epi.gelu_sh_in = d.fc1_sh_in;
         g.epi.gelu_sh_out = d.fc1_sh_out;
         g.epi.gelu_fast = d.fc1_fast;
+        g.epi.fast = gemm_epi_fast(EPI_GELU, g.epi);
         CUDA_TRY(launch_gemm(g, EPI_GELU, 0, rows_max, m->err, st));
         pr.end(st, rows_dev, 0);
     }
@@ -331,6 +334,7 @@ int run_block(hv_model *m, int b, int images, const int32_t *off, cudaStream_t s
         g.epi.bits_wide = d.fc2_wide;
         g.epi.res = m->Y;
         g.epi.add = d.res2;
+        g.epi.fast = gemm_epi_fast(EPI_I8_RES, g.epi);
         CUDA_TRY(launch_gemm(g, EPI_I8_RES, 0, rows_max, m->err, st));
         pr.end(st, rows_dev, 0);
     }
@@ -345,6 +349,7 @@ int run_patch(hv_model *m, const int8_t *images, int count, int8_t *out, cudaStr
     g.epi.bits_wide = m->patch_wide;
     g.epi.pos = m->w<int8_t>(m->pos);
     g.epi.add = m->patch_add;
+    g.epi.fast = gemm_epi_fast(EPI_PATCH, g.epi);
     CUDA_TRY(launch_gemm(g, EPI_PATCH, 0, count * HV_PATCHES, m->err, st));
     return HV_OK;
 }

@@ -93,10 +93,11 @@ __device__ __forceinline__ LnStats ln_stats(int32_t s, int64_t s2, const LnParam
 // The ties-away rounding floor((T + 2^47 - [T<0]) / 2^48) then equals
 // floor((U + 2^31 - [T<0 and B_lo == 0]) / 2^32), because the dropped low part
 // is a fraction in [0, 1) of the 2^16 unit.
+template <bool SPLIT>
 __device__ __forceinline__ int32_t ln_norm(int32_t v, const LnStats &st, const LnParams &p) {
     const int64_t d = ((int64_t)v << p.sh_sum) - st.mean;
     int64_t nr;
-    if (p.split) {
+    if (SPLIT) {
         const int64_t hi = (int64_t)(st.inv >> 16), lo = (int64_t)(st.inv & 0xFFFFu);
         const int64_t a = d * hi;
         const int64_t b = d * lo;
@@ -112,15 +113,17 @@ __device__ __forceinline__ int32_t ln_norm(int32_t v, const LnStats &st, const L
 }
 
 // out = requant((norm*gamma << sh_g) + (beta << sh_b), common, out, 8) (nonlinear.py:181-186).
+template <bool OUT32>
 __device__ __forceinline__ int32_t ln_out(int32_t norm, int32_t g, int32_t b, const LnParams &p) {
     const int32_t prodg = norm * g;
-    if (p.out32) return requant8_r(prodg + (b << p.sh_b), p.sh_out);
+    if (OUT32) return requant8_r(prodg + b * (1 << p.sh_b), p.sh_out);
     if (p.fast) return (int32_t)requant64(((int64_t)prodg << p.sh_g) + ((int64_t)b << p.sh_b), p.sh_out, 8);
     return requant128_8(((i128)prodg << p.sh_g) + ((i128)b << p.sh_b), p.sh_out);
 }
 
 // One row per 8-lane group; lane `sub` owns channels [24*sub, 24*sub + 24).
 // Returns true on negative variance.  All 32 lanes of the warp must call it.
+template <bool SPLIT, bool OUT32>
 __device__ __forceinline__ bool ln_row8(const int8_t *xr, int8_t *outr, const LnParams &p, int sub, bool active) {
     int32_t v[24];
     uint2 w[3] = {make_uint2(0, 0), make_uint2(0, 0), make_uint2(0, 0)};
@@ -169,7 +172,7 @@ __device__ __forceinline__ bool ln_row8(const int8_t *xr, int8_t *outr, const Ln
         for (int b = 0; b < 4; ++b) {
             const int vi = i * 4 + b;  // byte vi of this lane's 24-byte slice
             const int chan = 24 * sub + vi;
-            const int32_t o = ln_out(ln_norm(v[vi], st, p), p.gamma[chan], p.beta[chan], p);
+            const int32_t o = ln_out<OUT32>(ln_norm<SPLIT>(v[vi], st, p), p.gamma[chan], p.beta[chan], p);
             word |= ((uint32_t)o & 0xffu) << (8 * b);
         }
         ow[i] = word;
@@ -193,6 +196,7 @@ __device__ __forceinline__ int image_of_row(const int32_t *offsets, int images, 
     return lo;
 }
 
+template <bool SPLIT, bool OUT32>
 __global__ void __launch_bounds__(256) ln_kernel(const int8_t *x, int8_t *out, int rows_max, const int32_t *rows_dev,
                                                  LnParams p, uint8_t *negvar_row, const int32_t *offsets,
                                                  int images, uint8_t *warn) {
@@ -204,7 +208,7 @@ __global__ void __launch_bounds__(256) ln_kernel(const int8_t *x, int8_t *out, i
     for (int base = warp * 4; base < rows; base += warps * 4) {
         const int r = base + grp;
         const bool active = r < rows;
-        const bool neg = ln_row8(x + (size_t)(active ? r : 0) * 192, out + (size_t)(active ? r : 0) * 192, p, sub,
+        const bool neg = ln_row8<SPLIT, OUT32>(x + (size_t)(active ? r : 0) * 192, out + (size_t)(active ? r : 0) * 192, p, sub,
                                  active);
         if (active && sub == 0) {
             if (negvar_row) negvar_row[r] = neg ? 1 : 0;
@@ -216,12 +220,13 @@ __global__ void __launch_bounds__(256) ln_kernel(const int8_t *x, int8_t *out, i
     }
 }
 
+template <bool SPLIT, bool OUT32>
 __global__ void __launch_bounds__(256) ln_cls_kernel(const int8_t *x, const int32_t *offsets, int images, int8_t *out,
                                                      LnParams p, uint8_t *warn) {
     const int lane = threadIdx.x & 31, sub = lane & 7, grp = lane >> 3;
     const int i = ((blockIdx.x * blockDim.x + threadIdx.x) >> 5) * 4 + grp;
     const bool active = i < images;
-    const bool neg = ln_row8(x + (size_t)(active ? offsets[i] : 0) * 192, out + (size_t)(active ? i : 0) * 192, p,
+    const bool neg = ln_row8<SPLIT, OUT32>(x + (size_t)(active ? offsets[i] : 0) * 192, out + (size_t)(active ? i : 0) * 192, p,
                              sub, active);
     if (neg && active && sub == 0 && warn)
         atomicOr((unsigned int *)(warn + (i & ~3)), (unsigned int)HV_WARN_LN_NEG_VARIANCE << (8 * (i & 3)));
@@ -322,15 +327,18 @@ cudaError_t launch_layernorm(const int8_t *x, int8_t *out, int rows_max, const i
     const int rows_per_block = 8 * 4;  // 8 warps x 4 rows
     int blocks = (rows_max + rows_per_block - 1) / rows_per_block;
     if (blocks > 148 * 16) blocks = 148 * 16;
-    ln_kernel<<<blocks, 256, 0, st>>>(x, out, rows_max, rows_dev, p, negvar_row, offsets, images,
-                                                       warn);
+    auto kern = p.split ? (p.out32 ? ln_kernel<true, true> : ln_kernel<true, false>)
+                        : (p.out32 ? ln_kernel<false, true> : ln_kernel<false, false>);
+    kern<<<blocks, 256, 0, st>>>(x, out, rows_max, rows_dev, p, negvar_row, offsets, images, warn);
     return cudaGetLastError();
 }
 
 cudaError_t launch_layernorm_cls(const int8_t *x, const int32_t *offsets, int images, int8_t *out,
                                  const LnParams &p, uint8_t *warn, cudaStream_t st) {
     if (images <= 0) return cudaSuccess;
-    ln_cls_kernel<<<(images + 31) / 32, 256, 0, st>>>(x, offsets, images, out, p, warn);
+    auto kern = p.split ? (p.out32 ? ln_cls_kernel<true, true> : ln_cls_kernel<true, false>)
+                        : (p.out32 ? ln_cls_kernel<false, true> : ln_cls_kernel<false, false>);
+    kern<<<(images + 31) / 32, 256, 0, st>>>(x, offsets, images, out, p, warn);
     return cudaGetLastError();
 }
 
