@@ -959,3 +959,83 @@ int hv_token_selector(hv_model *m, int selector_index, const int8_t *d_x, const 
 }
 
 }  // extern "C"
+
+// ---- allocation-free accumulator GEMM ------------------------------------------------
+// hv_gemm_i8_acc_noalloc has no counterpart in the reference.  It serves callers that
+// must not call the device allocator mid-run: a process whose device memory is handed
+// out up front to a caching pool (a raw cudaMalloc can fail with memory free inside
+// the pool), or a latency-bound caller sharing the device with in-flight work, where
+// cudaFree's implicit device-wide synchronisation would stall everything.  It does the
+// work of hv_gemm_i8_acc with the padded operands and the error word placed in a fixed
+// __device__ array (one instance per device context) instead of cudaMalloc'd buffers.
+#include <mutex>
+
+static __device__ __align__(256) uint8_t g_noalloc_scratch[HV_NOALLOC_SCRATCH_BYTES];
+
+namespace {
+
+constexpr int kNoallocDevices = 64;
+std::mutex g_noalloc_mu;
+uint8_t *g_noalloc_base[kNoallocDevices];
+
+// Device address of g_noalloc_scratch on the current device, resolved once per
+// device with that device current and cached afterwards.
+int noalloc_scratch(uint8_t **base) {
+    int dev = -1;
+    CUDA_TRY(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= kNoallocDevices)
+        return fail(HV_ERR_VALUE, "device %d is beyond the %d devices the allocation-free GEMM tracks", dev,
+                    kNoallocDevices);
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (!g_noalloc_base[dev]) {
+        void *p = nullptr;
+        cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (e != cudaSuccess || !p)
+            return fail(HV_ERR_CUDA, "cudaGetSymbolAddress of the GEMM scratch on device %d: %s", dev,
+                        cudaGetErrorString(e));
+        g_noalloc_base[dev] = (uint8_t *)p;
+    }
+    *base = g_noalloc_base[dev];
+    return HV_OK;
+}
+
+}  // namespace
+
+extern "C" int hv_gemm_i8_acc_noalloc(const void *d_a, const int8_t *d_b, const int32_t *d_bias, int m, int n,
+                                      int k, int transpose_b, int a_unsigned, int64_t *d_acc, void *stream) {
+    if (m < 0 || n < 0 || k < 0) return fail(HV_ERR_VALUE, "negative dimension");
+    if (m == 0 || n == 0) return HV_OK;
+    if (!d_a || !d_b || !d_acc) return fail(HV_ERR_VALUE, "null buffer");
+    if (k > (a_unsigned ? 65793 : 131071))
+        return fail(HV_ERR_VALUE, "k=%d can overflow the int32 accumulator; not supported", k);
+    const int tn = gemm_tile_n(n);
+    const int64_t kp = std::max(64, (k + 63) / 64 * 64), np = ((int64_t)n + tn - 1) / tn * tn;
+    const int64_t a_bytes = ((int64_t)m * kp + 255) / 256 * 256;
+    const int64_t need = 256 + a_bytes + np * kp;
+    if (need > (int64_t)HV_NOALLOC_SCRATCH_BYTES)
+        return fail(HV_ERR_VALUE,
+                    "m=%d n=%d k=%d needs %lld bytes of scratch; the allocation-free GEMM holds at most %u "
+                    "(HV_NOALLOC_SCRATCH_BYTES); use hv_gemm_i8_acc",
+                    m, n, k, (long long)need, (unsigned)HV_NOALLOC_SCRATCH_BYTES);
+    uint8_t *base = nullptr;
+    int rc = noalloc_scratch(&base);
+    if (rc) return rc;
+    cudaStream_t st = (cudaStream_t)stream;
+    int *err = (int *)base;                        // bounded-wait status: must start at zero
+    uint8_t *ap = base + 256;                      // [m][kp], fully rewritten by pad_a_kernel
+    int8_t *bp = (int8_t *)(base + 256 + a_bytes); // [np][kp], fully rewritten by pad_b_kernel
+    CUDA_TRY(cudaMemsetAsync(err, 0, sizeof(int), st));
+    pad_a_kernel<<<148 * 4, 256, 0, st>>>((const uint8_t *)d_a, m, k, (int)kp, ap);
+    pad_b_kernel<<<148 * 4, 256, 0, st>>>(d_b, n, k, transpose_b, (int)np, (int)kp, bp);
+    CUDA_TRY(cudaGetLastError());
+    GemmArgs g = gemm_args(ap, (int)kp, 0, bp, n, (int)kp, m, nullptr, d_acc, n);
+    g.epi.bias = d_bias;
+    g.epi.bits_wide = 1;
+    cudaError_t e = launch_gemm(g, EPI_ACC64, a_unsigned, m, err, st);
+    if (e != cudaSuccess) return fail(HV_ERR_CUDA, "gemm launch: %s", cudaGetErrorString(e));
+    int code = 0;
+    CUDA_TRY(cudaMemcpyAsync(&code, err, sizeof(int), cudaMemcpyDeviceToHost, st));
+    CUDA_TRY(cudaStreamSynchronize(st));
+    if (code) return fail(HV_ERR_STATE, "a device-side bounded wait gave up (code %d)", code);
+    return HV_OK;
+}

@@ -240,6 +240,34 @@ HV_API int hv_gemm_i8_acc(const void *d_a, const int8_t *d_b, const int32_t *d_b
                    int m, int n, int k, int transpose_b, int a_unsigned,
                    int64_t *d_acc, void *stream);
 
+/* Allocation-free form of hv_gemm_i8_acc: same arguments, same result, same
+ * status codes.  No counterpart in the reference (the golden model is pure
+ * Python and never owns device memory); this entry point exists for callers
+ * that must not allocate or free device memory while they run, e.g. a process
+ * whose device memory is all reserved up front by a caching pool (a raw
+ * cudaMalloc can then fail although the pool has room), or a latency-bound
+ * caller that cannot afford the device-wide synchronisation cudaFree implies.
+ *
+ * The padded operands and the device error word live in one fixed per-device
+ * array of HV_NOALLOC_SCRATCH_BYTES inside the library.  The call needs
+ *   256 + roundup256(m * kp) + np * kp  bytes of it,
+ * with kp = max(64, roundup64(k)) and np = n rounded up to 64 (n % 64 == 0)
+ * or to 256 (otherwise); larger problems are rejected with HV_ERR_VALUE and a
+ * message naming the limit, before any work is enqueued.
+ *
+ * The first call on each device resolves the array's device address
+ * (cudaGetSymbolAddress, with that device current); make that first call
+ * before any stream capture starts on the device.  Each call clears the error
+ * word on `stream` before use, rewrites every padded byte it reads, and waits
+ * for `stream` before returning so it can report a bounded-wait timeout.
+ * The array is shared by all callers on a device: calls that overlap in time
+ * (two host threads, or work on another stream still reading the array) race
+ * and may return wrong results.  Serialise them. */
+#define HV_NOALLOC_SCRATCH_BYTES (8u << 20)
+HV_API int hv_gemm_i8_acc_noalloc(const void *d_a, const int8_t *d_b, const int32_t *d_bias,
+                   int m, int n, int k, int transpose_b, int a_unsigned,
+                   int64_t *d_acc, void *stream);
+
 /* Element-wise writeback requant(v, src_exp, dst_exp, out_bits) of int64 values to
  * int8 (out_bits 8) or int32 (out_bits 24 or 32; 24 saturates to Q8.16 range)
  * (gemm.py:123-139; fixed.py:37-45). */
