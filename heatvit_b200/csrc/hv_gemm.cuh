@@ -78,4 +78,11 @@ inline int gemm_epi_fast(int epi, const EpiParams &e) {
 }
 cudaError_t launch_gemm(const GemmArgs &g, int epi, int a_unsigned, int m_max, int *err, cudaStream_t st);
 
+// Persistent, warp-specialised form for the model's layer shapes (signed A,
+// K in {192, 768}, N in {192, 576, 768}, int8 epilogues; hv_gemm_persistent.cu).
+// The weights stay resident in shared memory; `bt` needs exactly n rows.
+// `sms` is the device's SM count (one CTA per SM).
+bool gemm_persistent_supported(int epi, int n, int k);
+cudaError_t launch_gemm_persistent(const GemmArgs &g, int epi, int m_max, int *err, int sms, cudaStream_t st);
+
 }  // namespace hv

@@ -1,0 +1,361 @@
+// hv_gemm_persistent.cu — persistent, warp-specialised tcgen05 GEMM for the
+// model's five layer shapes (patch, QKV, proj, FC1, FC2).
+//
+// One CTA per SM loops over 128-row tiles of A.  The whole weight matrix
+// (N x K int8, at most 147 KB) stays resident in shared memory for the CTA's
+// lifetime, so A (read once) and the output (written once) are the only DRAM
+// traffic.  Roles:
+//   warp 0      producer: cp.async of A into a ring of S stages in the
+//               no-swizzle K-major canonical layout; each of its 32 threads
+//               arrives on the stage's `full` mbarrier when its copies land
+//               (cp.async.mbarrier.arrive.noinc).
+//   warp 1      MMA issuer (one thread): tcgen05.mma kind::i8 into one of two
+//               TMEM accumulators (192 columns each, 256 apart); commits free
+//               the A stage (`empty`) and hand the accumulator to the epilogue
+//               (`acc_full`).
+//   warps 2-9   epilogue: thread = (TMEM lane, column half); reads its
+//               accumulator row with tcgen05.ld, applies the fused golden
+//               writeback, stores 32 contiguous bytes per step, then releases
+//               the accumulator (`acc_empty`).
+// For K = 192 one stage holds the whole A tile and feeds every 192-column
+// chunk of N; for K = 768 (N = 192) A streams through 4 stages of 64 columns.
+// Every mbarrier wait is bounded; a timeout sets the model's error word.
+#include "hv_gemm.cuh"
+#include "hv_tc05.cuh"
+
+namespace hv {
+
+namespace {
+
+constexpr int PT_PROD = 4;                       // producer warps
+constexpr int PT_MMA_WARP = PT_PROD;
+constexpr int PT_EPI0 = PT_PROD + 1;             // first epilogue warp
+constexpr int PT_THREADS = (PT_PROD + 1 + 8) * 32;
+constexpr int BN = 192;
+constexpr uint32_t PT_TMEM_COLS = 512;
+constexpr uint32_t PT_WAIT = 1u << 24;
+
+template <int KDIM, int N>
+struct PLayout {
+    static constexpr int NCH = N / BN;                 // n-chunks per tile
+    static constexpr int AK = KDIM == 192 ? 192 : 64;  // A stage width (bytes of K)
+    static constexpr int KST = KDIM / AK;              // A stages per tile
+    static constexpr int S = KDIM == 192 ? 3 : 8;      // ring depth
+    static constexpr int A_STAGE = 128 * AK;
+    // An A stage is released after its tile's last n-chunk, or after its own k-step.
+    static_assert(KST == 1 || NCH == 1, "streamed K with several n-chunks is not pipelined");
+    static constexpr int OFF_B = 0;
+    static constexpr int OFF_A = OFF_B + N * KDIM;
+    static constexpr int OFF_BIAS = OFF_A + S * A_STAGE;
+    static constexpr int OFF_BAR = OFF_BIAS + N * 4;
+    static constexpr int NBAR = 2 * S + 5;
+    static constexpr int USED = OFF_BAR + NBAR * 8 + 16;
+    // At least 116 KB so that two CTAs never share an SM: each takes all 512 TMEM columns.
+    static constexpr int SMEM = USED > 116 * 1024 ? USED : 116 * 1024;
+};
+
+__device__ __forceinline__ void cp_async16(uint32_t saddr, const void *g, int src_bytes) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(saddr), "l"(g), "r"(src_bytes) : "memory");
+}
+__device__ __forceinline__ void cp_arrive_noinc(uint64_t *mbar) {
+    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];\n" ::"r"(tc05::smem_u32(mbar)) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t *mbar) {
+    asm volatile("{\n.reg .b64 st;\nmbarrier.arrive.shared::cta.b64 st, [%0];\n}\n" ::"r"(tc05::smem_u32(mbar))
+                 : "memory");
+}
+
+template <bool FAST>
+__device__ __forceinline__ int32_t p_wb8(int32_t acc, int32_t bias, int shift) {
+    if (FAST) return requant8_r(acc + bias, shift);
+    return (int32_t)requant64((int64_t)acc + bias, shift, 8);
+}
+template <bool FAST>
+__device__ __forceinline__ int32_t p_add8(int32_t a, int32_t b, AlignAdd k) {
+    if (FAST) return requant8_r(a * (1 << k.sa) + b * (1 << k.sb), k.sh);
+    return (int32_t)requant64(((int64_t)a << k.sa) + ((int64_t)b << k.sb), k.sh, 8);
+}
+
+template <int EPI, bool FAST, int KDIM, int N>
+__global__ void __launch_bounds__(PT_THREADS, 1) tcp_gemm_kernel(GemmArgs g, int *err) {
+    using L = PLayout<KDIM, N>;
+    extern __shared__ __align__(1024) uint8_t smem[];
+    uint8_t *sB = smem + L::OFF_B;
+    uint8_t *sA = smem + L::OFF_A;
+    int32_t *sbias = (int32_t *)(smem + L::OFF_BIAS);
+    uint64_t *full = (uint64_t *)(smem + L::OFF_BAR);
+    uint64_t *empty = full + L::S;
+    uint64_t *accf = empty + L::S;
+    uint64_t *acce = accf + 2;
+    uint64_t *drain = acce + 2;
+    uint32_t *tslot = (uint32_t *)(drain + 1);
+    volatile int *abortf = (volatile int *)(tslot + 1);
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int m_lim = g.m_dev ? *g.m_dev : g.m_host;
+    const int mtiles = (m_lim + 127) / 128;
+
+    // ---- prologue: resident weights and bias, barriers, TMEM ---------------------
+    if (warp == 0) {
+        tc05::tmem_alloc(tslot, PT_TMEM_COLS);
+        tc05::tmem_relinquish();
+    }
+    if (tid == 0) {
+        for (int s = 0; s < L::S; ++s) {
+            tc05::mbar_init(&full[s], 32 * PT_PROD);
+            tc05::mbar_init(&empty[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            tc05::mbar_init(&accf[b], 1);
+            tc05::mbar_init(&acce[b], 8);
+        }
+        tc05::mbar_init(drain, 1);
+        *abortf = 0;
+        tc05::fence_mbar_init();
+    }
+    // B [N][KDIM] in canonical K-major layout: chunk c -> (row group, k chunk, row)
+    constexpr int KC = KDIM / 16;
+    for (int c = tid; c < N * KC; c += PT_THREADS) {
+        const int grp = c / (8 * KC), rem = c - grp * 8 * KC;
+        const int kc = rem >> 3, r8 = rem & 7;
+        const int row = grp * 8 + r8;
+        cp_async16(tc05::smem_u32(sB + grp * (8 * KDIM) + kc * 128 + r8 * 16), g.bt + (size_t)row * KDIM + kc * 16,
+                   16);
+    }
+    for (int i = tid; i < N; i += PT_THREADS) sbias[i] = g.epi.bias ? g.epi.bias[i] : 0;
+    asm volatile("cp.async.wait_all;\n" ::: "memory");
+    tc05::fence_proxy_async();
+    tc05::fence_before();
+    __syncthreads();
+    tc05::fence_after();
+    const uint32_t tbase = *tslot;
+    const uint8_t *abase = (const uint8_t *)g.a.ptr;
+
+    if (warp < PT_PROD) {
+        // ---- producer ------------------------------------------------------------
+        uint32_t q = 0;
+        for (int mt = blockIdx.x; mt < mtiles && !*abortf; mt += gridDim.x) {
+            const int m0 = mt * 128;
+            for (int ks = 0; ks < L::KST; ++ks, ++q) {
+                const int s = q % L::S;
+                if (q >= (uint32_t)L::S && !tc05::mbar_wait(&empty[s], ((q / L::S) - 1) & 1u, PT_WAIT)) {
+                    *abortf = 1;
+                    break;
+                }
+                uint8_t *dst = sA + s * L::A_STAGE;
+                constexpr int AKC = L::AK / 16;
+                for (int c = tid; c < 128 * AKC; c += 32 * PT_PROD) {
+                    const int grp = c / (8 * AKC), rem = c - grp * 8 * AKC;
+                    const int kc = rem >> 3, r8 = rem & 7;
+                    const int row = grp * 8 + r8, grow = m0 + row;
+                    const uint8_t *src = abase;
+                    int bytes = 0;
+                    if (grow < m_lim) {
+                        bytes = 16;
+                        const int k = ks * L::AK + kc * 16;
+                        if (g.a.patch_mode) {
+                            // layout.py:31-72 patch order; a 16-byte chunk stays inside one image row
+                            const int img = grow / 196, p = grow - img * 196;
+                            const int pr = p / 14, pc = p - pr * 14;
+                            const int ir = k / 48, w = k - ir * 48;
+                            src = abase + (size_t)img * 150528 + ((pr * 16 + ir) * 224 + pc * 16) * 3 + w;
+                        } else {
+                            src = abase + (size_t)grow * g.a.lda + k;
+                        }
+                    }
+                    cp_async16(tc05::smem_u32(dst + grp * (8 * L::AK) + kc * 128 + r8 * 16), src, bytes);
+                }
+                cp_arrive_noinc(&full[s]);
+            }
+        }
+    } else if (warp == PT_MMA_WARP) {
+        // ---- MMA issuer -------------------------------------------------------------
+        if (lane == 0) {
+            const uint32_t idesc = tc05::idesc_i8(128, BN, true, true);
+            uint32_t q = 0, a = 0;
+            bool ok = true;
+            for (int mt = blockIdx.x; mt < mtiles && ok && !*abortf; mt += gridDim.x) {
+                for (int c = 0; c < L::NCH && ok; ++c, ++a) {
+                    const int tb = a & 1;
+                    if (a >= 2 && !tc05::mbar_wait(&acce[tb], ((a >> 1) - 1) & 1u, PT_WAIT)) { ok = false; break; }
+                    tc05::fence_after();
+                    const uint32_t d = tbase + tb * 256;
+                    for (int ks = 0; ks < L::KST; ++ks) {
+                        const uint32_t qq = q + ks;
+                        const int s = qq % L::S;
+                        if (c == 0 || L::KST > 1) {
+                            if (!tc05::mbar_wait(&full[s], (qq / L::S) & 1u, PT_WAIT)) { ok = false; break; }
+                            tc05::fence_proxy_async();
+                            tc05::fence_after();
+                        }
+                        const uint32_t a0 = tc05::smem_u32(sA + s * L::A_STAGE);
+                        const uint32_t b0 = tc05::smem_u32(sB) + c * BN * KDIM + ks * (L::AK / 16) * 128;
+#pragma unroll
+                        for (int j = 0; j < L::AK / 32; ++j)
+                            tc05::mma_i8_ss(d, tc05::smem_desc(a0 + j * 256, 128, 8 * L::AK),
+                                            tc05::smem_desc(b0 + j * 256, 128, 8 * KDIM), idesc, (ks | j) != 0);
+                        if (L::KST > 1) tc05::commit(&empty[s]);
+                    }
+                    if (!ok) break;
+                    if (L::KST == 1 && c == L::NCH - 1) tc05::commit(&empty[q % L::S]);
+                    tc05::commit(&accf[tb]);
+                }
+                q += L::KST;
+            }
+            if (!ok) *abortf = 1;
+            // Every MMA this thread issued has completed once `drain` flips.
+            tc05::commit(drain);
+            if (!tc05::mbar_wait(drain, 0, PT_WAIT)) *abortf = 1;
+        }
+    } else {
+        // ---- epilogue (8 warps) ---------------------------------------------------------
+        const int quad = warp & 3, half = (warp - PT_EPI0) >> 2;
+        const int row = quad * 32 + lane;
+        const uint32_t lane_addr = tbase + ((uint32_t)(quad * 32) << 16);
+        uint32_t a = 0;
+        for (int mt = blockIdx.x; mt < mtiles; mt += gridDim.x) {
+            const int grow = mt * 128 + row;
+            const bool valid = grow < m_lim;
+            size_t orow = (size_t)grow;
+            int pidx = 0;
+            if (EPI == EPI_PATCH) {
+                const int img = valid ? grow / 196 : 0;
+                pidx = valid ? grow - img * 196 : 0;
+                orow = (size_t)img * 197 + 1 + pidx;
+            }
+            bool stop = false;
+            for (int c = 0; c < L::NCH; ++c, ++a) {
+                const int tb = a & 1;
+                if (!tc05::mbar_wait(&accf[tb], (a >> 1) & 1u, PT_WAIT)) {
+                    *abortf = 1;
+                    stop = true;
+                    break;
+                }
+                tc05::fence_after();
+#pragma unroll 1
+                for (int cc = 0; cc < BN / 64; ++cc) {
+                    const int col0 = half * (BN / 2) + cc * 32;  // chunk-local column of v[0]
+                    const int gcol0 = c * BN + col0;
+                    uint32_t v[32];
+                    tc05::ld32(lane_addr + tb * 256 + col0, v);
+                    tc05::wait_ld();
+                    uint4 r0 = make_uint4(0, 0, 0, 0), r1 = r0;
+                    if (EPI == EPI_I8_RES && valid) {
+                        const uint4 *r = (const uint4 *)(g.epi.res + orow * g.ldo + gcol0);
+                        r0 = r[0];
+                        r1 = r[1];
+                    }
+                    if (EPI == EPI_PATCH) {
+                        const uint4 *r = (const uint4 *)(g.epi.pos + (pidx + 1) * 192 + gcol0);
+                        r0 = r[0];
+                        r1 = r[1];
+                    }
+                    const uint32_t aux[8] = {r0.x, r0.y, r0.z, r0.w, r1.x, r1.y, r1.z, r1.w};
+                    uint32_t pk[8];
+#pragma unroll
+                    for (int w = 0; w < 8; ++w) {
+                        uint32_t word = 0;
+#pragma unroll
+                        for (int b = 0; b < 4; ++b) {
+                            const int j = w * 4 + b;
+                            const int32_t acc = (int32_t)v[j];
+                            const int32_t bb = sbias[gcol0 + j];
+                            const int32_t ax = (int8_t)((aux[w] >> (8 * b)) & 0xffu);
+                            int32_t o;
+                            if (EPI == EPI_GELU) {
+                                o = FAST ? gelu_chain_fast(acc + bb, g.epi.gelu_sh_in, g.epi.gelu_sh_out)
+                                         : gelu_chain((int64_t)acc + bb, g.epi.gelu_sh_in, g.epi.gelu_sh_out);
+                            } else {
+                                o = p_wb8<FAST>(acc, bb, g.epi.shift);
+                                if (EPI == EPI_I8_RES) o = p_add8<FAST>(ax, o, g.epi.add);
+                                else if (EPI == EPI_PATCH) o = p_add8<FAST>(o, ax, g.epi.add);
+                            }
+                            word |= ((uint32_t)o & 0xffu) << (8 * b);
+                        }
+                        pk[w] = word;
+                    }
+                    if (valid) {
+                        uint4 *dst = (uint4 *)((int8_t *)g.out + orow * g.ldo + gcol0);
+                        dst[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+                        dst[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+                    }
+                }
+                tc05::fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&acce[tb]);
+            }
+            if (stop || *abortf) break;
+        }
+    }
+
+    if (warp < PT_PROD) asm volatile("cp.async.wait_all;\n" ::: "memory");
+    tc05::fence_before();
+    __syncthreads();
+    if (*abortf && tid == 0) atomicExch(err, 3);
+    if (warp == 0) {
+        tc05::fence_after();
+        tc05::tmem_dealloc(tbase, PT_TMEM_COLS);
+    }
+}
+
+template <int EPI, bool FAST, int KDIM, int N>
+cudaError_t launch_p(const GemmArgs &g, int m_max, int *err, int sms, cudaStream_t st) {
+    auto kern = tcp_gemm_kernel<EPI, FAST, KDIM, N>;
+    constexpr int smem = PLayout<KDIM, N>::SMEM;
+    static_assert(smem <= 227 * 1024, "persistent GEMM shared memory");
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    const int tiles = (m_max + 127) / 128;
+    const int grid = tiles < sms ? tiles : sms;
+    if (grid <= 0) return cudaSuccess;
+    kern<<<grid, PT_THREADS, smem, st>>>(g, err);
+    return cudaGetLastError();
+}
+
+// The (epilogue, K, N) combinations the model uses: QKV (I8, 192 -> 576), proj and
+// FC2 (I8_RES, 192 -> 192 and 768 -> 192), FC1 (GELU, 192 -> 768), patch (768 -> 192).
+constexpr bool shape_used(int epi, int k, int n) {
+    return (epi == EPI_I8 && k == 192 && n == 576) || (epi == EPI_I8_RES && n == 192 && (k == 192 || k == 768)) ||
+           (epi == EPI_GELU && k == 192 && n == 768) || (epi == EPI_PATCH && k == 768 && n == 192);
+}
+
+template <int EPI, bool FAST, int KDIM, int N>
+cudaError_t launch_if_used(const GemmArgs &g, int m_max, int *err, int sms, cudaStream_t st) {
+    if constexpr (shape_used(EPI, KDIM, N)) return launch_p<EPI, FAST, KDIM, N>(g, m_max, err, sms, st);
+    return cudaErrorInvalidValue;
+}
+
+template <int EPI, bool FAST>
+cudaError_t launch_shape(const GemmArgs &g, int m_max, int *err, int sms, cudaStream_t st) {
+    if (g.k == 192 && g.n == 576) return launch_if_used<EPI, FAST, 192, 576>(g, m_max, err, sms, st);
+    if (g.k == 192 && g.n == 768) return launch_if_used<EPI, FAST, 192, 768>(g, m_max, err, sms, st);
+    if (g.k == 192 && g.n == 192) return launch_if_used<EPI, FAST, 192, 192>(g, m_max, err, sms, st);
+    if (g.k == 768 && g.n == 192) return launch_if_used<EPI, FAST, 768, 192>(g, m_max, err, sms, st);
+    return cudaErrorInvalidValue;
+}
+
+}  // namespace
+
+bool gemm_persistent_supported(int epi, int n, int k) { return shape_used(epi, k, n); }
+
+cudaError_t launch_gemm_persistent(const GemmArgs &g, int epi, int m_max, int *err, int sms, cudaStream_t st) {
+    const bool fast = g.epi.fast != 0;
+    switch (epi) {
+        case EPI_I8:
+            return fast ? launch_shape<EPI_I8, true>(g, m_max, err, sms, st)
+                        : launch_shape<EPI_I8, false>(g, m_max, err, sms, st);
+        case EPI_I8_RES:
+            return fast ? launch_shape<EPI_I8_RES, true>(g, m_max, err, sms, st)
+                        : launch_shape<EPI_I8_RES, false>(g, m_max, err, sms, st);
+        case EPI_GELU:
+            return fast ? launch_shape<EPI_GELU, true>(g, m_max, err, sms, st)
+                        : launch_shape<EPI_GELU, false>(g, m_max, err, sms, st);
+        case EPI_PATCH:
+            return fast ? launch_shape<EPI_PATCH, true>(g, m_max, err, sms, st)
+                        : launch_shape<EPI_PATCH, false>(g, m_max, err, sms, st);
+        default:
+            return cudaErrorInvalidValue;
+    }
+}
+
+}  // namespace hv

@@ -100,6 +100,8 @@ struct SelDev {
 
 struct hv_model {
     int device = 0;
+    int sms = 148;         // SM count: one persistent GEMM CTA per SM
+    int persistent = 1;    // layer GEMMs on the persistent kernel (HV_GEMM_TILED=1 selects the per-tile one)
     int has_patch = 0, has_head = 0, has_block[HV_BLOCKS] = {0};
     int used_sel = 0;  // selectors that actually run (strides of token counts / summaries)
     uint8_t *weights = nullptr;
@@ -249,6 +251,14 @@ GemmArgs gemm_args(const void *a, int lda, int patch_mode, const int8_t *bt, int
     return g;
 }
 
+// A layer GEMM of the model: the persistent kernel for the layer shapes it covers.
+cudaError_t model_gemm(const hv_model *m, GemmArgs &g, int epi, int m_max, cudaStream_t st) {
+    g.epi.fast = gemm_epi_fast(epi, g.epi);
+    if (m->persistent && gemm_persistent_supported(epi, g.n, g.k))
+        return launch_gemm_persistent(g, epi, m_max, m->err, m->sms, st);
+    return launch_gemm(g, epi, 0, m_max, m->err, st);
+}
+
 __global__ void copy_rows_kernel(const int32_t *src, int32_t *dst) { *dst = *src; }
 
 // Profiling bracket: begin/end around one launch of `stage` when enabled.
@@ -288,8 +298,7 @@ int run_block(hv_model *m, int b, int images, const int32_t *off, cudaStream_t s
         g.epi.bias = m->w<int32_t>(d.bqkv);
         g.epi.shift = d.qkv_shift;
         g.epi.bits_wide = d.qkv_wide;
-        g.epi.fast = gemm_epi_fast(EPI_I8, g.epi);
-        CUDA_TRY(launch_gemm(g, EPI_I8, 0, rows_max, m->err, st));
+        CUDA_TRY(model_gemm(m, g, EPI_I8, rows_max, st));
         pr.end(st, rows_dev, 0);
     }
     {
@@ -305,8 +314,7 @@ int run_block(hv_model *m, int b, int images, const int32_t *off, cudaStream_t s
         g.epi.bits_wide = d.proj_wide;
         g.epi.res = m->X;
         g.epi.add = d.res1;
-        g.epi.fast = gemm_epi_fast(EPI_I8_RES, g.epi);
-        CUDA_TRY(launch_gemm(g, EPI_I8_RES, 0, rows_max, m->err, st));
+        CUDA_TRY(model_gemm(m, g, EPI_I8_RES, rows_max, st));
         pr.end(st, rows_dev, 0);
     }
     {
@@ -322,8 +330,7 @@ int run_block(hv_model *m, int b, int images, const int32_t *off, cudaStream_t s
         g.epi.gelu_sh_in = d.fc1_sh_in;
         g.epi.gelu_sh_out = d.fc1_sh_out;
         g.epi.gelu_fast = d.fc1_fast;
-        g.epi.fast = gemm_epi_fast(EPI_GELU, g.epi);
-        CUDA_TRY(launch_gemm(g, EPI_GELU, 0, rows_max, m->err, st));
+        CUDA_TRY(model_gemm(m, g, EPI_GELU, rows_max, st));
         pr.end(st, rows_dev, 0);
     }
     {
@@ -334,8 +341,7 @@ int run_block(hv_model *m, int b, int images, const int32_t *off, cudaStream_t s
         g.epi.bits_wide = d.fc2_wide;
         g.epi.res = m->Y;
         g.epi.add = d.res2;
-        g.epi.fast = gemm_epi_fast(EPI_I8_RES, g.epi);
-        CUDA_TRY(launch_gemm(g, EPI_I8_RES, 0, rows_max, m->err, st));
+        CUDA_TRY(model_gemm(m, g, EPI_I8_RES, rows_max, st));
         pr.end(st, rows_dev, 0);
     }
     return HV_OK;
@@ -349,8 +355,7 @@ int run_patch(hv_model *m, const int8_t *images, int count, int8_t *out, cudaStr
     g.epi.bits_wide = m->patch_wide;
     g.epi.pos = m->w<int8_t>(m->pos);
     g.epi.add = m->patch_add;
-    g.epi.fast = gemm_epi_fast(EPI_PATCH, g.epi);
-    CUDA_TRY(launch_gemm(g, EPI_PATCH, 0, count * HV_PATCHES, m->err, st));
+    CUDA_TRY(model_gemm(m, g, EPI_PATCH, count * HV_PATCHES, st));
     return HV_OK;
 }
 
@@ -605,8 +610,15 @@ int hv_model_create(const hv_params *params, int device, hv_model **out) {
     if (!params || !out) return fail(HV_ERR_VALUE, "null argument");
     *out = nullptr;
     CUDA_TRY(cudaSetDevice(device));
+    int sms = 0;
+    CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device));
     hv_model *m = new hv_model();
     m->device = device;
+    m->sms = sms;
+    {
+        const char *t = getenv("HV_GEMM_TILED");
+        m->persistent = (t && t[0] == '1') ? 0 : 1;
+    }
     int rc = pack_model(m, params);
     if (rc) {
         hv_model_destroy(m);
