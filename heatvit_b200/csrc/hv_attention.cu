@@ -7,18 +7,23 @@
 //   ctx   = requant(prob(uint8)·V, prob_scale + q, context_out, 8)
 // written straight into the head-concatenated layout (layout.py:132-155).
 //
-// One CTA (4 warps) per (image, head), query rows in tiles of 128:
-//   1. K and Vᵀ (and each Q tile) are staged in shared memory in the
-//      no-swizzle K-major canonical layout (hv_tc05.cuh).
+// One CTA (8 warps) per (image, head), query rows in tiles of 128:
+//   1. K, V and each Q tile are staged in shared memory with 16-byte copies in
+//      the no-swizzle canonical layout (hv_tc05.cuh).  K and Q are K-major
+//      operands; V is the same byte layout read as an MN-major B operand
+//      (tokens along K, head dims along N), so no transpose is needed.
 //   2. One thread issues S = Q·Kᵀ as tcgen05.mma kind::i8 (M=128, N=np, K=64)
 //      into TMEM columns [0, np); completion arrives on an mbarrier.
-//   3. Thread t owns query row t = TMEM lane t: it reads its score row with
-//      tcgen05.ld (32 columns at a time) for the row max, writes the exp terms
-//      back into TMEM, then forms the UQ0.8 probabilities and stores them to
-//      shared memory as the A operand of the next MMA.  No shuffles: the whole
-//      row belongs to one thread.
+//   3. Query row r of the tile is TMEM lane r.  Warps w and w+4 own lanes
+//      32*(w%4)..+31 and split the row's 32-column chunks (even / odd); each
+//      reads its chunks with tcgen05.ld, and the two halves combine the row max
+//      and the exp sum through shared memory.  Exp terms are written back to
+//      TMEM, then turned into UQ0.8 probabilities stored to shared memory as
+//      the A operand of the next MMA.  Warps whose 32 rows all lie past the
+//      image's token count skip the softmax.
 //   4. ctx = P·V as tcgen05.mma kind::i8 with unsigned A (M=128, N=64, K=np)
-//      into TMEM columns [0, 64), then requantised and written out.
+//      into TMEM columns [0, 64), then requantised (half h: columns 32h..32h+31)
+//      and written out.
 // TMEM: 256 columns per CTA; shared memory is padded so two CTAs share an SM.
 #include "hv_internal.cuh"
 #include "hv_tc05.cuh"
@@ -27,16 +32,17 @@ namespace hv {
 
 namespace {
 
-constexpr int THREADS = 128;
+constexpr int THREADS = 256;
 constexpr int NPMAX = 224;        // 197 rounded up to 32
 constexpr uint32_t TMEM_COLS = 256;
 constexpr uint32_t WAIT_ITERS = 1u << 24;
 
-constexpr int OFF_K = 0;                      // [NPMAX][64]
-constexpr int OFF_V = OFF_K + NPMAX * 64;     // Vᵀ: [64][NPMAX]
-constexpr int OFF_Q = OFF_V + 64 * NPMAX;     // [128][64]
+constexpr int OFF_K = 0;                      // [NPMAX][64] K-major
+constexpr int OFF_V = OFF_K + NPMAX * 64;     // [NPMAX][64], read MN-major
+constexpr int OFF_Q = OFF_V + NPMAX * 64;     // [128][64]
 constexpr int OFF_P = OFF_Q + 128 * 64;       // [128][NPMAX] uint8
-constexpr int OFF_BAR = OFF_P + 128 * NPMAX;  // mbarrier, TMEM base, abort flag
+constexpr int OFF_RED = OFF_P + 128 * NPMAX;  // [2][2][128] int32 row partials (max, sum) of each half
+constexpr int OFF_BAR = OFF_RED + 4 * 128 * 4;  // mbarrier, TMEM base, abort flag
 constexpr int SMEM_BYTES = 80 * 1024;         // > 227 KB / 3: at most two CTAs per SM
 static_assert(OFF_BAR + 64 <= SMEM_BYTES, "attention shared memory layout");
 
@@ -74,6 +80,7 @@ __global__ void __launch_bounds__(THREADS) attention_tc_kernel(const int8_t *__r
     uint8_t *sV = smem + OFF_V;
     uint8_t *sQ = smem + OFF_Q;
     uint8_t *sP = smem + OFF_P;
+    int32_t *sred = (int32_t *)(smem + OFF_RED);
     uint64_t *bar = (uint64_t *)(smem + OFF_BAR);
     uint32_t *tmem_slot = (uint32_t *)(smem + OFF_BAR + 8);
     volatile int *abort_flag = (volatile int *)(smem + OFF_BAR + 12);
@@ -83,7 +90,9 @@ __global__ void __launch_bounds__(THREADS) attention_tc_kernel(const int8_t *__r
     const int n = offsets[img + 1] - row0;
     if (n <= 0) return;
     const int np = (n + 31) & ~31;
-    const int tid = threadIdx.x, warp = tid >> 5;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int quad = warp & 3, half = warp >> 2;
+    const int lrow = quad * 32 + lane;  // tile row = TMEM lane
 
     if (warp == 0) {
         tc05::tmem_alloc(tmem_slot, TMEM_COLS);
@@ -94,26 +103,20 @@ __global__ void __launch_bounds__(THREADS) attention_tc_kernel(const int8_t *__r
         *abort_flag = 0;
         tc05::fence_mbar_init();
     }
-    // K rows and Vᵀ (zero beyond n up to np).
-    for (int c = tid; c < np * 4; c += THREADS) {
-        const int r = c >> 2, ch = c & 3;
+    // K and V rows (zero beyond n up to np), both in the K-major byte layout.
+    for (int c = tid; c < np * 8; c += THREADS) {
+        const int r = c >> 3, ch = c & 3, isv = (c >> 2) & 1;
         int4 kv = make_int4(0, 0, 0, 0);
-        if (r < n) kv = *(const int4 *)(qkv + (size_t)(row0 + r) * 576 + 192 + head * 64 + ch * 16);
-        *(int4 *)(sK + tc05::kmajor_offset(r, ch * 16, 64)) = kv;
-    }
-    for (int c = tid; c < np * 16; c += THREADS) {
-        const int r = c >> 4, w = c & 15;
-        uint32_t word = 0;
-        if (r < n) word = *(const uint32_t *)(qkv + (size_t)(row0 + r) * 576 + 384 + head * 64 + w * 4);
-#pragma unroll
-        for (int b = 0; b < 4; ++b) sV[tc05::kmajor_offset(w * 4 + b, r, np)] = (uint8_t)(word >> (8 * b));
+        if (r < n) kv = *(const int4 *)(qkv + (size_t)(row0 + r) * 576 + 192 * (1 + isv) + head * 64 + ch * 16);
+        *(int4 *)((isv ? sV : sK) + tc05::kmajor_offset(r, ch * 16, 64)) = kv;
     }
     tc05::fence_before();
     __syncthreads();
     tc05::fence_after();
     const uint32_t tbase = *tmem_slot;
-    const uint32_t lane_addr = tbase + ((uint32_t)(warp * 32) << 16);
+    const uint32_t lane_addr = tbase + ((uint32_t)(quad * 32) << 16);
     const uint32_t sbo_np = (uint32_t)(np / 16) * 128;
+    const int nchunks = np >> 5;
     uint32_t phase = 0;
 
     for (int t = 0; t * 128 < n; ++t) {
@@ -142,73 +145,82 @@ __global__ void __launch_bounds__(THREADS) attention_tc_kernel(const int8_t *__r
         if (*abort_flag) break;
         tc05::fence_after();
 
-        // ---- thread-per-row softmax straight from TMEM ------------------------------
+        // ---- softmax straight from TMEM: this warp's rows, chunks c = half, half + 2, ...
         // q16 is monotone in the accumulator, so the row max is taken on raw
         // accumulators and converted once.
+        const bool live = t * 128 + quad * 32 < n;  // warp-uniform
         const int nfull = n & ~31;
-        int32_t mxa = INT32_MIN;
-        for (int c0 = 0; c0 < np; c0 += 32) {
-            uint32_t v[32];
-            tc05::ld32(lane_addr + c0, v);
-            tc05::wait_ld();
-            if (c0 < nfull) {
+        if (live) {
+            int32_t mxa = INT32_MIN;
+            for (int c = half; c < nchunks; c += 2) {
+                const int c0 = c * 32;
+                uint32_t v[32];
+                tc05::ld32(lane_addr + c0, v);
+                tc05::wait_ld();
+                if (c0 < nfull) {
 #pragma unroll
-                for (int j = 0; j < 32; ++j) mxa = max(mxa, (int32_t)v[j]);
-            } else {
+                    for (int j = 0; j < 32; ++j) mxa = max(mxa, (int32_t)v[j]);
+                } else {
 #pragma unroll
-                for (int j = 0; j < 32; ++j)
-                    if (c0 + j < n) mxa = max(mxa, (int32_t)v[j]);
-            }
-        }
-        const int32_t mx = q16_of<FAST>(mxa, p);
-        uint32_t sum = 0;
-        for (int c0 = 0; c0 < nfull; c0 += 32) {
-            uint32_t v[32];
-            tc05::ld32(lane_addr + c0, v);
-            tc05::wait_ld();
-            sum += chunk_exp<FAST, false>(v, 32, mx, p);
-            tc05::st32(lane_addr + c0, v);
-        }
-        if (nfull < np) {
-            uint32_t v[32];
-            tc05::ld32(lane_addr + nfull, v);
-            tc05::wait_ld();
-            sum += chunk_exp<FAST, true>(v, n - nfull, mx, p);
-            tc05::st32(lane_addr + nfull, v);
-        }
-        tc05::wait_st();
-        const uint64_t rc = softmax_recip(sum ? sum : 1u);
-        for (int c0 = 0; c0 < np; c0 += 32) {
-            uint32_t v[32];
-            tc05::ld32(lane_addr + c0, v);
-            tc05::wait_ld();
-            uint32_t pk[8];
-#pragma unroll
-            for (int w = 0; w < 8; ++w) {
-                uint32_t word = 0;
-#pragma unroll
-                for (int b = 0; b < 4; ++b) {
-                    // min(rsa(rsa(E*rc, 16), 8), 255) in one rounding step (nested floors).
-                    const uint64_t tt = (uint64_t)v[w * 4 + b] * rc + (32768u + (1u << 23));
-                    const uint32_t pr = (uint32_t)(tt >> 24);
-                    word |= (pr < 255u ? pr : 255u) << (8 * b);
+                    for (int j = 0; j < 32; ++j)
+                        if (c0 + j < n) mxa = max(mxa, (int32_t)v[j]);
                 }
-                pk[w] = word;
             }
-            *(uint4 *)(sP + tc05::kmajor_offset(tid, c0, np)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-            *(uint4 *)(sP + tc05::kmajor_offset(tid, c0 + 16, np)) = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+            sred[half * 128 + lrow] = mxa;
+        }
+        __syncthreads();
+        if (live) {
+            const int32_t mx = q16_of<FAST>(max(sred[lrow], sred[128 + lrow]), p);
+            uint32_t sum = 0;
+            for (int c = half; c < nchunks; c += 2) {
+                const int c0 = c * 32;
+                uint32_t v[32];
+                tc05::ld32(lane_addr + c0, v);
+                tc05::wait_ld();
+                if (c0 < nfull) sum += chunk_exp<FAST, false>(v, 32, mx, p);
+                else sum += chunk_exp<FAST, true>(v, n - c0, mx, p);
+                tc05::st32(lane_addr + c0, v);
+            }
+            tc05::wait_st();
+            sred[256 + half * 128 + lrow] = (int32_t)sum;
+        }
+        __syncthreads();
+        if (live) {
+            const uint32_t tot = (uint32_t)sred[256 + lrow] + (uint32_t)sred[384 + lrow];
+            const uint64_t rc = softmax_recip(tot ? tot : 1u);
+            for (int c = half; c < nchunks; c += 2) {
+                const int c0 = c * 32;
+                uint32_t v[32];
+                tc05::ld32(lane_addr + c0, v);
+                tc05::wait_ld();
+                uint32_t pk[8];
+#pragma unroll
+                for (int w = 0; w < 8; ++w) {
+                    uint32_t word = 0;
+#pragma unroll
+                    for (int b = 0; b < 4; ++b) {
+                        // min(rsa(rsa(E*rc, 16), 8), 255) in one rounding step (nested floors).
+                        const uint64_t tt = (uint64_t)v[w * 4 + b] * rc + (32768u + (1u << 23));
+                        const uint32_t pr = (uint32_t)(tt >> 24);
+                        word |= (pr < 255u ? pr : 255u) << (8 * b);
+                    }
+                    pk[w] = word;
+                }
+                *(uint4 *)(sP + tc05::kmajor_offset(lrow, c0, np)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+                *(uint4 *)(sP + tc05::kmajor_offset(lrow, c0 + 16, np)) = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+            }
         }
 
-        // ---- ctx = P·V -------------------------------------------------------------
+        // ---- ctx = P·V (rows of dead warps hold stale probabilities; their ctx rows are not stored)
         tc05::fence_proxy_async();
         tc05::fence_before();
         __syncthreads();
         if (tid == 0) {
             tc05::fence_after();
-            const uint32_t idesc = tc05::idesc_i8(128, 64, false, true);
+            const uint32_t idesc = tc05::idesc_i8(128, 64, false, true, true);
             for (int s = 0; s < np / 32; ++s)
                 tc05::mma_i8_ss(tbase, tc05::smem_desc(tc05::smem_u32(sP) + s * 256, 128, sbo_np),
-                                tc05::smem_desc(tc05::smem_u32(sV) + s * 256, 128, sbo_np), idesc, s);
+                                tc05::smem_desc(tc05::smem_u32(sV) + s * 2048, 512, 128), idesc, s);
             tc05::commit(bar);
         }
         if (tc05::mbar_wait(bar, phase, WAIT_ITERS)) phase ^= 1;
@@ -216,9 +228,8 @@ __global__ void __launch_bounds__(THREADS) attention_tc_kernel(const int8_t *__r
         __syncthreads();
         if (*abort_flag) break;
         tc05::fence_after();
-        const int r = t * 128 + tid;
-#pragma unroll
-        for (int half = 0; half < 2; ++half) {
+        const int r = t * 128 + lrow;
+        if (live) {
             uint32_t o[32];
             tc05::ld32(lane_addr + half * 32, o);
             tc05::wait_ld();

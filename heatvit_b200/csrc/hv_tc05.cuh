@@ -34,9 +34,11 @@ HV_DEV uint64_t smem_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
 }
 
 // Instruction descriptor for kind::i8 with an s32 accumulator, both operands K-major.
-__host__ __device__ __forceinline__ uint32_t idesc_i8(int m, int n, bool a_signed, bool b_signed) {
-    return (2u << 4) | ((a_signed ? 1u : 0u) << 7) | ((b_signed ? 1u : 0u) << 10) | ((uint32_t)(n >> 3) << 17) |
-           ((uint32_t)(m >> 4) << 24);
+// b_mn_major: B is stored MN-major (bit 16; valid for 8-bit integer operands).
+__host__ __device__ __forceinline__ uint32_t idesc_i8(int m, int n, bool a_signed, bool b_signed,
+                                                      bool b_mn_major = false) {
+    return (2u << 4) | ((a_signed ? 1u : 0u) << 7) | ((b_signed ? 1u : 0u) << 10) | ((b_mn_major ? 1u : 0u) << 16) |
+           ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
 }
 
 HV_DEV void tmem_alloc(uint32_t *smem_dst, uint32_t ncols) {
