@@ -146,6 +146,134 @@ HV_DEV int32_t gelu_chain_fast(int32_t v, int sh_in, int sh_out) {
     return sh_out >= 1 ? requant8_r(g, sh_out) : sat8(g * (1 << -sh_out));
 }
 
+// ---------------------------------------------------------------------------
+// FMA-pipe form of the GELU chain
+// ---------------------------------------------------------------------------
+// The integer ALU pipe issues at half the rate of the FP32/IMAD pipes, and the
+// chain above is almost all ALU work.  gelu_chain_fast2 computes the same value
+// with part of the work moved to multiplier forms:
+//   * mul.hi.s32(x, 2^(32-k)) = floor(x / 2^k) = x >> k  (k >= 2),
+//     mul.hi.u32(x, 2^(32-k)) = x >> k for unsigned x,
+//     mul.hi.s32(x, 2) = x >> 31 for |x| < 2^30;
+//   * mad.lo.s32 with a multiplier of 1 or -1 in place of an add;
+//   * the quotient floor(n / den) of shift_gelu from a single-precision
+//     reciprocal estimate (rcp.approx.ftz.f32, at most 1 ulp from 1/den by the
+//     PTX ISA), biased so that it is q or q + 1, then one exact integer
+//     correction;
+//   * integer <-> float conversions by exponent-bias arithmetic
+//     (2^23 + e has the bit pattern 0x4B000000 + e for 0 <= e < 2^23).
+// The multiplier constants are kernel arguments (GeluK) so the compiler cannot
+// fold them back into shifts.  Valid for sh_in in [0, 30] when |v| + 2^(sh_in-1)
+// < 2^30 and |rsa(v, sh_in)| < 2^23 (no saturation to 24 bits), and sh_out in
+// [-7, 30]; the result is the unsaturated requantised value, which the caller
+// saturates to int8 (pack_sat8).
+struct GeluK {
+    int32_t sh_in, hin, ksgn;          // x = (v + hin + mulhi(v, ksgn)) >> sh_in
+    int32_t one, m1, c11, m65536;      // 1, -1, 11, -65536
+    int32_t c28, c29, two;             // 2^28, 2^29, 2
+    uint32_t c16u, c28u, c31u;         // 2^16, 2^28, 2^31
+    int32_t so_r, hout, ksgn_o, mul_l; // requant of the GELU value to the output scale
+};
+
+inline GeluK make_gelu_k(int sh_in, int sh_out) {
+    GeluK k;
+    k.sh_in = sh_in;
+    k.hin = sh_in > 0 ? 1 << (sh_in - 1) : 0;
+    k.ksgn = sh_in > 0 ? 2 : 0;
+    k.one = 1;
+    k.m1 = -1;
+    k.c11 = 11;
+    k.m65536 = -65536;
+    k.c28 = 1 << 28;
+    k.c29 = 1 << 29;
+    k.two = 2;
+    k.c16u = 1u << 16;
+    k.c28u = 1u << 28;
+    k.c31u = 1u << 31;
+    if (sh_out >= 1) {
+        k.so_r = sh_out;
+        k.hout = 1 << (sh_out - 1);
+        k.ksgn_o = 2;
+        k.mul_l = 1;
+    } else {
+        k.so_r = 0;
+        k.hout = 0;
+        k.ksgn_o = 0;
+        k.mul_l = 1 << (-sh_out);
+    }
+    return k;
+}
+
+// Whether gelu_chain_fast2 applies for these shifts, and the largest |v| it
+// accepts: |v| + 2^(sh_in-1) < 2^30 and |rsa(v, sh_in)| < 2^23.
+inline int gelu_fast2_range(int sh_in, int sh_out, int32_t *vlim) {
+    if (sh_in < 0 || sh_in > 30 || sh_out < -7 || sh_out > 30) return 0;
+    const int64_t hin = sh_in > 0 ? (int64_t)1 << (sh_in - 1) : 0;
+    int64_t lim = ((int64_t)1 << 30) - hin - 1;
+    const int64_t sat = ((int64_t)1 << (23 + sh_in)) - hin - 1;
+    if (sat < lim) lim = sat;
+    *vlim = (int32_t)lim;
+    return 1;
+}
+
+HV_DEV int32_t mulhi_s(int32_t a, int32_t b) {
+    int32_t r;
+    asm("mul.hi.s32 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+    return r;
+}
+HV_DEV uint32_t mulhi_u(uint32_t a, uint32_t b) {
+    uint32_t r;
+    asm("mul.hi.u32 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+    return r;
+}
+HV_DEV int32_t mad_s(int32_t a, int32_t b, int32_t c) {
+    int32_t r;
+    asm("mad.lo.s32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(c));
+    return r;
+}
+
+HV_DEV int32_t gelu_chain_fast2(int32_t v, const GeluK &k) {
+    // q16 = rsa(v, sh_in), no saturation by the caller's range check.
+    const int32_t x = (v + k.hin + mulhi_s(v, k.ksgn)) >> k.sh_in;
+    // shift_gelu (nonlinear.py:60-80): ip = 1.702x, ip2 = ip * log2(e)
+    const int32_t ip = x + (x >> 1) + mulhi_s(x, k.c29) + mulhi_s(x, k.c28);
+    const int32_t ip2 = ip + (ip >> 1) - mulhi_s(ip, k.c28);
+    const uint32_t a = (uint32_t)(ip2 < 0 ? -ip2 : ip2);
+    const uint32_t q = mulhi_u(a, k.c16u);
+    const uint32_t lo = (uint32_t)mad_s((int32_t)q, k.m65536, (int32_t)a);
+    const uint32_t frac = mulhi_u((uint32_t)mad_s((int32_t)lo, k.c11, 15), k.c28u);
+    uint32_t en;
+    asm("shr.b32 %0, %1, %2;" : "=r"(en) : "r"(65536u - frac), "r"(q));  // shifts >= 32 give 0
+    const uint32_t tp = (65536u + frac) << (q < 8u ? q : 8u);
+    const uint32_t e = ip2 < 0 ? en : (tp < 8388607u ? tp : 8388607u);
+    // sig = 65535 - floor(n / den), den = 2^16 + e, n = 2^32 - 1 - floor(den / 2)
+    const float fe = __int_as_float(mad_s((int32_t)e, k.one, 0x4B000000)) - 8388608.0f;
+    float rc;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(rc) : "f"(fe + 65536.0f));
+    // n / den = 2^32 / den - (floor(den/2) + 1) / den, the last term in (0.5, 0.5 + 2^-16]:
+    // the estimate below lies within 0.03 of n / den + 0.25, so it rounds to q or q + 1.
+    const float fq = fmaf(4294967296.0f, rc, -0.25f);
+    int32_t qe = mad_s(__float_as_int(fq + 12582912.0f), k.one, -0x4B400000);
+    const int32_t nh = mad_s((int32_t)mulhi_u(e, k.c31u), k.m1, -32769);    // ~(den >> 1)
+    const int32_t r = mad_s(qe, mad_s((int32_t)e, k.m1, -65536), nh);       // n - qe * den
+    qe += mulhi_s(r, k.two);                                                 // r < 0: q + 1 -> q
+    const int32_t sig = 65535 - qe;
+    const int64_t p = (int64_t)x * sig;
+    const int32_t g = (int32_t)((p + 32768 + (x >> 31)) >> 16);             // rsa(x * sig, 16)
+    // requant to the output scale (saturated by the caller)
+    return ((g + k.hout + mulhi_s(g, k.ksgn_o)) >> k.so_r) * k.mul_l;
+}
+
+// Saturate four int32 values to int8 and pack them (w0 in the low byte):
+// cvt.pack.sat.s8.s32.b32 d, a, b, c puts sat(b) in byte 0, sat(a) in byte 1 and
+// the low half of c in bytes 2-3.
+HV_DEV uint32_t pack_sat8(int32_t w0, int32_t w1, int32_t w2, int32_t w3) {
+    uint32_t hi, d;
+    asm("cvt.pack.sat.s8.s32.b32 %0, %1, %2, 0;" : "=r"(hi) : "r"(w3), "r"(w2));
+    asm("cvt.pack.sat.s8.s32.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(w1), "r"(w0), "r"(hi));
+    return d;
+}
+
 // PLAN sigmoid (nonlinear.py:83-95), unsigned Q0.16.
 HV_HD int32_t plan_sigmoid(int32_t x) {
     int32_t ax = x < 0 ? -x : x, y;

@@ -38,6 +38,8 @@ struct EpiParams {
     // GELU chain (EPI_GELU): sh_in = -16 - src, sh_out = dst + 16
     int gelu_sh_in, gelu_sh_out;
     int gelu_fast;            // host-checked ranges of gelu_chain_fast hold
+    int gelu_k2;              // host-checked ranges of gelu_chain_fast2 hold (persistent kernel)
+    GeluK gk;                 // constants of gelu_chain_fast2
     // patch (EPI_PATCH): pos [197][192], add = (a = embed, b = pos)
     const int8_t *pos;
 };

@@ -65,15 +65,23 @@ __device__ __forceinline__ void mbar_arrive(uint64_t *mbar) {
                  : "memory");
 }
 
-template <bool FAST>
-__device__ __forceinline__ int32_t p_wb8(int32_t acc, int32_t bias, int shift) {
-    if (FAST) return requant8_r(acc + bias, shift);
-    return (int32_t)requant64((int64_t)acc + bias, shift, 8);
-}
-template <bool FAST>
-__device__ __forceinline__ int32_t p_add8(int32_t a, int32_t b, AlignAdd k) {
-    if (FAST) return requant8_r(a * (1 << k.sa) + b * (1 << k.sb), k.sh);
-    return (int32_t)requant64(((int64_t)a << k.sa) + ((int64_t)b << k.sb), k.sh, 8);
+// One output element before the final int8 saturation (pack_sat8 applies it).
+// FAST: the 32-bit forms (gemm_epi_fast; for EPI_GELU, gelu_chain_fast2).
+template <int EPI, bool FAST>
+__device__ __forceinline__ int32_t epi_elem(int32_t acc, int32_t bb, int32_t ax, const EpiParams &e) {
+    if (EPI == EPI_GELU)
+        return FAST ? gelu_chain_fast2(acc + bb, e.gk) : gelu_chain((int64_t)acc + bb, e.gelu_sh_in, e.gelu_sh_out);
+    if (FAST) {
+        const int32_t y = rsa32(acc + bb, e.shift);
+        if (EPI == EPI_I8) return y;
+        const int32_t ys = sat8(y);
+        if (EPI == EPI_I8_RES) return rsa32(ax * (1 << e.add.sa) + ys * (1 << e.add.sb), e.add.sh);
+        return rsa32(ys * (1 << e.add.sa) + ax * (1 << e.add.sb), e.add.sh);  // patch: a = embedding, b = pos
+    }
+    const int32_t y = (int32_t)requant64((int64_t)acc + bb, e.shift, 8);
+    if (EPI == EPI_I8) return y;
+    if (EPI == EPI_I8_RES) return (int32_t)requant64(((int64_t)ax << e.add.sa) + ((int64_t)y << e.add.sb), e.add.sh, 8);
+    return (int32_t)requant64(((int64_t)y << e.add.sa) + ((int64_t)ax << e.add.sb), e.add.sh, 8);
 }
 
 template <int EPI, bool FAST, int KDIM, int N>
@@ -236,9 +244,7 @@ __global__ void __launch_bounds__(PT_THREADS, 1) tcp_gemm_kernel(GemmArgs g, int
                 for (int cc = 0; cc < BN / 64; ++cc) {
                     const int col0 = half * (BN / 2) + cc * 32;  // chunk-local column of v[0]
                     const int gcol0 = c * BN + col0;
-                    uint32_t v[32];
-                    tc05::ld32(lane_addr + tb * 256 + col0, v);
-                    tc05::wait_ld();
+                    // residual / positional bytes first, so their latency overlaps the TMEM read
                     uint4 r0 = make_uint4(0, 0, 0, 0), r1 = r0;
                     if (EPI == EPI_I8_RES && valid) {
                         const uint4 *r = (const uint4 *)(g.epi.res + orow * g.ldo + gcol0);
@@ -250,29 +256,30 @@ __global__ void __launch_bounds__(PT_THREADS, 1) tcp_gemm_kernel(GemmArgs g, int
                         r0 = r[0];
                         r1 = r[1];
                     }
+                    uint32_t v[32];
+                    tc05::ld32(lane_addr + tb * 256 + col0, v);
+                    int32_t bv[32];
+#pragma unroll
+                    for (int q4 = 0; q4 < 8; ++q4) {
+                        const int4 b4 = *(const int4 *)(sbias + gcol0 + 4 * q4);
+                        bv[4 * q4] = b4.x;
+                        bv[4 * q4 + 1] = b4.y;
+                        bv[4 * q4 + 2] = b4.z;
+                        bv[4 * q4 + 3] = b4.w;
+                    }
+                    tc05::wait_ld();
                     const uint32_t aux[8] = {r0.x, r0.y, r0.z, r0.w, r1.x, r1.y, r1.z, r1.w};
                     uint32_t pk[8];
 #pragma unroll
                     for (int w = 0; w < 8; ++w) {
-                        uint32_t word = 0;
+                        int32_t o[4];
 #pragma unroll
                         for (int b = 0; b < 4; ++b) {
                             const int j = w * 4 + b;
-                            const int32_t acc = (int32_t)v[j];
-                            const int32_t bb = sbias[gcol0 + j];
                             const int32_t ax = (int8_t)((aux[w] >> (8 * b)) & 0xffu);
-                            int32_t o;
-                            if (EPI == EPI_GELU) {
-                                o = FAST ? gelu_chain_fast(acc + bb, g.epi.gelu_sh_in, g.epi.gelu_sh_out)
-                                         : gelu_chain((int64_t)acc + bb, g.epi.gelu_sh_in, g.epi.gelu_sh_out);
-                            } else {
-                                o = p_wb8<FAST>(acc, bb, g.epi.shift);
-                                if (EPI == EPI_I8_RES) o = p_add8<FAST>(ax, o, g.epi.add);
-                                else if (EPI == EPI_PATCH) o = p_add8<FAST>(o, ax, g.epi.add);
-                            }
-                            word |= ((uint32_t)o & 0xffu) << (8 * b);
+                            o[b] = epi_elem<EPI, FAST>((int32_t)v[j], bv[j], ax, g.epi);
                         }
-                        pk[w] = word;
+                        pk[w] = pack_sat8(o[0], o[1], o[2], o[3]);
                     }
                     if (valid) {
                         uint4 *dst = (uint4 *)((int8_t *)g.out + orow * g.ldo + gcol0);

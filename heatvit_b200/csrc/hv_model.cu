@@ -86,7 +86,8 @@ struct BlockDev {
     size_t ln1_g, ln1_b, wqkv, bqkv, wproj, bproj, ln2_g, ln2_b, w1, b1, w2, b2;
     int ln1_xs, ln1_gs, ln1_bs, ln1_os, ln2_xs, ln2_gs, ln2_bs, ln2_os;
     int qkv_shift, qkv_wide, proj_shift, proj_wide, fc2_shift, fc2_wide;
-    int fc1_sh_in, fc1_sh_out, fc1_wide, fc1_fast;
+    int fc1_sh_in, fc1_sh_out, fc1_wide, fc1_fast, fc1_k2;
+    GeluK fc1_gk;
     AlignAdd res1, res2;
     AttnParams attn;
 };
@@ -254,8 +255,10 @@ GemmArgs gemm_args(const void *a, int lda, int patch_mode, const int8_t *bt, int
 // A layer GEMM of the model: the persistent kernel for the layer shapes it covers.
 cudaError_t model_gemm(const hv_model *m, GemmArgs &g, int epi, int m_max, cudaStream_t st) {
     g.epi.fast = gemm_epi_fast(epi, g.epi);
-    if (m->persistent && gemm_persistent_supported(epi, g.n, g.k))
+    if (m->persistent && gemm_persistent_supported(epi, g.n, g.k)) {
+        if (epi == EPI_GELU) g.epi.fast = g.epi.gelu_k2;  // the persistent kernel's fast GELU form
         return launch_gemm_persistent(g, epi, m_max, m->err, m->sms, st);
+    }
     return launch_gemm(g, epi, 0, m_max, m->err, st);
 }
 
@@ -330,6 +333,8 @@ int run_block(hv_model *m, int b, int images, const int32_t *off, cudaStream_t s
         g.epi.gelu_sh_in = d.fc1_sh_in;
         g.epi.gelu_sh_out = d.fc1_sh_out;
         g.epi.gelu_fast = d.fc1_fast;
+        g.epi.gelu_k2 = d.fc1_k2;
+        g.epi.gk = d.fc1_gk;
         CUDA_TRY(model_gemm(m, g, EPI_GELU, rows_max, st));
         pr.end(st, rows_dev, 0);
     }
@@ -499,6 +504,13 @@ int pack_model(hv_model *m, const hv_params *P) {
         d.fc1_wide = needs_wide(q.b1, HV_FFN, 192);
         d.fc1_fast = (!d.fc1_wide && d.fc1_sh_in >= 1 && d.fc1_sh_in <= 30 && d.fc1_sh_out >= -7 &&
                       d.fc1_sh_out <= 30) ? 1 : 0;
+        {
+            // |acc + bias| <= 192 * 2^14 + max|b1| must stay inside gelu_chain_fast2's input range
+            int32_t vlim = 0;
+            const int64_t vmax = max_abs(q.b1, HV_FFN) + (int64_t)192 * 16384;
+            d.fc1_k2 = (!d.fc1_wide && gelu_fast2_range(d.fc1_sh_in, d.fc1_sh_out, &vlim) && vmax <= vlim) ? 1 : 0;
+            d.fc1_gk = make_gelu_k(d.fc1_k2 ? d.fc1_sh_in : 0, d.fc1_k2 ? d.fc1_sh_out : 0);
+        }
         d.fc2_shift = q.ffn_out_scale_exp - (q.hidden_out_scale_exp + q.w2_scale_exp);
         d.fc2_wide = needs_wide(q.b2, 192, HV_FFN);
         if (!align_ok(q.x_scale_exp, q.msa_out_scale_exp, q.ffn_x_scale_exp) ||

@@ -295,9 +295,32 @@ __global__ void plan_kernel(const int32_t *x, int64_t n, int32_t *out) {
         out[i] = plan_sigmoid(x[i]);
 }
 
-__global__ void gelu_requant_kernel(const int32_t *acc, int64_t n, int sh_in, int sh_out, int8_t *out) {
-    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
-        out[i] = (int8_t)gelu_chain(acc[i], sh_in, sh_out);
+// Four values per thread.  Groups whose values all lie in [-vlim, vlim] take the
+// FMA-pipe chain (gelu_chain_fast2) and the saturating pack; the others, and the
+// tail, take the exact 64-bit chain.  k2 = 0 disables the fast form.
+__global__ void gelu_requant_kernel(const int32_t *acc, int64_t n, int sh_in, int sh_out, GeluK k, int k2,
+                                    int32_t vlim, int8_t *out) {
+    const int64_t n4 = n >> 2;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n4; i += (int64_t)gridDim.x * blockDim.x) {
+        int32_t w[4];
+        bool ok = k2 != 0;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            w[j] = acc[4 * i + j];
+            ok = ok && w[j] >= -vlim && w[j] <= vlim;
+        }
+        if (ok) {
+            const uint32_t d = pack_sat8(gelu_chain_fast2(w[0], k), gelu_chain_fast2(w[1], k),
+                                         gelu_chain_fast2(w[2], k), gelu_chain_fast2(w[3], k));
+#pragma unroll
+            for (int j = 0; j < 4; ++j) out[4 * i + j] = (int8_t)(d >> (8 * j));
+        } else {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) out[4 * i + j] = (int8_t)gelu_chain(w[j], sh_in, sh_out);
+        }
+    }
+    if (blockIdx.x == 0 && threadIdx.x < (n & 3))
+        out[4 * n4 + threadIdx.x] = (int8_t)gelu_chain(acc[4 * n4 + threadIdx.x], sh_in, sh_out);
 }
 
 __global__ void writeback_kernel(const int64_t *acc, int64_t n, int shift, int bits, void *out) {
@@ -364,7 +387,11 @@ cudaError_t launch_plan(const int32_t *x, int64_t n, int32_t *out, cudaStream_t 
 cudaError_t launch_gelu_requant(const int32_t *acc, int64_t n, int sh_in, int sh_out, int8_t *out,
                                 cudaStream_t st) {
     if (n <= 0) return cudaSuccess;
-    gelu_requant_kernel<<<grid_for(n, 256), 256, 0, st>>>(acc, n, sh_in, sh_out, out);
+    int32_t vlim = 0;
+    const int k2 = gelu_fast2_range(sh_in, sh_out, &vlim);
+    gelu_requant_kernel<<<grid_for((n + 3) / 4, 256), 256, 0, st>>>(acc, n, sh_in, sh_out,
+                                                                   make_gelu_k(k2 ? sh_in : 0, k2 ? sh_out : 0),
+                                                                   k2, vlim, out);
     return cudaGetLastError();
 }
 

@@ -93,6 +93,20 @@ def test_gelu_requant_chain(cuda, oracle):
         np.testing.assert_array_equal(gelu_requant_array(acc, src, dst), oracle.gelu_chain_array(acc, src, dst))
 
 
+@pytest.mark.parametrize("src,sh_out", [(-17, -7), (-17, -1), (-17, 0), (-17, 1), (-17, 2), (-17, 6), (-17, 8),
+                                        (-17, 9), (-17, 12), (-17, 30), (-16, 0), (-16, 7)])
+def test_gelu_requant_fma_form_exhaustive(cuda, oracle, src, sh_out):
+    """The GELU chain's FMA-pipe form on every Q8.16 input it can see: with
+    src = -17 (input shift 1) the values [-2^24, 2^24) cover every q16 with both
+    rounding directions; src = -16 (no input shift) covers q16 = v directly.
+    Both ends of the range also exercise the exact fallback."""
+    from heatvit_b200.nonlinear import gelu_requant_array
+    span = 1 << (24 if src == -17 else 23)
+    v = np.arange(-span, span, dtype=np.int32)
+    dst = sh_out - 16
+    np.testing.assert_array_equal(gelu_requant_array(v, src, dst), oracle.gelu_chain_array(v, src, dst))
+
+
 def test_align_add(cuda, oracle):
     from heatvit_b200.transformer import align_add_array
     rng = np.random.default_rng(5)
