@@ -81,10 +81,63 @@ __device__ __forceinline__ LnStats ln_stats(int32_t s, int64_t s2, const LnParam
     st.neg = var < 0;
     if (st.neg) var = 0;
     const uint64_t sd = isqrt64((uint64_t)var + 4295u);
-    uint64_t inv = ((uint64_t)1 << 48) / sd;
-    if (2 * (((uint64_t)1 << 48) - inv * sd) >= sd) inv += 1;
+    // inv = round_div(2^48, sd): a double-precision quotient (within 1 of the
+    // floor, as 2^48 / sd < 2^42) corrected by the exact remainder.
+    uint64_t inv = (uint64_t)(281474976710656.0 / (double)sd);
+    int64_t rem = (int64_t)(((uint64_t)1 << 48) - inv * sd);
+    if (rem < 0) { inv -= 1; rem += (int64_t)sd; }
+    if (rem >= (int64_t)sd) { inv += 1; rem -= (int64_t)sd; }
+    if (2 * (uint64_t)rem >= sd) inv += 1;
     st.inv = inv;
     return st;
+}
+
+// Affine form of the normalisation for one row.  With s = sh_sum and v the int8
+// input, prod = (v*2^s - mean) * inv and T = prod + 2^47 = (v + 128) * A + K for
+// A = inv * 2^s and K = 2^47 - mean*inv - 128*A, both fixed per row.  Then
+// rsa(prod, 48) = floor((T - [prod < 0]) / 2^48), and prod < 0 iff v + 128 < vt.
+// `safe`: |prod| + 2^47 < 2^71 for every int8 v, so the result needs no 24-bit
+// saturation and fits 32 bits.  inv < 2^42 (sd >= 65) and s <= 32 give A < 2^74,
+// |K| < 2^82.
+struct LnAff {
+    uint32_t al, ah0, ah1, klo;  // A = ah1*2^64 + ah0*2^32 + al, K mod 2^32
+    int64_t khi;                 // floor(K / 2^32)
+    int32_t vt;
+    bool safe;
+};
+
+__device__ __forceinline__ LnAff ln_aff(const LnStats &st, const LnParams &p) {
+    LnAff f;
+    const u128 A = (u128)st.inv << p.sh_sum;
+    f.al = (uint32_t)A;
+    const uint64_t ah = (uint64_t)(A >> 32);
+    f.ah0 = (uint32_t)ah;
+    f.ah1 = (uint32_t)(ah >> 32);
+    const i128 K = ((i128)1 << 47) - (i128)st.mean * (i128)st.inv - (i128)128 * (i128)A;
+    f.klo = (uint32_t)(u128)K;
+    f.khi = (int64_t)(K >> 32);
+    int64_t vt = -((-st.mean) >> p.sh_sum);  // ceil(mean / 2^s): prod >= 0 iff v >= vt
+    vt = vt < -128 ? -128 : (vt > 128 ? 128 : vt);
+    f.vt = (int32_t)vt + 128;
+    const i128 d1 = ((i128)127 << p.sh_sum) - st.mean, d2 = st.mean + ((i128)128 << p.sh_sum);
+    const u128 dm = (u128)(d1 > d2 ? d1 : d2);
+    f.safe = dm * st.inv + ((u128)1 << 47) < ((u128)1 << 71);
+    return f;
+}
+
+// norm of one int8 input on a safe row (see LnAff).
+__device__ __forceinline__ int32_t ln_norm_aff(int32_t v, const LnAff &f) {
+    const uint32_t vp = (uint32_t)(v + 128);
+    const uint64_t S = (uint64_t)vp * f.al + f.klo;                          // < 2^41
+    const uint64_t Q = (uint64_t)vp * f.ah0 + ((uint64_t)(vp * f.ah1) << 32);  // < 2^50
+    const int64_t U = (int64_t)Q + f.khi + (int64_t)(S >> 32);              // floor(T / 2^32)
+    int32_t nr = (int32_t)(U >> 16);                                         // floor(T / 2^48)
+    if ((uint32_t)S == 0u) {
+        // T is a multiple of 2^48 only if its low 48 bits vanish; then a negative
+        // product rounds one lower.
+        if ((U & 0xFFFF) == 0 && (int32_t)vp < f.vt) nr -= 1;
+    }
+    return nr;
 }
 
 // norm = sat24(rsa((x_q32 - mean) * inv, 48)) (nonlinear.py:176-179).
@@ -121,10 +174,23 @@ __device__ __forceinline__ int32_t ln_out(int32_t norm, int32_t g, int32_t b, co
     return requant128_8(((i128)prodg << p.sh_g) + ((i128)b << p.sh_b), p.sh_out);
 }
 
+// Per-lane channel constants: lane `sub` owns channels [24*sub, 24*sub + 24) of
+// every row it processes, so gamma and the aligned beta term are loaded once.
+template <bool OUT32>
+__device__ __forceinline__ void ln_lane_consts(const LnParams &p, int sub, int32_t (&gam)[24], int32_t (&bet)[24]) {
+#pragma unroll
+    for (int i = 0; i < 24; ++i) {
+        gam[i] = p.gamma[24 * sub + i];
+        const int32_t b = p.beta[24 * sub + i];
+        bet[i] = OUT32 ? b * (1 << p.sh_b) : b;
+    }
+}
+
 // One row per 8-lane group; lane `sub` owns channels [24*sub, 24*sub + 24).
 // Returns true on negative variance.  All 32 lanes of the warp must call it.
 template <bool SPLIT, bool OUT32>
-__device__ __forceinline__ bool ln_row8(const int8_t *xr, int8_t *outr, const LnParams &p, int sub, bool active) {
+__device__ __forceinline__ bool ln_row8(const int8_t *xr, int8_t *outr, const LnParams &p, int sub, bool active,
+                                        const int32_t (&gam)[24], const int32_t (&bet)[24]) {
     int32_t v[24];
     uint2 w[3] = {make_uint2(0, 0), make_uint2(0, 0), make_uint2(0, 0)};
     if (active) {
@@ -164,19 +230,21 @@ __device__ __forceinline__ bool ln_row8(const int8_t *xr, int8_t *outr, const Ln
 #pragma unroll
     for (int o = 1; o < 8; o <<= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
     const LnStats st = ln_stats(s, s2, p);
+    const LnAff af = ln_aff(st, p);
+    int32_t o[24];
+    if (af.safe) {
+#pragma unroll
+        for (int i = 0; i < 24; ++i) {
+            const int32_t nr = ln_norm_aff(v[i], af);
+            o[i] = OUT32 ? rsa32(nr * gam[i] + bet[i], p.sh_out) : ln_out<false>(nr, gam[i], bet[i], p);
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < 24; ++i) o[i] = ln_out<OUT32>(ln_norm<SPLIT>(v[i], st, p), gam[i], p.beta[24 * sub + i], p);
+    }
     uint32_t ow[6];
 #pragma unroll
-    for (int i = 0; i < 6; ++i) {
-        uint32_t word = 0;
-#pragma unroll
-        for (int b = 0; b < 4; ++b) {
-            const int vi = i * 4 + b;  // byte vi of this lane's 24-byte slice
-            const int chan = 24 * sub + vi;
-            const int32_t o = ln_out<OUT32>(ln_norm<SPLIT>(v[vi], st, p), p.gamma[chan], p.beta[chan], p);
-            word |= ((uint32_t)o & 0xffu) << (8 * b);
-        }
-        ow[i] = word;
-    }
+    for (int i = 0; i < 6; ++i) ow[i] = pack_sat8(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
     if (active) {
         uint2 *dst = (uint2 *)(outr + 24 * sub);
         dst[0] = make_uint2(ow[0], ow[1]);
@@ -204,12 +272,14 @@ __global__ void __launch_bounds__(256) ln_kernel(const int8_t *x, int8_t *out, i
     const int lane = threadIdx.x & 31, sub = lane & 7, grp = lane >> 3;
     const int warps = (gridDim.x * blockDim.x) >> 5;
     const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    int32_t gam[24], bet[24];
+    ln_lane_consts<OUT32>(p, sub, gam, bet);
     // each warp handles 4 rows per iteration (one per 8-lane group)
     for (int base = warp * 4; base < rows; base += warps * 4) {
         const int r = base + grp;
         const bool active = r < rows;
-        const bool neg = ln_row8<SPLIT, OUT32>(x + (size_t)(active ? r : 0) * 192, out + (size_t)(active ? r : 0) * 192, p, sub,
-                                 active);
+        const bool neg = ln_row8<SPLIT, OUT32>(x + (size_t)(active ? r : 0) * 192, out + (size_t)(active ? r : 0) * 192, p,
+                                               sub, active, gam, bet);
         if (active && sub == 0) {
             if (negvar_row) negvar_row[r] = neg ? 1 : 0;
             if (neg && warn && offsets) {
@@ -226,8 +296,10 @@ __global__ void __launch_bounds__(256) ln_cls_kernel(const int8_t *x, const int3
     const int lane = threadIdx.x & 31, sub = lane & 7, grp = lane >> 3;
     const int i = ((blockIdx.x * blockDim.x + threadIdx.x) >> 5) * 4 + grp;
     const bool active = i < images;
+    int32_t gam[24], bet[24];
+    ln_lane_consts<OUT32>(p, sub, gam, bet);
     const bool neg = ln_row8<SPLIT, OUT32>(x + (size_t)(active ? offsets[i] : 0) * 192, out + (size_t)(active ? i : 0) * 192, p,
-                             sub, active);
+                                           sub, active, gam, bet);
     if (neg && active && sub == 0 && warn)
         atomicOr((unsigned int *)(warn + (i & ~3)), (unsigned int)HV_WARN_LN_NEG_VARIANCE << (8 * (i & 3)));
 }
