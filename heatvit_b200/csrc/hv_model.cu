@@ -128,6 +128,12 @@ struct hv_model {
     // host-pipeline staging
     int host_cap = 0;
     int8_t *himg[2] = {nullptr, nullptr};
+    // pinned host staging of hv_infer_host: outputs of a whole call, and two image
+    // chunks for callers whose image buffer is pageable
+    uint8_t *pin_out = nullptr;
+    size_t pin_out_cap = 0;
+    int8_t *pin_in[2] = {nullptr, nullptr};
+    int pin_in_cap = 0;
     int32_t *hlogits = nullptr, *htc = nullptr;
     hv_selector_summary *hsum = nullptr;
     uint8_t *hwarn = nullptr;
@@ -654,6 +660,9 @@ int hv_model_destroy(hv_model *m) {
     if (m->htc) cudaFree(m->htc);
     if (m->hsum) cudaFree(m->hsum);
     if (m->hwarn) cudaFree(m->hwarn);
+    if (m->pin_out) cudaFreeHost(m->pin_out);
+    for (int i = 0; i < 2; ++i)
+        if (m->pin_in[i]) cudaFreeHost(m->pin_in[i]);
     for (auto e : m->prof_ev) cudaEventDestroy(e);
     if (m->prof_rows) cudaFree(m->prof_rows);
     if (m->copy_stream) cudaStreamDestroy(m->copy_stream);
@@ -683,7 +692,14 @@ int hv_infer_host(hv_model *m, const int8_t *h_images, int batch, int32_t *h_log
     if (!m) return fail(HV_ERR_VALUE, "null model");
     if (batch <= 0 || !h_images || !h_logits) return fail(HV_ERR_VALUE, "bad arguments");
     CUDA_TRY(cudaSetDevice(m->device));
-    const int chunk = std::min(batch, 256);
+    // Chunk schedule: a small first chunk (its upload is the only exposed one), then
+    // chunks of up to kHostChunk images whose uploads overlap the previous chunk's
+    // compute.  Large chunks keep the per-launch fixed costs of the pipeline small.
+    const int kFirstChunk = 256, kHostChunk = 1024;
+    const int chunk = std::min(batch, kHostChunk);
+    std::vector<int> starts(1, 0);
+    for (int f = std::min(batch, kFirstChunk); f < batch; f += kHostChunk) starts.push_back(f);
+    starts.push_back(batch);
     const int ns = m->used_sel;
     if (!m->copy_stream) {
         CUDA_TRY(cudaStreamCreateWithFlags(&m->copy_stream, cudaStreamNonBlocking));
@@ -709,14 +725,50 @@ int hv_infer_host(hv_model *m, const int8_t *h_images, int batch, int32_t *h_log
     }
     int rc = ensure_capacity(m, chunk);
     if (rc) return rc;
-    const int nchunks = (batch + chunk - 1) / chunk;
+    // Outputs land in pinned staging (an asynchronous copy into pageable memory
+    // would block this thread until the chunk's compute finished, serialising the
+    // pipeline) and are copied to the caller's arrays once at the end.
+    const size_t o_log = 0, o_tc = o_log + (size_t)batch * HV_CLASSES * 4,
+                 o_sum = o_tc + (size_t)batch * (ns + 1) * 4,
+                 o_warn = o_sum + (size_t)batch * ns * sizeof(hv_selector_summary),
+                 o_end = o_warn + (size_t)batch;
+    if (o_end > m->pin_out_cap) {
+        if (m->pin_out) cudaFreeHost(m->pin_out);
+        m->pin_out = nullptr;
+        m->pin_out_cap = 0;
+        CUDA_TRY(cudaHostAlloc((void **)&m->pin_out, o_end, cudaHostAllocDefault));
+        m->pin_out_cap = o_end;
+    }
+    // Pageable images are staged through two pinned chunk buffers; the host copy of
+    // chunk c + 1 overlaps the device work on chunk c.
+    cudaPointerAttributes pa;
+    const bool pinned_in = cudaPointerGetAttributes(&pa, h_images) == cudaSuccess && pa.type == cudaMemoryTypeHost;
+    cudaGetLastError();  // clear a possible error from the query
+    if (!pinned_in && chunk > m->pin_in_cap) {
+        for (int i = 0; i < 2; ++i) {
+            if (m->pin_in[i]) cudaFreeHost(m->pin_in[i]);
+            m->pin_in[i] = nullptr;
+        }
+        m->pin_in_cap = 0;
+        for (int i = 0; i < 2; ++i)
+            CUDA_TRY(cudaHostAlloc((void **)&m->pin_in[i], (size_t)chunk * HV_IMAGE_BYTES, cudaHostAllocDefault));
+        m->pin_in_cap = chunk;
+    }
+    const int nchunks = (int)starts.size() - 1;
     for (int c = 0; c < nchunks; ++c) {
         const int buf = c & 1;
-        const int first = c * chunk, cnt = std::min(chunk, batch - first);
+        const int first = starts[c], cnt = starts[c + 1] - starts[c];
+        const int8_t *src = h_images + (size_t)first * HV_IMAGE_BYTES;
+        if (!pinned_in) {
+            // the copy out of pin_in[buf] issued two chunks back must have finished
+            if (c >= 2) CUDA_TRY(cudaEventSynchronize(m->ev_in[buf]));
+            memcpy(m->pin_in[buf], src, (size_t)cnt * HV_IMAGE_BYTES);
+            src = m->pin_in[buf];
+        }
         // The copy into buffer `buf` must wait until the compute two chunks back released it.
         if (c >= 2) CUDA_TRY(cudaStreamWaitEvent(m->copy_stream, m->ev_done[buf], 0));
-        CUDA_TRY(cudaMemcpyAsync(m->himg[buf], h_images + (size_t)first * HV_IMAGE_BYTES, (size_t)cnt * HV_IMAGE_BYTES,
-                                 cudaMemcpyHostToDevice, m->copy_stream));
+        CUDA_TRY(cudaMemcpyAsync(m->himg[buf], src, (size_t)cnt * HV_IMAGE_BYTES, cudaMemcpyHostToDevice,
+                                 m->copy_stream));
         CUDA_TRY(cudaEventRecord(m->ev_in[buf], m->copy_stream));
         CUDA_TRY(cudaStreamWaitEvent(m->compute_stream, m->ev_in[buf], 0));
         int32_t *dl = m->hlogits + (size_t)buf * m->host_cap * HV_CLASSES;
@@ -727,18 +779,23 @@ int hv_infer_host(hv_model *m, const int8_t *h_images, int batch, int32_t *h_log
                         h_warnings ? dw : nullptr, nullptr, nullptr, m->compute_stream);
         if (rc) return rc;
         CUDA_TRY(cudaEventRecord(m->ev_done[buf], m->compute_stream));
-        CUDA_TRY(cudaMemcpyAsync(h_logits + (size_t)first * HV_CLASSES, dl, (size_t)cnt * HV_CLASSES * 4,
+        CUDA_TRY(cudaMemcpyAsync(m->pin_out + o_log + (size_t)first * HV_CLASSES * 4, dl, (size_t)cnt * HV_CLASSES * 4,
                                  cudaMemcpyDeviceToHost, m->compute_stream));
         if (h_token_counts)
-            CUDA_TRY(cudaMemcpyAsync(h_token_counts + (size_t)first * (ns + 1), dtc, (size_t)cnt * (ns + 1) * 4,
+            CUDA_TRY(cudaMemcpyAsync(m->pin_out + o_tc + (size_t)first * (ns + 1) * 4, dtc, (size_t)cnt * (ns + 1) * 4,
                                      cudaMemcpyDeviceToHost, m->compute_stream));
         if (h_summary && ns)
-            CUDA_TRY(cudaMemcpyAsync(h_summary + (size_t)first * ns, dsum, (size_t)cnt * ns * sizeof(hv_selector_summary),
-                                     cudaMemcpyDeviceToHost, m->compute_stream));
+            CUDA_TRY(cudaMemcpyAsync(m->pin_out + o_sum + (size_t)first * ns * sizeof(hv_selector_summary), dsum,
+                                     (size_t)cnt * ns * sizeof(hv_selector_summary), cudaMemcpyDeviceToHost,
+                                     m->compute_stream));
         if (h_warnings)
-            CUDA_TRY(cudaMemcpyAsync(h_warnings + first, dw, cnt, cudaMemcpyDeviceToHost, m->compute_stream));
+            CUDA_TRY(cudaMemcpyAsync(m->pin_out + o_warn + first, dw, cnt, cudaMemcpyDeviceToHost, m->compute_stream));
     }
     CUDA_TRY(cudaStreamSynchronize(m->compute_stream));
+    memcpy(h_logits, m->pin_out + o_log, (size_t)batch * HV_CLASSES * 4);
+    if (h_token_counts) memcpy(h_token_counts, m->pin_out + o_tc, (size_t)batch * (ns + 1) * 4);
+    if (h_summary && ns) memcpy(h_summary, m->pin_out + o_sum, (size_t)batch * ns * sizeof(hv_selector_summary));
+    if (h_warnings) memcpy(h_warnings, m->pin_out + o_warn, (size_t)batch);
     int code = 0;
     CUDA_TRY(cudaMemcpy(&code, m->err, sizeof(int), cudaMemcpyDeviceToHost));
     if (code) return fail(HV_ERR_STATE, "a device-side bounded wait gave up (code %d)", code);

@@ -130,10 +130,19 @@ def test_host_entry_matches_device_entry(cuda):
     from heatvit_b200.engine import Engine
     params = synth.config_params(synth.SEED, pruned=True)
     eng = Engine(params)
-    imgs = synth.baseline_images(synth.SEED, 300, first=77)
-    host = eng.infer_host(imgs)
-    dev = eng.infer(torch.from_numpy(imgs).cuda())["logits"].cpu().numpy()
-    np.testing.assert_array_equal(host, dev)
+    n = 1400                                                   # chunks of 256, 1024 and 120 images
+    imgs = synth.baseline_images(synth.SEED, n, first=77)
+    dev = eng.infer(torch.from_numpy(imgs).cuda())
+    ns = eng.num_selectors
+    pinned = torch.empty(imgs.shape, dtype=torch.int8, pin_memory=True)
+    pinned.numpy()[:] = imgs
+    for src in (imgs, pinned.numpy()):                         # pageable (staged) and pinned input
+        tc = np.empty((n, ns + 1), np.int32)
+        warn = np.empty(n, np.uint8)
+        host = eng.infer_host(src, token_counts=tc, warnings=warn)
+        np.testing.assert_array_equal(host, dev["logits"].cpu().numpy())
+        np.testing.assert_array_equal(tc, dev["token_counts"].cpu().numpy())
+        np.testing.assert_array_equal(warn, dev["warnings"].cpu().numpy())
 
 
 def test_engine_input_errors(cuda):
