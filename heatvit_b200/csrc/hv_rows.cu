@@ -264,6 +264,36 @@ __device__ __forceinline__ int image_of_row(const int32_t *offsets, int images, 
     return lo;
 }
 
+// 24 bytes of a row (lane `sub` of its 8-lane group) as int32 values.
+__device__ __forceinline__ void ln_load24(const int8_t *xr, int sub, bool active, int32_t (&v)[24]) {
+    uint2 w[3] = {make_uint2(0, 0), make_uint2(0, 0), make_uint2(0, 0)};
+    if (active) {
+        const uint2 *src = (const uint2 *)(xr + 24 * sub);
+        w[0] = src[0];
+        w[1] = src[1];
+        w[2] = src[2];
+    }
+#pragma unroll
+    for (int i = 0; i < 3; ++i) {
+#pragma unroll
+        for (int b = 0; b < 4; ++b) {
+            v[i * 8 + b] = (int8_t)((w[i].x >> (8 * b)) & 0xffu);
+            v[i * 8 + 4 + b] = (int8_t)((w[i].y >> (8 * b)) & 0xffu);
+        }
+    }
+}
+
+__device__ __forceinline__ int64_t shfl64(int64_t v, int src) {
+    const int32_t lo = __shfl_sync(0xffffffffu, (int32_t)v, src);
+    const int32_t hi = __shfl_sync(0xffffffffu, (int32_t)(v >> 32), src);
+    return (int64_t)(((uint64_t)(uint32_t)hi << 32) | (uint32_t)lo);
+}
+
+// 32 rows per warp and pass.  Phase 1: eight 4-row sub-passes (8 lanes per row,
+// 24 channels per lane) reduce Σx and Σx² per row; lane L keeps row base + L.
+// Phase 2: every lane derives the statistics and affine constants of its own row
+// (one row per lane instead of eight lanes per row).  Phase 3: the sub-passes
+// again, each 8-lane group taking its row's constants from the owning lane.
 template <bool SPLIT, bool OUT32>
 __global__ void __launch_bounds__(256) ln_kernel(const int8_t *x, int8_t *out, int rows_max, const int32_t *rows_dev,
                                                  LnParams p, uint8_t *negvar_row, const int32_t *offsets,
@@ -274,17 +304,97 @@ __global__ void __launch_bounds__(256) ln_kernel(const int8_t *x, int8_t *out, i
     const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     int32_t gam[24], bet[24];
     ln_lane_consts<OUT32>(p, sub, gam, bet);
-    // each warp handles 4 rows per iteration (one per 8-lane group)
-    for (int base = warp * 4; base < rows; base += warps * 4) {
-        const int r = base + grp;
-        const bool active = r < rows;
-        const bool neg = ln_row8<SPLIT, OUT32>(x + (size_t)(active ? r : 0) * 192, out + (size_t)(active ? r : 0) * 192, p,
-                                               sub, active, gam, bet);
-        if (active && sub == 0) {
-            if (negvar_row) negvar_row[r] = neg ? 1 : 0;
-            if (neg && warn && offsets) {
-                const int img = image_of_row(offsets, images, r);
+    for (int base = warp * 32; base < rows; base += warps * 32) {
+        int32_t my_s = 0;
+        int64_t my_s2 = 0;
+#pragma unroll 1
+        for (int k = 0; k < 8; ++k) {
+            const int r = base + 4 * k + grp;
+            int32_t v[24];
+            ln_load24(x + (size_t)(r < rows ? r : 0) * 192, sub, r < rows, v);
+            int32_t s = 0;
+#pragma unroll
+            for (int i = 0; i < 24; ++i) s += v[i];
+            int64_t s2;
+            if (p.sq_shift >= 0) {
+                int32_t q = 0;
+#pragma unroll
+                for (int i = 0; i < 24; ++i) q += v[i] * v[i];
+#pragma unroll
+                for (int o = 1; o < 8; o <<= 1) q += __shfl_xor_sync(0xffffffffu, q, o);
+                s2 = (int64_t)q << p.sq_shift;
+            } else {
+                const int kk = -p.sq_shift;  // per-element ties-away right shift (x^2 >= 0)
+                int64_t q = 0;
+#pragma unroll
+                for (int i = 0; i < 24; ++i) q += ((int64_t)(v[i] * v[i]) + ((int64_t)1 << (kk - 1))) >> kk;
+#pragma unroll
+                for (int o = 1; o < 8; o <<= 1) q += __shfl_xor_sync(0xffffffffu, q, o);
+                s2 = q;
+            }
+#pragma unroll
+            for (int o = 1; o < 8; o <<= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+            // lane L = 4k + g takes the totals of group g (any of its lanes)
+            const int32_t ts = __shfl_sync(0xffffffffu, s, (lane & 3) * 8);
+            const int64_t tq = shfl64(s2, (lane & 3) * 8);
+            if ((lane >> 2) == k) {
+                my_s = ts;
+                my_s2 = tq;
+            }
+        }
+        const int myrow = base + lane;
+        const LnStats st = ln_stats(my_s, my_s2, p);
+        const LnAff af = ln_aff(st, p);
+        if (myrow < rows) {
+            if (negvar_row) negvar_row[myrow] = st.neg ? 1 : 0;
+            if (st.neg && warn && offsets) {
+                const int img = image_of_row(offsets, images, myrow);
                 atomicOr((unsigned int *)(warn + (img & ~3)), (unsigned int)HV_WARN_LN_NEG_VARIANCE << (8 * (img & 3)));
+            }
+        }
+        const bool all_safe = __all_sync(0xffffffffu, af.safe || myrow >= rows);
+#pragma unroll 1
+        for (int k = 0; k < 8; ++k) {
+            const int r = base + 4 * k + grp;
+            const bool active = r < rows;
+            const int owner = 4 * k + grp;
+            LnAff f;
+            f.al = __shfl_sync(0xffffffffu, af.al, owner);
+            f.ah0 = __shfl_sync(0xffffffffu, af.ah0, owner);
+            f.ah1 = __shfl_sync(0xffffffffu, af.ah1, owner);
+            f.klo = __shfl_sync(0xffffffffu, af.klo, owner);
+            f.khi = shfl64(af.khi, owner);
+            f.vt = __shfl_sync(0xffffffffu, af.vt, owner);
+            int32_t v[24];
+            ln_load24(x + (size_t)(active ? r : 0) * 192, sub, active, v);
+            int32_t o[24];
+            if (all_safe) {
+#pragma unroll
+                for (int i = 0; i < 24; ++i) {
+                    const int32_t nr = ln_norm_aff(v[i], f);
+                    o[i] = OUT32 ? rsa32(nr * gam[i] + bet[i], p.sh_out) : ln_out<false>(nr, gam[i], bet[i], p);
+                }
+            } else {
+                LnStats rs;
+                rs.mean = shfl64(st.mean, owner);
+                rs.inv = (uint64_t)shfl64((int64_t)st.inv, owner);
+                rs.neg = false;
+                const bool rsafe = __shfl_sync(0xffffffffu, af.safe ? 1 : 0, owner) != 0;
+#pragma unroll
+                for (int i = 0; i < 24; ++i) {
+                    if (rsafe) {
+                        const int32_t nr = ln_norm_aff(v[i], f);
+                        o[i] = OUT32 ? rsa32(nr * gam[i] + bet[i], p.sh_out) : ln_out<false>(nr, gam[i], bet[i], p);
+                    } else {
+                        o[i] = ln_out<OUT32>(ln_norm<SPLIT>(v[i], rs, p), gam[i], p.beta[24 * sub + i], p);
+                    }
+                }
+            }
+            if (active) {
+                uint2 *dst = (uint2 *)(out + (size_t)r * 192 + 24 * sub);
+                dst[0] = make_uint2(pack_sat8(o[0], o[1], o[2], o[3]), pack_sat8(o[4], o[5], o[6], o[7]));
+                dst[1] = make_uint2(pack_sat8(o[8], o[9], o[10], o[11]), pack_sat8(o[12], o[13], o[14], o[15]));
+                dst[2] = make_uint2(pack_sat8(o[16], o[17], o[18], o[19]), pack_sat8(o[20], o[21], o[22], o[23]));
             }
         }
     }
@@ -419,7 +529,7 @@ cudaError_t launch_layernorm(const int8_t *x, int8_t *out, int rows_max, const i
                              const LnParams &p, uint8_t *negvar_row, const int32_t *offsets, int images,
                              uint8_t *warn, cudaStream_t st) {
     if (rows_max <= 0) return cudaSuccess;
-    const int rows_per_block = 8 * 4;  // 8 warps x 4 rows
+    const int rows_per_block = 8 * 32;  // 8 warps x 32 rows
     int blocks = (rows_max + rows_per_block - 1) / rows_per_block;
     if (blocks > 148 * 16) blocks = 148 * 16;
     auto kern = p.split ? (p.out32 ? ln_kernel<true, true> : ln_kernel<true, false>)
