@@ -39,6 +39,12 @@ STAGE_MACS_PER_ROW = {"qkv": 192 * 576, "proj": 192 * 192, "fc1": 192 * 768, "fc
                       "patch": 768 * 192, "head": 192 * 1000}
 # Algorithmic HBM bytes per row for the row-wise kernels (int8 in + int8 out).
 STAGE_BYTES_PER_ROW = {"ln1": 384, "ln2": 384}
+# DRAM bytes (read + write) per row of one launch, from the committed ncu capture of a
+# full-size launch (block 1, 201,728 rows): profiles/tcp_gemm_fc1_fc2_block1_b1024.md,
+# profiles/ln_kernel_ln1_block1_b1024.md.  Traffic grows with the rows of a launch.
+STAGE_TRAFFIC_PER_ROW = {"fc1": (39_059_456 + 102_366_208) / 201_728,
+                         "fc2": (193_842_944 + 24_758_272) / 201_728,
+                         "ln1": (38_787_840 + 1_576_448) / 201_728}
 
 
 def algorithmic_macs(counts):
@@ -226,6 +232,7 @@ def main():
     import torch.distributed as dist
     from heatvit_b200 import _lib, synth
     from heatvit_b200.engine import Engine
+    from heatvit_b200.shard import gather_outputs, shard_range
 
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -239,20 +246,15 @@ def main():
     params = synth.config_params(synth.SEED, pruned=args.variant == "pruned")
     eng = Engine(params)
     b = args.batch
-    host_imgs = synth.baseline_images(synth.SEED, b, first=rank * b)
+    first, _ = shard_range(rank, world, b)
+    host_imgs = synth.baseline_images(synth.SEED, b, first=first)
     imgs = torch.from_numpy(host_imgs).cuda()
     ns = eng.num_selectors
     peaks = measured_peaks()
 
     def step():
         out = eng.infer(imgs)
-        if world > 1:
-            glog = torch.empty((world * b, 1000), dtype=torch.int32, device="cuda")
-            gcnt = torch.empty((world * b, ns + 1), dtype=torch.int32, device="cuda")
-            dist.all_gather_into_tensor(glog, out["logits"])
-            dist.all_gather_into_tensor(gcnt, out["token_counts"])
-            return glog, gcnt
-        return out["logits"], out["token_counts"]
+        return gather_outputs(out["logits"], out["token_counts"], world)
 
     for _ in range(args.warmup):
         logits, counts = step()
@@ -314,18 +316,20 @@ def main():
         model_frac = max(t_compute / world, t_mem) / (ms_per_step * 1e-3)
         st = args.profile_stage
         kavg = kms.value / max(1, launches.value)
+        rows_avg = krows.value / max(1, launches.value)
+        traffic = STAGE_TRAFFIC_PER_ROW[st] * rows_avg if st in STAGE_TRAFFIC_PER_ROW else None
         if st in STAGE_MACS_PER_ROW:
             work = 2.0 * STAGE_MACS_PER_ROW[st] * krows.value / max(1, launches.value)
             achieved = work / (kavg * 1e-3) / 1e12
             roof = {"bound": "tensor", "achieved": achieved, "peak": int8_tops, "unit": "TOPS",
-                    "frac": achieved / int8_tops, "traffic": None,
+                    "frac": achieved / int8_tops, "traffic": traffic, "traffic_unit": "bytes per launch",
                     "kernel": f"{st} (int8 GEMM, {launches.value} launches, {kavg:.4f} ms avg)",
                     "peak_source": int8_src, "work": "2*rows*K*N int8 ops per launch"}
         else:
             work = STAGE_BYTES_PER_ROW.get(st, 384) * krows.value / max(1, launches.value)
             achieved = work / (kavg * 1e-3) / 1e9
             roof = {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
-                    "traffic": None, "kernel": f"{st} ({launches.value} launches, {kavg:.4f} ms avg)",
+                    "traffic": traffic, "traffic_unit": "bytes per launch", "kernel": f"{st} ({launches.value} launches, {kavg:.4f} ms avg)",
                     "peak_source": "MEASURED_PEAKS.json hbm_gbs (of measured)"}
         line = {
             "metric": METRIC, "value": value, "unit": "images/s", "n_gpus": world, "steps": args.steps,
