@@ -7,22 +7,22 @@
 //   ctx   = requant(prob(uint8)·V, prob_scale + q, context_out, 8)
 // written straight into the head-concatenated layout (layout.py:132-155).
 //
-// One CTA (8 warps) per (image, head), query rows in tiles of 128:
+// One CTA (16 warps) per (image, head), query rows in tiles of 128:
 //   1. K, V and each Q tile are staged in shared memory with 16-byte copies in
 //      the no-swizzle canonical layout (hv_tc05.cuh).  K and Q are K-major
 //      operands; V is the same byte layout read as an MN-major B operand
 //      (tokens along K, head dims along N), so no transpose is needed.
 //   2. One thread issues S = Q·Kᵀ as tcgen05.mma kind::i8 (M=128, N=np, K=64)
 //      into TMEM columns [0, np); completion arrives on an mbarrier.
-//   3. Query row r of the tile is TMEM lane r.  Warps w and w+4 own lanes
-//      32*(w%4)..+31 and split the row's 32-column chunks (even / odd); each
-//      reads its chunks with tcgen05.ld, and the two halves combine the row max
-//      and the exp sum through shared memory.  Exp terms are written back to
+//   3. Query row r of the tile is TMEM lane r.  Warps w, w+4, w+8, w+12 own
+//      lanes 32*(w%4)..+31 and split the row's 16-column chunks round-robin;
+//      each reads its chunks with tcgen05.ld, and the four parts combine the
+//      row max and the exp sum through shared memory.  Exp terms are written back to
 //      TMEM, then turned into UQ0.8 probabilities stored to shared memory as
 //      the A operand of the next MMA.  Warps whose 32 rows all lie past the
 //      image's token count skip the softmax.
 //   4. ctx = P·V as tcgen05.mma kind::i8 with unsigned A (M=128, N=64, K=np)
-//      into TMEM columns [0, 64), then requantised (half h: columns 32h..32h+31)
+//      into TMEM columns [0, 64), then requantised (part p: columns 16p..16p+15)
 //      and written out.
 // TMEM: 256 columns per CTA; shared memory is padded so two CTAs share an SM.
 #include "hv_internal.cuh"
@@ -32,7 +32,8 @@ namespace hv {
 
 namespace {
 
-constexpr int THREADS = 256;
+constexpr int SPLIT = 4;                  // warps per TMEM lane quadrant (column parts)
+constexpr int THREADS = 128 * SPLIT;
 constexpr int NPMAX = 224;        // 197 rounded up to 32
 constexpr uint32_t TMEM_COLS = 256;
 constexpr uint32_t WAIT_ITERS = 1u << 24;
@@ -41,8 +42,8 @@ constexpr int OFF_K = 0;                      // [NPMAX][64] K-major
 constexpr int OFF_V = OFF_K + NPMAX * 64;     // [NPMAX][64], read MN-major
 constexpr int OFF_Q = OFF_V + NPMAX * 64;     // [128][64]
 constexpr int OFF_P = OFF_Q + 128 * 64;       // [128][NPMAX] uint8
-constexpr int OFF_RED = OFF_P + 128 * NPMAX;  // [2][2][128] int32 row partials (max, sum) of each half
-constexpr int OFF_BAR = OFF_RED + 4 * 128 * 4;  // mbarrier, TMEM base, abort flag
+constexpr int OFF_RED = OFF_P + 128 * NPMAX;  // [2][SPLIT][128] int32 row partials (max, sum) of each part
+constexpr int OFF_BAR = OFF_RED + 2 * SPLIT * 128 * 4;  // mbarrier, TMEM base, abort flag
 constexpr int SMEM_BYTES = 80 * 1024;         // > 227 KB / 3: at most two CTAs per SM
 static_assert(OFF_BAR + 64 <= SMEM_BYTES, "attention shared memory layout");
 
@@ -56,12 +57,12 @@ __device__ __forceinline__ int32_t q16_of(int32_t acc, const AttnParams &p) {
     return (int32_t)requant64(score, p.q16_shift, 24);
 }
 
-// exp terms of one 32-column chunk (columns >= valid are masked to 0); returns their sum.
+// exp terms of one 16-column chunk (columns >= valid are masked to 0); returns their sum.
 template <bool FAST, bool MASK>
-__device__ __forceinline__ uint32_t chunk_exp(uint32_t (&v)[32], int valid, int32_t mx, const AttnParams &p) {
+__device__ __forceinline__ uint32_t chunk_exp(uint32_t (&v)[16], int valid, int32_t mx, const AttnParams &p) {
     uint32_t sum = 0;
 #pragma unroll
-    for (int j = 0; j < 32; ++j) {
+    for (int j = 0; j < 16; ++j) {
         uint32_t e = softmax_exp_q16(q16_of<FAST>((int32_t)v[j], p) - mx);
         if (MASK && j >= valid) e = 0u;
         v[j] = e;
@@ -91,7 +92,7 @@ __global__ void __launch_bounds__(THREADS) attention_tc_kernel(const int8_t *__r
     if (n <= 0) return;
     const int np = (n + 31) & ~31;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int quad = warp & 3, half = warp >> 2;
+    const int quad = warp & 3, part = warp >> 2;
     const int lrow = quad * 32 + lane;  // tile row = TMEM lane
 
     if (warp == 0) {
@@ -116,7 +117,7 @@ __global__ void __launch_bounds__(THREADS) attention_tc_kernel(const int8_t *__r
     const uint32_t tbase = *tmem_slot;
     const uint32_t lane_addr = tbase + ((uint32_t)(quad * 32) << 16);
     const uint32_t sbo_np = (uint32_t)(np / 16) * 128;
-    const int nchunks = np >> 5;
+    const int nchunks = np >> 4;  // 16-column chunks
     uint32_t phase = 0;
 
     for (int t = 0; t * 128 < n; ++t) {
@@ -145,57 +146,62 @@ __global__ void __launch_bounds__(THREADS) attention_tc_kernel(const int8_t *__r
         if (*abort_flag) break;
         tc05::fence_after();
 
-        // ---- softmax straight from TMEM: this warp's rows, chunks c = half, half + 2, ...
+        // ---- softmax straight from TMEM: this warp's rows, 16-column chunks c = part + SPLIT*i
         // q16 is monotone in the accumulator, so the row max is taken on raw
         // accumulators and converted once.
         const bool live = t * 128 + quad * 32 < n;  // warp-uniform
-        const int nfull = n & ~31;
+        const int nfull = n & ~15;
         if (live) {
             int32_t mxa = INT32_MIN;
-            for (int c = half; c < nchunks; c += 2) {
-                const int c0 = c * 32;
-                uint32_t v[32];
-                tc05::ld32(lane_addr + c0, v);
+            for (int c = part; c < nchunks; c += SPLIT) {
+                const int c0 = c * 16;
+                uint32_t v[16];
+                tc05::ld16(lane_addr + c0, v);
                 tc05::wait_ld();
                 if (c0 < nfull) {
 #pragma unroll
-                    for (int j = 0; j < 32; ++j) mxa = max(mxa, (int32_t)v[j]);
+                    for (int j = 0; j < 16; ++j) mxa = max(mxa, (int32_t)v[j]);
                 } else {
 #pragma unroll
-                    for (int j = 0; j < 32; ++j)
+                    for (int j = 0; j < 16; ++j)
                         if (c0 + j < n) mxa = max(mxa, (int32_t)v[j]);
                 }
             }
-            sred[half * 128 + lrow] = mxa;
+            sred[part * 128 + lrow] = mxa;
         }
         __syncthreads();
         if (live) {
-            const int32_t mx = q16_of<FAST>(max(sred[lrow], sred[128 + lrow]), p);
+            int32_t mraw = sred[lrow];
+#pragma unroll
+            for (int q = 1; q < SPLIT; ++q) mraw = max(mraw, sred[q * 128 + lrow]);
+            const int32_t mx = q16_of<FAST>(mraw, p);
             uint32_t sum = 0;
-            for (int c = half; c < nchunks; c += 2) {
-                const int c0 = c * 32;
-                uint32_t v[32];
-                tc05::ld32(lane_addr + c0, v);
+            for (int c = part; c < nchunks; c += SPLIT) {
+                const int c0 = c * 16;
+                uint32_t v[16];
+                tc05::ld16(lane_addr + c0, v);
                 tc05::wait_ld();
-                if (c0 < nfull) sum += chunk_exp<FAST, false>(v, 32, mx, p);
+                if (c0 < nfull) sum += chunk_exp<FAST, false>(v, 16, mx, p);
                 else sum += chunk_exp<FAST, true>(v, n - c0, mx, p);
-                tc05::st32(lane_addr + c0, v);
+                tc05::st16(lane_addr + c0, v);
             }
             tc05::wait_st();
-            sred[256 + half * 128 + lrow] = (int32_t)sum;
+            sred[(SPLIT + part) * 128 + lrow] = (int32_t)sum;
         }
         __syncthreads();
         if (live) {
-            const uint32_t tot = (uint32_t)sred[256 + lrow] + (uint32_t)sred[384 + lrow];
-            const uint64_t rc = softmax_recip(tot ? tot : 1u);
-            for (int c = half; c < nchunks; c += 2) {
-                const int c0 = c * 32;
-                uint32_t v[32];
-                tc05::ld32(lane_addr + c0, v);
-                tc05::wait_ld();
-                uint32_t pk[8];
+            uint32_t tot = 0;
 #pragma unroll
-                for (int w = 0; w < 8; ++w) {
+            for (int q = 0; q < SPLIT; ++q) tot += (uint32_t)sred[(SPLIT + q) * 128 + lrow];
+            const uint64_t rc = softmax_recip(tot ? tot : 1u);
+            for (int c = part; c < nchunks; c += SPLIT) {
+                const int c0 = c * 16;
+                uint32_t v[16];
+                tc05::ld16(lane_addr + c0, v);
+                tc05::wait_ld();
+                uint32_t pk[4];
+#pragma unroll
+                for (int w = 0; w < 4; ++w) {
                     uint32_t word = 0;
 #pragma unroll
                     for (int b = 0; b < 4; ++b) {
@@ -207,7 +213,6 @@ __global__ void __launch_bounds__(THREADS) attention_tc_kernel(const int8_t *__r
                     pk[w] = word;
                 }
                 *(uint4 *)(sP + tc05::kmajor_offset(lrow, c0, np)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-                *(uint4 *)(sP + tc05::kmajor_offset(lrow, c0 + 16, np)) = make_uint4(pk[4], pk[5], pk[6], pk[7]);
             }
         }
 
@@ -230,26 +235,22 @@ __global__ void __launch_bounds__(THREADS) attention_tc_kernel(const int8_t *__r
         tc05::fence_after();
         const int r = t * 128 + lrow;
         if (live) {
-            uint32_t o[32];
-            tc05::ld32(lane_addr + half * 32, o);
+            uint32_t o[16];
+            tc05::ld16(lane_addr + part * 16, o);
             tc05::wait_ld();
-            uint32_t pk[8];
+            uint32_t pk[4];
 #pragma unroll
-            for (int w = 0; w < 8; ++w) {
-                uint32_t word = 0;
+            for (int w = 0; w < 4; ++w) {
+                int32_t q[4];
 #pragma unroll
                 for (int b = 0; b < 4; ++b) {
                     const int32_t a = (int32_t)o[w * 4 + b];
-                    const int32_t v = p.ctx_fast ? requant8_r(a, p.ctx_shift) : (int32_t)requant64(a, p.ctx_shift, 8);
-                    word |= ((uint32_t)v & 0xffu) << (8 * b);
+                    q[b] = p.ctx_fast ? rsa32(a, p.ctx_shift) : (int32_t)requant64(a, p.ctx_shift, 8);
                 }
-                pk[w] = word;
+                pk[w] = pack_sat8(q[0], q[1], q[2], q[3]);
             }
-            if (r < n) {
-                uint4 *dst = (uint4 *)(ctx + (size_t)(row0 + r) * 192 + head * 64 + half * 32);
-                dst[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-                dst[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
-            }
+            if (r < n)
+                *(uint4 *)(ctx + (size_t)(row0 + r) * 192 + head * 64 + part * 16) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
         }
         tc05::fence_before();
         __syncthreads();
