@@ -22,7 +22,7 @@
 //      the A operand of the next MMA.  Warps whose 32 rows all lie past the
 //      image's token count skip the softmax.
 //   4. ctx = P·V as tcgen05.mma kind::i8 with unsigned A (M=128, N=64, K=np)
-//      into TMEM columns [0, 64), then requantised (part p: columns 16p..16p+15)
+//      into TMEM columns [0, 64), then requantised in 16-column pieces per part
 //      and written out.
 // TMEM: 256 columns per CTA; shared memory is padded so two CTAs share an SM.
 #include "hv_internal.cuh"
@@ -32,20 +32,29 @@ namespace hv {
 
 namespace {
 
-constexpr int SPLIT = 4;                  // warps per TMEM lane quadrant (column parts)
-constexpr int THREADS = 128 * SPLIT;
-constexpr int NPMAX = 224;        // 197 rounded up to 32
-constexpr uint32_t TMEM_COLS = 256;
 constexpr uint32_t WAIT_ITERS = 1u << 24;
 
-constexpr int OFF_K = 0;                      // [NPMAX][64] K-major
-constexpr int OFF_V = OFF_K + NPMAX * 64;     // [NPMAX][64], read MN-major
-constexpr int OFF_Q = OFF_V + NPMAX * 64;     // [128][64]
-constexpr int OFF_P = OFF_Q + 128 * 64;       // [128][NPMAX] uint8
-constexpr int OFF_RED = OFF_P + 128 * NPMAX;  // [2][SPLIT][128] int32 row partials (max, sum) of each part
-constexpr int OFF_BAR = OFF_RED + 2 * SPLIT * 128 * 4;  // mbarrier, TMEM base, abort flag
-constexpr int SMEM_BYTES = 80 * 1024;         // > 227 KB / 3: at most two CTAs per SM
-static_assert(OFF_BAR + 64 <= SMEM_BYTES, "attention shared memory layout");
+// Two CTA shapes.  Images of up to 128 tokens use the small one (128 TMEM
+// columns, 8 warps, about 46 KB of shared memory: four CTAs per SM); longer
+// images use the large one (256 TMEM columns, 16 warps, 80 KB: two per SM).
+// Shared memory is padded so that TMEM is never oversubscribed.
+template <int NPM, int SPL>
+struct AttnCfg {
+    static constexpr int NPMAX = NPM;                 // longest image rounded up to 32
+    static constexpr int SPLIT = SPL;                 // warps per TMEM lane quadrant (column parts)
+    static constexpr int THREADS = 128 * SPL;
+    static constexpr uint32_t TMEM_COLS = NPM <= 128 ? 128 : 256;
+    static constexpr int OFF_K = 0;                            // [NPMAX][64] K-major
+    static constexpr int OFF_V = OFF_K + NPM * 64;             // [NPMAX][64], read MN-major
+    static constexpr int OFF_Q = OFF_V + NPM * 64;             // [128][64]
+    static constexpr int OFF_P = OFF_Q + 128 * 64;             // [128][NPMAX] uint8
+    static constexpr int OFF_RED = OFF_P + 128 * NPM;          // [2][SPLIT][128] int32 row partials
+    static constexpr int OFF_BAR = OFF_RED + 2 * SPL * 128 * 4;  // mbarrier, TMEM base, abort flag
+    static constexpr int SMEM = NPM <= 128 ? 46 * 1024 : 80 * 1024;  // > 228 KB / 5, resp. / 3
+    static_assert(OFF_BAR + 64 <= SMEM, "attention shared memory layout");
+};
+using AttnSmall = AttnCfg<128, 2>;
+using AttnLarge = AttnCfg<224, 4>;
 
 // q16 of one score accumulator.  FAST: host-proven that the int32 score
 // writeback and the sat24 cannot clip, so q16 = rsa(acc, fast_shift), written
@@ -71,32 +80,33 @@ __device__ __forceinline__ uint32_t chunk_exp(uint32_t (&v)[16], int valid, int3
     return sum;
 }
 
-template <bool FAST>
-__global__ void __launch_bounds__(THREADS) attention_tc_kernel(const int8_t *__restrict__ qkv,
+template <bool FAST, class CFG>
+__global__ void __launch_bounds__(CFG::THREADS) attention_tc_kernel(const int8_t *__restrict__ qkv,
                                                                const int32_t *__restrict__ offsets,
                                                                int8_t *__restrict__ ctx, AttnParams p,
-                                                               int *__restrict__ err) {
+                                                               int *__restrict__ err, int np_lo, int np_hi) {
     extern __shared__ __align__(1024) uint8_t smem[];
-    uint8_t *sK = smem + OFF_K;
-    uint8_t *sV = smem + OFF_V;
-    uint8_t *sQ = smem + OFF_Q;
-    uint8_t *sP = smem + OFF_P;
-    int32_t *sred = (int32_t *)(smem + OFF_RED);
-    uint64_t *bar = (uint64_t *)(smem + OFF_BAR);
-    uint32_t *tmem_slot = (uint32_t *)(smem + OFF_BAR + 8);
-    volatile int *abort_flag = (volatile int *)(smem + OFF_BAR + 12);
+    uint8_t *sK = smem + CFG::OFF_K;
+    uint8_t *sV = smem + CFG::OFF_V;
+    uint8_t *sQ = smem + CFG::OFF_Q;
+    uint8_t *sP = smem + CFG::OFF_P;
+    int32_t *sred = (int32_t *)(smem + CFG::OFF_RED);
+    uint64_t *bar = (uint64_t *)(smem + CFG::OFF_BAR);
+    uint32_t *tmem_slot = (uint32_t *)(smem + CFG::OFF_BAR + 8);
+    volatile int *abort_flag = (volatile int *)(smem + CFG::OFF_BAR + 12);
 
     const int img = blockIdx.x, head = blockIdx.y;
     const int row0 = offsets[img];
     const int n = offsets[img + 1] - row0;
     if (n <= 0) return;
     const int np = (n + 31) & ~31;
+    if (np <= np_lo || np > np_hi) return;  // the other CTA shape takes this image
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int quad = warp & 3, part = warp >> 2;
     const int lrow = quad * 32 + lane;  // tile row = TMEM lane
 
     if (warp == 0) {
-        tc05::tmem_alloc(tmem_slot, TMEM_COLS);
+        tc05::tmem_alloc(tmem_slot, CFG::TMEM_COLS);
         tc05::tmem_relinquish();
     }
     if (tid == 0) {
@@ -105,7 +115,7 @@ __global__ void __launch_bounds__(THREADS) attention_tc_kernel(const int8_t *__r
         tc05::fence_mbar_init();
     }
     // K and V rows (zero beyond n up to np), both in the K-major byte layout.
-    for (int c = tid; c < np * 8; c += THREADS) {
+    for (int c = tid; c < np * 8; c += CFG::THREADS) {
         const int r = c >> 3, ch = c & 3, isv = (c >> 2) & 1;
         int4 kv = make_int4(0, 0, 0, 0);
         if (r < n) kv = *(const int4 *)(qkv + (size_t)(row0 + r) * 576 + 192 * (1 + isv) + head * 64 + ch * 16);
@@ -122,7 +132,7 @@ __global__ void __launch_bounds__(THREADS) attention_tc_kernel(const int8_t *__r
 
     for (int t = 0; t * 128 < n; ++t) {
         // ---- Q tile ------------------------------------------------------------
-        for (int c = tid; c < 128 * 4; c += THREADS) {
+        for (int c = tid; c < 128 * 4; c += CFG::THREADS) {
             const int r = c >> 2, ch = c & 3, gr = t * 128 + r;
             int4 qv = make_int4(0, 0, 0, 0);
             if (gr < n) qv = *(const int4 *)(qkv + (size_t)(row0 + gr) * 576 + head * 64 + ch * 16);
@@ -146,14 +156,14 @@ __global__ void __launch_bounds__(THREADS) attention_tc_kernel(const int8_t *__r
         if (*abort_flag) break;
         tc05::fence_after();
 
-        // ---- softmax straight from TMEM: this warp's rows, 16-column chunks c = part + SPLIT*i
+        // ---- softmax straight from TMEM: this warp's rows, 16-column chunks c = part + CFG::SPLIT*i
         // q16 is monotone in the accumulator, so the row max is taken on raw
         // accumulators and converted once.
         const bool live = t * 128 + quad * 32 < n;  // warp-uniform
         const int nfull = n & ~15;
         if (live) {
             int32_t mxa = INT32_MIN;
-            for (int c = part; c < nchunks; c += SPLIT) {
+            for (int c = part; c < nchunks; c += CFG::SPLIT) {
                 const int c0 = c * 16;
                 uint32_t v[16];
                 tc05::ld16(lane_addr + c0, v);
@@ -173,10 +183,10 @@ __global__ void __launch_bounds__(THREADS) attention_tc_kernel(const int8_t *__r
         if (live) {
             int32_t mraw = sred[lrow];
 #pragma unroll
-            for (int q = 1; q < SPLIT; ++q) mraw = max(mraw, sred[q * 128 + lrow]);
+            for (int q = 1; q < CFG::SPLIT; ++q) mraw = max(mraw, sred[q * 128 + lrow]);
             const int32_t mx = q16_of<FAST>(mraw, p);
             uint32_t sum = 0;
-            for (int c = part; c < nchunks; c += SPLIT) {
+            for (int c = part; c < nchunks; c += CFG::SPLIT) {
                 const int c0 = c * 16;
                 uint32_t v[16];
                 tc05::ld16(lane_addr + c0, v);
@@ -186,15 +196,15 @@ __global__ void __launch_bounds__(THREADS) attention_tc_kernel(const int8_t *__r
                 tc05::st16(lane_addr + c0, v);
             }
             tc05::wait_st();
-            sred[(SPLIT + part) * 128 + lrow] = (int32_t)sum;
+            sred[(CFG::SPLIT + part) * 128 + lrow] = (int32_t)sum;
         }
         __syncthreads();
         if (live) {
             uint32_t tot = 0;
 #pragma unroll
-            for (int q = 0; q < SPLIT; ++q) tot += (uint32_t)sred[(SPLIT + q) * 128 + lrow];
+            for (int q = 0; q < CFG::SPLIT; ++q) tot += (uint32_t)sred[(CFG::SPLIT + q) * 128 + lrow];
             const uint64_t rc = softmax_recip(tot ? tot : 1u);
-            for (int c = part; c < nchunks; c += SPLIT) {
+            for (int c = part; c < nchunks; c += CFG::SPLIT) {
                 const int c0 = c * 16;
                 uint32_t v[16];
                 tc05::ld16(lane_addr + c0, v);
@@ -235,22 +245,25 @@ __global__ void __launch_bounds__(THREADS) attention_tc_kernel(const int8_t *__r
         tc05::fence_after();
         const int r = t * 128 + lrow;
         if (live) {
-            uint32_t o[16];
-            tc05::ld16(lane_addr + part * 16, o);
-            tc05::wait_ld();
-            uint32_t pk[4];
+            for (int pc = part; pc < 4; pc += CFG::SPLIT) {  // 16-column pieces of the 64 head dims
+                uint32_t o[16];
+                tc05::ld16(lane_addr + pc * 16, o);
+                tc05::wait_ld();
+                uint32_t pk[4];
 #pragma unroll
-            for (int w = 0; w < 4; ++w) {
-                int32_t q[4];
+                for (int w = 0; w < 4; ++w) {
+                    int32_t q[4];
 #pragma unroll
-                for (int b = 0; b < 4; ++b) {
-                    const int32_t a = (int32_t)o[w * 4 + b];
-                    q[b] = p.ctx_fast ? rsa32(a, p.ctx_shift) : (int32_t)requant64(a, p.ctx_shift, 8);
+                    for (int b = 0; b < 4; ++b) {
+                        const int32_t a = (int32_t)o[w * 4 + b];
+                        q[b] = p.ctx_fast ? rsa32(a, p.ctx_shift) : (int32_t)requant64(a, p.ctx_shift, 8);
+                    }
+                    pk[w] = pack_sat8(q[0], q[1], q[2], q[3]);
                 }
-                pk[w] = pack_sat8(q[0], q[1], q[2], q[3]);
+                if (r < n)
+                    *(uint4 *)(ctx + (size_t)(row0 + r) * 192 + head * 64 + pc * 16) =
+                        make_uint4(pk[0], pk[1], pk[2], pk[3]);
             }
-            if (r < n)
-                *(uint4 *)(ctx + (size_t)(row0 + r) * 192 + head * 64 + part * 16) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
         }
         tc05::fence_before();
         __syncthreads();
@@ -264,7 +277,7 @@ __global__ void __launch_bounds__(THREADS) attention_tc_kernel(const int8_t *__r
     __syncthreads();
     if (warp == 0) {
         tc05::fence_after();
-        tc05::tmem_dealloc(tbase, TMEM_COLS);
+        tc05::tmem_dealloc(tbase, CFG::TMEM_COLS);
     }
 }
 
@@ -285,12 +298,22 @@ AttnParams make_attn(int qkv_out_scale, int score_scale, int prob_scale, int con
 }
 
 cudaError_t launch_attention(const int8_t *qkv, const int32_t *offsets, int images, int8_t *ctx,
-                             const AttnParams &p, int *err, cudaStream_t st) {
+                             const AttnParams &p, int may_be_short, int *err, cudaStream_t st) {
     if (images <= 0) return cudaSuccess;
-    auto kern = p.fast ? attention_tc_kernel<true> : attention_tc_kernel<false>;
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    // Images of up to 128 tokens (np <= 128) go to the small shape when any may exist.
+    if (may_be_short) {
+        auto ks = p.fast ? attention_tc_kernel<true, AttnSmall> : attention_tc_kernel<false, AttnSmall>;
+        cudaError_t e = cudaFuncSetAttribute(ks, cudaFuncAttributeMaxDynamicSharedMemorySize, AttnSmall::SMEM);
+        if (e != cudaSuccess) return e;
+        ks<<<dim3(images, 3), AttnSmall::THREADS, AttnSmall::SMEM, st>>>(qkv, offsets, ctx, p, err, 0, 128);
+        e = cudaGetLastError();
+        if (e != cudaSuccess) return e;
+    }
+    auto kl = p.fast ? attention_tc_kernel<true, AttnLarge> : attention_tc_kernel<false, AttnLarge>;
+    cudaError_t e = cudaFuncSetAttribute(kl, cudaFuncAttributeMaxDynamicSharedMemorySize, AttnLarge::SMEM);
     if (e != cudaSuccess) return e;
-    kern<<<dim3(images, 3), THREADS, SMEM_BYTES, st>>>(qkv, offsets, ctx, p, err);
+    kl<<<dim3(images, 3), AttnLarge::THREADS, AttnLarge::SMEM, st>>>(qkv, offsets, ctx, p, err,
+                                                                     may_be_short ? 128 : 0, AttnLarge::NPMAX);
     return cudaGetLastError();
 }
 

@@ -47,8 +47,10 @@ struct AttnParams {
 };
 AttnParams make_attn(int qkv_out_scale, int score_scale, int prob_scale, int context_out_scale);
 // err: device word set to a non-zero code when a bounded wait gave up.
+// may_be_short: some image may hold at most 128 tokens (any selector has run, or
+// the caller's ragged batch is arbitrary); those go to a smaller CTA shape.
 cudaError_t launch_attention(const int8_t *qkv, const int32_t *offsets, int images, int8_t *ctx,
-                             const AttnParams &p, int *err, cudaStream_t st);
+                             const AttnParams &p, int may_be_short, int *err, cudaStream_t st);
 
 // Device-resident selector weights and constants.
 struct SelParams {

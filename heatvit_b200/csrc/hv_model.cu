@@ -290,7 +290,9 @@ struct Prof {
 };
 
 // One transformer block over the ragged batch in m->X (in place).
-int run_block(hv_model *m, int b, int images, const int32_t *off, cudaStream_t st) {
+// may_be_short: some image may hold fewer than 197 tokens (after a selector, or a
+// caller-supplied ragged batch).
+int run_block(hv_model *m, int b, int images, const int32_t *off, int may_be_short, cudaStream_t st) {
     const BlockDev &d = m->blocks[b];
     const int rows_max = images * HV_TOKENS;
     const int32_t *rows_dev = off + images;
@@ -312,7 +314,7 @@ int run_block(hv_model *m, int b, int images, const int32_t *off, cudaStream_t s
     }
     {
         Prof pr(m, HV_STAGE_ATTN, st);
-        CUDA_TRY(launch_attention(m->QKV, off, images, m->CTX, d.attn, m->err, st));
+        CUDA_TRY(launch_attention(m->QKV, off, images, m->CTX, d.attn, may_be_short, m->err, st));
         pr.end(st, rows_dev, 0);
     }
     {
@@ -417,7 +419,7 @@ int infer_impl(hv_model *m, const int8_t *d_images, int batch, int32_t *d_logits
                 CUDA_TRY(cudaGetLastError());
             }
         }
-        rc = run_block(m, b, batch, m->off[cur], st);
+        rc = run_block(m, b, batch, m->off[cur], sel_no > 0, st);
         if (rc) return rc;
         if (d_ckpt) {
             ckpt_copy_kernel<<<batch, 256, 0, st>>>(m->X, m->off[cur], d_ckpt, d_ckpt_rows, HV_CKPT_BLOCK(b + 1));
@@ -999,7 +1001,7 @@ int hv_transformer_block(hv_model *m, int block_index, const int8_t *d_x, const 
     cudaStream_t st = (cudaStream_t)stream;
     CUDA_TRY(cudaMemcpyAsync(m->X, d_x, (size_t)total_rows * 192, cudaMemcpyDeviceToDevice, st));
     CUDA_TRY(cudaMemsetAsync(m->warn, 0, ((size_t)images + 3) & ~(size_t)3, st));
-    rc = run_block(m, block_index, images, d_offsets, st);
+    rc = run_block(m, block_index, images, d_offsets, 1, st);
     if (rc) return rc;
     CUDA_TRY(cudaMemcpyAsync(d_z, m->X, (size_t)total_rows * 192, cudaMemcpyDeviceToDevice, st));
     return HV_OK;
