@@ -75,6 +75,9 @@ struct SelParams {
     int hw_q16_shift;                 // head-weight acc -> Q16 (24 bit)
     // 1 when gelu_chain_fast's ranges hold for that layer (host-checked)
     int local_fast, h1_fast, h2_fast, hw_fast;
+    // 1 when gelu_chain_fast2's ranges hold (host-checked), and its constants
+    int local_k2, h1_k2, h2_k2, hw_k2;
+    GeluK local_k, h1_k, h2_k, hw_k;
 };
 
 // Optional selector intermediates (token_selector API), image stride 196.

@@ -594,6 +594,17 @@ int pack_model(hv_model *m, const hv_params *P) {
         p.h1_fast = fast(p.h1_sh_in, p.h1_sh_out, max_abs(q.score_b1, 96) + 64 * 16384);
         p.h2_fast = fast(p.h2_sh_in, p.h2_sh_out, max_abs(q.score_b2, 48) + 32 * 16384);
         p.hw_fast = fast(p.hw_sh_in, p.hw_sh_out, max_abs(q.hw_b1, 3) + 3 * 16384);
+        // FMA-pipe GELU chain: |acc + bias| must stay inside its input range
+        auto k2 = [](int sh_in, int sh_out, int64_t bound, int wide_ok, GeluK *k) {
+            int32_t vlim = 0;
+            const int ok = (wide_ok && gelu_fast2_range(sh_in, sh_out, &vlim) && bound <= vlim) ? 1 : 0;
+            *k = make_gelu_k(ok ? sh_in : 0, ok ? sh_out : 0);
+            return ok;
+        };
+        p.local_k2 = k2(p.local_sh_in, p.local_sh_out, max_abs(q.local_b, 96) + 64 * 16384, 1, &p.local_k);
+        p.h1_k2 = k2(p.h1_sh_in, p.h1_sh_out, max_abs(q.score_b1, 96) + 64 * 16384, 1, &p.h1_k);
+        p.h2_k2 = k2(p.h2_sh_in, p.h2_sh_out, max_abs(q.score_b2, 48) + 32 * 16384, 1, &p.h2_k);
+        p.hw_k2 = k2(p.hw_sh_in, p.hw_sh_out, max_abs(q.hw_b1, 3) + 3 * 16384, 1, &p.hw_k);
     }
     if (m->has_head) {
     if (!P->final_gamma || !P->final_beta || !P->head_b) return fail(HV_ERR_VALUE, "head parameters missing");

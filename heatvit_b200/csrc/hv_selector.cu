@@ -19,7 +19,7 @@ namespace hv {
 
 namespace {
 
-constexpr int THREADS = 256;
+constexpr int THREADS = 512;
 constexpr int MAXC = 196;
 constexpr int LSTR = 36;   // local row stride (32 data bytes + 4 pad)
 constexpr int WSTR = 68;   // transposed 64-wide weight row stride
@@ -54,10 +54,22 @@ constexpr int SZ_FLAGS = MAXC;  // bit0 keep, bit1 participant
 constexpr int OFF_STATS = (OFF_FLAGS + SZ_FLAGS + 15) & ~15;
 constexpr int SZ_STATS = MAXC * 3;
 constexpr int OFF_MISC = (OFF_STATS + SZ_STATS + 15) & ~15;
-constexpr int SZ_MISC = 64;
-constexpr int SMEM_BYTES = OFF_MISC + SZ_MISC;
+constexpr int SZ_MISC = 128;  // [0] warn, [1] kept, [2] participants, [4..4+THREADS/32) scan
+constexpr int OFF_H1 = OFF_MISC + SZ_MISC;  // score layer-1 outputs [3][MAXC][LSTR]
+constexpr int SZ_H1 = 3 * MAXC * LSTR;
+constexpr int OFF_H2 = OFF_H1 + SZ_H1;      // score layer-2 outputs [3][MAXC][16]
+constexpr int SZ_H2 = 3 * MAXC * 16;
+constexpr int SMEM_BYTES = OFF_H2 + SZ_H2;
+static_assert(2 * (SMEM_BYTES + 1024) <= 228 * 1024, "two selector CTAs per SM");
 
 __device__ __forceinline__ int32_t sat_q016(int64_t v) { return (int32_t)(v < 0 ? 0 : (v > 65536 ? 65536 : v)); }
+
+// One selector GELU chain (selector.py:89-99) in the fastest form the host proved exact.
+__device__ __forceinline__ int32_t sel_gelu(int64_t v, int k2, const GeluK &k, int fast, int sh_in, int sh_out) {
+    if (k2) return sat8(gelu_chain_fast2((int32_t)v, k));
+    if (fast) return gelu_chain_fast((int32_t)v, sh_in, sh_out);
+    return gelu_chain(v, sh_in, sh_out);
+}
 
 // Keep score of one candidate-head: softmax_selector([q0, q1])[1]
 // (selector.py:345-354, nonlinear.py:109-127).
@@ -131,9 +143,8 @@ __global__ void __launch_bounds__(THREADS) selector_kernel(
         int32_t acc = 0;
 #pragma unroll
         for (int w = 0; w < 16; ++w) acc = __dp4a(trow[w], wrow[w], acc);
-        local[(h * MAXC + c) * LSTR + j] =
-            (int8_t)(p.local_fast ? gelu_chain_fast(acc + p.local_b[h * 32 + j], p.local_sh_in, p.local_sh_out)
-                                  : gelu_chain((int64_t)acc + p.local_b[h * 32 + j], p.local_sh_in, p.local_sh_out));
+        local[(h * MAXC + c) * LSTR + j] = (int8_t)sel_gelu((int64_t)acc + p.local_b[h * 32 + j], p.local_k2,
+                                                            p.local_k, p.local_fast, p.local_sh_in, p.local_sh_out);
     }
     __syncthreads();
 
@@ -154,55 +165,43 @@ __global__ void __launch_bounds__(THREADS) selector_kernel(
     }
     __syncthreads();
 
-    // ---- score MLP per (head, candidate) ------------------------------------------
+    // ---- score MLP (selector.py:307-355), one thread per (head, candidate, output) ---
+    int8_t *h1s = (int8_t *)(smem + OFF_H1);
+    int8_t *h2s = (int8_t *)(smem + OFF_H2);
+    for (int idx = tid; idx < 3 * C * 32; idx += THREADS) {
+        const int j = idx & 31, hc = idx >> 5;
+        const int h = hc / C, c = hc - h * C;
+        const int32_t *lrow = (const int32_t *)(local + (h * MAXC + c) * LSTR);
+        const int32_t *wrow = (const int32_t *)(w1t + (h * 32 + j) * WSTR);
+        int32_t acc = 0;
+#pragma unroll
+        for (int w = 0; w < 8; ++w) acc = __dp4a(lrow[w], wrow[w], acc);
+        h1s[(h * MAXC + c) * LSTR + j] =
+            (int8_t)sel_gelu(acc + g1[h * 32 + j], p.h1_k2, p.h1_k, p.h1_fast, p.h1_sh_in, p.h1_sh_out);
+    }
+    __syncthreads();
+    for (int idx = tid; idx < 3 * C * 16; idx += THREADS) {
+        const int m = idx & 15, hc = idx >> 4;
+        const int h = hc / C, c = hc - h * C;
+        const int32_t *hrow = (const int32_t *)(h1s + (h * MAXC + c) * LSTR);
+        const int32_t *wrow = (const int32_t *)(w2t + (h * 16 + m) * W2STR);
+        int32_t acc = 0;
+#pragma unroll
+        for (int w = 0; w < 8; ++w) acc = __dp4a(hrow[w], wrow[w], acc);
+        h2s[(h * MAXC + c) * 16 + m] =
+            (int8_t)sel_gelu((int64_t)acc + p.b2[h * 16 + m], p.h2_k2, p.h2_k, p.h2_fast, p.h2_sh_in, p.h2_sh_out);
+    }
+    __syncthreads();
     for (int it = tid; it < 3 * C; it += THREADS) {
         const int h = it / C, c = it - h * C;
-        int32_t lw[8];
-#pragma unroll
-        for (int w = 0; w < 8; ++w) lw[w] = *(const int32_t *)(local + (h * MAXC + c) * LSTR + 4 * w);
-        uint32_t h1w[8];
-#pragma unroll
-        for (int jw = 0; jw < 8; ++jw) {
-            uint32_t packed = 0;
-#pragma unroll
-            for (int b = 0; b < 4; ++b) {
-                const int j = jw * 4 + b;
-                const int32_t *wrow = (const int32_t *)(w1t + (h * 32 + j) * WSTR);
-                int32_t acc = 0;
-#pragma unroll
-                for (int w = 0; w < 8; ++w) acc = __dp4a(lw[w], wrow[w], acc);
-                const int64_t x = acc + g1[h * 32 + j];
-                const int32_t o = p.h1_fast ? gelu_chain_fast((int32_t)x, p.h1_sh_in, p.h1_sh_out)
-                                            : gelu_chain(x, p.h1_sh_in, p.h1_sh_out);
-                packed |= ((uint32_t)o & 0xffu) << (8 * b);
-            }
-            h1w[jw] = packed;
-        }
-        uint32_t h2w[4];
-#pragma unroll
-        for (int mw = 0; mw < 4; ++mw) {
-            uint32_t packed = 0;
-#pragma unroll
-            for (int b = 0; b < 4; ++b) {
-                const int m = mw * 4 + b;
-                const int32_t *wrow = (const int32_t *)(w2t + (h * 16 + m) * W2STR);
-                int32_t acc = 0;
-#pragma unroll
-                for (int w = 0; w < 8; ++w) acc = __dp4a((int32_t)h1w[w], wrow[w], acc);
-                const int64_t x = (int64_t)acc + p.b2[h * 16 + m];
-                const int32_t o = p.h2_fast ? gelu_chain_fast((int32_t)x, p.h2_sh_in, p.h2_sh_out)
-                                            : gelu_chain(x, p.h2_sh_in, p.h2_sh_out);
-                packed |= ((uint32_t)o & 0xffu) << (8 * b);
-            }
-            h2w[mw] = packed;
-        }
+        const int32_t *hrow = (const int32_t *)(h2s + (h * MAXC + c) * 16);
         int32_t q[2];
 #pragma unroll
         for (int o = 0; o < 2; ++o) {
             const int32_t *wrow = (const int32_t *)(w3t + (h * 2 + o) * 16);
             int32_t acc = 0;
 #pragma unroll
-            for (int w = 0; w < 4; ++w) acc = __dp4a((int32_t)h2w[w], wrow[w], acc);
+            for (int w = 0; w < 4; ++w) acc = __dp4a(hrow[w], wrow[w], acc);
             const int32_t logit = (int32_t)requant64((int64_t)acc + p.b3[h * 2 + o], p.logit_shift, 8);
             q[o] = (int32_t)requant64(logit, p.logit_q16_shift, 24);
         }
@@ -227,8 +226,7 @@ __global__ void __launch_bounds__(THREADS) selector_kernel(
             int64_t acc = p.hb1[j];
 #pragma unroll
             for (int i = 0; i < 3; ++i) acc += st[i] * (int32_t)p.hw1[i * 3 + j];
-            hid[j] = p.hw_fast ? gelu_chain_fast((int32_t)acc, p.hw_sh_in, p.hw_sh_out)
-                               : gelu_chain(acc, p.hw_sh_in, p.hw_sh_out);
+            hid[j] = sel_gelu(acc, p.hw_k2, p.hw_k, p.hw_fast, p.hw_sh_in, p.hw_sh_out);
         }
 #pragma unroll
         for (int j = 0; j < 3; ++j) {
