@@ -25,6 +25,9 @@ namespace hv {
 
 enum Epi { EPI_I8 = 0, EPI_I8_RES = 1, EPI_GELU = 2, EPI_PATCH = 3, EPI_I32 = 4, EPI_ACC64 = 5 };
 
+// Largest exact GELU-chain output table (bytes) an FC1 launch keeps in shared memory.
+constexpr int kGeluTableMax = 4096;
+
 // Per-launch epilogue constants (all derived on the host from the golden
 // scale exponents).
 struct EpiParams {
@@ -39,7 +42,11 @@ struct EpiParams {
     int gelu_sh_in, gelu_sh_out;
     int gelu_fast;            // host-checked ranges of gelu_chain_fast hold
     int gelu_k2;              // host-checked ranges of gelu_chain_fast2 hold (persistent kernel)
-    GeluK gk;                 // constants of gelu_chain_fast2
+    GeluK gk;                 // constants of gelu_chain_fast2 (also the input shift of the table form)
+    // exact output table of the GELU chain over its reachable inputs (persistent
+    // kernel): out = gtab[clamp(rsa(acc + bias, sh_in) - gtab_lo, 0, gtab_n - 1)]
+    const int8_t *gtab;
+    int gtab_lo, gtab_n;      // gtab_n in [1, kGeluTableMax]; 0 = no table
     // patch (EPI_PATCH): pos [197][192], add = (a = embed, b = pos)
     const int8_t *pos;
 };

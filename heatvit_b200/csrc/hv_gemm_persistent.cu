@@ -40,14 +40,17 @@ struct PLayout {
     static constexpr int NCH = N / BN;                 // n-chunks per tile
     static constexpr int AK = KDIM == 192 ? 192 : 64;  // A stage width (bytes of K)
     static constexpr int KST = KDIM / AK;              // A stages per tile
-    static constexpr int S = KDIM == 192 ? 3 : 8;      // ring depth
+    // ring depth; FC1 (N = 768) keeps two stages to leave room for its GELU table
+    static constexpr int S = KDIM == 192 ? (N == 768 ? 2 : 3) : 8;
+    static constexpr int TABB = N == 768 ? kGeluTableMax : 0;  // exact GELU-chain table (EPI_GELU)
     static constexpr int A_STAGE = 128 * AK;
     // An A stage is released after its tile's last n-chunk, or after its own k-step.
     static_assert(KST == 1 || NCH == 1, "streamed K with several n-chunks is not pipelined");
     static constexpr int OFF_B = 0;
     static constexpr int OFF_A = OFF_B + N * KDIM;
     static constexpr int OFF_BIAS = OFF_A + S * A_STAGE;
-    static constexpr int OFF_BAR = OFF_BIAS + N * 4;
+    static constexpr int OFF_TAB = OFF_BIAS + N * 4;
+    static constexpr int OFF_BAR = OFF_TAB + TABB;
     static constexpr int NBAR = 2 * S + 5;
     static constexpr int USED = OFF_BAR + NBAR * 8 + 16;
     // At least 116 KB so that two CTAs never share an SM: each takes all 512 TMEM columns.
@@ -131,6 +134,9 @@ __global__ void __launch_bounds__(PT_THREADS, 1) tcp_gemm_kernel(GemmArgs g, int
                    16);
     }
     for (int i = tid; i < N; i += PT_THREADS) sbias[i] = g.epi.bias ? g.epi.bias[i] : 0;
+    int8_t *stab = (int8_t *)(smem + L::OFF_TAB);
+    if (EPI == EPI_GELU && L::TABB > 0)
+        for (int i = tid; i < g.epi.gtab_n; i += PT_THREADS) stab[i] = g.epi.gtab[i];
     asm volatile("cp.async.wait_all;\n" ::: "memory");
     tc05::fence_proxy_async();
     tc05::fence_before();
@@ -270,16 +276,33 @@ __global__ void __launch_bounds__(PT_THREADS, 1) tcp_gemm_kernel(GemmArgs g, int
                     tc05::wait_ld();
                     const uint32_t aux[8] = {r0.x, r0.y, r0.z, r0.w, r1.x, r1.y, r1.z, r1.w};
                     uint32_t pk[8];
+                    if (EPI == EPI_GELU && FAST && L::TABB > 0 && g.epi.gtab_n > 0) {
+                        // exact table of the GELU chain over the reachable Q8.16 window
+                        const GeluK &k = g.epi.gk;
+                        const int lo = g.epi.gtab_lo, last = g.epi.gtab_n - 1;
 #pragma unroll
-                    for (int w = 0; w < 8; ++w) {
-                        int32_t o[4];
+                        for (int w = 0; w < 8; ++w) {
+                            int32_t o[4];
 #pragma unroll
-                        for (int b = 0; b < 4; ++b) {
-                            const int j = w * 4 + b;
-                            const int32_t ax = (int8_t)((aux[w] >> (8 * b)) & 0xffu);
-                            o[b] = epi_elem<EPI, FAST>((int32_t)v[j], bv[j], ax, g.epi);
+                            for (int b = 0; b < 4; ++b) {
+                                const int32_t x = (int32_t)v[w * 4 + b] + bv[w * 4 + b];
+                                const int32_t q = (x + k.hin + mulhi_s(x, k.ksgn)) >> k.sh_in;
+                                o[b] = stab[min(max(q - lo, 0), last)];
+                            }
+                            pk[w] = pack_sat8(o[0], o[1], o[2], o[3]);
                         }
-                        pk[w] = pack_sat8(o[0], o[1], o[2], o[3]);
+                    } else {
+#pragma unroll
+                        for (int w = 0; w < 8; ++w) {
+                            int32_t o[4];
+#pragma unroll
+                            for (int b = 0; b < 4; ++b) {
+                                const int j = w * 4 + b;
+                                const int32_t ax = (int8_t)((aux[w] >> (8 * b)) & 0xffu);
+                                o[b] = epi_elem<EPI, FAST>((int32_t)v[j], bv[j], ax, g.epi);
+                            }
+                            pk[w] = pack_sat8(o[0], o[1], o[2], o[3]);
+                        }
                     }
                     if (valid) {
                         uint4 *dst = (uint4 *)((int8_t *)g.out + orow * g.ldo + gcol0);

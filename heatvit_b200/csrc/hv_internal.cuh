@@ -49,6 +49,14 @@ AttnParams make_attn(int qkv_out_scale, int score_scale, int prob_scale, int con
 // err: device word set to a non-zero code when a bounded wait gave up.
 // may_be_short: some image may hold at most 128 tokens (any selector has run, or
 // the caller's ragged batch is arbitrary); those go to a smaller CTA shape.
+// Exact lookup table of the FFN GELU chain over its reachable Q8.16 inputs
+// [-qmax, qmax]: the window [wlo, wlo + wn) outside which the int8 output is
+// constant (gelu_table_window; synchronises `st`), then the table itself,
+// tab[i] = requant(shift_gelu(wlo + i), -16, dst, 8) (launch_gelu_table_fill).
+// d_mm: two device ints of scratch.
+cudaError_t gelu_table_window(int32_t qmax, int sh_out, int *d_mm, int32_t *wlo, int32_t *wn, cudaStream_t st);
+cudaError_t launch_gelu_table_fill(int8_t *tab, int32_t wlo, int32_t wn, int sh_out, cudaStream_t st);
+
 cudaError_t launch_attention(const int8_t *qkv, const int32_t *offsets, int images, int8_t *ctx,
                              const AttnParams &p, int may_be_short, int *err, cudaStream_t st);
 

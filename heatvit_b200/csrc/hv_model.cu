@@ -88,6 +88,8 @@ struct BlockDev {
     int qkv_shift, qkv_wide, proj_shift, proj_wide, fc2_shift, fc2_wide;
     int fc1_sh_in, fc1_sh_out, fc1_wide, fc1_fast, fc1_k2;
     GeluK fc1_gk;
+    size_t fc1_tab;            // exact GELU-chain table in the arena (fc1_tab_n > 0)
+    int fc1_tab_lo, fc1_tab_n;
     AlignAdd res1, res2;
     AttnParams attn;
 };
@@ -262,7 +264,7 @@ GemmArgs gemm_args(const void *a, int lda, int patch_mode, const int8_t *bt, int
 cudaError_t model_gemm(const hv_model *m, GemmArgs &g, int epi, int m_max, cudaStream_t st) {
     g.epi.fast = gemm_epi_fast(epi, g.epi);
     if (m->persistent && gemm_persistent_supported(epi, g.n, g.k)) {
-        if (epi == EPI_GELU) g.epi.fast = g.epi.gelu_k2;  // the persistent kernel's fast GELU form
+        if (epi == EPI_GELU) g.epi.fast = g.epi.gelu_k2 || g.epi.gtab_n > 0;  // the persistent kernel's fast forms
         return launch_gemm_persistent(g, epi, m_max, m->err, m->sms, st);
     }
     return launch_gemm(g, epi, 0, m_max, m->err, st);
@@ -343,6 +345,9 @@ int run_block(hv_model *m, int b, int images, const int32_t *off, int may_be_sho
         g.epi.gelu_fast = d.fc1_fast;
         g.epi.gelu_k2 = d.fc1_k2;
         g.epi.gk = d.fc1_gk;
+        g.epi.gtab = d.fc1_tab_n > 0 ? m->w<int8_t>(d.fc1_tab) : nullptr;
+        g.epi.gtab_lo = d.fc1_tab_lo;
+        g.epi.gtab_n = d.fc1_tab_n;
         CUDA_TRY(model_gemm(m, g, EPI_GELU, rows_max, st));
         pr.end(st, rows_dev, 0);
     }
@@ -452,6 +457,14 @@ int infer_impl(hv_model *m, const int8_t *d_images, int batch, int32_t *d_logits
 bool ln_scale_ok(int xs) { return xs >= -32 && xs <= 0; }
 
 int pack_model(hv_model *m, const hv_params *P) {
+    // two device ints of scratch for the GELU table window search, freed on every return
+    struct ScratchInts {
+        int *p = nullptr;
+        ~ScratchInts() {
+            if (p) cudaFree(p);
+        }
+    } mm_hold;
+    int *&mm = mm_hold.p;
     Arena A;
     const hv_patch_params &pp = P->patch;
     m->has_patch = pp.weight != nullptr;
@@ -518,6 +531,24 @@ int pack_model(hv_model *m, const hv_params *P) {
             const int64_t vmax = max_abs(q.b1, HV_FFN) + (int64_t)192 * 16384;
             d.fc1_k2 = (!d.fc1_wide && gelu_fast2_range(d.fc1_sh_in, d.fc1_sh_out, &vlim) && vmax <= vlim) ? 1 : 0;
             d.fc1_gk = make_gelu_k(d.fc1_k2 ? d.fc1_sh_in : 0, d.fc1_k2 ? d.fc1_sh_out : 0);
+            // Exact table form when the output varies only over a short window of the
+            // reachable Q8.16 inputs [-qmax, qmax], qmax = rsa(vmax, sh_in).
+            d.fc1_tab_n = 0;
+            if (!d.fc1_wide && d.fc1_sh_in >= 0 && d.fc1_sh_in <= 30 && vmax < ((int64_t)1 << 30)) {
+                const int64_t hin = d.fc1_sh_in > 0 ? (int64_t)1 << (d.fc1_sh_in - 1) : 0;
+                const int64_t qmax = (vmax + hin) >> d.fc1_sh_in;
+                if (qmax < ((int64_t)1 << 23)) {
+                    if (!mm) CUDA_TRY(cudaMalloc(&mm, 2 * sizeof(int)));
+                    int32_t wlo = 0, wn = 0;
+                    CUDA_TRY(gelu_table_window((int32_t)qmax, d.fc1_sh_out, mm, &wlo, &wn, nullptr));
+                    if (wn <= kGeluTableMax) {
+                        d.fc1_tab = A.add(nullptr, (size_t)wn);
+                        d.fc1_tab_lo = wlo;
+                        d.fc1_tab_n = wn;
+                        d.fc1_gk = make_gelu_k(d.fc1_sh_in, d.fc1_k2 ? d.fc1_sh_out : 0);
+                    }
+                }
+            }
         }
         d.fc2_shift = q.ffn_out_scale_exp - (q.hidden_out_scale_exp + q.w2_scale_exp);
         d.fc2_wide = needs_wide(q.b2, 192, HV_FFN);
@@ -623,6 +654,13 @@ int pack_model(hv_model *m, const hv_params *P) {
     CUDA_TRY(cudaMalloc(&m->weights, A.host.size()));
     m->weights_bytes = A.host.size();
     CUDA_TRY(cudaMemcpy(m->weights, A.host.data(), A.host.size(), cudaMemcpyHostToDevice));
+    for (int b = 0; b < HV_BLOCKS; ++b) {
+        const BlockDev &d = m->blocks[b];
+        if (m->has_block[b] && d.fc1_tab_n > 0)
+            CUDA_TRY(launch_gelu_table_fill((int8_t *)(m->weights + d.fc1_tab), d.fc1_tab_lo, d.fc1_tab_n, d.fc1_sh_out,
+                                            nullptr));
+    }
+    CUDA_TRY(cudaDeviceSynchronize());
     return HV_OK;
 }
 

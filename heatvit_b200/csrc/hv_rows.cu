@@ -31,16 +31,6 @@ LnParams make_ln(const int8_t *gamma, const int8_t *beta, int x_scale, int gamma
 
 namespace {
 
-__device__ __forceinline__ int32_t warp_sum_i32(int32_t v) {
-#pragma unroll
-    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-    return v;
-}
-__device__ __forceinline__ int64_t warp_sum_i64(int64_t v) {
-#pragma unroll
-    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-    return v;
-}
 __device__ __forceinline__ int32_t warp_max_i32(int32_t v) {
 #pragma unroll
     for (int o = 16; o; o >>= 1) v = max(v, __shfl_xor_sync(0xffffffffu, v, o));
@@ -518,6 +508,28 @@ __global__ void align_add_kernel(const int8_t *a, const int8_t *b, AlignAdd k, i
         out[i] = (int8_t)align_add8(a[i], b[i], k);
 }
 
+// Output of the GELU chain's second half for a Q8.16 input q (|q| < 2^23):
+// requant(shift_gelu(q), -16, dst, 8) with sh_out = dst + 16.
+__device__ __forceinline__ int32_t gelu_out_q16(int32_t q, int sh_out) {
+    return (int32_t)requant64(shift_gelu(q), sh_out, 8);
+}
+
+// Change points of gelu_out_q16 over q in [qlo, qlo + n): positions i in [1, n)
+// with out(qlo + i) != out(qlo + i - 1); first / last of them land in mm[0] / mm[1].
+__global__ void gelu_window_kernel(int32_t qlo, int32_t n, int sh_out, int *mm) {
+    for (int32_t i = 1 + blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+        if (gelu_out_q16(qlo + i, sh_out) != gelu_out_q16(qlo + i - 1, sh_out)) {
+            atomicMin(&mm[0], i);
+            atomicMax(&mm[1], i);
+        }
+    }
+}
+
+__global__ void gelu_table_fill_kernel(int8_t *tab, int32_t wlo, int32_t wn, int sh_out) {
+    for (int32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < wn; i += gridDim.x * blockDim.x)
+        tab[i] = (int8_t)gelu_out_q16(wlo + i, sh_out);
+}
+
 inline int grid_for(int64_t n, int threads) {
     int64_t b = (n + threads - 1) / threads;
     return (int)(b < 148 * 16 ? (b < 1 ? 1 : b) : 148 * 16);
@@ -551,6 +563,31 @@ cudaError_t launch_softmax_rows(const int32_t *x, const int32_t *offsets, int ro
                                 cudaStream_t st) {
     if (rows <= 0) return cudaSuccess;
     softmax_rows_kernel<<<(rows + 7) / 8, 256, 0, st>>>(x, offsets, rows, mode, out);
+    return cudaGetLastError();
+}
+
+cudaError_t gelu_table_window(int32_t qmax, int sh_out, int *d_mm, int32_t *wlo, int32_t *wn, cudaStream_t st) {
+    const int32_t qlo = -qmax, n = 2 * qmax + 1;
+    const int init[2] = {0x7fffffff, -1};
+    cudaError_t e = cudaMemcpyAsync(d_mm, init, sizeof(init), cudaMemcpyHostToDevice, st);
+    if (e != cudaSuccess) return e;
+    gelu_window_kernel<<<grid_for(n, 256), 256, 0, st>>>(qlo, n, sh_out, d_mm);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    int mm[2];
+    if ((e = cudaMemcpyAsync(mm, d_mm, sizeof(mm), cudaMemcpyDeviceToHost, st)) != cudaSuccess) return e;
+    if ((e = cudaStreamSynchronize(st)) != cudaSuccess) return e;
+    if (mm[1] < 0) {  // constant over the whole range
+        *wlo = qlo;
+        *wn = 1;
+    } else {
+        *wlo = qlo + mm[0] - 1;
+        *wn = mm[1] - mm[0] + 2;
+    }
+    return cudaSuccess;
+}
+
+cudaError_t launch_gelu_table_fill(int8_t *tab, int32_t wlo, int32_t wn, int sh_out, cudaStream_t st) {
+    gelu_table_fill_kernel<<<grid_for(wn, 256), 256, 0, st>>>(tab, wlo, wn, sh_out);
     return cudaGetLastError();
 }
 

@@ -278,10 +278,12 @@ def test_model_parameter_errors(cuda):
 
 
 @pytest.mark.parametrize("l2,w1,hid", [(-12, -8, -11), (-20, -20, -8), (-9, -8, -20), (-8, -8, -9), (-14, -2, -5),
-                                       (-7, -10, -13)])
+                                       (-7, -10, -13),
+                                       # short output windows: the exact table form
+                                       (-13, -10, -15), (-14, -13, -18), (-12, -12, -16), (-12, -14, -14)])
 def test_ffn_gelu_epilogue_exponents(cuda, oracle, l2, w1, hid):
-    """FC1's fused GELU epilogue (32-bit fast form and 64-bit generic form)
-    across input/output exponents, through the fused block kernel."""
+    """FC1's fused GELU epilogue (table, FMA-pipe and 64-bit forms) across
+    input/output exponents, through the fused block kernel."""
     from dataclasses import replace
     from heatvit_b200 import synth
     from heatvit_b200.transformer import transformer_block_batch
