@@ -66,13 +66,23 @@ __device__ __forceinline__ int32_t q16_of(int32_t acc, const AttnParams &p) {
     return (int32_t)requant64(score, p.q16_shift, 24);
 }
 
+// xt = q16(acc) - mx.  FAST: q16(acc) - mx = (acc + half - mx*2^s + sign) >> s exactly,
+// since mx*2^s is a multiple of 2^s; `cm` = half - mx*2^s is computed once per row
+// (|acc| <= 2^20 and |cm| <= 2^30 + 2^20 keep the sum inside int32).
+template <bool FAST>
+__device__ __forceinline__ int32_t xt_of(int32_t acc, int32_t mx, int32_t cm, const AttnParams &p) {
+    if (FAST) return (acc + cm + ((acc >> 31) & p.fast_negmask)) >> p.fast_shift;
+    return q16_of<false>(acc, p) - mx;
+}
+
 // exp terms of one 16-column chunk (columns >= valid are masked to 0); returns their sum.
 template <bool FAST, bool MASK>
-__device__ __forceinline__ uint32_t chunk_exp(uint32_t (&v)[16], int valid, int32_t mx, const AttnParams &p) {
+__device__ __forceinline__ uint32_t chunk_exp(uint32_t (&v)[16], int valid, int32_t mx, int32_t cm,
+                                              const AttnParams &p) {
     uint32_t sum = 0;
 #pragma unroll
     for (int j = 0; j < 16; ++j) {
-        uint32_t e = softmax_exp_q16(q16_of<FAST>((int32_t)v[j], p) - mx);
+        uint32_t e = softmax_exp_q16(xt_of<FAST>((int32_t)v[j], mx, cm, p));
         if (MASK && j >= valid) e = 0u;
         v[j] = e;
         sum += e;
@@ -185,14 +195,15 @@ __global__ void __launch_bounds__(CFG::THREADS) attention_tc_kernel(const int8_t
 #pragma unroll
             for (int q = 1; q < CFG::SPLIT; ++q) mraw = max(mraw, sred[q * 128 + lrow]);
             const int32_t mx = q16_of<FAST>(mraw, p);
+            const int32_t cm = (int32_t)((int64_t)p.fast_half - ((int64_t)mx << p.fast_shift));
             uint32_t sum = 0;
             for (int c = part; c < nchunks; c += CFG::SPLIT) {
                 const int c0 = c * 16;
                 uint32_t v[16];
                 tc05::ld16(lane_addr + c0, v);
                 tc05::wait_ld();
-                if (c0 < nfull) sum += chunk_exp<FAST, false>(v, 16, mx, p);
-                else sum += chunk_exp<FAST, true>(v, n - c0, mx, p);
+                if (c0 < nfull) sum += chunk_exp<FAST, false>(v, 16, mx, cm, p);
+                else sum += chunk_exp<FAST, true>(v, n - c0, mx, cm, p);
                 tc05::st16(lane_addr + c0, v);
             }
             tc05::wait_st();
@@ -212,15 +223,15 @@ __global__ void __launch_bounds__(CFG::THREADS) attention_tc_kernel(const int8_t
                 uint32_t pk[4];
 #pragma unroll
                 for (int w = 0; w < 4; ++w) {
-                    uint32_t word = 0;
+                    int32_t pr[4];
 #pragma unroll
                     for (int b = 0; b < 4; ++b) {
-                        // min(rsa(rsa(E*rc, 16), 8), 255) in one rounding step (nested floors).
+                        // rsa(rsa(E*rc, 16), 8) in one rounding step (nested floors); <= 256,
+                        // and the saturating pack applies the min(., 255)
                         const uint64_t tt = (uint64_t)v[w * 4 + b] * rc + (32768u + (1u << 23));
-                        const uint32_t pr = (uint32_t)(tt >> 24);
-                        word |= (pr < 255u ? pr : 255u) << (8 * b);
+                        pr[b] = (int32_t)(tt >> 24);
                     }
-                    pk[w] = word;
+                    pk[w] = pack_satu8(pr[0], pr[1], pr[2], pr[3]);
                 }
                 *(uint4 *)(sP + tc05::kmajor_offset(lrow, c0, np)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
             }
@@ -289,7 +300,7 @@ AttnParams make_attn(int qkv_out_scale, int score_scale, int prob_scale, int con
     a.q16_shift = -(score_scale + 13);
     a.ctx_shift = context_out_scale - (prob_scale + qkv_out_scale);
     const int k = -a.score_shift;
-    a.fast = (k >= 0 && k <= 10 && a.q16_shift >= k) ? 1 : 0;
+    a.fast = (k >= 0 && k <= 10 && a.q16_shift >= k && a.q16_shift - k <= 30) ? 1 : 0;
     a.fast_shift = a.fast ? a.q16_shift - k : 0;
     a.fast_half = a.fast_shift ? (1 << (a.fast_shift - 1)) : 0;
     a.fast_negmask = a.fast_shift ? -1 : 0;

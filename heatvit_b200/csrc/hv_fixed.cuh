@@ -274,6 +274,14 @@ HV_DEV uint32_t pack_sat8(int32_t w0, int32_t w1, int32_t w2, int32_t w3) {
     return d;
 }
 
+// Saturate four non-negative int32 values to [0, 255] and pack them (w0 low).
+HV_DEV uint32_t pack_satu8(int32_t w0, int32_t w1, int32_t w2, int32_t w3) {
+    uint32_t hi, d;
+    asm("cvt.pack.sat.u8.s32.b32 %0, %1, %2, 0;" : "=r"(hi) : "r"(w3), "r"(w2));
+    asm("cvt.pack.sat.u8.s32.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(w1), "r"(w0), "r"(hi));
+    return d;
+}
+
 // PLAN sigmoid (nonlinear.py:83-95), unsigned Q0.16.
 HV_HD int32_t plan_sigmoid(int32_t x) {
     int32_t ax = x < 0 ? -x : x, y;
@@ -288,19 +296,22 @@ HV_HD int32_t plan_sigmoid(int32_t x) {
 // Shift-softmax pieces (nonlinear.py:98-133)
 // ---------------------------------------------------------------------------
 // exp of a non-positive Q8.16 argument xt = x - max, |xt| < 2^31.
-// z = floor(-xt / 45426) by a multiply-high estimate with M = floor(2^32/45426)
-// = 94548: n*M/2^32 = (n/45426)(1 - 6.95e-6), so the estimate is q or q-1 for
-// every n < 2^31, and one remainder correction makes it exact.  Then
-// p = xt + z*45426 = -r, where r is the remainder.
+// z = floor(-xt / 45426) is a multiply-high by the invariant reciprocal
+// m = ceil(2^47 / 45426) = 3098170395 followed by a 15-bit shift (division by an
+// invariant integer, Granlund & Montgomery 1994): m * 45426 - 2^47 < 2^16, so the
+// quotient is exact for every n < 2^31 (checked exhaustively).  Then
+// p = xt + z*45426 = -r with r the remainder.  A shift by z >= 32 gives 0 under
+// PTX shr semantics, and e < 2^17 makes z = 31 give 0 as well.
 HV_DEV uint32_t softmax_exp_q16(int32_t xt) {
-    uint32_t n = (uint32_t)(-xt);
-    uint32_t z = __umulhi(n, 94548u);
-    uint32_t r = n - z * 45426u;
-    if (r >= 45426u) { z += 1; r -= 45426u; }
-    uint32_t sh = 88670u - r;                                   // p + 88670, in (43244, 88670]
-    uint64_t sq = ((uint64_t)sh * sh + 32768u) >> 16;           // rsa(sh^2, 16), <= 119970
-    uint32_t e = ((uint32_t)(23495u * (uint32_t)sq + 32768u) >> 16) + 22544u;
-    return z >= 31u ? 0u : (e >> z);
+    const uint32_t n = (uint32_t)(-xt);
+    const uint32_t z = __umulhi(n, 3098170395u) >> 15;
+    const uint32_t r = n - z * 45426u;
+    const uint32_t sh = 88670u - r;                                   // p + 88670, in (43244, 88670]
+    const uint64_t sq = ((uint64_t)sh * sh + 32768u) >> 16;           // rsa(sh^2, 16), <= 119970
+    const uint32_t e = ((uint32_t)(23495u * (uint32_t)sq + 32768u) >> 16) + 22544u;
+    uint32_t out;
+    asm("shr.b32 %0, %1, %2;" : "=r"(out) : "r"(e), "r"(z));
+    return out;
 }
 
 // recip = round_div(2^32, S) for S >= 1.
