@@ -101,6 +101,19 @@ struct SelDev {
 
 }  // namespace
 
+// One set of activation scratch (ragged token buffers, offsets, counts, package
+// flags, warnings and the device error word).  The model holds two, so two
+// inferences can be in flight on two streams at once (hv_infer_host).
+struct Workspace {
+    int cap = 0;
+    uint8_t *scratch = nullptr;
+    int8_t *X = nullptr, *Y = nullptr, *LN = nullptr, *QKV = nullptr, *CTX = nullptr, *HID = nullptr, *STAGE = nullptr,
+           *CLSLN = nullptr;
+    int32_t *off[2] = {nullptr, nullptr}, *counts = nullptr;
+    uint8_t *pkg[2] = {nullptr, nullptr}, *warn = nullptr;
+    int *err = nullptr;
+};
+
 struct hv_model {
     int device = 0;
     int sms = 148;         // SM count: one persistent GEMM CTA per SM
@@ -119,9 +132,9 @@ struct hv_model {
     SelDev sels[HV_MAX_SELECTORS];
     size_t fin_g = 0, fin_b = 0, head_wt = 0, head_b = 0;
     int fin_xs = 0, fin_gs = 0, fin_bs = 0, fin_os = 0, head_shift = 0;
-    // scratch
-    int cap = 0;
-    uint8_t *scratch = nullptr;
+    // scratch: two workspaces; the fields below point into the one that the next
+    // enqueued work uses (use_workspace)
+    Workspace ws[2];
     int8_t *X = nullptr, *Y = nullptr, *LN = nullptr, *QKV = nullptr, *CTX = nullptr, *HID = nullptr, *STAGE = nullptr,
            *CLSLN = nullptr;
     int32_t *off[2] = {nullptr, nullptr}, *counts = nullptr;
@@ -139,7 +152,7 @@ struct hv_model {
     int32_t *hlogits = nullptr, *htc = nullptr;
     hv_selector_summary *hsum = nullptr;
     uint8_t *hwarn = nullptr;
-    cudaStream_t copy_stream = nullptr, compute_stream = nullptr;
+    cudaStream_t copy_stream = nullptr, compute_stream[2] = {nullptr, nullptr};
     cudaEvent_t ev_in[2] = {nullptr, nullptr}, ev_done[2] = {nullptr, nullptr};
 
     // kernel timing (hv_profile_*)
@@ -174,45 +187,70 @@ SelParams bind_sel(const hv_model *m, const SelDev &s) {
     return p;
 }
 
-int ensure_capacity(hv_model *m, int images) {
-    if (images <= m->cap) return HV_OK;
-    if (m->scratch) {
-        cudaFree(m->scratch);
-        m->scratch = nullptr;
-        m->cap = 0;
+// Point the model's working fields at workspace i.  Kernels capture these
+// pointers when they are enqueued, so switching between enqueues is safe.
+void use_workspace(hv_model *m, int i) {
+    const Workspace &w = m->ws[i];
+    m->X = w.X;
+    m->Y = w.Y;
+    m->LN = w.LN;
+    m->QKV = w.QKV;
+    m->CTX = w.CTX;
+    m->HID = w.HID;
+    m->STAGE = w.STAGE;
+    m->CLSLN = w.CLSLN;
+    m->off[0] = w.off[0];
+    m->off[1] = w.off[1];
+    m->counts = w.counts;
+    m->pkg[0] = w.pkg[0];
+    m->pkg[1] = w.pkg[1];
+    m->warn = w.warn;
+    m->err = w.err;
+}
+
+// Workspace i holds at least `images` images; it becomes the current one.
+int ensure_capacity(hv_model *m, int images, int i = 0) {
+    Workspace &w = m->ws[i];
+    if (images > w.cap) {
+        if (w.scratch) {
+            cudaFree(w.scratch);
+            w = Workspace();
+        }
+        const size_t rows = (size_t)images * HV_TOKENS;
+        size_t total = 0;
+        auto take = [&](size_t bytes) {
+            size_t o = total;
+            total += (bytes + 255) & ~(size_t)255;
+            return o;
+        };
+        const size_t oX = take(rows * 192), oY = take(rows * 192), oLN = take(rows * 192), oQKV = take(rows * 576),
+                     oCTX = take(rows * 192), oHID = take(rows * 768), oSTAGE = take(rows * 192),
+                     oCLS = take((size_t)images * 192), oOff0 = take((size_t)(images + 1) * 4),
+                     oOff1 = take((size_t)(images + 1) * 4), oCnt = take((size_t)images * 4), oPkg0 = take(images),
+                     oPkg1 = take(images), oWarn = take(((size_t)images + 3) & ~(size_t)3), oErr = take(16);
+        uint8_t *base = nullptr;
+        if (cudaMalloc(&base, total) != cudaSuccess)
+            return fail(HV_ERR_NOMEM, "cannot allocate %zu bytes of scratch", total);
+        w.scratch = base;
+        w.X = (int8_t *)(base + oX);
+        w.Y = (int8_t *)(base + oY);
+        w.LN = (int8_t *)(base + oLN);
+        w.QKV = (int8_t *)(base + oQKV);
+        w.CTX = (int8_t *)(base + oCTX);
+        w.HID = (int8_t *)(base + oHID);
+        w.STAGE = (int8_t *)(base + oSTAGE);
+        w.CLSLN = (int8_t *)(base + oCLS);
+        w.off[0] = (int32_t *)(base + oOff0);
+        w.off[1] = (int32_t *)(base + oOff1);
+        w.counts = (int32_t *)(base + oCnt);
+        w.pkg[0] = base + oPkg0;
+        w.pkg[1] = base + oPkg1;
+        w.warn = base + oWarn;
+        w.err = (int *)(base + oErr);
+        if (cudaMemset(w.err, 0, 16) != cudaSuccess) return fail(HV_ERR_CUDA, "cannot clear the error word");
+        w.cap = images;
     }
-    const size_t rows = (size_t)images * HV_TOKENS;
-    size_t total = 0;
-    auto take = [&](size_t bytes) {
-        size_t o = total;
-        total += (bytes + 255) & ~(size_t)255;
-        return o;
-    };
-    const size_t oX = take(rows * 192), oY = take(rows * 192), oLN = take(rows * 192), oQKV = take(rows * 576),
-                 oCTX = take(rows * 192), oHID = take(rows * 768), oSTAGE = take(rows * 192),
-                 oCLS = take((size_t)images * 192), oOff0 = take((size_t)(images + 1) * 4),
-                 oOff1 = take((size_t)(images + 1) * 4), oCnt = take((size_t)images * 4), oPkg0 = take(images),
-                 oPkg1 = take(images), oWarn = take(((size_t)images + 3) & ~(size_t)3), oErr = take(16);
-    uint8_t *base = nullptr;
-    if (cudaMalloc(&base, total) != cudaSuccess) return fail(HV_ERR_NOMEM, "cannot allocate %zu bytes of scratch", total);
-    m->scratch = base;
-    m->X = (int8_t *)(base + oX);
-    m->Y = (int8_t *)(base + oY);
-    m->LN = (int8_t *)(base + oLN);
-    m->QKV = (int8_t *)(base + oQKV);
-    m->CTX = (int8_t *)(base + oCTX);
-    m->HID = (int8_t *)(base + oHID);
-    m->STAGE = (int8_t *)(base + oSTAGE);
-    m->CLSLN = (int8_t *)(base + oCLS);
-    m->off[0] = (int32_t *)(base + oOff0);
-    m->off[1] = (int32_t *)(base + oOff1);
-    m->counts = (int32_t *)(base + oCnt);
-    m->pkg[0] = base + oPkg0;
-    m->pkg[1] = base + oPkg1;
-    m->warn = base + oWarn;
-    m->err = (int *)(base + oErr);
-    if (cudaMemset(m->err, 0, 16) != cudaSuccess) return fail(HV_ERR_CUDA, "cannot clear the error word");
-    m->cap = images;
+    use_workspace(m, i);
     return HV_OK;
 }
 
@@ -379,14 +417,14 @@ int run_patch(hv_model *m, const int8_t *images, int count, int8_t *out, cudaStr
 
 int infer_impl(hv_model *m, const int8_t *d_images, int batch, int32_t *d_logits, int32_t *d_tc,
                hv_selector_summary *d_summary, uint8_t *d_warnings, int8_t *d_ckpt, int32_t *d_ckpt_rows,
-               cudaStream_t st) {
+               cudaStream_t st, int wsi = 0) {
     if (batch <= 0) return fail(HV_ERR_VALUE, "batch must be positive");
     if (!d_images || !d_logits) return fail(HV_ERR_VALUE, "images and logits are required");
     if (!m->has_patch || !m->has_head) return fail(HV_ERR_STATE, "model has no patch embedding or head");
     for (int b = 0; b < HV_BLOCKS; ++b)
         if (!m->has_block[b]) return fail(HV_ERR_STATE, "model has no block %d", b + 1);
     CUDA_TRY(cudaSetDevice(m->device));
-    int rc = ensure_capacity(m, batch);
+    int rc = ensure_capacity(m, batch, wsi);
     if (rc) return rc;
     const int ns = m->used_sel;
     const int tc_stride = ns + 1;
@@ -701,7 +739,8 @@ int hv_model_destroy(hv_model *m) {
     if (!m) return HV_OK;
     cudaSetDevice(m->device);
     if (m->weights) cudaFree(m->weights);
-    if (m->scratch) cudaFree(m->scratch);
+    for (int i = 0; i < 2; ++i)
+        if (m->ws[i].scratch) cudaFree(m->ws[i].scratch);
     for (int i = 0; i < 2; ++i) {
         if (m->himg[i]) cudaFree(m->himg[i]);
         if (m->ev_in[i]) cudaEventDestroy(m->ev_in[i]);
@@ -717,7 +756,8 @@ int hv_model_destroy(hv_model *m) {
     for (auto e : m->prof_ev) cudaEventDestroy(e);
     if (m->prof_rows) cudaFree(m->prof_rows);
     if (m->copy_stream) cudaStreamDestroy(m->copy_stream);
-    if (m->compute_stream) cudaStreamDestroy(m->compute_stream);
+    for (int i = 0; i < 2; ++i)
+        if (m->compute_stream[i]) cudaStreamDestroy(m->compute_stream[i]);
     delete m;
     return HV_OK;
 }
@@ -743,10 +783,11 @@ int hv_infer_host(hv_model *m, const int8_t *h_images, int batch, int32_t *h_log
     if (!m) return fail(HV_ERR_VALUE, "null model");
     if (batch <= 0 || !h_images || !h_logits) return fail(HV_ERR_VALUE, "bad arguments");
     CUDA_TRY(cudaSetDevice(m->device));
-    // Chunk schedule: a small first chunk (its upload is the only exposed one), then
-    // chunks of up to kHostChunk images whose uploads overlap the previous chunk's
-    // compute.  Large chunks keep the per-launch fixed costs of the pipeline small.
-    const int kFirstChunk = 256, kHostChunk = 1024;
+    // Chunk schedule: chunks of kHostChunk images.  The first chunk's upload is the
+    // only exposed one; later uploads overlap compute, and consecutive chunks run
+    // on two streams.  Measured on B200 at 1024 images: 512-image chunks beat
+    // smaller ones, whose per-launch fixed costs dominate.
+    const int kFirstChunk = 512, kHostChunk = 512;
     const int chunk = std::min(batch, kHostChunk);
     std::vector<int> starts(1, 0);
     for (int f = std::min(batch, kFirstChunk); f < batch; f += kHostChunk) starts.push_back(f);
@@ -754,7 +795,7 @@ int hv_infer_host(hv_model *m, const int8_t *h_images, int batch, int32_t *h_log
     const int ns = m->used_sel;
     if (!m->copy_stream) {
         CUDA_TRY(cudaStreamCreateWithFlags(&m->copy_stream, cudaStreamNonBlocking));
-        CUDA_TRY(cudaStreamCreateWithFlags(&m->compute_stream, cudaStreamNonBlocking));
+        for (int i = 0; i < 2; ++i) CUDA_TRY(cudaStreamCreateWithFlags(&m->compute_stream[i], cudaStreamNonBlocking));
         for (int i = 0; i < 2; ++i) {
             CUDA_TRY(cudaEventCreateWithFlags(&m->ev_in[i], cudaEventDisableTiming));
             CUDA_TRY(cudaEventCreateWithFlags(&m->ev_done[i], cudaEventDisableTiming));
@@ -774,8 +815,11 @@ int hv_infer_host(hv_model *m, const int8_t *h_images, int batch, int32_t *h_log
         CUDA_TRY(cudaMalloc(&m->hwarn, (size_t)chunk * 2));
         m->host_cap = chunk;
     }
-    int rc = ensure_capacity(m, chunk);
+    // Consecutive chunks alternate between two workspaces and two compute streams,
+    // so one chunk's kernels fill the idle tails of the other's.
+    int rc = ensure_capacity(m, chunk, 0);
     if (rc) return rc;
+    if (batch > std::min(batch, kFirstChunk) && (rc = ensure_capacity(m, chunk, 1)) != 0) return rc;
     // Outputs land in pinned staging (an asynchronous copy into pageable memory
     // would block this thread until the chunk's compute finished, serialising the
     // pipeline) and are copied to the caller's arrays once at the end.
@@ -821,45 +865,57 @@ int hv_infer_host(hv_model *m, const int8_t *h_images, int batch, int32_t *h_log
         CUDA_TRY(cudaMemcpyAsync(m->himg[buf], src, (size_t)cnt * HV_IMAGE_BYTES, cudaMemcpyHostToDevice,
                                  m->copy_stream));
         CUDA_TRY(cudaEventRecord(m->ev_in[buf], m->copy_stream));
-        CUDA_TRY(cudaStreamWaitEvent(m->compute_stream, m->ev_in[buf], 0));
+        cudaStream_t cst = m->compute_stream[buf];
+        use_workspace(m, buf);
+        CUDA_TRY(cudaStreamWaitEvent(cst, m->ev_in[buf], 0));
         int32_t *dl = m->hlogits + (size_t)buf * m->host_cap * HV_CLASSES;
         int32_t *dtc = m->htc + (size_t)buf * m->host_cap * (HV_MAX_SELECTORS + 1);
         hv_selector_summary *dsum = m->hsum + (size_t)buf * m->host_cap * HV_MAX_SELECTORS;
         uint8_t *dw = m->hwarn + (size_t)buf * m->host_cap;
         rc = infer_impl(m, m->himg[buf], cnt, dl, h_token_counts ? dtc : nullptr, h_summary ? dsum : nullptr,
-                        h_warnings ? dw : nullptr, nullptr, nullptr, m->compute_stream);
+                        h_warnings ? dw : nullptr, nullptr, nullptr, cst, buf);
         if (rc) return rc;
-        CUDA_TRY(cudaEventRecord(m->ev_done[buf], m->compute_stream));
+        CUDA_TRY(cudaEventRecord(m->ev_done[buf], cst));
         CUDA_TRY(cudaMemcpyAsync(m->pin_out + o_log + (size_t)first * HV_CLASSES * 4, dl, (size_t)cnt * HV_CLASSES * 4,
-                                 cudaMemcpyDeviceToHost, m->compute_stream));
+                                 cudaMemcpyDeviceToHost, cst));
         if (h_token_counts)
             CUDA_TRY(cudaMemcpyAsync(m->pin_out + o_tc + (size_t)first * (ns + 1) * 4, dtc, (size_t)cnt * (ns + 1) * 4,
-                                     cudaMemcpyDeviceToHost, m->compute_stream));
+                                     cudaMemcpyDeviceToHost, cst));
         if (h_summary && ns)
             CUDA_TRY(cudaMemcpyAsync(m->pin_out + o_sum + (size_t)first * ns * sizeof(hv_selector_summary), dsum,
                                      (size_t)cnt * ns * sizeof(hv_selector_summary), cudaMemcpyDeviceToHost,
-                                     m->compute_stream));
+                                     cst));
         if (h_warnings)
-            CUDA_TRY(cudaMemcpyAsync(m->pin_out + o_warn + first, dw, cnt, cudaMemcpyDeviceToHost, m->compute_stream));
+            CUDA_TRY(cudaMemcpyAsync(m->pin_out + o_warn + first, dw, cnt, cudaMemcpyDeviceToHost, cst));
     }
-    CUDA_TRY(cudaStreamSynchronize(m->compute_stream));
+    for (int i = 0; i < 2; ++i) CUDA_TRY(cudaStreamSynchronize(m->compute_stream[i]));
+    use_workspace(m, 0);
     memcpy(h_logits, m->pin_out + o_log, (size_t)batch * HV_CLASSES * 4);
     if (h_token_counts) memcpy(h_token_counts, m->pin_out + o_tc, (size_t)batch * (ns + 1) * 4);
     if (h_summary && ns) memcpy(h_summary, m->pin_out + o_sum, (size_t)batch * ns * sizeof(hv_selector_summary));
     if (h_warnings) memcpy(h_warnings, m->pin_out + o_warn, (size_t)batch);
-    int code = 0;
-    CUDA_TRY(cudaMemcpy(&code, m->err, sizeof(int), cudaMemcpyDeviceToHost));
-    if (code) return fail(HV_ERR_STATE, "a device-side bounded wait gave up (code %d)", code);
+    for (int i = 0; i < 2; ++i) {
+        if (!m->ws[i].err) continue;
+        int code = 0;
+        CUDA_TRY(cudaMemcpy(&code, m->ws[i].err, sizeof(int), cudaMemcpyDeviceToHost));
+        if (code) return fail(HV_ERR_STATE, "a device-side bounded wait gave up (code %d)", code);
+    }
     return HV_OK;
 }
 
 int hv_device_error(hv_model *m, int *code) {
     if (!m || !code) return fail(HV_ERR_VALUE, "null argument");
     *code = 0;
-    if (!m->err) return HV_OK;
     CUDA_TRY(cudaSetDevice(m->device));
-    CUDA_TRY(cudaMemcpy(code, m->err, sizeof(int), cudaMemcpyDeviceToHost));
-    if (*code) CUDA_TRY(cudaMemset(m->err, 0, sizeof(int)));
+    for (int i = 0; i < 2; ++i) {
+        if (!m->ws[i].err) continue;
+        int c = 0;
+        CUDA_TRY(cudaMemcpy(&c, m->ws[i].err, sizeof(int), cudaMemcpyDeviceToHost));
+        if (c) {
+            CUDA_TRY(cudaMemset(m->ws[i].err, 0, sizeof(int)));
+            if (!*code) *code = c;
+        }
+    }
     return HV_OK;
 }
 

@@ -130,7 +130,7 @@ def test_host_entry_matches_device_entry(cuda):
     from heatvit_b200.engine import Engine
     params = synth.config_params(synth.SEED, pruned=True)
     eng = Engine(params)
-    n = 1400                                                   # chunks of 256, 1024 and 120 images
+    n = 1400                                                   # chunks of 512, 512 and 376 images, two workspaces
     imgs = synth.baseline_images(synth.SEED, n, first=77)
     dev = eng.infer(torch.from_numpy(imgs).cuda())
     ns = eng.num_selectors
