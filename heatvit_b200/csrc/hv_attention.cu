@@ -7,7 +7,7 @@
 //   ctx   = requant(prob(uint8)·V, prob_scale + q, context_out, 8)
 // written straight into the head-concatenated layout (layout.py:132-155).
 //
-// One CTA (16 warps) per (image, head), query rows in tiles of 128:
+// Persistent CTAs (16 warps) walk (image, head) items, query rows in tiles of 128:
 //   1. K, V and each Q tile are staged in shared memory with 16-byte copies in
 //      the no-swizzle canonical layout (hv_tc05.cuh).  K and Q are K-major
 //      operands; V is the same byte layout read as an MN-major B operand
@@ -25,6 +25,8 @@
 //      into TMEM columns [0, 64), then requantised in 16-column pieces per part
 //      and written out.
 // TMEM: 256 columns per CTA; shared memory is padded so two CTAs share an SM.
+#include <algorithm>
+
 #include "hv_internal.cuh"
 #include "hv_tc05.cuh"
 
@@ -94,7 +96,8 @@ template <bool FAST, class CFG>
 __global__ void __launch_bounds__(CFG::THREADS) attention_tc_kernel(const int8_t *__restrict__ qkv,
                                                                const int32_t *__restrict__ offsets,
                                                                int8_t *__restrict__ ctx, AttnParams p,
-                                                               int *__restrict__ err, int np_lo, int np_hi) {
+                                                               int *__restrict__ err, int items, int np_lo,
+                                                               int np_hi) {
     extern __shared__ __align__(1024) uint8_t smem[];
     uint8_t *sK = smem + CFG::OFF_K;
     uint8_t *sV = smem + CFG::OFF_V;
@@ -105,12 +108,6 @@ __global__ void __launch_bounds__(CFG::THREADS) attention_tc_kernel(const int8_t
     uint32_t *tmem_slot = (uint32_t *)(smem + CFG::OFF_BAR + 8);
     volatile int *abort_flag = (volatile int *)(smem + CFG::OFF_BAR + 12);
 
-    const int img = blockIdx.x, head = blockIdx.y;
-    const int row0 = offsets[img];
-    const int n = offsets[img + 1] - row0;
-    if (n <= 0) return;
-    const int np = (n + 31) & ~31;
-    if (np <= np_lo || np > np_hi) return;  // the other CTA shape takes this image
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int quad = warp & 3, part = warp >> 2;
     const int lrow = quad * 32 + lane;  // tile row = TMEM lane
@@ -124,6 +121,21 @@ __global__ void __launch_bounds__(CFG::THREADS) attention_tc_kernel(const int8_t
         *abort_flag = 0;
         tc05::fence_mbar_init();
     }
+    tc05::fence_before();
+    __syncthreads();
+    tc05::fence_after();
+    const uint32_t tbase = *tmem_slot;
+    const uint32_t lane_addr = tbase + ((uint32_t)(quad * 32) << 16);
+    uint32_t phase = 0;
+
+    // Persistent: the CTA walks (image, head) items; images of the other CTA shape
+    // are skipped (a CTA-uniform test).
+    for (int item = blockIdx.x; item < items && !*abort_flag; item += gridDim.x) {
+    const int img = item / 3, head = item - img * 3;
+    const int row0 = offsets[img];
+    const int n = offsets[img + 1] - row0;
+    const int np = (n + 31) & ~31;
+    if (n <= 0 || np <= np_lo || np > np_hi) continue;
     // K and V rows (zero beyond n up to np), both in the K-major byte layout.
     for (int c = tid; c < np * 8; c += CFG::THREADS) {
         const int r = c >> 3, ch = c & 3, isv = (c >> 2) & 1;
@@ -131,14 +143,8 @@ __global__ void __launch_bounds__(CFG::THREADS) attention_tc_kernel(const int8_t
         if (r < n) kv = *(const int4 *)(qkv + (size_t)(row0 + r) * 576 + 192 * (1 + isv) + head * 64 + ch * 16);
         *(int4 *)((isv ? sV : sK) + tc05::kmajor_offset(r, ch * 16, 64)) = kv;
     }
-    tc05::fence_before();
-    __syncthreads();
-    tc05::fence_after();
-    const uint32_t tbase = *tmem_slot;
-    const uint32_t lane_addr = tbase + ((uint32_t)(quad * 32) << 16);
     const uint32_t sbo_np = (uint32_t)(np / 16) * 128;
     const int nchunks = np >> 4;  // 16-column chunks
-    uint32_t phase = 0;
 
     for (int t = 0; t * 128 < n; ++t) {
         // ---- Q tile ------------------------------------------------------------
@@ -279,6 +285,7 @@ __global__ void __launch_bounds__(CFG::THREADS) attention_tc_kernel(const int8_t
         tc05::fence_before();
         __syncthreads();
     }
+    }  // items
 
     if (*abort_flag) {
         if (tid == 0) atomicExch(err, 1);
@@ -309,22 +316,24 @@ AttnParams make_attn(int qkv_out_scale, int score_scale, int prob_scale, int con
 }
 
 cudaError_t launch_attention(const int8_t *qkv, const int32_t *offsets, int images, int8_t *ctx,
-                             const AttnParams &p, int may_be_short, int *err, cudaStream_t st) {
+                             const AttnParams &p, int may_be_short, int sms, int *err, cudaStream_t st) {
     if (images <= 0) return cudaSuccess;
+    const int items = images * 3;
     // Images of up to 128 tokens (np <= 128) go to the small shape when any may exist.
     if (may_be_short) {
         auto ks = p.fast ? attention_tc_kernel<true, AttnSmall> : attention_tc_kernel<false, AttnSmall>;
         cudaError_t e = cudaFuncSetAttribute(ks, cudaFuncAttributeMaxDynamicSharedMemorySize, AttnSmall::SMEM);
         if (e != cudaSuccess) return e;
-        ks<<<dim3(images, 3), AttnSmall::THREADS, AttnSmall::SMEM, st>>>(qkv, offsets, ctx, p, err, 0, 128);
+        ks<<<std::min(items, sms * 4), AttnSmall::THREADS, AttnSmall::SMEM, st>>>(qkv, offsets, ctx, p, err, items, 0,
+                                                                                128);
         e = cudaGetLastError();
         if (e != cudaSuccess) return e;
     }
     auto kl = p.fast ? attention_tc_kernel<true, AttnLarge> : attention_tc_kernel<false, AttnLarge>;
     cudaError_t e = cudaFuncSetAttribute(kl, cudaFuncAttributeMaxDynamicSharedMemorySize, AttnLarge::SMEM);
     if (e != cudaSuccess) return e;
-    kl<<<dim3(images, 3), AttnLarge::THREADS, AttnLarge::SMEM, st>>>(qkv, offsets, ctx, p, err,
-                                                                     may_be_short ? 128 : 0, AttnLarge::NPMAX);
+    kl<<<std::min(items, sms * 2), AttnLarge::THREADS, AttnLarge::SMEM, st>>>(qkv, offsets, ctx, p, err, items,
+                                                                              may_be_short ? 128 : 0, AttnLarge::NPMAX);
     return cudaGetLastError();
 }
 

@@ -58,7 +58,7 @@ cudaError_t gelu_table_window(int32_t qmax, int sh_out, int *d_mm, int32_t *wlo,
 cudaError_t launch_gelu_table_fill(int8_t *tab, int32_t wlo, int32_t wn, int sh_out, cudaStream_t st);
 
 cudaError_t launch_attention(const int8_t *qkv, const int32_t *offsets, int images, int8_t *ctx,
-                             const AttnParams &p, int may_be_short, int *err, cudaStream_t st);
+                             const AttnParams &p, int may_be_short, int sms, int *err, cudaStream_t st);
 
 // Device-resident selector weights and constants.
 struct SelParams {

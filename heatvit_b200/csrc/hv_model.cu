@@ -354,7 +354,7 @@ int run_block(hv_model *m, int b, int images, const int32_t *off, int may_be_sho
     }
     {
         Prof pr(m, HV_STAGE_ATTN, st);
-        CUDA_TRY(launch_attention(m->QKV, off, images, m->CTX, d.attn, may_be_short, m->err, st));
+        CUDA_TRY(launch_attention(m->QKV, off, images, m->CTX, d.attn, may_be_short, m->sms, m->err, st));
         pr.end(st, rows_dev, 0);
     }
     {
