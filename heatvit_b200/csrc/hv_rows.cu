@@ -285,15 +285,24 @@ __device__ __forceinline__ int64_t shfl64(int64_t v, int src) {
 // (one row per lane instead of eight lanes per row).  Phase 3: the sub-passes
 // again, each 8-lane group taking its row's constants from the owning lane.
 template <bool SPLIT, bool OUT32>
-__global__ void __launch_bounds__(256) ln_kernel(const int8_t *x, int8_t *out, int rows_max, const int32_t *rows_dev,
+__global__ void __launch_bounds__(256, 3) ln_kernel(const int8_t *x, int8_t *out, int rows_max, const int32_t *rows_dev,
                                                  LnParams p, uint8_t *negvar_row, const int32_t *offsets,
                                                  int images, uint8_t *warn) {
     const int rows = rows_dev ? *rows_dev : rows_max;
     const int lane = threadIdx.x & 31, sub = lane & 7, grp = lane >> 3;
     const int warps = (gridDim.x * blockDim.x) >> 5;
     const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-    int32_t gam[24], bet[24];
-    ln_lane_consts<OUT32>(p, sub, gam, bet);
+    // gamma and the aligned beta term per channel, in shared memory (lane stride 25
+    // words: the 8 lanes of a row group hit distinct banks)
+    __shared__ int32_t s_gam[8 * 25], s_bet[8 * 25];
+    for (int c = threadIdx.x; c < 192; c += blockDim.x) {
+        const int slot = (c / 24) * 25 + c % 24;
+        s_gam[slot] = p.gamma[c];
+        const int32_t b = p.beta[c];
+        s_bet[slot] = OUT32 ? b * (1 << p.sh_b) : b;
+    }
+    __syncthreads();
+    const int32_t *gam = s_gam + sub * 25, *bet = s_bet + sub * 25;
     for (int base = warp * 32; base < rows; base += warps * 32) {
         int32_t my_s = 0;
         int64_t my_s2 = 0;
