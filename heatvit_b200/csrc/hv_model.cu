@@ -112,6 +112,22 @@ struct Workspace {
     int32_t *off[2] = {nullptr, nullptr}, *counts = nullptr;
     uint8_t *pkg[2] = {nullptr, nullptr}, *warn = nullptr;
     int *err = nullptr;
+    // outputs of graph-replayed batches (copied to the caller's buffers after the replay)
+    int32_t *o_logits = nullptr, *o_tc = nullptr;
+    hv_selector_summary *o_sum = nullptr;
+    uint8_t *o_warn = nullptr;
+};
+
+// A captured inference (hv_infer_batch / one hv_infer_host chunk) and what it was
+// captured for: input, batch, workspace and output buffers.
+struct GraphEntry {
+    cudaGraphExec_t exec = nullptr;
+    const int8_t *img = nullptr;
+    int batch = 0, ws = 0;
+    int32_t *lg = nullptr, *tc = nullptr;
+    hv_selector_summary *sum = nullptr;
+    uint8_t *warn = nullptr;
+    unsigned long long stamp = 0;
 };
 
 struct hv_model {
@@ -153,6 +169,12 @@ struct hv_model {
     hv_selector_summary *hsum = nullptr;
     uint8_t *hwarn = nullptr;
     cudaStream_t copy_stream = nullptr, compute_stream[2] = {nullptr, nullptr};
+    // CUDA graphs of whole inferences (HV_NO_GRAPH=1 launches kernel by kernel)
+    int use_graphs = 1;
+    GraphEntry graphs[6];
+    unsigned long long graph_clock = 0;
+    cudaStream_t graph_stream = nullptr;
+    cudaEvent_t ev_fork = nullptr, ev_join = nullptr;
     cudaEvent_t ev_in[2] = {nullptr, nullptr}, ev_done[2] = {nullptr, nullptr};
 
     // kernel timing (hv_profile_*)
@@ -227,7 +249,9 @@ int ensure_capacity(hv_model *m, int images, int i = 0) {
                      oCTX = take(rows * 192), oHID = take(rows * 768), oSTAGE = take(rows * 192),
                      oCLS = take((size_t)images * 192), oOff0 = take((size_t)(images + 1) * 4),
                      oOff1 = take((size_t)(images + 1) * 4), oCnt = take((size_t)images * 4), oPkg0 = take(images),
-                     oPkg1 = take(images), oWarn = take(((size_t)images + 3) & ~(size_t)3), oErr = take(16);
+                     oPkg1 = take(images), oWarn = take(((size_t)images + 3) & ~(size_t)3), oErr = take(16),
+                     oOL = take((size_t)images * HV_CLASSES * 4), oOT = take((size_t)images * (HV_MAX_SELECTORS + 1) * 4),
+                     oOS = take((size_t)images * HV_MAX_SELECTORS * sizeof(hv_selector_summary)), oOW = take(images);
         uint8_t *base = nullptr;
         if (cudaMalloc(&base, total) != cudaSuccess)
             return fail(HV_ERR_NOMEM, "cannot allocate %zu bytes of scratch", total);
@@ -247,6 +271,10 @@ int ensure_capacity(hv_model *m, int images, int i = 0) {
         w.pkg[1] = base + oPkg1;
         w.warn = base + oWarn;
         w.err = (int *)(base + oErr);
+        w.o_logits = (int32_t *)(base + oOL);
+        w.o_tc = (int32_t *)(base + oOT);
+        w.o_sum = (hv_selector_summary *)(base + oOS);
+        w.o_warn = base + oOW;
         if (cudaMemset(w.err, 0, 16) != cudaSuccess) return fail(HV_ERR_CUDA, "cannot clear the error word");
         w.cap = images;
     }
@@ -704,6 +732,46 @@ int pack_model(hv_model *m, const hv_params *P) {
 
 }  // namespace
 
+// Enqueue one inference on `st` (a non-default stream) as a CUDA graph: replay the
+// cached capture for the same input, batch, workspace and outputs, else capture
+// and instantiate one (the least recently used entry is replaced).  The kernels
+// read the live token counts from device memory, so a capture is valid for any
+// input contents.
+int run_graph(hv_model *m, const int8_t *img, int batch, int32_t *lg, int32_t *tc, hv_selector_summary *sum,
+              uint8_t *warn, int wsi, cudaStream_t st) {
+    GraphEntry *hit = nullptr, *victim = &m->graphs[0];
+    for (GraphEntry &g : m->graphs) {
+        if (g.exec && g.img == img && g.batch == batch && g.ws == wsi && g.lg == lg && g.tc == tc && g.sum == sum &&
+            g.warn == warn)
+            hit = &g;
+        if (!g.exec || g.stamp < victim->stamp) victim = &g;
+    }
+    if (!hit) {
+        int rc = ensure_capacity(m, batch, wsi);  // allocations stay outside the capture
+        if (rc) return rc;
+        cudaGraph_t graph = nullptr;
+        CUDA_TRY(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
+        rc = infer_impl(m, img, batch, lg, tc, sum, warn, nullptr, nullptr, st, wsi);
+        const cudaError_t ce = cudaStreamEndCapture(st, &graph);
+        if (rc) {
+            if (graph) cudaGraphDestroy(graph);
+            return rc;
+        }
+        if (ce != cudaSuccess) return fail(HV_ERR_CUDA, "graph capture: %s", cudaGetErrorString(ce));
+        cudaGraphExec_t exec = nullptr;
+        const cudaError_t ie = cudaGraphInstantiate(&exec, graph, 0);
+        cudaGraphDestroy(graph);
+        if (ie != cudaSuccess) return fail(HV_ERR_CUDA, "graph instantiate: %s", cudaGetErrorString(ie));
+        if (victim->exec) cudaGraphExecDestroy(victim->exec);
+        *victim = GraphEntry{exec, img, batch, wsi, lg, tc, sum, warn, 0};
+        hit = victim;
+    }
+    hit->stamp = ++m->graph_clock;
+    use_workspace(m, wsi);
+    CUDA_TRY(cudaGraphLaunch(hit->exec, st));
+    return HV_OK;
+}
+
 // =============================================================================
 // C ABI
 // =============================================================================
@@ -725,6 +793,8 @@ int hv_model_create(const hv_params *params, int device, hv_model **out) {
     {
         const char *t = getenv("HV_GEMM_TILED");
         m->persistent = (t && t[0] == '1') ? 0 : 1;
+        const char *g = getenv("HV_NO_GRAPH");
+        m->use_graphs = (g && g[0] == '1') ? 0 : 1;
     }
     int rc = pack_model(m, params);
     if (rc) {
@@ -738,6 +808,11 @@ int hv_model_create(const hv_params *params, int device, hv_model **out) {
 int hv_model_destroy(hv_model *m) {
     if (!m) return HV_OK;
     cudaSetDevice(m->device);
+    for (GraphEntry &g : m->graphs)
+        if (g.exec) cudaGraphExecDestroy(g.exec);
+    if (m->graph_stream) cudaStreamDestroy(m->graph_stream);
+    if (m->ev_fork) cudaEventDestroy(m->ev_fork);
+    if (m->ev_join) cudaEventDestroy(m->ev_join);
     if (m->weights) cudaFree(m->weights);
     for (int i = 0; i < 2; ++i)
         if (m->ws[i].scratch) cudaFree(m->ws[i].scratch);
@@ -765,8 +840,36 @@ int hv_model_destroy(hv_model *m) {
 int hv_infer_batch(hv_model *m, const int8_t *d_images, int batch, int32_t *d_logits, int32_t *d_token_counts,
                    hv_selector_summary *d_summary, uint8_t *d_warnings, void *stream) {
     if (!m) return fail(HV_ERR_VALUE, "null model");
-    return infer_impl(m, d_images, batch, d_logits, d_token_counts, d_summary, d_warnings, nullptr, nullptr,
-                      (cudaStream_t)stream);
+    cudaStream_t st = (cudaStream_t)stream;
+    if (!m->use_graphs || m->prof_stage || batch <= 0 || !d_images || !d_logits)
+        return infer_impl(m, d_images, batch, d_logits, d_token_counts, d_summary, d_warnings, nullptr, nullptr, st);
+    // Replay on the model's own stream, ordered after and before the caller's work on
+    // `stream`; outputs go to workspace buffers and are copied out on `stream`.
+    CUDA_TRY(cudaSetDevice(m->device));
+    if (!m->graph_stream) {
+        CUDA_TRY(cudaStreamCreateWithFlags(&m->graph_stream, cudaStreamNonBlocking));
+        CUDA_TRY(cudaEventCreateWithFlags(&m->ev_fork, cudaEventDisableTiming));
+        CUDA_TRY(cudaEventCreateWithFlags(&m->ev_join, cudaEventDisableTiming));
+    }
+    int rc = ensure_capacity(m, batch, 0);
+    if (rc) return rc;
+    const Workspace &w = m->ws[0];
+    const int ns = m->used_sel;
+    CUDA_TRY(cudaEventRecord(m->ev_fork, st));
+    CUDA_TRY(cudaStreamWaitEvent(m->graph_stream, m->ev_fork, 0));
+    rc = run_graph(m, d_images, batch, w.o_logits, d_token_counts ? w.o_tc : nullptr, d_summary ? w.o_sum : nullptr,
+                   d_warnings ? w.o_warn : nullptr, 0, m->graph_stream);
+    if (rc) return rc;
+    CUDA_TRY(cudaEventRecord(m->ev_join, m->graph_stream));
+    CUDA_TRY(cudaStreamWaitEvent(st, m->ev_join, 0));
+    CUDA_TRY(cudaMemcpyAsync(d_logits, w.o_logits, (size_t)batch * HV_CLASSES * 4, cudaMemcpyDeviceToDevice, st));
+    if (d_token_counts)
+        CUDA_TRY(cudaMemcpyAsync(d_token_counts, w.o_tc, (size_t)batch * (ns + 1) * 4, cudaMemcpyDeviceToDevice, st));
+    if (d_summary && ns)
+        CUDA_TRY(cudaMemcpyAsync(d_summary, w.o_sum, (size_t)batch * ns * sizeof(hv_selector_summary),
+                                 cudaMemcpyDeviceToDevice, st));
+    if (d_warnings) CUDA_TRY(cudaMemcpyAsync(d_warnings, w.o_warn, (size_t)batch, cudaMemcpyDeviceToDevice, st));
+    return HV_OK;
 }
 
 int hv_infer_batch_checkpoints(hv_model *m, const int8_t *d_images, int batch, int32_t *d_logits,
@@ -872,8 +975,12 @@ int hv_infer_host(hv_model *m, const int8_t *h_images, int batch, int32_t *h_log
         int32_t *dtc = m->htc + (size_t)buf * m->host_cap * (HV_MAX_SELECTORS + 1);
         hv_selector_summary *dsum = m->hsum + (size_t)buf * m->host_cap * HV_MAX_SELECTORS;
         uint8_t *dw = m->hwarn + (size_t)buf * m->host_cap;
-        rc = infer_impl(m, m->himg[buf], cnt, dl, h_token_counts ? dtc : nullptr, h_summary ? dsum : nullptr,
-                        h_warnings ? dw : nullptr, nullptr, nullptr, cst, buf);
+        if (m->use_graphs && !m->prof_stage)
+            rc = run_graph(m, m->himg[buf], cnt, dl, h_token_counts ? dtc : nullptr, h_summary ? dsum : nullptr,
+                           h_warnings ? dw : nullptr, buf, cst);
+        else
+            rc = infer_impl(m, m->himg[buf], cnt, dl, h_token_counts ? dtc : nullptr, h_summary ? dsum : nullptr,
+                            h_warnings ? dw : nullptr, nullptr, nullptr, cst, buf);
         if (rc) return rc;
         CUDA_TRY(cudaEventRecord(m->ev_done[buf], cst));
         CUDA_TRY(cudaMemcpyAsync(m->pin_out + o_log + (size_t)first * HV_CLASSES * 4, dl, (size_t)cnt * HV_CLASSES * 4,
