@@ -121,6 +121,8 @@ __global__ void __launch_bounds__(CFG::THREADS) attention_tc_kernel(const int8_t
         *abort_flag = 0;
         tc05::fence_mbar_init();
     }
+    griddep_wait();  // QKV and the offsets come from earlier kernels
+    griddep_launch();
     tc05::fence_before();
     __syncthreads();
     tc05::fence_after();
@@ -324,17 +326,15 @@ cudaError_t launch_attention(const int8_t *qkv, const int32_t *offsets, int imag
         auto ks = p.fast ? attention_tc_kernel<true, AttnSmall> : attention_tc_kernel<false, AttnSmall>;
         cudaError_t e = cudaFuncSetAttribute(ks, cudaFuncAttributeMaxDynamicSharedMemorySize, AttnSmall::SMEM);
         if (e != cudaSuccess) return e;
-        ks<<<std::min(items, sms * 4), AttnSmall::THREADS, AttnSmall::SMEM, st>>>(qkv, offsets, ctx, p, err, items, 0,
-                                                                                128);
-        e = cudaGetLastError();
+        e = launch_pdl(ks, dim3(std::min(items, sms * 4)), dim3(AttnSmall::THREADS), AttnSmall::SMEM, st, qkv, offsets,
+                       ctx, p, err, items, 0, 128);
         if (e != cudaSuccess) return e;
     }
     auto kl = p.fast ? attention_tc_kernel<true, AttnLarge> : attention_tc_kernel<false, AttnLarge>;
     cudaError_t e = cudaFuncSetAttribute(kl, cudaFuncAttributeMaxDynamicSharedMemorySize, AttnLarge::SMEM);
     if (e != cudaSuccess) return e;
-    kl<<<std::min(items, sms * 2), AttnLarge::THREADS, AttnLarge::SMEM, st>>>(qkv, offsets, ctx, p, err, items,
-                                                                              may_be_short ? 128 : 0, AttnLarge::NPMAX);
-    return cudaGetLastError();
+    return launch_pdl(kl, dim3(std::min(items, sms * 2)), dim3(AttnLarge::THREADS), AttnLarge::SMEM, st, qkv, offsets,
+                      ctx, p, err, items, may_be_short ? 128 : 0, AttnLarge::NPMAX);
 }
 
 }  // namespace hv

@@ -68,6 +68,8 @@ __device__ __forceinline__ int32_t byte_of(const uint32_t (&w)[8], int j) {
 
 template <int EPI, bool U8, bool FAST, int BN>
 __global__ void __launch_bounds__(THREADS) tc_gemm_kernel(GemmArgs g, int *err) {
+    griddep_wait();
+    griddep_launch();
     using L = Layout<BN>;
     extern __shared__ __align__(1024) uint8_t smem[];
     int32_t *sbias = (int32_t *)(smem + L::OFF_BIAS);
@@ -288,8 +290,7 @@ cudaError_t launch_t(const GemmArgs &g, int m_max, int *err, cudaStream_t st) {
     if (e != cudaSuccess) return e;
     dim3 grid((g.n + BN - 1) / BN, (m_max + BM - 1) / BM);
     if (grid.x == 0 || grid.y == 0) return cudaSuccess;
-    kern<<<grid, THREADS, smem, st>>>(g, err);
-    return cudaGetLastError();
+    return launch_pdl(kern, grid, dim3(THREADS), smem, st, g, err);
 }
 
 template <int EPI, bool U8, bool FAST>

@@ -20,6 +20,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 #include "hv_fixed.cuh"
+#include "hv_launch.cuh"
 
 namespace hv {
 

@@ -103,8 +103,6 @@ __global__ void __launch_bounds__(PT_THREADS, 1) tcp_gemm_kernel(GemmArgs g, int
     volatile int *abortf = (volatile int *)(tslot + 1);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int m_lim = g.m_dev ? *g.m_dev : g.m_host;
-    const int mtiles = (m_lim + 127) / 128;
 
     // ---- prologue: resident weights and bias, barriers, TMEM ---------------------
     if (warp == 0) {
@@ -138,6 +136,12 @@ __global__ void __launch_bounds__(PT_THREADS, 1) tcp_gemm_kernel(GemmArgs g, int
     if (EPI == EPI_GELU && L::TABB > 0)
         for (int i = tid; i < g.epi.gtab_n; i += PT_THREADS) stab[i] = g.epi.gtab[i];
     asm volatile("cp.async.wait_all;\n" ::: "memory");
+    // Everything above touches only weights and on-chip state; from here on the
+    // kernel reads activations and row counts that the previous kernel writes.
+    griddep_wait();
+    griddep_launch();
+    const int m_lim = g.m_dev ? *g.m_dev : g.m_host;
+    const int mtiles = (m_lim + 127) / 128;
     tc05::fence_proxy_async();
     tc05::fence_before();
     __syncthreads();
@@ -338,8 +342,7 @@ cudaError_t launch_p(const GemmArgs &g, int m_max, int *err, int sms, cudaStream
     const int tiles = (m_max + 127) / 128;
     const int grid = tiles < sms ? tiles : sms;
     if (grid <= 0) return cudaSuccess;
-    kern<<<grid, PT_THREADS, smem, st>>>(g, err);
-    return cudaGetLastError();
+    return launch_pdl(kern, dim3(grid), dim3(PT_THREADS), smem, st, g, err);
 }
 
 // The (epilogue, K, N) combinations the model uses: QKV (I8, 192 -> 576), proj and

@@ -285,6 +285,8 @@ int ensure_capacity(hv_model *m, int images, int i = 0) {
 // ---- small pipeline kernels ----------------------------------------------------
 __global__ void init_batch_kernel(int images, int32_t *off, uint8_t *pkg, uint8_t *warn, int32_t *tc, int tc_stride,
                                   int8_t *x, const int8_t *cls_row) {
+    griddep_wait();  // the previous inference may still read these buffers
+    griddep_launch();
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i <= images; i += gridDim.x * blockDim.x) {
         off[i] = i * HV_TOKENS;
         if (i < images) {
@@ -458,8 +460,8 @@ int infer_impl(hv_model *m, const int8_t *d_images, int batch, int32_t *d_logits
     const int tc_stride = ns + 1;
     if (d_ckpt_rows) CUDA_TRY(cudaMemsetAsync(d_ckpt_rows, 0, sizeof(int32_t) * (size_t)batch * HV_CKPT_SLOTS, st));
     int cur = 0;
-    init_batch_kernel<<<std::min(148 * 4, (batch * 12 + 255) / 256 + 1), 256, 0, st>>>(
-        batch, m->off[0], m->pkg[0], m->warn, d_tc, tc_stride, m->X, m->w<int8_t>(m->cls_row));
+    CUDA_TRY(launch_pdl(init_batch_kernel, dim3(std::min(148 * 4, (batch * 12 + 255) / 256 + 1)), dim3(256), 0, st, 
+        batch, m->off[0], m->pkg[0], m->warn, d_tc, tc_stride, m->X, m->w<int8_t>(m->cls_row)));
     CUDA_TRY(cudaGetLastError());
     {
         Prof pr(m, HV_STAGE_PATCH, st);
@@ -1227,8 +1229,8 @@ int hv_patch_embedding(hv_model *m, const int8_t *d_images, int batch, int8_t *d
     int rc = ensure_capacity(m, batch);
     if (rc) return rc;
     cudaStream_t st = (cudaStream_t)stream;
-    init_batch_kernel<<<std::min(148 * 4, (batch * 12 + 255) / 256 + 1), 256, 0, st>>>(
-        batch, m->off[0], m->pkg[0], m->warn, nullptr, 0, d_tokens, m->w<int8_t>(m->cls_row));
+    CUDA_TRY(launch_pdl(init_batch_kernel, dim3(std::min(148 * 4, (batch * 12 + 255) / 256 + 1)), dim3(256), 0, st, 
+        batch, m->off[0], m->pkg[0], m->warn, nullptr, 0, d_tokens, m->w<int8_t>(m->cls_row)));
     CUDA_TRY(cudaGetLastError());
     return run_patch(m, d_images, batch, d_tokens, st);
 }

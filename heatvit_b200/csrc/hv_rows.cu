@@ -288,7 +288,6 @@ template <bool SPLIT, bool OUT32>
 __global__ void __launch_bounds__(256, 3) ln_kernel(const int8_t *x, int8_t *out, int rows_max, const int32_t *rows_dev,
                                                  LnParams p, uint8_t *negvar_row, const int32_t *offsets,
                                                  int images, uint8_t *warn) {
-    const int rows = rows_dev ? *rows_dev : rows_max;
     const int lane = threadIdx.x & 31, sub = lane & 7, grp = lane >> 3;
     const int warps = (gridDim.x * blockDim.x) >> 5;
     const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
@@ -303,6 +302,9 @@ __global__ void __launch_bounds__(256, 3) ln_kernel(const int8_t *x, int8_t *out
     }
     __syncthreads();
     const int32_t *gam = s_gam + sub * 25, *bet = s_bet + sub * 25;
+    griddep_wait();  // rows and their count come from earlier kernels
+    griddep_launch();
+    const int rows = rows_dev ? *rows_dev : rows_max;
     for (int base = warp * 32; base < rows; base += warps * 32) {
         int32_t my_s = 0;
         int64_t my_s2 = 0;
@@ -402,6 +404,8 @@ __global__ void __launch_bounds__(256, 3) ln_kernel(const int8_t *x, int8_t *out
 template <bool SPLIT, bool OUT32>
 __global__ void __launch_bounds__(256) ln_cls_kernel(const int8_t *x, const int32_t *offsets, int images, int8_t *out,
                                                      LnParams p, uint8_t *warn) {
+    griddep_wait();
+    griddep_launch();
     const int lane = threadIdx.x & 31, sub = lane & 7, grp = lane >> 3;
     const int i = ((blockIdx.x * blockDim.x + threadIdx.x) >> 5) * 4 + grp;
     const bool active = i < images;
@@ -555,8 +559,8 @@ cudaError_t launch_layernorm(const int8_t *x, int8_t *out, int rows_max, const i
     if (blocks > 148 * 16) blocks = 148 * 16;
     auto kern = p.split ? (p.out32 ? ln_kernel<true, true> : ln_kernel<true, false>)
                         : (p.out32 ? ln_kernel<false, true> : ln_kernel<false, false>);
-    kern<<<blocks, 256, 0, st>>>(x, out, rows_max, rows_dev, p, negvar_row, offsets, images, warn);
-    return cudaGetLastError();
+    return launch_pdl(kern, dim3(blocks), dim3(256), 0, st, x, out, rows_max, rows_dev, p, negvar_row, offsets, images,
+                      warn);
 }
 
 cudaError_t launch_layernorm_cls(const int8_t *x, const int32_t *offsets, int images, int8_t *out,
@@ -564,8 +568,7 @@ cudaError_t launch_layernorm_cls(const int8_t *x, const int32_t *offsets, int im
     if (images <= 0) return cudaSuccess;
     auto kern = p.split ? (p.out32 ? ln_cls_kernel<true, true> : ln_cls_kernel<true, false>)
                         : (p.out32 ? ln_cls_kernel<false, true> : ln_cls_kernel<false, false>);
-    kern<<<(images + 31) / 32, 256, 0, st>>>(x, offsets, images, out, p, warn);
-    return cudaGetLastError();
+    return launch_pdl(kern, dim3((images + 31) / 32), dim3(256), 0, st, x, offsets, images, out, p, warn);
 }
 
 cudaError_t launch_softmax_rows(const int32_t *x, const int32_t *offsets, int rows, int mode, void *out,

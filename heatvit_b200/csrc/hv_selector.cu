@@ -86,6 +86,8 @@ __global__ void __launch_bounds__(THREADS) selector_kernel(
     SelParams p, int8_t *__restrict__ stage, int32_t *__restrict__ counts_out, uint8_t *__restrict__ pkg_out,
     hv_selector_summary *__restrict__ summary, int sum_stride, uint8_t *__restrict__ warn,
     int32_t *__restrict__ token_counts, int tc_stride, int tc_col, SelDebug dbg) {
+    griddep_wait();
+    griddep_launch();
     extern __shared__ __align__(16) uint8_t smem[];
     int8_t *tok = (int8_t *)(smem + OFF_TOK);
     int8_t *local = (int8_t *)(smem + OFF_LOCAL);
@@ -353,6 +355,8 @@ __global__ void __launch_bounds__(THREADS) selector_kernel(
 __global__ void __launch_bounds__(256) pack_kernel(const int8_t *__restrict__ stage,
                                                    const int32_t *__restrict__ counts, int images,
                                                    int8_t *__restrict__ x, int32_t *__restrict__ offsets_out) {
+    griddep_wait();
+    griddep_launch();
     __shared__ int part[8];
     const int img = blockIdx.x, tid = threadIdx.x;
     int s = 0;
@@ -384,16 +388,14 @@ cudaError_t launch_selector(const int8_t *x, const int32_t *offsets, const uint8
     cudaError_t e = cudaFuncSetAttribute(selector_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
     if (e != cudaSuccess) return e;
     SelDebug d = dbg ? *dbg : SelDebug{nullptr, nullptr, nullptr, nullptr, nullptr, nullptr};
-    selector_kernel<<<images, THREADS, SMEM_BYTES, st>>>(x, offsets, pkg_in, p, stage, counts_out, pkg_out, summary,
-                                                        sum_stride, warn, token_counts, tc_stride, tc_col, d);
-    return cudaGetLastError();
+    return launch_pdl(selector_kernel, dim3(images), dim3(THREADS), SMEM_BYTES, st, x, offsets, pkg_in, p, stage,
+                      counts_out, pkg_out, summary, sum_stride, warn, token_counts, tc_stride, tc_col, d);
 }
 
 cudaError_t launch_pack(const int8_t *stage, const int32_t *counts, int images, int8_t *x, int32_t *offsets_out,
                         cudaStream_t st) {
     if (images <= 0) return cudaSuccess;
-    pack_kernel<<<images, 256, 0, st>>>(stage, counts, images, x, offsets_out);
-    return cudaGetLastError();
+    return launch_pdl(pack_kernel, dim3(images), dim3(256), 0, st, stage, counts, images, x, offsets_out);
 }
 
 }  // namespace hv
