@@ -242,6 +242,15 @@ __global__ void __launch_bounds__(PT_THREADS, 1) tcp_gemm_kernel(GemmArgs g, int
                 orow = (size_t)img * 197 + 1 + pidx;
             }
             bool stop = false;
+            // Residual rows (N = 192: one chunk per tile): this thread's 96 bytes are
+            // requested before the accumulator wait, so their latency overlaps the MMA.
+            uint4 rpre[6];
+            if (EPI == EPI_I8_RES && L::NCH == 1) {
+#pragma unroll
+                for (int i = 0; i < 6; ++i)
+                    rpre[i] = valid ? ((const uint4 *)(g.epi.res + orow * g.ldo + half * (BN / 2)))[i]
+                                    : make_uint4(0, 0, 0, 0);
+            }
             for (int c = 0; c < L::NCH; ++c, ++a) {
                 const int tb = a & 1;
                 if (!tc05::mbar_wait(&accf[tb], (a >> 1) & 1u, PT_WAIT)) {
@@ -250,13 +259,18 @@ __global__ void __launch_bounds__(PT_THREADS, 1) tcp_gemm_kernel(GemmArgs g, int
                     break;
                 }
                 tc05::fence_after();
-#pragma unroll 1
+                // unrolled for the residual epilogue only (its prefetched registers need
+                // compile-time indices); the others stay rolled to keep registers low
+#pragma unroll (EPI == EPI_I8_RES ? BN / 64 : 1)
                 for (int cc = 0; cc < BN / 64; ++cc) {
                     const int col0 = half * (BN / 2) + cc * 32;  // chunk-local column of v[0]
                     const int gcol0 = c * BN + col0;
                     // residual / positional bytes first, so their latency overlaps the TMEM read
                     uint4 r0 = make_uint4(0, 0, 0, 0), r1 = r0;
-                    if (EPI == EPI_I8_RES && valid) {
+                    if (EPI == EPI_I8_RES && L::NCH == 1) {
+                        r0 = rpre[2 * cc];
+                        r1 = rpre[2 * cc + 1];
+                    } else if (EPI == EPI_I8_RES && valid) {
                         const uint4 *r = (const uint4 *)(g.epi.res + orow * g.ldo + gcol0);
                         r0 = r[0];
                         r1 = r[1];
