@@ -17,6 +17,7 @@
 // A may be int8 or uint8 (P·V in attention uses uint8 probabilities;
 // gemm.py:81-84).  The pre-bias accumulator fits int32 for K <= 131071.
 #pragma once
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 #include "hv_fixed.cuh"
@@ -61,6 +62,9 @@ struct ASrc {
 
 struct GemmArgs {
     ASrc a;
+    // TMA descriptor of A (row-major int8 [rows][k]) for the persistent kernel, or
+    // nullptr for cp.async loads (the patch GEMM gathers A from images)
+    const CUtensorMap *tma;
     const int8_t *bt;         // [Npad][K] K-major weights (Npad: see launch_gemm)
     int n, k;                 // logical N (stores guarded), K multiple of 64
     int m_host;               // row count when m_dev == nullptr
@@ -93,6 +97,9 @@ cudaError_t launch_gemm(const GemmArgs &g, int epi, int a_unsigned, int m_max, i
 // The weights stay resident in shared memory; `bt` needs exactly n rows.
 // `sms` is the device's SM count (one CTA per SM).
 bool gemm_persistent_supported(int epi, int n, int k);
+// Tensor map of a row-major int8 A operand [rows][k] (k a multiple of 16) read as
+// 16-byte x 128-row boxes; rows past `rows` read as zero.  Returns 0 on success.
+int make_tmap_a(CUtensorMap *map, const void *base, int k, int rows);
 cudaError_t launch_gemm_persistent(const GemmArgs &g, int epi, int m_max, int *err, int sms, cudaStream_t st);
 
 }  // namespace hv

@@ -20,6 +20,9 @@
 // For K = 192 one stage holds the whole A tile and feeds every 192-column
 // chunk of N; for K = 768 (N = 192) A streams through 4 stages of 64 columns.
 // Every mbarrier wait is bounded; a timeout sets the model's error word.
+#include <cudaTypedefs.h>
+#include <string.h>
+
 #include "hv_gemm.cuh"
 #include "hv_tc05.cuh"
 
@@ -60,6 +63,18 @@ struct PLayout {
 __device__ __forceinline__ void cp_async16(uint32_t saddr, const void *g, int src_bytes) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(saddr), "l"(g), "r"(src_bytes) : "memory");
 }
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *mbar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(tc05::smem_u32(mbar)), "r"(bytes)
+                 : "memory");
+}
+// One 16-byte x 128-row box of A at (x = k byte, y = row) into shared memory (no multicast).
+__device__ __forceinline__ void tma_load_a(uint32_t dst, const CUtensorMap *map, int x, int y, uint64_t *mbar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];\n" ::
+            "r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(tc05::smem_u32(mbar))
+        : "memory");
+}
+
 __device__ __forceinline__ void cp_arrive_noinc(uint64_t *mbar) {
     asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];\n" ::"r"(tc05::smem_u32(mbar)) : "memory");
 }
@@ -88,7 +103,8 @@ __device__ __forceinline__ int32_t epi_elem(int32_t acc, int32_t bb, int32_t ax,
 }
 
 template <int EPI, bool FAST, int KDIM, int N>
-__global__ void __launch_bounds__(PT_THREADS, 1) tcp_gemm_kernel(GemmArgs g, int *err) {
+__global__ void __launch_bounds__(PT_THREADS, 1) tcp_gemm_kernel(GemmArgs g, int *err,
+                                                                  const __grid_constant__ CUtensorMap tmA, int use_tma) {
     using L = PLayout<KDIM, N>;
     extern __shared__ __align__(1024) uint8_t smem[];
     uint8_t *sB = smem + L::OFF_B;
@@ -111,7 +127,7 @@ __global__ void __launch_bounds__(PT_THREADS, 1) tcp_gemm_kernel(GemmArgs g, int
     }
     if (tid == 0) {
         for (int s = 0; s < L::S; ++s) {
-            tc05::mbar_init(&full[s], 32 * PT_PROD);
+            tc05::mbar_init(&full[s], use_tma ? 1 : 32 * PT_PROD);
             tc05::mbar_init(&empty[s], 1);
         }
         for (int b = 0; b < 2; ++b) {
@@ -149,7 +165,29 @@ __global__ void __launch_bounds__(PT_THREADS, 1) tcp_gemm_kernel(GemmArgs g, int
     const uint32_t tbase = *tslot;
     const uint8_t *abase = (const uint8_t *)g.a.ptr;
 
-    if (warp < PT_PROD) {
+    if (warp < PT_PROD && use_tma) {
+        // ---- producer (TMA): one thread; stage = AK/16 boxes of [128 rows][16 bytes],
+        // strip kc at byte offset kc * 2048 (core matrices: LBO 2048, SBO 128)
+        if (tid == 0) {
+            uint32_t q = 0;
+            bool ok = true;
+            for (int mt = blockIdx.x; mt < mtiles && ok && !*abortf; mt += gridDim.x) {
+                for (int ks = 0; ks < L::KST; ++ks, ++q) {
+                    const int s = q % L::S;
+                    if (q >= (uint32_t)L::S && !tc05::mbar_wait(&empty[s], ((q / L::S) - 1) & 1u, PT_WAIT)) {
+                        ok = false;
+                        break;
+                    }
+                    const uint32_t dst = tc05::smem_u32(sA + s * L::A_STAGE);
+                    mbar_expect_tx(&full[s], 128u * L::AK);
+#pragma unroll
+                    for (int kc = 0; kc < L::AK / 16; ++kc)
+                        tma_load_a(dst + kc * 2048, &tmA, ks * L::AK + kc * 16, mt * 128, &full[s]);
+                }
+            }
+            if (!ok) *abortf = 1;
+        }
+    } else if (warp < PT_PROD) {
         // ---- producer ------------------------------------------------------------
         uint32_t q = 0;
         for (int mt = blockIdx.x; mt < mtiles && !*abortf; mt += gridDim.x) {
@@ -208,9 +246,12 @@ __global__ void __launch_bounds__(PT_THREADS, 1) tcp_gemm_kernel(GemmArgs g, int
                         }
                         const uint32_t a0 = tc05::smem_u32(sA + s * L::A_STAGE);
                         const uint32_t b0 = tc05::smem_u32(sB) + c * BN * KDIM + ks * (L::AK / 16) * 128;
+                        // A: TMA strips (LBO 2048, SBO 128) or the cp.async canonical tile
+                        const uint32_t a_step = use_tma ? 4096u : 256u, a_lbo = use_tma ? 2048u : 128u,
+                                       a_sbo = use_tma ? 128u : 8u * L::AK;
 #pragma unroll
                         for (int j = 0; j < L::AK / 32; ++j)
-                            tc05::mma_i8_ss(d, tc05::smem_desc(a0 + j * 256, 128, 8 * L::AK),
+                            tc05::mma_i8_ss(d, tc05::smem_desc(a0 + j * a_step, a_lbo, a_sbo),
                                             tc05::smem_desc(b0 + j * 256, 128, 8 * KDIM), idesc, (ks | j) != 0);
                         if (L::KST > 1) tc05::commit(&empty[s]);
                     }
@@ -356,7 +397,10 @@ cudaError_t launch_p(const GemmArgs &g, int m_max, int *err, int sms, cudaStream
     const int tiles = (m_max + 127) / 128;
     const int grid = tiles < sms ? tiles : sms;
     if (grid <= 0) return cudaSuccess;
-    return launch_pdl(kern, dim3(grid), dim3(PT_THREADS), smem, st, g, err);
+    CUtensorMap tm;
+    if (g.tma) tm = *g.tma;
+    else memset(&tm, 0, sizeof(tm));
+    return launch_pdl(kern, dim3(grid), dim3(PT_THREADS), smem, st, g, err, tm, g.tma ? 1 : 0);
 }
 
 // The (epilogue, K, N) combinations the model uses: QKV (I8, 192 -> 576), proj and
@@ -403,6 +447,26 @@ cudaError_t launch_gemm_persistent(const GemmArgs &g, int epi, int m_max, int *e
         default:
             return cudaErrorInvalidValue;
     }
+}
+
+int make_tmap_a(CUtensorMap *map, const void *base, int k, int rows) {
+    static PFN_cuTensorMapEncodeTiled encode = nullptr;
+    if (!encode) {
+        void *fn = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess || !fn)
+            return 1;
+        encode = (PFN_cuTensorMapEncodeTiled)fn;
+    }
+    const cuuint64_t dims[2] = {(cuuint64_t)k, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)k};
+    const cuuint32_t box[2] = {16, 128};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(base), dims, strides, box, estr,
+                              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                              CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? 0 : 2;
 }
 
 }  // namespace hv

@@ -112,6 +112,9 @@ struct Workspace {
     int32_t *off[2] = {nullptr, nullptr}, *counts = nullptr;
     uint8_t *pkg[2] = {nullptr, nullptr}, *warn = nullptr;
     int *err = nullptr;
+    // TMA descriptors of the GEMM A operands LN, CTX ([rows][192]) and HID ([rows][768])
+    CUtensorMap tm_ln, tm_ctx, tm_hid;
+    int tm_ok = 0;
     // outputs of graph-replayed batches (copied to the caller's buffers after the replay)
     int32_t *o_logits = nullptr, *o_tc = nullptr;
     hv_selector_summary *o_sum = nullptr;
@@ -156,6 +159,7 @@ struct hv_model {
     int32_t *off[2] = {nullptr, nullptr}, *counts = nullptr;
     uint8_t *pkg[2] = {nullptr, nullptr}, *warn = nullptr;
     int *err = nullptr;  // device error word (bounded waits that gave up)
+    const CUtensorMap *tm_ln = nullptr, *tm_ctx = nullptr, *tm_hid = nullptr;  // nullptr: cp.async loads
     // host-pipeline staging
     int host_cap = 0;
     int8_t *himg[2] = {nullptr, nullptr};
@@ -228,6 +232,9 @@ void use_workspace(hv_model *m, int i) {
     m->pkg[1] = w.pkg[1];
     m->warn = w.warn;
     m->err = w.err;
+    m->tm_ln = w.tm_ok ? &w.tm_ln : nullptr;
+    m->tm_ctx = w.tm_ok ? &w.tm_ctx : nullptr;
+    m->tm_hid = w.tm_ok ? &w.tm_hid : nullptr;
 }
 
 // Workspace i holds at least `images` images; it becomes the current one.
@@ -276,6 +283,9 @@ int ensure_capacity(hv_model *m, int images, int i = 0) {
         w.o_sum = (hv_selector_summary *)(base + oOS);
         w.o_warn = base + oOW;
         if (cudaMemset(w.err, 0, 16) != cudaSuccess) return fail(HV_ERR_CUDA, "cannot clear the error word");
+        const int r = (int)rows;
+        w.tm_ok = make_tmap_a(&w.tm_ln, w.LN, 192, r) == 0 && make_tmap_a(&w.tm_ctx, w.CTX, 192, r) == 0 &&
+                  make_tmap_a(&w.tm_hid, w.HID, HV_FFN, r) == 0;
         w.cap = images;
     }
     use_workspace(m, i);
@@ -376,6 +386,7 @@ int run_block(hv_model *m, int b, int images, const int32_t *off, int may_be_sho
     {
         Prof pr(m, HV_STAGE_QKV, st);
         GemmArgs g = gemm_args(m->LN, 192, 0, m->w<int8_t>(d.wqkv), HV_QKV, 192, 0, rows_dev, m->QKV, HV_QKV);
+        g.tma = m->tm_ln;
         g.epi.bias = m->w<int32_t>(d.bqkv);
         g.epi.shift = d.qkv_shift;
         g.epi.bits_wide = d.qkv_wide;
@@ -390,6 +401,7 @@ int run_block(hv_model *m, int b, int images, const int32_t *off, int may_be_sho
     {
         Prof pr(m, HV_STAGE_PROJ, st);
         GemmArgs g = gemm_args(m->CTX, 192, 0, m->w<int8_t>(d.wproj), HV_EMBED, 192, 0, rows_dev, m->Y, HV_EMBED);
+        g.tma = m->tm_ctx;
         g.epi.bias = m->w<int32_t>(d.bproj);
         g.epi.shift = d.proj_shift;
         g.epi.bits_wide = d.proj_wide;
@@ -406,6 +418,7 @@ int run_block(hv_model *m, int b, int images, const int32_t *off, int may_be_sho
     {
         Prof pr(m, HV_STAGE_FC1, st);
         GemmArgs g = gemm_args(m->LN, 192, 0, m->w<int8_t>(d.w1), HV_FFN, 192, 0, rows_dev, m->HID, HV_FFN);
+        g.tma = m->tm_ln;
         g.epi.bias = m->w<int32_t>(d.b1);
         g.epi.bits_wide = d.fc1_wide;
         g.epi.gelu_sh_in = d.fc1_sh_in;
@@ -422,6 +435,7 @@ int run_block(hv_model *m, int b, int images, const int32_t *off, int may_be_sho
     {
         Prof pr(m, HV_STAGE_FC2, st);
         GemmArgs g = gemm_args(m->HID, HV_FFN, 0, m->w<int8_t>(d.w2), HV_EMBED, HV_FFN, 0, rows_dev, m->X, HV_EMBED);
+        g.tma = m->tm_hid;
         g.epi.bias = m->w<int32_t>(d.b2);
         g.epi.shift = d.fc2_shift;
         g.epi.bits_wide = d.fc2_wide;
