@@ -39,12 +39,13 @@ STAGE_MACS_PER_ROW = {"qkv": 192 * 576, "proj": 192 * 192, "fc1": 192 * 768, "fc
                       "patch": 768 * 192, "head": 192 * 1000}
 # Algorithmic HBM bytes per row for the row-wise kernels (int8 in + int8 out).
 STAGE_BYTES_PER_ROW = {"ln1": 384, "ln2": 384}
-# DRAM bytes (read + write) per row of one launch, from the committed ncu capture of a
-# full-size launch (block 1, 201,728 rows): profiles/tcp_gemm_fc1_fc2_block1_b1024.md,
-# profiles/ln_kernel_ln1_block1_b1024.md.  Traffic grows with the rows of a launch.
-STAGE_TRAFFIC_PER_ROW = {"fc1": (39_059_456 + 102_366_208) / 201_728,
-                         "fc2": (193_842_944 + 24_758_272) / 201_728,
-                         "ln1": (38_787_840 + 1_576_448) / 201_728}
+# DRAM bytes (read + write) per row of one launch, from the committed ncu captures of a
+# full-size launch (block 1, 201,728 rows): profiles/tcp_gemm_qkv_proj_fc1_block1_b1024.md,
+# profiles/tcp_gemm_fc2_block1_b1024.md, profiles/ln_kernel_ln1_block1_b1024.md.
+# Traffic grows with the rows of a launch.
+STAGE_TRAFFIC_PER_ROW = {"fc1": (38_987_776 + 101_157_632) / 201_728,
+                         "fc2": (193_862_656 + 23_533_568) / 201_728,
+                         "ln1": (38_791_424 + 1_806_336) / 201_728}
 
 
 def algorithmic_macs(counts):
