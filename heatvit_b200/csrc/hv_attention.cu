@@ -130,14 +130,31 @@ __global__ void __launch_bounds__(CFG::THREADS) attention_tc_kernel(const int8_t
     const uint32_t lane_addr = tbase + ((uint32_t)(quad * 32) << 16);
     uint32_t phase = 0;
 
-    // Persistent: the CTA walks (image, head) items; images of the other CTA shape
-    // are skipped (a CTA-uniform test).
-    for (int item = blockIdx.x; item < items && !*abort_flag; item += gridDim.x) {
+    // Persistent: the CTA's items are blockIdx.x + j * gridDim.x.  Its threads test a
+    // batch of THREADS candidates at once (one offsets read each) and list the items
+    // of this CTA shape; the CTA then processes the list.
+    __shared__ int s_items[CFG::THREADS];
+    __shared__ int s_nitems;
+    for (int jb = 0; blockIdx.x + jb * gridDim.x < items && !*abort_flag; jb += CFG::THREADS) {
+    if (tid == 0) s_nitems = 0;
+    __syncthreads();
+    {
+        const int it = blockIdx.x + (jb + tid) * gridDim.x;
+        if (it < items) {
+            const int im = it / 3;
+            const int nn = offsets[im + 1] - offsets[im];
+            const int npp = (nn + 31) & ~31;
+            if (nn > 0 && npp > np_lo && npp <= np_hi) s_items[atomicAdd(&s_nitems, 1)] = it;
+        }
+    }
+    __syncthreads();
+    const int nlist = s_nitems;
+    for (int li = 0; li < nlist && !*abort_flag; ++li) {
+    const int item = s_items[li];
     const int img = item / 3, head = item - img * 3;
     const int row0 = offsets[img];
     const int n = offsets[img + 1] - row0;
     const int np = (n + 31) & ~31;
-    if (n <= 0 || np <= np_lo || np > np_hi) continue;
     // K and V rows (zero beyond n up to np), both in the K-major byte layout.
     for (int c = tid; c < np * 8; c += CFG::THREADS) {
         const int r = c >> 3, ch = c & 3, isv = (c >> 2) & 1;
@@ -287,7 +304,9 @@ __global__ void __launch_bounds__(CFG::THREADS) attention_tc_kernel(const int8_t
         tc05::fence_before();
         __syncthreads();
     }
-    }  // items
+    }  // listed items
+    __syncthreads();  // s_items is rewritten by the next batch
+    }  // candidate batches
 
     if (*abort_flag) {
         if (tid == 0) atomicExch(err, 1);

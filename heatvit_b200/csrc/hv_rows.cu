@@ -305,11 +305,16 @@ __global__ void __launch_bounds__(256, 3) ln_kernel(const int8_t *x, int8_t *out
     griddep_wait();  // rows and their count come from earlier kernels
     griddep_launch();
     const int rows = rows_dev ? *rows_dev : rows_max;
-    for (int base = warp * 32; base < rows; base += warps * 32) {
+    // Rows per warp pass: 4 * g for g 4-row sub-passes.  Few rows spread over all
+    // warps with short passes (the pass latency bounds small launches); many rows use
+    // full 32-row passes, which amortise the per-row statistics best.
+    const int g = max(1, min(8, (rows + 4 * warps - 1) / (4 * warps)));
+    const int R = 4 * g;
+    for (int base = warp * R; base < rows; base += warps * R) {
         int32_t my_s = 0;
         int64_t my_s2 = 0;
 #pragma unroll 1
-        for (int k = 0; k < 8; ++k) {
+        for (int k = 0; k < g; ++k) {
             const int r = base + 4 * k + grp;
             int32_t v[24];
             ln_load24(x + (size_t)(r < rows ? r : 0) * 192, sub, r < rows, v);
@@ -343,7 +348,7 @@ __global__ void __launch_bounds__(256, 3) ln_kernel(const int8_t *x, int8_t *out
                 my_s2 = tq;
             }
         }
-        const int myrow = base + lane;
+        const int myrow = lane < R ? base + lane : rows;  // lanes past the pass own no row
         const LnStats st = ln_stats(my_s, my_s2, p);
         const LnAff af = ln_aff(st, p);
         if (myrow < rows) {
@@ -355,7 +360,7 @@ __global__ void __launch_bounds__(256, 3) ln_kernel(const int8_t *x, int8_t *out
         }
         const bool all_safe = __all_sync(0xffffffffu, af.safe || myrow >= rows);
 #pragma unroll 1
-        for (int k = 0; k < 8; ++k) {
+        for (int k = 0; k < g; ++k) {
             const int r = base + 4 * k + grp;
             const bool active = r < rows;
             const int owner = 4 * k + grp;
