@@ -184,7 +184,7 @@ def run_reference(args):
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import hv_oracle
     hv_oracle.build()
-    params = synth.config_params(synth.SEED, pruned=args.variant == "pruned")
+    params = bench_params(synth, args.variant)
     threads = hv_oracle.num_cpus()
     per_step = max(4 * threads, 16)
     imgs = synth.baseline_images(synth.SEED, per_step)
@@ -200,7 +200,7 @@ def run_reference(args):
         "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "int8/int32", "data": "synthetic",
         "config": {"workload": f"config4-{args.variant}: batch {args.batch}/GPU, 224x224x3 int8 images, "
-                               "seeded benchmark DeiT-T (heatvit_b200.synth.config_params)",
+                               "seeded benchmark DeiT-T (heatvit_b200.synth." + PARAMS_FN[args.variant] + ")",
                    "per_step_sample_images": per_step},
         "impl": "reference",
         "cpu_baseline": {"value": value, "unit": "images/s", "cores": threads, "kind": "port",
@@ -209,6 +209,16 @@ def run_reference(args):
         "e2e": {"value": value, "unit": "images/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
+
+
+# Config 4 runs the benchmark model unpruned, or pruned with config 3's selectors.
+PARAMS_FN = {"pruned": "config3_params", "unpruned": "config_params(pruned=False)"}
+
+
+def bench_params(synth, variant):
+    if variant == "pruned":
+        return synth.config3_params(synth.SEED)
+    return synth.config_params(synth.SEED, pruned=False)
 
 
 def main():
@@ -244,7 +254,7 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local))
 
-    params = synth.config_params(synth.SEED, pruned=args.variant == "pruned")
+    params = bench_params(synth, args.variant)
     eng = Engine(params)
     b = args.batch
     first, _ = shard_range(rank, world, b)
@@ -337,7 +347,7 @@ def main():
             "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "int8/int32", "data": "synthetic",
             "config": {"workload": f"config4-{args.variant}: batch {b}/GPU of seeded 224x224x3 int8 images, "
-                                   "benchmark DeiT-T (synth.config_params), selectors before blocks 4/7/10",
+                                   "benchmark DeiT-T (synth." + PARAMS_FN[args.variant] + "), selectors before blocks 4/7/10",
                        "images_per_gpu": b, "parallelism": f"image-sharded x{world}",
                        "l2": "inputs larger than L2 (images 154 MB/GPU per step)",
                        "mean_token_counts": [float(v) for v in counts_np.mean(0)]},

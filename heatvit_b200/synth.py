@@ -339,20 +339,25 @@ TARGET_COUNTS = (88, 45, 32)
 
 
 def calibrate_keep_bias(seed, infer_counts, images=64, targets=TARGET_COUNTS, lo=-(1 << 22),
-                        hi=(1 << 22), **kw):
+                        hi=(1 << 22), make=None, stages=(0, 1, 2), **kw):
     """Bisect keep_bias stage by stage so the mean selector output count over
     ``baseline_images(seed, images)`` is as close as possible to ``targets``.
 
-    ``infer_counts(params, images) -> counts [B, 4]`` may be any backend."""
+    ``infer_counts(params, images) -> counts [B, 4]`` may be any backend;
+    ``make(bias) -> params`` builds the model for a bias triple (default:
+    ``baseline_params``); only ``stages`` are calibrated."""
     imgs = baseline_images(seed, images)
+    if make is None:
+        def make(bias):
+            return baseline_params(seed, True, keep_bias=bias, **kw)
     bias = [0, 0, 0]
-    for s in range(3):
+    for s in stages:
         a, b = lo, hi
         best = None
         while a <= b:
             mid = (a + b) // 2
             bias[s] = mid
-            mean = float(np.mean(infer_counts(baseline_params(seed, True, keep_bias=bias, **kw), imgs)[:, s + 1]))
+            mean = float(np.mean(infer_counts(make(bias), imgs)[:, s + 1]))
             if best is None or abs(mean - targets[s]) < abs(best[1] - targets[s]):
                 best = (mid, mean)
             if mean < targets[s]:
@@ -364,5 +369,81 @@ def calibrate_keep_bias(seed, infer_counts, images=64, targets=TARGET_COUNTS, lo
 
 
 def config_params(seed=SEED, pruned=True):
-    """The benchmark model with its calibrated keep biases (configs 3 and 4)."""
+    """The benchmark model with its calibrated keep biases (config 4)."""
     return baseline_params(seed, pruned=pruned, keep_bias=BASELINE_KEEP_BIAS.get(seed, (0, 0, 0)))
+
+
+# ----------------------------------------------------------------------------
+# Config 3: a ragged batch in which some images have a zero package denominator
+# ----------------------------------------------------------------------------
+#
+# The package denominator of finalize_tokens (selector.py:421-500) is the sum of
+# the fused keep scores of the pruned tokens, and it is zero only when every one
+# of them scores exactly 0.  A keep score softmax_selector([drop, keep])[1] is 0
+# only when the logit gap reaches 16 * 45426 in Q16 (the exp term shifts out),
+# i.e. (drop - keep) * 2^(logits_exp + 16) >= 726816.  Int8 logits differ by at
+# most 255, so no logits exponent <= -5 (in particular none in [-20, -8]) can
+# produce it.  Config 3 therefore gives its first selector logits at 2^-4 and
+# lets head 0 alone vote:
+#
+# * head weights: head_weight.w2 = 0 and b2 = (+2^30, -2^30, -2^30) at
+#   exponents -8/-8, so PLAN gives every candidate the weights (1.0, 0, 0) and
+#   fuse_head_scores returns head 0's score unchanged;
+# * head 0's drop logit saturates at +127 (w3[0, :, 0] = 0, b3[0][0] = 2^30);
+# * head 0's keep logit is one seeded int8 column over the 16 h2 features plus a
+#   keep bias, at score_w3 exponent logits_exp - h2_exp + shift.
+#
+# A candidate is kept when its keep logit saturates at +127 too (score 0.5,
+# inclusive threshold) and scores exactly 0 when the keep logit is <= -51; an
+# image has a zero package denominator when none of its pruned candidates falls
+# in between.  The column attempt, shift and bias are searched (seeded, like the
+# reference's per-stage calibration, weights.py:281-327) for an output count
+# near 88 with the budget's spread and a zero-denominator rate of a few percent;
+# selectors 2 and 3 then get keep biases recalibrated for 45 and 32.
+
+ZERO_DEN_LOGITS_EXP = -4
+
+
+def zero_den_column(seed, attempt):
+    """Head 0's keep-logit column (16 int8) for calibration attempt ``attempt``."""
+    return np.random.default_rng([seed, 3, attempt]).integers(-127, 128, 16).astype(np.int8)
+
+
+def zero_den_selector(sel, column, shift, keep_bias):
+    """``sel`` rebuilt as config 3's first selector (see above)."""
+    from dataclasses import replace
+    w3 = np.array(sel.score.w3, np.int8, copy=True)
+    b3 = np.array(sel.score.b3, np.int64, copy=True)
+    w3[0, :, 0] = 0
+    w3[0, :, 1] = column
+    b3[0, 0] = 1 << 30
+    b3[0, 1] = keep_bias
+    hw = replace(sel.head_weight, w2=np.zeros((3, 3), np.int8),
+                 b2=np.array([1 << 30, -(1 << 30), -(1 << 30)], np.int32))
+    return replace(sel, score=replace(sel.score, w3=w3, b3=b3.astype(np.int32)), head_weight=hw,
+                   hw_w2_scale_exp=-8, hw_hidden_out_scale_exp=-8,
+                   logits_out_scale_exp=ZERO_DEN_LOGITS_EXP,
+                   score_w3_scale_exp=ZERO_DEN_LOGITS_EXP - sel.h2_out_scale_exp + shift)
+
+
+def config3_from(seed, attempt, shift, keep_bias, later_keep_bias):
+    """Config-3 parameters for explicit calibration values."""
+    from dataclasses import replace
+    base = baseline_params(seed, True, keep_bias=(0,) + tuple(later_keep_bias))
+    first = zero_den_selector(base.selectors[0], zero_den_column(seed, attempt), shift, keep_bias)
+    return replace(base, selectors=(first,) + tuple(base.selectors[1:]))
+
+
+# seed -> (attempt, shift, keep_bias of selector 1, keep biases of selectors 2/3),
+# found by tests/golden/calibrate_config3.py over baseline_images(seed, 256).
+CONFIG3_CALIBRATION = {
+    20260815: (172, 1, 5113, (-703, 9635)),
+}
+
+
+def config3_params(seed=SEED):
+    """Config 3: the benchmark model with the zero-denominator first selector."""
+    if seed not in CONFIG3_CALIBRATION:
+        raise KeyError(f"no config-3 calibration for seed {seed}")
+    attempt, shift, kb, later = CONFIG3_CALIBRATION[seed]
+    return config3_from(seed, attempt, shift, kb, later)

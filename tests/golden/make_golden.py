@@ -290,6 +290,29 @@ def golden_baseline(R, seed, images, pruned, tag):
     return out
 
 
+def golden_config3(R, seed, indices):
+    """Config-3 model (zero-denominator first selector) on chosen images of
+    baseline_images(seed, .): a zero-package-denominator image and a regular one."""
+    from heatvit_b200 import synth
+    from heatvit_b200.params import to_reference
+    from verification.heatvit_ref import model as M
+    params = synth.config3_params(seed)
+    gparams = to_reference(params, ref_namespace())
+    imgs = synth.baseline_images(seed, max(indices) + 1)
+    out = {"config3_seed": np.array(seed), "config3_indices": np.array(indices),
+           "config3_params_sha256": np.array(params_digest(params))}
+    from verification.heatvit_ref import selector as S
+    for j, i in enumerate(indices):
+        res = M.HeatViTModel().infer([int(v) for v in imgs[i]], gparams)
+        out.update(pack_result(res, f"config3_{j}"))
+        # the first selector again on its input, for its warning bits and scores
+        r = S.token_selector(res.checkpoints["block_03"], 0, gparams.selectors[0])
+        out[f"config3_{j}_sel1_warnings"] = np.array(r.warnings)
+        out[f"config3_{j}_sel1_fused"] = np.array(r.fused_scores)
+        out[f"config3_{j}_sel1_head_weights"] = np.array(r.head_weights)
+    return out
+
+
 def golden_units(R, seed):
     """Per-operator golden outputs on seeded random inputs."""
     from verification.heatvit_ref import fixed as F
@@ -439,6 +462,8 @@ def main():
         save("golden_seeded.npz", golden_seeded(ref))
     if on("baseline"):
         save("golden_baseline.npz", golden_baseline(ref, 20260815, 2, True, "pruned"))
+    if on("config3"):
+        save("golden_config3.npz", golden_config3(ref, 20260815, (2, 0)))
     if on("unpruned"):
         save("golden_unpruned.npz", golden_baseline(ref, 20260815, 1, False, "unpruned"))
     print(f"done in {time.time() - t0:.1f}s")

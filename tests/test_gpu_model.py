@@ -58,16 +58,29 @@ def _compare_batch(out, ref, ns):
 
 
 def test_config3_batch256_bit_exact(cuda, oracle):
-    """Config 3: pruned, batch 256 on one GPU, every image against the oracle."""
+    """Config 3: pruned, batch 256 on one GPU, every image against the oracle;
+    at least 1% of the images take the zero-package-denominator fallback."""
     from heatvit_b200 import synth
     from heatvit_b200.model import HeatViTModel
-    params = synth.config_params(synth.SEED, pruned=True)
+    params = synth.config3_params(synth.SEED)
     imgs = synth.baseline_images(synth.SEED, 256)
     out = HeatViTModel().infer_batch(imgs, params)
     ref = _oracle_batch(oracle, params, imgs)
     _compare_batch(out, ref, 3)
     counts = out["token_counts"]
     assert counts[:, 0].min() == 197 and counts[:, 1].std() > 5  # ragged after the selectors
+    assert ((np.asarray(out["warnings"]) & 2) != 0).sum() >= 0.01 * 256
+
+
+def test_config4_pruned_sample_bit_exact(cuda, oracle):
+    """The pruned benchmark model without the config-3 selector (calibrated
+    keep biases on all three selectors), batch 96."""
+    from heatvit_b200 import synth
+    from heatvit_b200.model import HeatViTModel
+    params = synth.config_params(synth.SEED, pruned=True)
+    imgs = synth.baseline_images(synth.SEED, 96)
+    out = HeatViTModel().infer_batch(imgs, params)
+    _compare_batch(out, _oracle_batch(oracle, params, imgs), 3)
 
 
 def test_unpruned_batch_bit_exact(cuda, oracle):
@@ -99,7 +112,7 @@ def test_batch_invariance_full_size(cuda):
     import torch
     from heatvit_b200 import synth
     from heatvit_b200.engine import Engine
-    params = synth.config_params(synth.SEED, pruned=True)
+    params = synth.config3_params(synth.SEED)
     eng = Engine(params)
     imgs = torch.from_numpy(synth.baseline_images(synth.SEED, 1024, first=5000)).cuda()
     full = eng.infer(imgs)
@@ -113,7 +126,7 @@ def test_full_size_sample_vs_oracle(cuda, oracle):
     import torch
     from heatvit_b200 import synth
     from heatvit_b200.engine import Engine
-    params = synth.config_params(synth.SEED, pruned=True)
+    params = synth.config3_params(synth.SEED)
     imgs = synth.baseline_images(synth.SEED, 1024, first=9000)
     eng = Engine(params)
     out = eng.infer(torch.from_numpy(imgs).cuda())
@@ -128,7 +141,7 @@ def test_host_entry_matches_device_entry(cuda):
     import torch
     from heatvit_b200 import synth
     from heatvit_b200.engine import Engine
-    params = synth.config_params(synth.SEED, pruned=True)
+    params = synth.config3_params(synth.SEED)
     eng = Engine(params)
     n = 1400                                                   # chunks of 512, 512 and 376 images, two workspaces
     imgs = synth.baseline_images(synth.SEED, n, first=77)

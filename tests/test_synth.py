@@ -30,6 +30,19 @@ def test_benchmark_params_are_deterministic():
         assert _digest(p) == str(g[f"{tag}_params_sha256"])
 
 
+def test_config3_params_match_golden():
+    from heatvit_b200 import synth
+    g = load_golden("golden_config3.npz")
+    p = synth.config3_params(int(g["config3_seed"]))
+    assert _digest(p) == str(g["config3_params_sha256"])
+    sel = p.selectors[0]
+    # only the first selector's logits leave [-20, -8]: a zero keep score needs
+    # (drop - keep) * 2^(logits_exp + 16) >= 16 * 45426 with |drop - keep| <= 255
+    assert sel.logits_out_scale_exp == synth.ZERO_DEN_LOGITS_EXP
+    assert 255 << (sel.logits_out_scale_exp + 16) >= 16 * 45426
+    assert 255 << (-8 + 16) < 16 * 45426
+
+
 def test_benchmark_exponents_in_range():
     from heatvit_b200 import synth
     p = synth.config_params(20260815)
