@@ -28,7 +28,7 @@ namespace hv {
 enum Epi { EPI_I8 = 0, EPI_I8_RES = 1, EPI_GELU = 2, EPI_PATCH = 3, EPI_I32 = 4, EPI_ACC64 = 5 };
 
 // Largest exact GELU-chain output table (bytes) an FC1 launch keeps in shared memory.
-constexpr int kGeluTableMax = 4096;
+constexpr int kGeluTableMax = 20480;
 
 // Per-launch epilogue constants (all derived on the host from the golden
 // scale exponents).
@@ -45,10 +45,13 @@ struct EpiParams {
     int gelu_fast;            // host-checked ranges of gelu_chain_fast hold
     int gelu_k2;              // host-checked ranges of gelu_chain_fast2 hold (persistent kernel)
     GeluK gk;                 // constants of gelu_chain_fast2 (also the input shift of the table form)
-    // exact output table of the GELU chain over its reachable inputs (persistent
-    // kernel): out = gtab[clamp(rsa(acc + bias, sh_in) - gtab_lo, 0, gtab_n - 1)]
+    // exact output table of the GELU chain (persistent kernel):
+    // out = gtab[clamp(q - gtab_lo, 0, gtab_n - 1)], q = rsa(acc + bias, sh_in), exact
+    // for q in [gtab_elo, gtab_ehi); a warp whose 32 values include one outside that
+    // range evaluates them with gelu_chain_fast2 instead (gelu_k2 must then hold)
     const int8_t *gtab;
     int gtab_lo, gtab_n;      // gtab_n in [1, kGeluTableMax]; 0 = no table
+    int gtab_elo, gtab_ehi;
     // patch (EPI_PATCH): pos [197][192], add = (a = embed, b = pos)
     const int8_t *pos;
 };

@@ -149,8 +149,9 @@ __global__ void __launch_bounds__(PT_THREADS, 1) tcp_gemm_kernel(GemmArgs g, int
     }
     for (int i = tid; i < N; i += PT_THREADS) sbias[i] = g.epi.bias ? g.epi.bias[i] : 0;
     int8_t *stab = (int8_t *)(smem + L::OFF_TAB);
-    if (EPI == EPI_GELU && L::TABB > 0)
-        for (int i = tid; i < g.epi.gtab_n; i += PT_THREADS) stab[i] = g.epi.gtab[i];
+    if (EPI == EPI_GELU && L::TABB > 0)  // the table allocation is padded to 16 bytes
+        for (int i = tid; i < (g.epi.gtab_n + 15) / 16; i += PT_THREADS)
+            ((uint4 *)stab)[i] = ((const uint4 *)g.epi.gtab)[i];
     asm volatile("cp.async.wait_all;\n" ::: "memory");
     // Everything above touches only weights and on-chip state; from here on the
     // kernel reads activations and row counts that the previous kernel writes.
@@ -335,10 +336,13 @@ __global__ void __launch_bounds__(PT_THREADS, 1) tcp_gemm_kernel(GemmArgs g, int
                     tc05::wait_ld();
                     const uint32_t aux[8] = {r0.x, r0.y, r0.z, r0.w, r1.x, r1.y, r1.z, r1.w};
                     uint32_t pk[8];
+                    bool slow = true;
                     if (EPI == EPI_GELU && FAST && L::TABB > 0 && g.epi.gtab_n > 0) {
-                        // exact table of the GELU chain over the reachable Q8.16 window
+                        // exact table of the GELU chain, valid for q in [elo, ehi)
                         const GeluK &k = g.epi.gk;
                         const int lo = g.epi.gtab_lo, last = g.epi.gtab_n - 1;
+                        const int elo = g.epi.gtab_elo, ehi = g.epi.gtab_ehi;
+                        bool esc = false;
 #pragma unroll
                         for (int w = 0; w < 8; ++w) {
                             int32_t o[4];
@@ -346,11 +350,15 @@ __global__ void __launch_bounds__(PT_THREADS, 1) tcp_gemm_kernel(GemmArgs g, int
                             for (int b = 0; b < 4; ++b) {
                                 const int32_t x = (int32_t)v[w * 4 + b] + bv[w * 4 + b];
                                 const int32_t q = (x + k.hin + mulhi_s(x, k.ksgn)) >> k.sh_in;
+                                esc |= (q < elo) | (q >= ehi);
                                 o[b] = stab[min(max(q - lo, 0), last)];
                             }
                             pk[w] = pack_sat8(o[0], o[1], o[2], o[3]);
                         }
-                    } else {
+                        // every lane of an epilogue warp runs this loop (stores are guarded by valid)
+                        slow = __any_sync(0xffffffffu, esc);
+                    }
+                    if (slow) {
 #pragma unroll
                         for (int w = 0; w < 8; ++w) {
                             int32_t o[4];

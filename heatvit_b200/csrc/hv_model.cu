@@ -90,6 +90,7 @@ struct BlockDev {
     GeluK fc1_gk;
     size_t fc1_tab;            // exact GELU-chain table in the arena (fc1_tab_n > 0)
     int fc1_tab_lo, fc1_tab_n;
+    int fc1_tab_elo, fc1_tab_ehi;  // the table is exact for q in [elo, ehi)
     AlignAdd res1, res2;
     AttnParams attn;
 };
@@ -429,6 +430,8 @@ int run_block(hv_model *m, int b, int images, const int32_t *off, int may_be_sho
         g.epi.gtab = d.fc1_tab_n > 0 ? m->w<int8_t>(d.fc1_tab) : nullptr;
         g.epi.gtab_lo = d.fc1_tab_lo;
         g.epi.gtab_n = d.fc1_tab_n;
+        g.epi.gtab_elo = d.fc1_tab_elo;
+        g.epi.gtab_ehi = d.fc1_tab_ehi;
         CUDA_TRY(model_gemm(m, g, EPI_GELU, rows_max, st));
         pr.end(st, rows_dev, 0);
     }
@@ -538,6 +541,65 @@ int infer_impl(hv_model *m, const int8_t *d_images, int batch, int32_t *d_logits
 // ---- parameter validation and packing -------------------------------------------
 bool ln_scale_ok(int xs) { return xs >= -32 && xs <= 0; }
 
+// A GELU-chain table [lo, lo + n) in Q8.16 input units, exact for inputs in [elo, ehi).
+struct TabWindow {
+    int32_t lo, n, elo, ehi;
+};
+
+// Smallest escape distance (in Q8.16 input units, one real unit = 65536) a central
+// table must reach on both sides of 0 before it replaces the FMA form: inputs
+// beyond it would take the slower escape path.
+constexpr int64_t kEscapeRadiusMin = 65536;
+
+// Choose a table of at most kGeluTableMax entries for a GELU chain whose output
+// varies over more than that across the reachable inputs [-qmax, qmax].  The table
+// [t0, t1) must contain q = 0; with its first and last entries repeated by the
+// clamp, it is exact from the start of the constant run holding t0 to the end of
+// the run holding t1 - 1.  Among the tables that start at the end of a run, the one
+// whose exact range reaches farthest from 0 on its nearer side is taken, if that
+// distance is at least kEscapeRadiusMin.  *ok = false leaves the FMA form.
+int gelu_escape_window(int32_t qmax, int sh_out, TabWindow *tw, bool *ok) {
+    *ok = false;
+    const int64_t total = 2 * (int64_t)qmax + 1;
+    int8_t *d_f = nullptr;
+    std::vector<int8_t> f((size_t)total);
+    cudaError_t e = cudaMalloc(&d_f, (size_t)total);
+    if (e == cudaSuccess) e = launch_gelu_table_fill(d_f, -qmax, (int32_t)total, sh_out, nullptr);
+    if (e == cudaSuccess) e = cudaMemcpy(f.data(), d_f, (size_t)total, cudaMemcpyDeviceToHost);
+    if (d_f) cudaFree(d_f);
+    if (e != cudaSuccess) return fail(HV_ERR_CUDA, "GELU table scan: %s", cudaGetErrorString(e));
+    // run r covers indices [starts[r], starts[r + 1]); index i is q = i - qmax
+    std::vector<int64_t> starts{0};
+    for (int64_t i = 1; i < total; ++i)
+        if (f[(size_t)i] != f[(size_t)i - 1]) starts.push_back(i);
+    starts.push_back(total);
+    const int64_t nruns = (int64_t)starts.size() - 1, i0 = qmax;
+    auto run_of = [&](int64_t i) {  // run holding index i
+        return (int64_t)(std::upper_bound(starts.begin(), starts.end(), i) - starts.begin()) - 1;
+    };
+    const int64_t inf = INT64_MAX / 4;
+    int64_t best = -1;
+    for (int64_t r = 0; r < nruns; ++r) {
+        const int64_t t0 = starts[(size_t)r + 1] - 1;  // the table starts at the run's last index
+        if (t0 > i0) break;
+        const int64_t t1 = std::min(t0 + (int64_t)kGeluTableMax, total);
+        if (t1 <= i0) continue;
+        const int64_t rr = run_of(t1 - 1);
+        const int64_t f0 = starts[(size_t)r], f1 = starts[(size_t)rr + 1];
+        const int64_t left = f0 == 0 ? inf : i0 - f0, right = f1 == total ? inf : f1 - 1 - i0;
+        const int64_t reach = std::min(left, right);
+        if (reach > best) {
+            best = reach;
+            tw->lo = (int32_t)(t0 - qmax);
+            tw->n = (int32_t)(std::max(starts[(size_t)rr], t0) + 1 - t0);  // to the last run's first index
+            tw->elo = f0 == 0 ? INT32_MIN : (int32_t)(f0 - qmax);
+            tw->ehi = f1 == total ? INT32_MAX : (int32_t)(f1 - qmax);
+        }
+    }
+    *ok = best >= kEscapeRadiusMin;
+    return HV_OK;
+}
+
 int pack_model(hv_model *m, const hv_params *P) {
     // two device ints of scratch for the GELU table window search, freed on every return
     struct ScratchInts {
@@ -616,6 +678,8 @@ int pack_model(hv_model *m, const hv_params *P) {
             // Exact table form when the output varies only over a short window of the
             // reachable Q8.16 inputs [-qmax, qmax], qmax = rsa(vmax, sh_in).
             d.fc1_tab_n = 0;
+            d.fc1_tab_elo = INT32_MIN;
+            d.fc1_tab_ehi = INT32_MAX;
             if (!d.fc1_wide && d.fc1_sh_in >= 0 && d.fc1_sh_in <= 30 && vmax < ((int64_t)1 << 30)) {
                 const int64_t hin = d.fc1_sh_in > 0 ? (int64_t)1 << (d.fc1_sh_in - 1) : 0;
                 const int64_t qmax = (vmax + hin) >> d.fc1_sh_in;
@@ -623,10 +687,20 @@ int pack_model(hv_model *m, const hv_params *P) {
                     if (!mm) CUDA_TRY(cudaMalloc(&mm, 2 * sizeof(int)));
                     int32_t wlo = 0, wn = 0;
                     CUDA_TRY(gelu_table_window((int32_t)qmax, d.fc1_sh_out, mm, &wlo, &wn, nullptr));
-                    if (wn <= kGeluTableMax) {
-                        d.fc1_tab = A.add(nullptr, (size_t)wn);
-                        d.fc1_tab_lo = wlo;
-                        d.fc1_tab_n = wn;
+                    TabWindow tw{wlo, wn, INT32_MIN, INT32_MAX};
+                    bool ok = wn <= kGeluTableMax;
+                    if (!ok && d.fc1_k2) {
+                        // too wide for a whole-window table: a central table whose clamped
+                        // ends cover long constant runs, with gelu_chain_fast2 outside them
+                        int rc = gelu_escape_window((int32_t)qmax, d.fc1_sh_out, &tw, &ok);
+                        if (rc != HV_OK) return rc;
+                    }
+                    if (ok) {
+                        d.fc1_tab = A.add(nullptr, ((size_t)tw.n + 15) & ~(size_t)15);
+                        d.fc1_tab_lo = tw.lo;
+                        d.fc1_tab_n = tw.n;
+                        d.fc1_tab_elo = tw.elo;
+                        d.fc1_tab_ehi = tw.ehi;
                         d.fc1_gk = make_gelu_k(d.fc1_sh_in, d.fc1_k2 ? d.fc1_sh_out : 0);
                     }
                 }

@@ -293,7 +293,9 @@ def test_model_parameter_errors(cuda):
 @pytest.mark.parametrize("l2,w1,hid", [(-12, -8, -11), (-20, -20, -8), (-9, -8, -20), (-8, -8, -9), (-14, -2, -5),
                                        (-7, -10, -13),
                                        # short output windows: the exact table form
-                                       (-13, -10, -15), (-14, -13, -18), (-12, -12, -16), (-12, -14, -14)])
+                                       (-13, -10, -15), (-14, -13, -18), (-12, -12, -16), (-12, -14, -14),
+                                       # central tables with FMA-form escapes: often / seldom taken
+                                       (-8, -8, -11), (-9, -8, -11)])
 def test_ffn_gelu_epilogue_exponents(cuda, oracle, l2, w1, hid):
     """FC1's fused GELU epilogue (table, FMA-pipe and 64-bit forms) across
     input/output exponents, through the fused block kernel."""
