@@ -46,14 +46,18 @@ struct AttnCfg {
     static constexpr int SPLIT = SPL;                 // warps per TMEM lane quadrant (column parts)
     static constexpr int THREADS = 128 * SPL;
     static constexpr uint32_t TMEM_COLS = NPM <= 128 ? 128 : 256;
-    static constexpr int OFF_K = 0;                            // [NPMAX][64] K-major
-    static constexpr int OFF_V = OFF_K + NPM * 64;             // [NPMAX][64], read MN-major
-    static constexpr int OFF_Q = OFF_V + NPM * 64;             // [128][64]
-    static constexpr int OFF_P = OFF_Q + 128 * 64;             // [128][NPMAX] uint8
+    static constexpr int KV = NPM * 64;                        // one [NPMAX][64] K-major operand
+    static constexpr int OFF_KV = 0;                           // two (K, V) buffers: item j uses j & 1
+    static constexpr int OFF_P = OFF_KV + 4 * KV;              // [128][NPMAX] uint8
+    static constexpr int OFF_Q = OFF_P;                        // [128][64]; Q is dead before P is written
     static constexpr int OFF_RED = OFF_P + 128 * NPM;          // [2][SPLIT][128] int32 row partials
     static constexpr int OFF_BAR = OFF_RED + 2 * SPL * 128 * 4;  // mbarrier, TMEM base, abort flag
-    static constexpr int SMEM = NPM <= 128 ? 46 * 1024 : 80 * 1024;  // > 228 KB / 5, resp. / 3
-    static_assert(OFF_BAR + 64 <= SMEM, "attention shared memory layout");
+    static constexpr int SMEM = (OFF_BAR + 64 + 1023) / 1024 * 1024;
+    // Shared memory alone keeps the resident CTAs within the 512 TMEM columns, so
+    // tcgen05.alloc never waits: at most 4 small (128 columns) or 2 large (256) per SM.
+    static_assert(NPM <= 128 ? (5 * SMEM > 228 * 1024 && 4 * (SMEM + 2048) <= 228 * 1024)
+                             : (3 * SMEM > 228 * 1024 && 2 * (SMEM + 3072) <= 228 * 1024),
+                  "attention shared memory sizing");
 };
 using AttnSmall = AttnCfg<128, 2>;
 using AttnLarge = AttnCfg<224, 4>;
@@ -92,6 +96,29 @@ __device__ __forceinline__ uint32_t chunk_exp(uint32_t (&v)[16], int valid, int3
     return sum;
 }
 
+// Asynchronous copy of item `item`'s K and V rows into a (K, V) buffer pair, both in
+// the K-major byte layout; rows n..np-1 are zero-filled (src-size 0).
+template <class CFG>
+__device__ __forceinline__ void attn_load_kv(const int8_t *qkv, const int32_t *offsets, int item, uint8_t *kv,
+                                             int tid) {
+    const int img = item / 3, head = item - img * 3;
+    const int row0 = offsets[img], n = offsets[img + 1] - row0, np = (n + 31) & ~31;
+    for (int c = tid; c < np * 8; c += CFG::THREADS) {
+        const int r = c >> 3, ch = c & 3, isv = (c >> 2) & 1;
+        const int8_t *src = qkv + (size_t)(row0 + (r < n ? r : 0)) * 576 + 192 * (1 + isv) + head * 64 + ch * 16;
+        const uint32_t dst = tc05::smem_u32(kv + isv * CFG::KV + tc05::kmajor_offset(r, ch * 16, 64));
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(dst), "l"(src), "r"(r < n ? 16 : 0)
+                     : "memory");
+    }
+    asm volatile("cp.async.commit_group;\n" ::: "memory");
+}
+
+// Barrier of the SPLIT warps that share TMEM lane quadrant `quad` (ids 1..4).
+template <class CFG>
+__device__ __forceinline__ void quad_sync(int quad) {
+    asm volatile("bar.sync %0, %1;\n" ::"r"(1 + quad), "r"(32 * CFG::SPLIT) : "memory");
+}
+
 template <bool FAST, class CFG>
 __global__ void __launch_bounds__(CFG::THREADS) attention_tc_kernel(const int8_t *__restrict__ qkv,
                                                                const int32_t *__restrict__ offsets,
@@ -99,8 +126,6 @@ __global__ void __launch_bounds__(CFG::THREADS) attention_tc_kernel(const int8_t
                                                                int *__restrict__ err, int items, int np_lo,
                                                                int np_hi) {
     extern __shared__ __align__(1024) uint8_t smem[];
-    uint8_t *sK = smem + CFG::OFF_K;
-    uint8_t *sV = smem + CFG::OFF_V;
     uint8_t *sQ = smem + CFG::OFF_Q;
     uint8_t *sP = smem + CFG::OFF_P;
     int32_t *sred = (int32_t *)(smem + CFG::OFF_RED);
@@ -149,19 +174,22 @@ __global__ void __launch_bounds__(CFG::THREADS) attention_tc_kernel(const int8_t
     }
     __syncthreads();
     const int nlist = s_nitems;
+    if (nlist > 0) attn_load_kv<CFG>(qkv, offsets, s_items[0], smem + CFG::OFF_KV, tid);
     for (int li = 0; li < nlist && !*abort_flag; ++li) {
     const int item = s_items[li];
     const int img = item / 3, head = item - img * 3;
     const int row0 = offsets[img];
     const int n = offsets[img + 1] - row0;
     const int np = (n + 31) & ~31;
-    // K and V rows (zero beyond n up to np), both in the K-major byte layout.
-    for (int c = tid; c < np * 8; c += CFG::THREADS) {
-        const int r = c >> 3, ch = c & 3, isv = (c >> 2) & 1;
-        int4 kv = make_int4(0, 0, 0, 0);
-        if (r < n) kv = *(const int4 *)(qkv + (size_t)(row0 + r) * 576 + 192 * (1 + isv) + head * 64 + ch * 16);
-        *(int4 *)((isv ? sV : sK) + tc05::kmajor_offset(r, ch * 16, 64)) = kv;
-    }
+    // This item's K/V copies (issued during the previous item) land; then the next
+    // item's copies go to the other buffer, whose last reader (that item's P.V) has
+    // completed.
+    asm volatile("cp.async.wait_all;\n" ::: "memory");
+    __syncthreads();
+    uint8_t *sK = smem + CFG::OFF_KV + (li & 1) * 2 * CFG::KV;
+    uint8_t *sV = sK + CFG::KV;
+    if (li + 1 < nlist)
+        attn_load_kv<CFG>(qkv, offsets, s_items[li + 1], smem + CFG::OFF_KV + ((li + 1) & 1) * 2 * CFG::KV, tid);
     const uint32_t sbo_np = (uint32_t)(np / 16) * 128;
     const int nchunks = np >> 4;  // 16-column chunks
 
@@ -213,9 +241,7 @@ __global__ void __launch_bounds__(CFG::THREADS) attention_tc_kernel(const int8_t
                 }
             }
             sred[part * 128 + lrow] = mxa;
-        }
-        __syncthreads();
-        if (live) {
+            quad_sync<CFG>(quad);  // the SPLIT warps of this lane quadrant (live is quad-uniform)
             int32_t mraw = sred[lrow];
 #pragma unroll
             for (int q = 1; q < CFG::SPLIT; ++q) mraw = max(mraw, sred[q * 128 + lrow]);
@@ -233,9 +259,7 @@ __global__ void __launch_bounds__(CFG::THREADS) attention_tc_kernel(const int8_t
             }
             tc05::wait_st();
             sred[(CFG::SPLIT + part) * 128 + lrow] = (int32_t)sum;
-        }
-        __syncthreads();
-        if (live) {
+            quad_sync<CFG>(quad);
             uint32_t tot = 0;
 #pragma unroll
             for (int q = 0; q < CFG::SPLIT; ++q) tot += (uint32_t)sred[(CFG::SPLIT + q) * 128 + lrow];
@@ -308,6 +332,7 @@ __global__ void __launch_bounds__(CFG::THREADS) attention_tc_kernel(const int8_t
     __syncthreads();  // s_items is rewritten by the next batch
     }  // candidate batches
 
+    asm volatile("cp.async.wait_all;\n" ::: "memory");  // a prefetch may be left after an abort
     if (*abort_flag) {
         if (tid == 0) atomicExch(err, 1);
         // let any MMA still in flight drain (bounded) before the TMEM is released
