@@ -113,6 +113,23 @@ __device__ __forceinline__ void attn_load_kv(const int8_t *qkv, const int32_t *o
     asm volatile("cp.async.commit_group;\n" ::: "memory");
 }
 
+// Asynchronous copy of the 128-row Q tile t of item `item` (rows past the image are
+// zero-filled) into the K-major Q buffer.
+template <class CFG>
+__device__ __forceinline__ void attn_load_q(const int8_t *qkv, const int32_t *offsets, int item, int t, uint8_t *sq,
+                                            int tid) {
+    const int img = item / 3, head = item - img * 3;
+    const int row0 = offsets[img], n = offsets[img + 1] - row0;
+    for (int c = tid; c < 128 * 4; c += CFG::THREADS) {
+        const int r = c >> 2, ch = c & 3, gr = t * 128 + r;
+        const int8_t *src = qkv + (size_t)(row0 + (gr < n ? gr : 0)) * 576 + head * 64 + ch * 16;
+        const uint32_t dst = tc05::smem_u32(sq + tc05::kmajor_offset(r, ch * 16, 64));
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(dst), "l"(src), "r"(gr < n ? 16 : 0)
+                     : "memory");
+    }
+    asm volatile("cp.async.commit_group;\n" ::: "memory");
+}
+
 // Barrier of the SPLIT warps that share TMEM lane quadrant `quad` (ids 1..4).
 template <class CFG>
 __device__ __forceinline__ void quad_sync(int quad) {
@@ -174,7 +191,10 @@ __global__ void __launch_bounds__(CFG::THREADS) attention_tc_kernel(const int8_t
     }
     __syncthreads();
     const int nlist = s_nitems;
-    if (nlist > 0) attn_load_kv<CFG>(qkv, offsets, s_items[0], smem + CFG::OFF_KV, tid);
+    if (nlist > 0) {
+        attn_load_kv<CFG>(qkv, offsets, s_items[0], smem + CFG::OFF_KV, tid);
+        attn_load_q<CFG>(qkv, offsets, s_items[0], 0, sQ, tid);
+    }
     for (int li = 0; li < nlist && !*abort_flag; ++li) {
     const int item = s_items[li];
     const int img = item / 3, head = item - img * 3;
@@ -191,16 +211,12 @@ __global__ void __launch_bounds__(CFG::THREADS) attention_tc_kernel(const int8_t
     if (li + 1 < nlist)
         attn_load_kv<CFG>(qkv, offsets, s_items[li + 1], smem + CFG::OFF_KV + ((li + 1) & 1) * 2 * CFG::KV, tid);
     const uint32_t sbo_np = (uint32_t)(np / 16) * 128;
-    const int nchunks = np >> 4;  // 16-column chunks
+    const int nchunks = np >> 4;       // 16-column chunks of P
+    const int nvalid = (n + 15) >> 4;  // chunks holding at least one real column
 
     for (int t = 0; t * 128 < n; ++t) {
-        // ---- Q tile ------------------------------------------------------------
-        for (int c = tid; c < 128 * 4; c += CFG::THREADS) {
-            const int r = c >> 2, ch = c & 3, gr = t * 128 + r;
-            int4 qv = make_int4(0, 0, 0, 0);
-            if (gr < n) qv = *(const int4 *)(qkv + (size_t)(row0 + gr) * 576 + head * 64 + ch * 16);
-            *(int4 *)(sQ + tc05::kmajor_offset(r, ch * 16, 64)) = qv;
-        }
+        // ---- Q tile: its copies were issued when the previous P.V completed --------
+        asm volatile("cp.async.wait_all;\n" ::: "memory");
         tc05::fence_proxy_async();
         tc05::fence_before();
         __syncthreads();
@@ -226,7 +242,7 @@ __global__ void __launch_bounds__(CFG::THREADS) attention_tc_kernel(const int8_t
         const int nfull = n & ~15;
         if (live) {
             int32_t mxa = INT32_MIN;
-            for (int c = part; c < nchunks; c += CFG::SPLIT) {
+            for (int c = part; c < nvalid; c += CFG::SPLIT) {
                 const int c0 = c * 16;
                 uint32_t v[16];
                 tc05::ld16(lane_addr + c0, v);
@@ -248,7 +264,7 @@ __global__ void __launch_bounds__(CFG::THREADS) attention_tc_kernel(const int8_t
             const int32_t mx = q16_of<FAST>(mraw, p);
             const int32_t cm = (int32_t)((int64_t)p.fast_half - ((int64_t)mx << p.fast_shift));
             uint32_t sum = 0;
-            for (int c = part; c < nchunks; c += CFG::SPLIT) {
+            for (int c = part; c < nvalid; c += CFG::SPLIT) {
                 const int c0 = c * 16;
                 uint32_t v[16];
                 tc05::ld16(lane_addr + c0, v);
@@ -266,6 +282,10 @@ __global__ void __launch_bounds__(CFG::THREADS) attention_tc_kernel(const int8_t
             const uint64_t rc = softmax_recip(tot ? tot : 1u);
             for (int c = part; c < nchunks; c += CFG::SPLIT) {
                 const int c0 = c * 16;
+                if (c >= nvalid) {  // padding columns: zero probabilities
+                    *(uint4 *)(sP + tc05::kmajor_offset(lrow, c0, np)) = make_uint4(0, 0, 0, 0);
+                    continue;
+                }
                 uint32_t v[16];
                 tc05::ld16(lane_addr + c0, v);
                 tc05::wait_ld();
@@ -303,6 +323,10 @@ __global__ void __launch_bounds__(CFG::THREADS) attention_tc_kernel(const int8_t
         __syncthreads();
         if (*abort_flag) break;
         tc05::fence_after();
+        // P (and with it the Q buffer it overlays) is free: the next tile's Q copies
+        // overlap this tile's context epilogue
+        if ((t + 1) * 128 < n) attn_load_q<CFG>(qkv, offsets, item, t + 1, sQ, tid);
+        else if (li + 1 < nlist) attn_load_q<CFG>(qkv, offsets, s_items[li + 1], 0, sQ, tid);
         const int r = t * 128 + lrow;
         if (live) {
             for (int pc = part; pc < 4; pc += CFG::SPLIT) {  // 16-column pieces of the 64 head dims
