@@ -267,6 +267,11 @@ def main():
         out = eng.infer(imgs)
         return gather_outputs(out["logits"], out["token_counts"], world)
 
+    # The first launch of the profiled stage in each step (block 1's, the largest) is
+    # bracketed by CUDA events inside the replayed graph; the warm-up captures that
+    # graph, so the timed steps only replay it.  One bracketed launch per step keeps
+    # the events from breaking more than one programmatic-launch edge.
+    _lib.check(_lib.lib().hv_profile_start(eng.handle, STAGES[args.profile_stage], 1))
     for _ in range(args.warmup):
         logits, counts = step()
     torch.cuda.synchronize()
@@ -275,7 +280,7 @@ def main():
     stream = torch.cuda.current_stream()
     sampler = ClockSampler(physical_gpu_index(torch, local)) if rank == 0 else None
     time.sleep(0.3 if sampler else 0)
-    _lib.check(_lib.lib().hv_profile_start(eng.handle, STAGES[args.profile_stage], 64 * args.steps))
+    _lib.check(_lib.lib().hv_profile_start(eng.handle, STAGES[args.profile_stage], 1))
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
@@ -288,8 +293,11 @@ def main():
     if world > 1:
         dist.barrier()
     elapsed_ms = ev0.elapsed_time(ev1)
+    # the profiled launches of the last timed step (events recorded by its replay)
     launches, kms, krows = C.c_int(), C.c_double(), C.c_longlong()
     _lib.check(_lib.lib().hv_profile_stop(eng.handle, C.byref(launches), C.byref(kms), C.byref(krows)))
+    graph_kernels = C.c_int()
+    _lib.check(_lib.lib().hv_graph_kernels(eng.handle, C.byref(graph_kernels)))
     clocks = sampler.stop() if sampler else None
     if world > 1:
         t = torch.tensor([elapsed_ms], dtype=torch.float64, device="cuda")
@@ -334,13 +342,13 @@ def main():
             achieved = work / (kavg * 1e-3) / 1e12
             roof = {"bound": "tensor", "achieved": achieved, "peak": int8_tops, "unit": "TOPS",
                     "frac": achieved / int8_tops, "traffic": traffic, "traffic_unit": "bytes per launch",
-                    "kernel": f"{st} (int8 GEMM, {launches.value} launches, {kavg:.4f} ms avg)",
+                    "kernel": f"{st} (int8 GEMM; block 1's launch in the last timed step: {kavg:.4f} ms, {rows_avg:.0f} rows)",
                     "peak_source": int8_src, "work": "2*rows*K*N int8 ops per launch"}
         else:
             work = STAGE_BYTES_PER_ROW.get(st, 384) * krows.value / max(1, launches.value)
             achieved = work / (kavg * 1e-3) / 1e9
             roof = {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
-                    "traffic": traffic, "traffic_unit": "bytes per launch", "kernel": f"{st} ({launches.value} launches, {kavg:.4f} ms avg)",
+                    "traffic": traffic, "traffic_unit": "bytes per launch", "kernel": f"{st} (block 1's launch in the last timed step: {kavg:.4f} ms, {rows_avg:.0f} rows)",
                     "peak_source": "MEASURED_PEAKS.json hbm_gbs (of measured)"}
         line = {
             "metric": METRIC, "value": value, "unit": "images/s", "n_gpus": world, "steps": args.steps,
@@ -360,7 +368,7 @@ def main():
                     "d2h_bytes_per_step": b * 4000},
             # init + patch + 12 x 7 block kernels + 2 per selector + CLS LN + head, plus one
             # row-count copy per profiled launch
-            "gpu_launches": (7 * 12 + 2 * ns + 4) * args.steps + launches.value,
+            "gpu_launches": graph_kernels.value * args.steps,
             "clocks": clocks,
         }
         if world == 1 and not args.no_cpu_baseline:

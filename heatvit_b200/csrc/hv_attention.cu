@@ -72,23 +72,23 @@ __device__ __forceinline__ int32_t q16_of(int32_t acc, const AttnParams &p) {
     return (int32_t)requant64(score, p.q16_shift, 24);
 }
 
-// xt = q16(acc) - mx.  FAST: q16(acc) - mx = (acc + half - mx*2^s + sign) >> s exactly,
-// since mx*2^s is a multiple of 2^s; `cm` = half - mx*2^s is computed once per row
-// (|acc| <= 2^20 and |cm| <= 2^30 + 2^20 keep the sum inside int32).
+// n = mx - q16(acc) >= 0 (the negated softmax argument).  FAST: q16(acc) - mx =
+// (acc + cm + sign) >> s exactly with cm = half - mx*2^s, since mx*2^s is a multiple
+// of 2^s; its negation is (cmn - acc - sign) >> s with cmn = 2^s - 1 - cm, computed
+// once per row.  |acc| <= 2^20 and |mx*2^s| <= 2^30 + 2^20 keep the sum inside int32.
 template <bool FAST>
-__device__ __forceinline__ int32_t xt_of(int32_t acc, int32_t mx, int32_t cm, const AttnParams &p) {
-    if (FAST) return (acc + cm + ((acc >> 31) & p.fast_negmask)) >> p.fast_shift;
-    return q16_of<false>(acc, p) - mx;
+__device__ __forceinline__ uint32_t negxt_of(int32_t acc, int32_t mx, int32_t cmn, const AttnParams &p) {
+    if (FAST) return (uint32_t)((cmn - acc - ((acc >> 31) & p.fast_negmask)) >> p.fast_shift);
+    return (uint32_t)(mx - q16_of<false>(acc, p));
 }
 
-// exp terms of one 16-column chunk (columns >= valid are masked to 0); returns their sum.
 template <bool FAST, bool MASK>
-__device__ __forceinline__ uint32_t chunk_exp(uint32_t (&v)[16], int valid, int32_t mx, int32_t cm,
+__device__ __forceinline__ uint32_t chunk_exp(uint32_t (&v)[16], int valid, int32_t mx, int32_t cmn,
                                               const AttnParams &p) {
     uint32_t sum = 0;
 #pragma unroll
     for (int j = 0; j < 16; ++j) {
-        uint32_t e = softmax_exp_q16(xt_of<FAST>((int32_t)v[j], mx, cm, p));
+        uint32_t e = softmax_exp_q16_n(negxt_of<FAST>((int32_t)v[j], mx, cmn, p));
         if (MASK && j >= valid) e = 0u;
         v[j] = e;
         sum += e;
@@ -262,15 +262,16 @@ __global__ void __launch_bounds__(CFG::THREADS) attention_tc_kernel(const int8_t
 #pragma unroll
             for (int q = 1; q < CFG::SPLIT; ++q) mraw = max(mraw, sred[q * 128 + lrow]);
             const int32_t mx = q16_of<FAST>(mraw, p);
-            const int32_t cm = (int32_t)((int64_t)p.fast_half - ((int64_t)mx << p.fast_shift));
+            const int32_t cmn =
+                (int32_t)(((int64_t)1 << p.fast_shift) - 1 - p.fast_half + ((int64_t)mx << p.fast_shift));
             uint32_t sum = 0;
             for (int c = part; c < nvalid; c += CFG::SPLIT) {
                 const int c0 = c * 16;
                 uint32_t v[16];
                 tc05::ld16(lane_addr + c0, v);
                 tc05::wait_ld();
-                if (c0 < nfull) sum += chunk_exp<FAST, false>(v, 16, mx, cm, p);
-                else sum += chunk_exp<FAST, true>(v, n - c0, mx, cm, p);
+                if (c0 < nfull) sum += chunk_exp<FAST, false>(v, 16, mx, cmn, p);
+                else sum += chunk_exp<FAST, true>(v, n - c0, mx, cmn, p);
                 tc05::st16(lane_addr + c0, v);
             }
             tc05::wait_st();

@@ -314,6 +314,22 @@ HV_DEV uint32_t softmax_exp_q16(int32_t xt) {
     return out;
 }
 
+// softmax_exp_q16 of xt = -n, in 32-bit pieces.  With sh' = 88670 - r - 65536 =
+// z*45426 + 23134 - n in [-22291, 23134]: rsa(sh^2, 16) = 65536 + 2*sh' + t,
+// t = (sh'^2 + 32768) >> 16, so e = 46039 + floor((46990*sh' + 23495*t + 32768) / 2^16)
+// (the 2^32 and 2^17*sh' parts are whole multiples of 2^16).  Equal to
+// softmax_exp_q16(-n) for every n in [0, 2^31), checked exhaustively on the host.
+HV_DEV uint32_t softmax_exp_q16_n(uint32_t n) {
+    const uint32_t z = __umulhi(n, 3098170395u) >> 15;
+    const int32_t shp = (int32_t)(z * 45426u + 23134u - n);
+    const int32_t t = (int32_t)(((uint32_t)(shp * shp) + 32768u) >> 16);
+    const int32_t u = 46990 * shp + 23495 * t + 32768;
+    const uint32_t e = (uint32_t)((u >> 16) + 46039);
+    uint32_t out;
+    asm("shr.b32 %0, %1, %2;" : "=r"(out) : "r"(e), "r"(z));
+    return out;
+}
+
 // recip = round_div(2^32, S) for S >= 1.
 HV_DEV uint64_t softmax_recip(uint64_t s) {
     uint64_t q = ((uint64_t)1 << 32) / s, r = ((uint64_t)1 << 32) - q * s;

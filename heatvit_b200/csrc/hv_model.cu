@@ -132,6 +132,9 @@ struct GraphEntry {
     hv_selector_summary *sum = nullptr;
     uint8_t *warn = nullptr;
     unsigned long long stamp = 0;
+    int prof_stage = 0;  // stage whose launches the graph brackets with profiling events
+    int prof_n = 0;      // profiling event pairs recorded by one replay
+    int kernels = 0;     // kernel nodes in the graph
 };
 
 struct hv_model {
@@ -184,6 +187,7 @@ struct hv_model {
 
     // kernel timing (hv_profile_*)
     int prof_stage = 0, prof_max = 0, prof_n = 0;
+    int last_graph_kernels = 0;  // kernel nodes of the last replayed graph
     std::vector<cudaEvent_t> prof_ev;
     int32_t *prof_rows = nullptr;  // device [prof_max] live row counts
 
@@ -350,6 +354,15 @@ cudaError_t model_gemm(const hv_model *m, GemmArgs &g, int epi, int m_max, cudaS
 }
 
 __global__ void copy_rows_kernel(const int32_t *src, int32_t *dst) { *dst = *src; }
+__global__ void set_rows_kernel(int32_t v, int32_t *dst) { *dst = v; }
+
+// Record a profiling event; under stream capture it becomes an external event
+// record node, so the host can time it after each replay.
+inline void prof_record(cudaEvent_t e, cudaStream_t st) {
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    cudaStreamIsCapturing(st, &cs);
+    cudaEventRecordWithFlags(e, st, cs == cudaStreamCaptureStatusActive ? cudaEventRecordExternal : cudaEventRecordDefault);
+}
 
 // Profiling bracket: begin/end around one launch of `stage` when enabled.
 struct Prof {
@@ -358,14 +371,15 @@ struct Prof {
     Prof(hv_model *m_, int stage, cudaStream_t st) : m(m_), on(0) {
         if (m->prof_stage == stage && m->prof_n < m->prof_max) {
             on = 1;
-            cudaEventRecord(m->prof_ev[2 * m->prof_n], st);
+            prof_record(m->prof_ev[2 * m->prof_n], st);
         }
     }
     void end(cudaStream_t st, const int32_t *rows_dev, int rows_host) {
         if (!on) return;
-        cudaEventRecord(m->prof_ev[2 * m->prof_n + 1], st);
+        prof_record(m->prof_ev[2 * m->prof_n + 1], st);
+        // a kernel, not a host copy, so that a captured graph holds the value itself
         if (rows_dev) copy_rows_kernel<<<1, 1, 0, st>>>(rows_dev, m->prof_rows + m->prof_n);
-        else cudaMemcpyAsync(m->prof_rows + m->prof_n, &rows_host, 4, cudaMemcpyHostToDevice, st);
+        else set_rows_kernel<<<1, 1, 0, st>>>(rows_host, m->prof_rows + m->prof_n);
         m->prof_n++;
     }
 };
@@ -832,13 +846,16 @@ int run_graph(hv_model *m, const int8_t *img, int batch, int32_t *lg, int32_t *t
     GraphEntry *hit = nullptr, *victim = &m->graphs[0];
     for (GraphEntry &g : m->graphs) {
         if (g.exec && g.img == img && g.batch == batch && g.ws == wsi && g.lg == lg && g.tc == tc && g.sum == sum &&
-            g.warn == warn)
+            g.warn == warn && g.prof_stage == m->prof_stage)
             hit = &g;
         if (!g.exec || g.stamp < victim->stamp) victim = &g;
     }
     if (!hit) {
         int rc = ensure_capacity(m, batch, wsi);  // allocations stay outside the capture
         if (rc) return rc;
+        // Under profiling, the capture records the event pairs 0..n-1 around the
+        // stage's launches; every replay records the same events again.
+        m->prof_n = 0;
         cudaGraph_t graph = nullptr;
         CUDA_TRY(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
         rc = infer_impl(m, img, batch, lg, tc, sum, warn, nullptr, nullptr, st, wsi);
@@ -848,15 +865,27 @@ int run_graph(hv_model *m, const int8_t *img, int batch, int32_t *lg, int32_t *t
             return rc;
         }
         if (ce != cudaSuccess) return fail(HV_ERR_CUDA, "graph capture: %s", cudaGetErrorString(ce));
+        int kernels = 0;
+        size_t nn = 0;
+        if (cudaGraphGetNodes(graph, nullptr, &nn) == cudaSuccess && nn > 0) {
+            std::vector<cudaGraphNode_t> nodes(nn);
+            if (cudaGraphGetNodes(graph, nodes.data(), &nn) == cudaSuccess)
+                for (size_t i = 0; i < nn; ++i) {
+                    cudaGraphNodeType ty;
+                    if (cudaGraphNodeGetType(nodes[i], &ty) == cudaSuccess && ty == cudaGraphNodeTypeKernel) ++kernels;
+                }
+        }
         cudaGraphExec_t exec = nullptr;
         const cudaError_t ie = cudaGraphInstantiate(&exec, graph, 0);
         cudaGraphDestroy(graph);
         if (ie != cudaSuccess) return fail(HV_ERR_CUDA, "graph instantiate: %s", cudaGetErrorString(ie));
         if (victim->exec) cudaGraphExecDestroy(victim->exec);
-        *victim = GraphEntry{exec, img, batch, wsi, lg, tc, sum, warn, 0};
+        *victim = GraphEntry{exec, img, batch, wsi, lg, tc, sum, warn, 0, m->prof_stage, m->prof_n, kernels};
         hit = victim;
     }
     hit->stamp = ++m->graph_clock;
+    if (m->prof_stage) m->prof_n = hit->prof_n;
+    m->last_graph_kernels = hit->kernels;
     use_workspace(m, wsi);
     CUDA_TRY(cudaGraphLaunch(hit->exec, st));
     return HV_OK;
@@ -931,7 +960,7 @@ int hv_infer_batch(hv_model *m, const int8_t *d_images, int batch, int32_t *d_lo
                    hv_selector_summary *d_summary, uint8_t *d_warnings, void *stream) {
     if (!m) return fail(HV_ERR_VALUE, "null model");
     cudaStream_t st = (cudaStream_t)stream;
-    if (!m->use_graphs || m->prof_stage || batch <= 0 || !d_images || !d_logits)
+    if (!m->use_graphs || batch <= 0 || !d_images || !d_logits)
         return infer_impl(m, d_images, batch, d_logits, d_token_counts, d_summary, d_warnings, nullptr, nullptr, st);
     // Replay on the model's own stream, ordered after and before the caller's work on
     // `stream`; outputs go to workspace buffers and are copied out on `stream`.
@@ -1159,6 +1188,12 @@ int hv_profile_stop(hv_model *m, int *launches, double *total_ms, long long *row
     if (launches) *launches = n;
     if (total_ms) *total_ms = tot;
     if (rows) *rows = rsum;
+    return HV_OK;
+}
+
+int hv_graph_kernels(hv_model *m, int *kernels) {
+    if (!m || !kernels) return fail(HV_ERR_VALUE, "null argument");
+    *kernels = m->last_graph_kernels;
     return HV_OK;
 }
 

@@ -219,6 +219,11 @@ HV_API int hv_profile_start(hv_model *model, int stage, int max_launches);
  * in milliseconds and the summed live row count of those launches (read back
  * from the device after the events complete). */
 HV_API int hv_profile_stop(hv_model *model, int *launches, double *total_ms, long long *rows);
+/* Kernel nodes of the CUDA graph that the last graph-replayed hv_infer_batch ran
+ * (0 before any replay).  Under profiling, hv_infer_batch replays a graph that holds
+ * the profiling events, and hv_profile_stop reports the launches of its last replay.
+ * No counterpart in the reference. */
+HV_API int hv_graph_kernels(hv_model *model, int *kernels);
 
 /* ---- per-operator entry points (unit configs; device buffers) --------------------- */
 
