@@ -28,7 +28,7 @@ namespace hv {
 enum Epi { EPI_I8 = 0, EPI_I8_RES = 1, EPI_GELU = 2, EPI_PATCH = 3, EPI_I32 = 4, EPI_ACC64 = 5 };
 
 // Largest exact GELU-chain output table (bytes) an FC1 launch keeps in shared memory.
-constexpr int kGeluTableMax = 20480;
+constexpr int kGeluTableMax = 22528;
 
 // Per-launch epilogue constants (all derived on the host from the golden
 // scale exponents).
@@ -45,13 +45,19 @@ struct EpiParams {
     int gelu_fast;            // host-checked ranges of gelu_chain_fast hold
     int gelu_k2;              // host-checked ranges of gelu_chain_fast2 hold (persistent kernel)
     GeluK gk;                 // constants of gelu_chain_fast2 (also the input shift of the table form)
-    // exact output table of the GELU chain (persistent kernel):
-    // out = gtab[clamp(q - gtab_lo, 0, gtab_n - 1)], q = rsa(acc + bias, sh_in), exact
-    // for q in [gtab_elo, gtab_ehi); a warp whose 32 values include one outside that
-    // range evaluates them with gelu_chain_fast2 instead (gelu_k2 must then hold)
+    // exact output tables of the GELU chain (persistent kernel), q = rsa(acc + bias, sh_in),
+    // u = clamp(q - gtab_lo, 0, gtab_n - 1):
+    //  gtab_mode 1: out = gtab[u], exact for q in [gtab_elo, gtab_ehi); a warp whose 32
+    //    values include one outside that range evaluates them with gelu_chain_fast2
+    //    instead (gelu_k2 must then hold);
+    //  gtab_mode 2 (buckets of 2^gtab_k inputs): e = coarse[u >> k] (uint32 at gtab),
+    //    p = e >> 16; p == 0xFFFF: out = fine[(e & 0xFFFF) * 2^k + (u & (2^k - 1))]
+    //    (bytes at gtab + gtab_fine), else out = (int8)(u & (2^k - 1) >= p ? e >> 8 : e)
     const int8_t *gtab;
-    int gtab_lo, gtab_n;      // gtab_n in [1, kGeluTableMax]; 0 = no table
+    int gtab_lo, gtab_n;      // gtab_n = input span; 0 = no table
     int gtab_elo, gtab_ehi;
+    int gtab_mode, gtab_k, gtab_fine;
+    int gtab_bytes;           // bytes to stage in shared memory, at most kGeluTableMax
     // patch (EPI_PATCH): pos [197][192], add = (a = embed, b = pos)
     const int8_t *pos;
 };

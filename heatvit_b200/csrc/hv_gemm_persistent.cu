@@ -150,7 +150,7 @@ __global__ void __launch_bounds__(PT_THREADS, 1) tcp_gemm_kernel(GemmArgs g, int
     for (int i = tid; i < N; i += PT_THREADS) sbias[i] = g.epi.bias ? g.epi.bias[i] : 0;
     int8_t *stab = (int8_t *)(smem + L::OFF_TAB);
     if (EPI == EPI_GELU && L::TABB > 0)  // the table allocation is padded to 16 bytes
-        for (int i = tid; i < (g.epi.gtab_n + 15) / 16; i += PT_THREADS)
+        for (int i = tid; i < (g.epi.gtab_bytes + 15) / 16; i += PT_THREADS)
             ((uint4 *)stab)[i] = ((const uint4 *)g.epi.gtab)[i];
     asm volatile("cp.async.wait_all;\n" ::: "memory");
     // Everything above touches only weights and on-chip state; from here on the
@@ -337,7 +337,31 @@ __global__ void __launch_bounds__(PT_THREADS, 1) tcp_gemm_kernel(GemmArgs g, int
                     const uint32_t aux[8] = {r0.x, r0.y, r0.z, r0.w, r1.x, r1.y, r1.z, r1.w};
                     uint32_t pk[8];
                     bool slow = true;
-                    if (EPI == EPI_GELU && FAST && L::TABB > 0 && g.epi.gtab_n > 0) {
+                    if (EPI == EPI_GELU && FAST && L::TABB > 0 && g.epi.gtab_mode == 2) {
+                        // exact bucket table over the whole window (see EpiParams)
+                        const GeluK &k = g.epi.gk;
+                        const int lo = g.epi.gtab_lo, last = g.epi.gtab_n - 1, kb = g.epi.gtab_k;
+                        const int msk = (1 << kb) - 1;
+                        const uint32_t *coarse = (const uint32_t *)stab;
+                        const int8_t *fine = stab + g.epi.gtab_fine;
+#pragma unroll
+                        for (int w = 0; w < 8; ++w) {
+                            int32_t o[4];
+#pragma unroll
+                            for (int b = 0; b < 4; ++b) {
+                                const int32_t x = (int32_t)v[w * 4 + b] + bv[w * 4 + b];
+                                const int32_t q = (x + k.hin + mulhi_s(x, k.ksgn)) >> k.sh_in;
+                                const int u = min(max(q - lo, 0), last);
+                                const uint32_t e = coarse[u >> kb];
+                                const int off = u & msk;
+                                const uint32_t pcut = e >> 16;
+                                o[b] = off >= (int)pcut ? (int32_t)(int8_t)(e >> 8) : (int32_t)(int8_t)e;
+                                if (pcut == 0xFFFFu) o[b] = fine[(int)((e & 0xFFFFu) << kb) + off];
+                            }
+                            pk[w] = pack_sat8(o[0], o[1], o[2], o[3]);
+                        }
+                        slow = false;
+                    } else if (EPI == EPI_GELU && FAST && L::TABB > 0 && g.epi.gtab_mode == 1) {
                         // exact table of the GELU chain, valid for q in [elo, ehi)
                         const GeluK &k = g.epi.gk;
                         const int lo = g.epi.gtab_lo, last = g.epi.gtab_n - 1;

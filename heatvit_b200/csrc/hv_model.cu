@@ -91,6 +91,7 @@ struct BlockDev {
     size_t fc1_tab;            // exact GELU-chain table in the arena (fc1_tab_n > 0)
     int fc1_tab_lo, fc1_tab_n;
     int fc1_tab_elo, fc1_tab_ehi;  // the table is exact for q in [elo, ehi)
+    int fc1_tab_mode, fc1_tab_k, fc1_tab_fine, fc1_tab_bytes;  // EpiParams gtab_* fields
     AlignAdd res1, res2;
     AttnParams attn;
 };
@@ -446,6 +447,10 @@ int run_block(hv_model *m, int b, int images, const int32_t *off, int may_be_sho
         g.epi.gtab_n = d.fc1_tab_n;
         g.epi.gtab_elo = d.fc1_tab_elo;
         g.epi.gtab_ehi = d.fc1_tab_ehi;
+        g.epi.gtab_mode = d.fc1_tab_n > 0 ? d.fc1_tab_mode : 0;
+        g.epi.gtab_k = d.fc1_tab_k;
+        g.epi.gtab_fine = d.fc1_tab_fine;
+        g.epi.gtab_bytes = d.fc1_tab_bytes;
         CUDA_TRY(model_gemm(m, g, EPI_GELU, rows_max, st));
         pr.end(st, rows_dev, 0);
     }
@@ -565,23 +570,30 @@ struct TabWindow {
 // beyond it would take the slower escape path.
 constexpr int64_t kEscapeRadiusMin = 65536;
 
+// The int8 output of the GELU chain for every Q8.16 input in [-qmax, qmax] (index
+// i is q = i - qmax), from the device functions the exhaustive tests cover.
+int gelu_scan(int32_t qmax, int sh_out, std::vector<int8_t> &f) {
+    const int64_t total = 2 * (int64_t)qmax + 1;
+    int8_t *d_f = nullptr;
+    f.resize((size_t)total);
+    cudaError_t e = cudaMalloc(&d_f, (size_t)total);
+    if (e == cudaSuccess) e = launch_gelu_table_fill(d_f, -qmax, (int32_t)total, sh_out, nullptr);
+    if (e == cudaSuccess) e = cudaMemcpy(f.data(), d_f, (size_t)total, cudaMemcpyDeviceToHost);
+    if (d_f) cudaFree(d_f);
+    if (e != cudaSuccess) return fail(HV_ERR_CUDA, "GELU table scan: %s", cudaGetErrorString(e));
+    return HV_OK;
+}
+
 // Choose a table of at most kGeluTableMax entries for a GELU chain whose output
 // varies over more than that across the reachable inputs [-qmax, qmax].  The table
 // [t0, t1) must contain q = 0; with its first and last entries repeated by the
 // clamp, it is exact from the start of the constant run holding t0 to the end of
 // the run holding t1 - 1.  Among the tables that start at the end of a run, the one
 // whose exact range reaches farthest from 0 on its nearer side is taken, if that
-// distance is at least kEscapeRadiusMin.  *ok = false leaves the FMA form.
-int gelu_escape_window(int32_t qmax, int sh_out, TabWindow *tw, bool *ok) {
+// distance is at least kEscapeRadiusMin.  *ok = false when none qualifies.
+void gelu_escape_window(const std::vector<int8_t> &f, int32_t qmax, TabWindow *tw, bool *ok) {
     *ok = false;
-    const int64_t total = 2 * (int64_t)qmax + 1;
-    int8_t *d_f = nullptr;
-    std::vector<int8_t> f((size_t)total);
-    cudaError_t e = cudaMalloc(&d_f, (size_t)total);
-    if (e == cudaSuccess) e = launch_gelu_table_fill(d_f, -qmax, (int32_t)total, sh_out, nullptr);
-    if (e == cudaSuccess) e = cudaMemcpy(f.data(), d_f, (size_t)total, cudaMemcpyDeviceToHost);
-    if (d_f) cudaFree(d_f);
-    if (e != cudaSuccess) return fail(HV_ERR_CUDA, "GELU table scan: %s", cudaGetErrorString(e));
+    const int64_t total = (int64_t)f.size();
     // run r covers indices [starts[r], starts[r + 1]); index i is q = i - qmax
     std::vector<int64_t> starts{0};
     for (int64_t i = 1; i < total; ++i)
@@ -611,7 +623,69 @@ int gelu_escape_window(int32_t qmax, int sh_out, TabWindow *tw, bool *ok) {
         }
     }
     *ok = best >= kEscapeRadiusMin;
-    return HV_OK;
+}
+
+// Two-level exact table of the whole window [w0, w1] outside which the output is
+// constant (clamped indices repeat its end values).  The window is cut into buckets
+// of 2^k inputs.  A bucket whose output changes at most once is one uint32
+// coarse entry: v0 | v1 << 8 | p << 16 (v0 before offset p, v1 from it; p = 0x8000
+// when constant).  A bucket with more changes gets p = 0xFFFF, and its low 16 bits
+// index a 2^k-byte fine table stored after the coarse entries.  The smallest k in
+// [3, 10] whose table fits kGeluTableMax is taken; *ok = false when none does.
+struct BucketTable {
+    int32_t lo, n;
+    int k, fine_off;
+    std::vector<uint8_t> blob;
+};
+void gelu_bucket_table(const std::vector<int8_t> &f, int32_t qmax, BucketTable *bt, bool *ok) {
+    *ok = false;
+    const int64_t total = (int64_t)f.size();
+    int64_t w0 = -1, w1 = -1;
+    for (int64_t i = 1; i < total; ++i)
+        if (f[(size_t)i] != f[(size_t)i - 1]) {
+            if (w0 < 0) w0 = i - 1;
+            w1 = i;
+        }
+    if (w0 < 0) return;  // constant: the plain window table applies
+    const int64_t W = w1 - w0 + 1;
+    auto at = [&](int64_t u) { return f[(size_t)(w0 + std::min(u, W - 1))]; };
+    for (int k = 3; k <= 10; ++k) {
+        const int64_t B = (int64_t)1 << k, nb = (W + B - 1) / B;
+        int64_t nfine = 0;
+        for (int64_t b = 0; b < nb; ++b) {
+            int ch = 0;
+            for (int64_t j = 1; j < B; ++j) ch += at(b * B + j) != at(b * B + j - 1);
+            if (ch >= 2) ++nfine;
+        }
+        const int64_t fine_off = 4 * nb, bytes = fine_off + nfine * B;
+        if (bytes > kGeluTableMax || nfine > 0xFFFF) continue;
+        bt->lo = (int32_t)(w0 - qmax);
+        bt->n = (int32_t)W;
+        bt->k = k;
+        bt->fine_off = (int)fine_off;
+        bt->blob.assign((size_t)bytes, 0);
+        int64_t fi = 0;
+        for (int64_t b = 0; b < nb; ++b) {
+            int ch = 0, pos = 0;
+            for (int64_t j = 1; j < B; ++j)
+                if (at(b * B + j) != at(b * B + j - 1)) {
+                    ++ch;
+                    pos = (int)j;
+                }
+            uint32_t e;
+            if (ch >= 2) {
+                for (int64_t j = 0; j < B; ++j) bt->blob[(size_t)(fine_off + fi * B + j)] = (uint8_t)at(b * B + j);
+                e = (uint32_t)fi | (0xFFFFu << 16);
+                ++fi;
+            } else {
+                const uint32_t v0 = (uint8_t)at(b * B), v1 = (uint8_t)at(b * B + (ch ? pos : 0));
+                e = v0 | v1 << 8 | (uint32_t)(ch ? pos : 0x8000) << 16;
+            }
+            memcpy(bt->blob.data() + 4 * b, &e, 4);
+        }
+        *ok = true;
+        return;
+    }
 }
 
 int pack_model(hv_model *m, const hv_params *P) {
@@ -694,6 +768,7 @@ int pack_model(hv_model *m, const hv_params *P) {
             d.fc1_tab_n = 0;
             d.fc1_tab_elo = INT32_MIN;
             d.fc1_tab_ehi = INT32_MAX;
+            d.fc1_tab_mode = d.fc1_tab_k = d.fc1_tab_fine = d.fc1_tab_bytes = 0;
             if (!d.fc1_wide && d.fc1_sh_in >= 0 && d.fc1_sh_in <= 30 && vmax < ((int64_t)1 << 30)) {
                 const int64_t hin = d.fc1_sh_in > 0 ? (int64_t)1 << (d.fc1_sh_in - 1) : 0;
                 const int64_t qmax = (vmax + hin) >> d.fc1_sh_in;
@@ -703,18 +778,36 @@ int pack_model(hv_model *m, const hv_params *P) {
                     CUDA_TRY(gelu_table_window((int32_t)qmax, d.fc1_sh_out, mm, &wlo, &wn, nullptr));
                     TabWindow tw{wlo, wn, INT32_MIN, INT32_MAX};
                     bool ok = wn <= kGeluTableMax;
-                    if (!ok && d.fc1_k2) {
+                    BucketTable bt;
+                    bool bucket = false;
+                    if (!ok) {
                         // too wide for a whole-window table: a central table whose clamped
                         // ends cover long constant runs, with gelu_chain_fast2 outside them
-                        int rc = gelu_escape_window((int32_t)qmax, d.fc1_sh_out, &tw, &ok);
+                        // (needs the FMA form), else a two-level bucket table
+                        std::vector<int8_t> f;
+                        int rc = gelu_scan((int32_t)qmax, d.fc1_sh_out, f);
                         if (rc != HV_OK) return rc;
+                        if (d.fc1_k2) gelu_escape_window(f, (int32_t)qmax, &tw, &ok);
+                        if (!ok) gelu_bucket_table(f, (int32_t)qmax, &bt, &bucket);
                     }
                     if (ok) {
+                        d.fc1_tab_mode = 1;
                         d.fc1_tab = A.add(nullptr, ((size_t)tw.n + 15) & ~(size_t)15);
                         d.fc1_tab_lo = tw.lo;
                         d.fc1_tab_n = tw.n;
                         d.fc1_tab_elo = tw.elo;
                         d.fc1_tab_ehi = tw.ehi;
+                        d.fc1_tab_bytes = tw.n;
+                        d.fc1_gk = make_gelu_k(d.fc1_sh_in, d.fc1_k2 ? d.fc1_sh_out : 0);
+                    } else if (bucket) {
+                        bt.blob.resize((bt.blob.size() + 15) & ~(size_t)15, 0);
+                        d.fc1_tab_mode = 2;
+                        d.fc1_tab = A.add(bt.blob.data(), bt.blob.size());
+                        d.fc1_tab_lo = bt.lo;
+                        d.fc1_tab_n = bt.n;
+                        d.fc1_tab_k = bt.k;
+                        d.fc1_tab_fine = bt.fine_off;
+                        d.fc1_tab_bytes = (int)bt.blob.size();
                         d.fc1_gk = make_gelu_k(d.fc1_sh_in, d.fc1_k2 ? d.fc1_sh_out : 0);
                     }
                 }
@@ -826,7 +919,7 @@ int pack_model(hv_model *m, const hv_params *P) {
     CUDA_TRY(cudaMemcpy(m->weights, A.host.data(), A.host.size(), cudaMemcpyHostToDevice));
     for (int b = 0; b < HV_BLOCKS; ++b) {
         const BlockDev &d = m->blocks[b];
-        if (m->has_block[b] && d.fc1_tab_n > 0)
+        if (m->has_block[b] && d.fc1_tab_n > 0 && d.fc1_tab_mode == 1)
             CUDA_TRY(launch_gelu_table_fill((int8_t *)(m->weights + d.fc1_tab), d.fc1_tab_lo, d.fc1_tab_n, d.fc1_sh_out,
                                             nullptr));
     }

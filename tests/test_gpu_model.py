@@ -295,7 +295,9 @@ def test_model_parameter_errors(cuda):
                                        # short output windows: the exact table form
                                        (-13, -10, -15), (-14, -13, -18), (-12, -12, -16), (-12, -14, -14),
                                        # central tables with FMA-form escapes: often / seldom taken
-                                       (-8, -8, -11), (-9, -8, -11)])
+                                       (-8, -8, -11), (-9, -8, -11),
+                                       # two-level bucket tables over 300k+ input windows
+                                       (-8, -8, -8), (-9, -8, -10)])
 def test_ffn_gelu_epilogue_exponents(cuda, oracle, l2, w1, hid):
     """FC1's fused GELU epilogue (table, FMA-pipe and 64-bit forms) across
     input/output exponents, through the fused block kernel."""
