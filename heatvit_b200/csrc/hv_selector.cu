@@ -21,9 +21,9 @@ namespace {
 
 constexpr int THREADS = 512;
 constexpr int MAXC = 196;
-constexpr int LSTR = 36;   // local row stride (32 data bytes + 4 pad)
-constexpr int WSTR = 68;   // transposed 64-wide weight row stride
-constexpr int W2STR = 36;  // transposed 32-wide weight row stride
+constexpr int LSTR = 32;   // local / layer-1 row stride (read as two 16-byte words)
+constexpr int WSTR = 80;   // transposed 64-wide weight row stride: 16-byte rows, conflict-free per 8 lanes
+constexpr int W2STR = 48;  // transposed 32-wide weight row stride (same property)
 
 constexpr int OFF_TOK = 0;
 constexpr int SZ_TOK = 197 * 192;
@@ -57,12 +57,33 @@ constexpr int OFF_MISC = (OFF_STATS + SZ_STATS + 15) & ~15;
 constexpr int SZ_MISC = 128;  // [0] warn, [1] kept, [2] participants, [4..4+THREADS/32) scan
 constexpr int OFF_H1 = OFF_MISC + SZ_MISC;  // score layer-1 outputs [3][MAXC][LSTR]
 constexpr int SZ_H1 = 3 * MAXC * LSTR;
-constexpr int OFF_H2 = OFF_H1 + SZ_H1;      // score layer-2 outputs [3][MAXC][16]
+constexpr int OFF_H2 = OFF_LOCAL;           // score layer-2 outputs [3][MAXC][16], over the dead local rows
 constexpr int SZ_H2 = 3 * MAXC * 16;
-constexpr int SMEM_BYTES = OFF_H2 + SZ_H2;
+static_assert(SZ_H2 <= SZ_LOCAL, "layer-2 outputs overlay the local features");
+constexpr int SMEM_BYTES = OFF_H1 + SZ_H1;
 static_assert(2 * (SMEM_BYTES + 1024) <= 228 * 1024, "two selector CTAs per SM");
 
 __device__ __forceinline__ int32_t sat_q016(int64_t v) { return (int32_t)(v < 0 ? 0 : (v > 65536 ? 65536 : v)); }
+
+// acc + a · b over W 16-byte words of packed int8 (shared memory, 16-byte aligned).
+template <int W>
+__device__ __forceinline__ int32_t dot16(const int8_t *a, const int8_t *b, int32_t acc) {
+#pragma unroll
+    for (int w = 0; w < W; ++w) {
+        const int4 x = ((const int4 *)a)[w], y = ((const int4 *)b)[w];
+        acc = __dp4a(x.x, y.x, acc);
+        acc = __dp4a(x.y, y.y, acc);
+        acc = __dp4a(x.z, y.z, acc);
+        acc = __dp4a(x.w, y.w, acc);
+    }
+    return acc;
+}
+
+// (head, candidate) of a flattened head-major index hc = h * C + c, without a division.
+__device__ __forceinline__ void split_hc(int hc, int C, int &h, int &c) {
+    h = (hc >= C) + (hc >= 2 * C);
+    c = hc - h * C;
+}
 
 // One selector GELU chain (selector.py:89-99) in the fastest form the host proved exact.
 __device__ __forceinline__ int32_t sel_gelu(int64_t v, int k2, const GeluK &k, int fast, int sh_in, int sh_out) {
@@ -138,17 +159,21 @@ __global__ void __launch_bounds__(THREADS) selector_kernel(
 
     // ---- local MLP: local[h][c][j] ------------------------------------------------
     for (int idx = tid; idx < 3 * C * 32; idx += THREADS) {
-        const int j = idx & 31, hc = idx >> 5;
-        const int h = hc / C, c = hc - h * C;
-        const int32_t *trow = (const int32_t *)(tok + (1 + c) * 192 + 64 * h);
-        const int32_t *wrow = (const int32_t *)(lwt + (h * 32 + j) * WSTR);
-        int32_t acc = 0;
-#pragma unroll
-        for (int w = 0; w < 16; ++w) acc = __dp4a(trow[w], wrow[w], acc);
+        const int j = idx & 31;
+        int h, c;
+        split_hc(idx >> 5, C, h, c);
+        const int32_t acc = dot16<4>(tok + (1 + c) * 192 + 64 * h, lwt + (h * 32 + j) * WSTR, 0);
         local[(h * MAXC + c) * LSTR + j] = (int8_t)sel_gelu((int64_t)acc + p.local_b[h * 32 + j], p.local_k2,
                                                             p.local_k, p.local_fast, p.local_sh_in, p.local_sh_out);
     }
     __syncthreads();
+    if (dbg.local)  // exported now: the layer-2 outputs overwrite these rows later
+        for (int i = tid; i < 3 * C * 32; i += THREADS) {
+            const int j = i & 31;
+            int h, c;
+            split_hc(i >> 5, C, h, c);
+            dbg.local[(((size_t)img * 3 + h) * MAXC + c) * 32 + j] = local[(h * MAXC + c) * LSTR + j];
+        }
 
     // ---- global mean (selector.py:273-289) -----------------------------------------
     if (tid < 96) {
@@ -171,39 +196,31 @@ __global__ void __launch_bounds__(THREADS) selector_kernel(
     int8_t *h1s = (int8_t *)(smem + OFF_H1);
     int8_t *h2s = (int8_t *)(smem + OFF_H2);
     for (int idx = tid; idx < 3 * C * 32; idx += THREADS) {
-        const int j = idx & 31, hc = idx >> 5;
-        const int h = hc / C, c = hc - h * C;
-        const int32_t *lrow = (const int32_t *)(local + (h * MAXC + c) * LSTR);
-        const int32_t *wrow = (const int32_t *)(w1t + (h * 32 + j) * WSTR);
-        int32_t acc = 0;
-#pragma unroll
-        for (int w = 0; w < 8; ++w) acc = __dp4a(lrow[w], wrow[w], acc);
+        const int j = idx & 31;
+        int h, c;
+        split_hc(idx >> 5, C, h, c);
+        const int32_t acc = dot16<2>(local + (h * MAXC + c) * LSTR, w1t + (h * 32 + j) * WSTR, 0);
         h1s[(h * MAXC + c) * LSTR + j] =
             (int8_t)sel_gelu(acc + g1[h * 32 + j], p.h1_k2, p.h1_k, p.h1_fast, p.h1_sh_in, p.h1_sh_out);
     }
     __syncthreads();
     for (int idx = tid; idx < 3 * C * 16; idx += THREADS) {
-        const int m = idx & 15, hc = idx >> 4;
-        const int h = hc / C, c = hc - h * C;
-        const int32_t *hrow = (const int32_t *)(h1s + (h * MAXC + c) * LSTR);
-        const int32_t *wrow = (const int32_t *)(w2t + (h * 16 + m) * W2STR);
-        int32_t acc = 0;
-#pragma unroll
-        for (int w = 0; w < 8; ++w) acc = __dp4a(hrow[w], wrow[w], acc);
+        const int m = idx & 15;
+        int h, c;
+        split_hc(idx >> 4, C, h, c);
+        const int32_t acc = dot16<2>(h1s + (h * MAXC + c) * LSTR, w2t + (h * 16 + m) * W2STR, 0);
         h2s[(h * MAXC + c) * 16 + m] =
             (int8_t)sel_gelu((int64_t)acc + p.b2[h * 16 + m], p.h2_k2, p.h2_k, p.h2_fast, p.h2_sh_in, p.h2_sh_out);
     }
     __syncthreads();
     for (int it = tid; it < 3 * C; it += THREADS) {
-        const int h = it / C, c = it - h * C;
-        const int32_t *hrow = (const int32_t *)(h2s + (h * MAXC + c) * 16);
+        int h, c;
+        split_hc(it, C, h, c);
+        const int8_t *hrow = h2s + (h * MAXC + c) * 16;
         int32_t q[2];
 #pragma unroll
         for (int o = 0; o < 2; ++o) {
-            const int32_t *wrow = (const int32_t *)(w3t + (h * 2 + o) * 16);
-            int32_t acc = 0;
-#pragma unroll
-            for (int w = 0; w < 4; ++w) acc = __dp4a(hrow[w], wrow[w], acc);
+            const int32_t acc = dot16<1>(hrow, w3t + (h * 2 + o) * 16, 0);
             const int32_t logit = (int32_t)requant64((int64_t)acc + p.b3[h * 2 + o], p.logit_shift, 8);
             q[o] = (int32_t)requant64(logit, p.logit_q16_shift, 24);
         }
@@ -215,10 +232,16 @@ __global__ void __launch_bounds__(THREADS) selector_kernel(
         int32_t st[3];
 #pragma unroll
         for (int h = 0; h < 3; ++h) {
-            const int32_t *trow = (const int32_t *)(tok + (1 + c) * 192 + 64 * h);
+            const int4 *trow = (const int4 *)(tok + (1 + c) * 192 + 64 * h);
             int32_t t = 0;
 #pragma unroll
-            for (int w = 0; w < 16; ++w) t = __dp4a(trow[w], 0x01010101, t);
+            for (int w = 0; w < 4; ++w) {
+                const int4 x4 = trow[w];
+                t = __dp4a(x4.x, 0x01010101, t);
+                t = __dp4a(x4.y, 0x01010101, t);
+                t = __dp4a(x4.z, 0x01010101, t);
+                t = __dp4a(x4.w, 0x01010101, t);
+            }
             st[h] = sat8((int32_t)round_div64(t, 64));
             stats[c * 3 + h] = (int8_t)st[h];
         }
@@ -337,16 +360,12 @@ __global__ void __launch_bounds__(THREADS) selector_kernel(
         for (int c = tid; c < C; c += THREADS) dbg.fused[(size_t)img * MAXC + c] = fused[c];
     if (dbg.head_scores)
         for (int i = tid; i < 3 * C; i += THREADS) {
-            const int h = i / C, c = i - h * C;
+            int h, c;
+            split_hc(i, C, h, c);
             dbg.head_scores[((size_t)img * 3 + h) * MAXC + c] = hs[h * MAXC + c];
         }
     if (dbg.head_weights)
         for (int i = tid; i < 3 * C; i += THREADS) dbg.head_weights[(size_t)img * MAXC * 3 + i] = hwt[i];
-    if (dbg.local)
-        for (int i = tid; i < 3 * C * 32; i += THREADS) {
-            const int j = i & 31, hc = i >> 5, h = hc / C, c = hc - h * C;
-            dbg.local[(((size_t)img * 3 + h) * MAXC + c) * 32 + j] = local[(h * MAXC + c) * LSTR + j];
-        }
     if (dbg.global_ && tid < 96) dbg.global_[(size_t)img * 96 + tid] = glob[tid];
     if (dbg.stats)
         for (int i = tid; i < 3 * C; i += THREADS) dbg.stats[(size_t)img * MAXC * 3 + i] = stats[i];
