@@ -94,6 +94,10 @@ struct LnAff {
     int64_t khi;                 // floor(K / 2^32)
     int32_t vt;
     bool safe;
+    // short form (safe rows): A = aq*2^48 + ahh*2^16 + (A mod 2^16),
+    // K = kq*2^48 + khh*2^16 + (K mod 2^16), see ln_norm_short
+    uint32_t aq, ahh, khh;
+    int32_t kq;
 };
 
 __device__ __forceinline__ LnAff ln_aff(const LnStats &st, const LnParams &p) {
@@ -112,7 +116,26 @@ __device__ __forceinline__ LnAff ln_aff(const LnStats &st, const LnParams &p) {
     const i128 d1 = ((i128)127 << p.sh_sum) - st.mean, d2 = st.mean + ((i128)128 << p.sh_sum);
     const u128 dm = (u128)(d1 > d2 ? d1 : d2);
     f.safe = dm * st.inv + ((u128)1 << 47) < ((u128)1 << 71);
+    const u128 m48 = ((u128)1 << 48) - 1;
+    f.aq = (uint32_t)(A >> 48);
+    f.ahh = (uint32_t)((A & m48) >> 16);
+    f.kq = (int32_t)(K >> 48);                    // floor; in int32 range on safe rows
+    f.khh = (uint32_t)(((u128)K & m48) >> 16);    // K - kq*2^48 in [0, 2^48)
     return f;
+}
+
+// ln_norm_aff in 32-bit pieces, valid on safe rows.  With vp = v + 128 < 2^8,
+// R = vp*(A mod 2^48) + (K mod 2^48) = 2^16*t + e, t = vp*ahh + khh and
+// e = vp*(A mod 2^16) + (K mod 2^16) < 2^24, so floor(T / 2^48) =
+// vp*aq + kq + floor((t + floor(e / 2^16)) / 2^32) with floor(e / 2^16) <= 255.
+// When the low word of t lies in [1, 2^32 - 256] that is vp*aq + kq + (t >> 32)
+// exactly, and T is no multiple of 2^48 (no tie correction).  *ok = false
+// otherwise (about 2^-24 of inputs): the caller takes the exact form.
+__device__ __forceinline__ int32_t ln_norm_short(int32_t v, const LnAff &f, bool &ok) {
+    const uint32_t vp = (uint32_t)(v + 128);
+    const uint64_t t = (uint64_t)vp * f.ahh + f.khh;
+    ok = (uint32_t)t - 1u < 0xFFFFFF00u;
+    return (int32_t)(vp * f.aq) + f.kq + (int32_t)(t >> 32);
 }
 
 // norm of one int8 input on a safe row (see LnAff).
@@ -316,27 +339,37 @@ __global__ void __launch_bounds__(256, 3) ln_kernel(const int8_t *x, int8_t *out
 #pragma unroll 1
         for (int k = 0; k < g; ++k) {
             const int r = base + 4 * k + grp;
-            int32_t v[24];
-            ln_load24(x + (size_t)(r < rows ? r : 0) * 192, sub, r < rows, v);
-            int32_t s = 0;
+            uint2 w[3] = {make_uint2(0, 0), make_uint2(0, 0), make_uint2(0, 0)};
+            if (r < rows) {
+                const uint2 *src = (const uint2 *)(x + (size_t)r * 192 + 24 * sub);
+                w[0] = src[0];
+                w[1] = src[1];
+                w[2] = src[2];
+            }
+            // Σx and Σx² of the 24 bytes with 4-way byte dot products (|Σx²| < 2^21)
+            int32_t s = 0, q = 0;
 #pragma unroll
-            for (int i = 0; i < 24; ++i) s += v[i];
+            for (int i = 0; i < 3; ++i) {
+                s = __dp4a((int)w[i].x, 0x01010101, s);
+                s = __dp4a((int)w[i].y, 0x01010101, s);
+                q = __dp4a((int)w[i].x, (int)w[i].x, q);
+                q = __dp4a((int)w[i].y, (int)w[i].y, q);
+            }
             int64_t s2;
             if (p.sq_shift >= 0) {
-                int32_t q = 0;
-#pragma unroll
-                for (int i = 0; i < 24; ++i) q += v[i] * v[i];
 #pragma unroll
                 for (int o = 1; o < 8; o <<= 1) q += __shfl_xor_sync(0xffffffffu, q, o);
                 s2 = (int64_t)q << p.sq_shift;
             } else {
+                int32_t v[24];
+                ln_load24(x + (size_t)(r < rows ? r : 0) * 192, sub, r < rows, v);
                 const int kk = -p.sq_shift;  // per-element ties-away right shift (x^2 >= 0)
-                int64_t q = 0;
+                int64_t q64 = 0;
 #pragma unroll
-                for (int i = 0; i < 24; ++i) q += ((int64_t)(v[i] * v[i]) + ((int64_t)1 << (kk - 1))) >> kk;
+                for (int i = 0; i < 24; ++i) q64 += ((int64_t)(v[i] * v[i]) + ((int64_t)1 << (kk - 1))) >> kk;
 #pragma unroll
-                for (int o = 1; o < 8; o <<= 1) q += __shfl_xor_sync(0xffffffffu, q, o);
-                s2 = q;
+                for (int o = 1; o < 8; o <<= 1) q64 += __shfl_xor_sync(0xffffffffu, q64, o);
+                s2 = q64;
             }
 #pragma unroll
             for (int o = 1; o < 8; o <<= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
@@ -364,27 +397,34 @@ __global__ void __launch_bounds__(256, 3) ln_kernel(const int8_t *x, int8_t *out
             const int r = base + 4 * k + grp;
             const bool active = r < rows;
             const int owner = 4 * k + grp;
-            LnAff f;
-            f.al = __shfl_sync(0xffffffffu, af.al, owner);
-            f.ah0 = __shfl_sync(0xffffffffu, af.ah0, owner);
-            f.ah1 = __shfl_sync(0xffffffffu, af.ah1, owner);
-            f.klo = __shfl_sync(0xffffffffu, af.klo, owner);
-            f.khi = shfl64(af.khi, owner);
-            f.vt = __shfl_sync(0xffffffffu, af.vt, owner);
+            LnStats rs;
+            rs.mean = shfl64(st.mean, owner);
+            rs.inv = (uint64_t)shfl64((int64_t)st.inv, owner);
+            rs.neg = false;
             int32_t v[24];
             ln_load24(x + (size_t)(active ? r : 0) * 192, sub, active, v);
             int32_t o[24];
             if (all_safe) {
+                LnAff f;
+                f.aq = __shfl_sync(0xffffffffu, af.aq, owner);
+                f.ahh = __shfl_sync(0xffffffffu, af.ahh, owner);
+                f.khh = __shfl_sync(0xffffffffu, af.khh, owner);
+                f.kq = __shfl_sync(0xffffffffu, af.kq, owner);
 #pragma unroll
                 for (int i = 0; i < 24; ++i) {
-                    const int32_t nr = ln_norm_aff(v[i], f);
+                    bool ok;
+                    int32_t nr = ln_norm_short(v[i], f, ok);
+                    if (!ok) nr = ln_norm<SPLIT>(v[i], rs, p);
                     o[i] = OUT32 ? rsa32(nr * gam[i] + bet[i], p.sh_out) : ln_out<false>(nr, gam[i], bet[i], p);
                 }
             } else {
-                LnStats rs;
-                rs.mean = shfl64(st.mean, owner);
-                rs.inv = (uint64_t)shfl64((int64_t)st.inv, owner);
-                rs.neg = false;
+                LnAff f;
+                f.al = __shfl_sync(0xffffffffu, af.al, owner);
+                f.ah0 = __shfl_sync(0xffffffffu, af.ah0, owner);
+                f.ah1 = __shfl_sync(0xffffffffu, af.ah1, owner);
+                f.klo = __shfl_sync(0xffffffffu, af.klo, owner);
+                f.khi = shfl64(af.khi, owner);
+                f.vt = __shfl_sync(0xffffffffu, af.vt, owner);
                 const bool rsafe = __shfl_sync(0xffffffffu, af.safe ? 1 : 0, owner) != 0;
 #pragma unroll
                 for (int i = 0; i < 24; ++i) {
