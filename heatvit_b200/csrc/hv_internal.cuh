@@ -61,6 +61,23 @@ cudaError_t launch_attention(const int8_t *qkv, const int32_t *offsets, int imag
                              const AttnParams &p, int may_be_short, int sms, int *err, cudaStream_t st);
 
 // Device-resident selector weights and constants.
+// Exact output table of one GELU chain over the Q8.16 inputs q = rsa(v, sh_in) its
+// layer can reach; outside [lo, lo + n) the output is constant (clamped index):
+//   mode 1: out = tab[u], u = clamp(q - lo, 0, n - 1);
+//   mode 2: buckets of 2^k inputs: e = ((uint32 *)tab)[u >> k], p = e >> 16;
+//           p == 0xFFFF: out = tab[fine + (e & 0xFFFF) * 2^k + (u mod 2^k)],
+//           else out = (int8)(u mod 2^k >= p ? e >> 8 : e).
+// mode 0: no table.  bytes: the staged size (a multiple of 16).
+struct GeluTab {
+    const int8_t *tab;
+    int mode, lo, n, k, fine, bytes, sh_in;
+};
+
+// Shared-memory budgets of the selector GELU tables (selector_kernel layout).
+constexpr int kSelTabLocalBytes = 14080;
+constexpr int kSelTabH1Bytes = 18432;
+constexpr int kSelTabH2Bytes = 19392;
+
 struct SelParams {
     const int8_t *local_wt;   // [3][32][64]  (transposed local_w)
     const int32_t *local_b;   // [3][32]
@@ -86,6 +103,8 @@ struct SelParams {
     // 1 when gelu_chain_fast2's ranges hold (host-checked), and its constants
     int local_k2, h1_k2, h2_k2, hw_k2;
     GeluK local_k, h1_k, h2_k, hw_k;
+    // exact tables of the local, score layer-1 and layer-2 chains (mode 0: none)
+    GeluTab tab_local, tab_h1, tab_h2;
 };
 
 // Optional selector intermediates (token_selector API), image stride 196.

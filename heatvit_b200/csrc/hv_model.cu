@@ -98,6 +98,7 @@ struct BlockDev {
 
 struct SelDev {
     size_t lwt, lb, w1t, b1, w2t, b2, w3t, b3, hw1, hb1, hw2, hb2;
+    size_t tab_local, tab_h1, tab_h2;  // GELU tables in the arena (when their mode is set)
     SelParams p;  // shifts only until bind()
 };
 
@@ -216,6 +217,9 @@ SelParams bind_sel(const hv_model *m, const SelDev &s) {
     p.hb1 = m->w<int32_t>(s.hb1);
     p.hw2 = m->w<int8_t>(s.hw2);
     p.hb2 = m->w<int32_t>(s.hb2);
+    p.tab_local.tab = p.tab_local.mode ? m->w<int8_t>(s.tab_local) : nullptr;
+    p.tab_h1.tab = p.tab_h1.mode ? m->w<int8_t>(s.tab_h1) : nullptr;
+    p.tab_h2.tab = p.tab_h2.mode ? m->w<int8_t>(s.tab_h2) : nullptr;
     return p;
 }
 
@@ -631,13 +635,14 @@ void gelu_escape_window(const std::vector<int8_t> &f, int32_t qmax, TabWindow *t
 // coarse entry: v0 | v1 << 8 | p << 16 (v0 before offset p, v1 from it; p = 0x8000
 // when constant).  A bucket with more changes gets p = 0xFFFF, and its low 16 bits
 // index a 2^k-byte fine table stored after the coarse entries.  The smallest k in
-// [3, 10] whose table fits kGeluTableMax is taken; *ok = false when none does.
+// [3, 10] whose table fits `budget` bytes is taken; *ok = false when none does.
 struct BucketTable {
     int32_t lo, n;
     int k, fine_off;
     std::vector<uint8_t> blob;
 };
-void gelu_bucket_table(const std::vector<int8_t> &f, int32_t qmax, BucketTable *bt, bool *ok) {
+void gelu_bucket_table(const std::vector<int8_t> &f, int32_t qmax, BucketTable *bt, bool *ok,
+                       int budget = kGeluTableMax) {
     *ok = false;
     const int64_t total = (int64_t)f.size();
     int64_t w0 = -1, w1 = -1;
@@ -658,7 +663,7 @@ void gelu_bucket_table(const std::vector<int8_t> &f, int32_t qmax, BucketTable *
             if (ch >= 2) ++nfine;
         }
         const int64_t fine_off = 4 * nb, bytes = fine_off + nfine * B;
-        if (bytes > kGeluTableMax || nfine > 0xFFFF) continue;
+        if (bytes > budget || nfine > 0xFFFF) continue;
         bt->lo = (int32_t)(w0 - qmax);
         bt->n = (int32_t)W;
         bt->k = k;
@@ -686,6 +691,57 @@ void gelu_bucket_table(const std::vector<int8_t> &f, int32_t qmax, BucketTable *
         *ok = true;
         return;
     }
+}
+
+// Exact table of a selector GELU chain with input v = acc + bias, |v| <= vmax, and
+// q = rsa(v, sh_in): a byte table of the whole non-constant window when it fits
+// `budget`, else a bucket table (gelu_bucket_table) when one fits, else none
+// (t->mode = 0).  The table bytes go to the arena at *off.
+int sel_gelu_table(int sh_in, int sh_out, int64_t vmax, int budget, Arena &A, GeluTab *t, size_t *off) {
+    memset(t, 0, sizeof(*t));
+    if (sh_in < 0 || sh_in > 30) return HV_OK;
+    const int64_t hin = sh_in > 0 ? (int64_t)1 << (sh_in - 1) : 0;
+    if (vmax + hin >= ((int64_t)1 << 31)) return HV_OK;
+    const int64_t qmax = (vmax + hin) >> sh_in;
+    if (qmax >= ((int64_t)1 << 23)) return HV_OK;  // no 24-bit saturation of the GELU input
+    std::vector<int8_t> f;
+    int rc = gelu_scan((int32_t)qmax, sh_out, f);
+    if (rc != HV_OK) return rc;
+    int64_t w0 = -1, w1 = -1;
+    for (int64_t i = 1; i < (int64_t)f.size(); ++i)
+        if (f[(size_t)i] != f[(size_t)i - 1]) {
+            if (w0 < 0) w0 = i - 1;
+            w1 = i;
+        }
+    if (w0 < 0) w0 = w1 = 0;  // constant: a one-entry table
+    const int64_t W = w1 - w0 + 1;
+    std::vector<uint8_t> blob;
+    if (W <= budget) {
+        blob.assign(f.begin() + w0, f.begin() + w1 + 1);
+        t->mode = 1;
+        t->lo = (int32_t)(w0 - qmax);
+        t->n = (int32_t)W;
+    } else {
+        BucketTable bt;
+        bool ok = false;
+        gelu_bucket_table(f, (int32_t)qmax, &bt, &ok, budget - 15);  // room for the 16-byte padding
+        if (!ok) return HV_OK;
+        blob = bt.blob;
+        t->mode = 2;
+        t->lo = bt.lo;
+        t->n = bt.n;
+        t->k = bt.k;
+        t->fine = bt.fine_off;
+    }
+    blob.resize((blob.size() + 15) & ~(size_t)15, 0);
+    if ((int)blob.size() > budget) {
+        t->mode = 0;
+        return HV_OK;
+    }
+    t->bytes = (int)blob.size();
+    t->sh_in = sh_in;
+    *off = A.add(blob.data(), blob.size());
+    return HV_OK;
 }
 
 int pack_model(hv_model *m, const hv_params *P) {
@@ -899,6 +955,17 @@ int pack_model(hv_model *m, const hv_params *P) {
         p.h1_k2 = k2(p.h1_sh_in, p.h1_sh_out, max_abs(q.score_b1, 96) + 64 * 16384, 1, &p.h1_k);
         p.h2_k2 = k2(p.h2_sh_in, p.h2_sh_out, max_abs(q.score_b2, 48) + 32 * 16384, 1, &p.h2_k);
         p.hw_k2 = k2(p.hw_sh_in, p.hw_sh_out, max_abs(q.hw_b1, 3) + 3 * 16384, 1, &p.hw_k);
+        // exact tables (selector_kernel's shared-memory budgets: local in its own
+        // region, layers 1 and 2 together in the token region)
+        int trc = sel_gelu_table(p.local_sh_in, p.local_sh_out, max_abs(q.local_b, 96) + 64 * 16384,
+                                 kSelTabLocalBytes, A, &p.tab_local, &d.tab_local);
+        if (trc == HV_OK)
+            trc = sel_gelu_table(p.h1_sh_in, p.h1_sh_out, max_abs(q.score_b1, 96) + 64 * 16384, kSelTabH1Bytes, A,
+                                 &p.tab_h1, &d.tab_h1);
+        if (trc == HV_OK)
+            trc = sel_gelu_table(p.h2_sh_in, p.h2_sh_out, max_abs(q.score_b2, 48) + 32 * 16384, kSelTabH2Bytes, A,
+                                 &p.tab_h2, &d.tab_h2);
+        if (trc != HV_OK) return trc;
     }
     if (m->has_head) {
     if (!P->final_gamma || !P->final_beta || !P->head_b) return fail(HV_ERR_VALUE, "head parameters missing");

@@ -60,10 +60,37 @@ constexpr int SZ_H1 = 3 * MAXC * LSTR;
 constexpr int OFF_H2 = OFF_LOCAL;           // score layer-2 outputs [3][MAXC][16], over the dead local rows
 constexpr int SZ_H2 = 3 * MAXC * 16;
 static_assert(SZ_H2 <= SZ_LOCAL, "layer-2 outputs overlay the local features");
-constexpr int SMEM_BYTES = OFF_H1 + SZ_H1;
+constexpr int OFF_TABL = OFF_H1 + SZ_H1;    // GELU table of the local MLP
+constexpr int SMEM_BYTES = OFF_TABL + kSelTabLocalBytes;
+// The score-layer tables use the token rows while those are not needed (after the
+// head statistics; the rows are copied in again for the compaction).
+constexpr int OFF_TAB1 = OFF_TOK;
+constexpr int OFF_TAB2 = OFF_TOK + kSelTabH1Bytes;
+static_assert(kSelTabH1Bytes + kSelTabH2Bytes <= SZ_TOK, "score-layer tables fit the token rows");
+static_assert(OFF_TABL % 16 == 0 && OFF_TAB2 % 16 == 0, "16-byte table staging");
 static_assert(2 * (SMEM_BYTES + 1024) <= 228 * 1024, "two selector CTAs per SM");
 
 __device__ __forceinline__ int32_t sat_q016(int64_t v) { return (int32_t)(v < 0 ? 0 : (v > 65536 ? 65536 : v)); }
+
+// Copy a GELU table (t.bytes, a multiple of 16) into shared memory.
+__device__ __forceinline__ void stage_tab(const GeluTab &t, int8_t *dst, int tid) {
+    if (!t.mode) return;
+    for (int i = tid; i < t.bytes / 16; i += THREADS) ((int4 *)dst)[i] = ((const int4 *)t.tab)[i];
+}
+
+// GELU chain output from its exact table (GeluTab) staged at s; v = acc + bias with
+// |v| + 2^(sh_in-1) < 2^31 (host-checked).
+__device__ __forceinline__ int32_t tab_gelu(int32_t v, const GeluTab &t, const int8_t *s) {
+    const int32_t q = t.sh_in ? rsa32(v, t.sh_in) : v;
+    const int u = min(max(q - t.lo, 0), t.n - 1);
+    if (t.mode == 1) return s[u];
+    const uint32_t e = ((const uint32_t *)s)[u >> t.k];
+    const int off = u & ((1 << t.k) - 1);
+    const uint32_t pc = e >> 16;
+    int32_t o = off >= (int)pc ? (int32_t)(int8_t)(e >> 8) : (int32_t)(int8_t)e;
+    if (pc == 0xFFFFu) o = s[t.fine + (int)((e & 0xFFFFu) << t.k) + off];
+    return o;
+}
 
 // acc + a · b over W 16-byte words of packed int8 (shared memory, 16-byte aligned).
 template <int W>
@@ -116,6 +143,9 @@ __global__ void __launch_bounds__(THREADS) selector_kernel(
     int8_t *w1t = (int8_t *)(smem + OFF_W1T);
     int8_t *w2t = (int8_t *)(smem + OFF_W2T);
     int8_t *w3t = (int8_t *)(smem + OFF_W3T);
+    int8_t *tabl = (int8_t *)(smem + OFF_TABL);
+    int8_t *tab1 = (int8_t *)(smem + OFF_TAB1);
+    int8_t *tab2 = (int8_t *)(smem + OFF_TAB2);
     int64_t *g1 = (int64_t *)(smem + OFF_G1);
     int8_t *glob = (int8_t *)(smem + OFF_GLOB);
     int32_t *hs = (int32_t *)(smem + OFF_HS);
@@ -155,6 +185,7 @@ __global__ void __launch_bounds__(THREADS) selector_kernel(
         *(int32_t *)(w2t + row * W2STR + 4 * w) = ((const int32_t *)p.w2t)[c];
     }
     if (tid < 24) ((int32_t *)w3t)[tid] = ((const int32_t *)p.w3t)[tid];
+    stage_tab(p.tab_local, tabl, tid);
     __syncthreads();
 
     // ---- local MLP: local[h][c][j] ------------------------------------------------
@@ -163,8 +194,11 @@ __global__ void __launch_bounds__(THREADS) selector_kernel(
         int h, c;
         split_hc(idx >> 5, C, h, c);
         const int32_t acc = dot16<4>(tok + (1 + c) * 192 + 64 * h, lwt + (h * 32 + j) * WSTR, 0);
-        local[(h * MAXC + c) * LSTR + j] = (int8_t)sel_gelu((int64_t)acc + p.local_b[h * 32 + j], p.local_k2,
-                                                            p.local_k, p.local_fast, p.local_sh_in, p.local_sh_out);
+        const int32_t lb = p.local_b[h * 32 + j];
+        local[(h * MAXC + c) * LSTR + j] =
+            (int8_t)(p.tab_local.mode ? tab_gelu(acc + lb, p.tab_local, tabl)
+                                      : sel_gelu((int64_t)acc + lb, p.local_k2, p.local_k, p.local_fast, p.local_sh_in,
+                                                 p.local_sh_out));
     }
     __syncthreads();
     if (dbg.local)  // exported now: the layer-2 outputs overwrite these rows later
@@ -175,14 +209,33 @@ __global__ void __launch_bounds__(THREADS) selector_kernel(
             dbg.local[(((size_t)img * 3 + h) * MAXC + c) * 32 + j] = local[(h * MAXC + c) * LSTR + j];
         }
 
-    // ---- global mean (selector.py:273-289) -----------------------------------------
+    // ---- global mean (selector.py:273-289) and head stats (358-367), the last reads
+    // of the token rows before the score-layer tables take their place ----------------
     if (tid < 96) {
         const int h = tid >> 5, j = tid & 31;
         int32_t t = 0;
         for (int c = 0; c < C; ++c) t += local[(h * MAXC + c) * LSTR + j];
         glob[h * 32 + j] = (int8_t)sat8((int32_t)round_div64(t, C));
     }
+    for (int c = tid; c < C; c += THREADS) {
+#pragma unroll
+        for (int h = 0; h < 3; ++h) {
+            const int4 *trow = (const int4 *)(tok + (1 + c) * 192 + 64 * h);
+            int32_t t = 0;
+#pragma unroll
+            for (int w = 0; w < 4; ++w) {
+                const int4 x4 = trow[w];
+                t = __dp4a(x4.x, 0x01010101, t);
+                t = __dp4a(x4.y, 0x01010101, t);
+                t = __dp4a(x4.z, 0x01010101, t);
+                t = __dp4a(x4.w, 0x01010101, t);
+            }
+            stats[c * 3 + h] = (int8_t)sat8((int32_t)round_div64(t, 64));
+        }
+    }
     __syncthreads();
+    stage_tab(p.tab_h1, tab1, tid);
+    stage_tab(p.tab_h2, tab2, tid);
     if (tid < 96) {
         const int h = tid >> 5, j = tid & 31;
         int32_t acc = 0;
@@ -201,7 +254,9 @@ __global__ void __launch_bounds__(THREADS) selector_kernel(
         split_hc(idx >> 5, C, h, c);
         const int32_t acc = dot16<2>(local + (h * MAXC + c) * LSTR, w1t + (h * 32 + j) * WSTR, 0);
         h1s[(h * MAXC + c) * LSTR + j] =
-            (int8_t)sel_gelu(acc + g1[h * 32 + j], p.h1_k2, p.h1_k, p.h1_fast, p.h1_sh_in, p.h1_sh_out);
+            (int8_t)(p.tab_h1.mode ? tab_gelu((int32_t)(acc + g1[h * 32 + j]), p.tab_h1, tab1)
+                                   : sel_gelu(acc + g1[h * 32 + j], p.h1_k2, p.h1_k, p.h1_fast, p.h1_sh_in,
+                                              p.h1_sh_out));
     }
     __syncthreads();
     for (int idx = tid; idx < 3 * C * 16; idx += THREADS) {
@@ -209,10 +264,22 @@ __global__ void __launch_bounds__(THREADS) selector_kernel(
         int h, c;
         split_hc(idx >> 4, C, h, c);
         const int32_t acc = dot16<2>(h1s + (h * MAXC + c) * LSTR, w2t + (h * 16 + m) * W2STR, 0);
+        const int32_t b2 = p.b2[h * 16 + m];
         h2s[(h * MAXC + c) * 16 + m] =
-            (int8_t)sel_gelu((int64_t)acc + p.b2[h * 16 + m], p.h2_k2, p.h2_k, p.h2_fast, p.h2_sh_in, p.h2_sh_out);
+            (int8_t)(p.tab_h2.mode ? tab_gelu(acc + b2, p.tab_h2, tab2)
+                                   : sel_gelu((int64_t)acc + b2, p.h2_k2, p.h2_k, p.h2_fast, p.h2_sh_in, p.h2_sh_out));
     }
     __syncthreads();
+    // the token rows come back for the compaction (their copies overlap the phases below)
+    if (p.tab_h1.mode || p.tab_h2.mode) {
+        for (int c = tid; c < n * 12; c += THREADS) {
+            const uint32_t dst = (uint32_t)__cvta_generic_to_shared(tok + c * 16);
+            asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(dst),
+                         "l"(x + (size_t)row0 * 192 + c * 16)
+                         : "memory");
+        }
+        asm volatile("cp.async.commit_group;\n" ::: "memory");
+    }
     for (int it = tid; it < 3 * C; it += THREADS) {
         int h, c;
         split_hc(it, C, h, c);
@@ -227,24 +294,11 @@ __global__ void __launch_bounds__(THREADS) selector_kernel(
         hs[h * MAXC + c] = keep_score(q[0], q[1]);
     }
 
-    // ---- head stats + head-weight MLP per candidate --------------------------------
+    // ---- head-weight MLP per candidate (selector.py:370-389) -------------------------
     for (int c = tid; c < C; c += THREADS) {
         int32_t st[3];
 #pragma unroll
-        for (int h = 0; h < 3; ++h) {
-            const int4 *trow = (const int4 *)(tok + (1 + c) * 192 + 64 * h);
-            int32_t t = 0;
-#pragma unroll
-            for (int w = 0; w < 4; ++w) {
-                const int4 x4 = trow[w];
-                t = __dp4a(x4.x, 0x01010101, t);
-                t = __dp4a(x4.y, 0x01010101, t);
-                t = __dp4a(x4.z, 0x01010101, t);
-                t = __dp4a(x4.w, 0x01010101, t);
-            }
-            st[h] = sat8((int32_t)round_div64(t, 64));
-            stats[c * 3 + h] = (int8_t)st[h];
-        }
+        for (int h = 0; h < 3; ++h) st[h] = stats[c * 3 + h];
         int32_t hid[3];
 #pragma unroll
         for (int j = 0; j < 3; ++j) {
@@ -282,6 +336,7 @@ __global__ void __launch_bounds__(THREADS) selector_kernel(
         const int keep = (c < normals) && f >= 32768;
         flags[c] = (uint8_t)(keep | ((keep ? 0 : 1) << 1));
     }
+    asm volatile("cp.async.wait_all;\n" ::: "memory");  // the token rows are back
     __syncthreads();
 
     // ---- stable compaction index: exclusive scan of keep flags (C <= 196 < 256) -----
