@@ -43,9 +43,9 @@ STAGE_BYTES_PER_ROW = {"ln1": 384, "ln2": 384}
 # full-size launch (block 1, 201,728 rows): profiles/tcp_gemm_qkv_proj_fc1_block1_b1024.md,
 # profiles/tcp_gemm_fc2_block1_b1024.md, profiles/ln_kernel_ln1_block1_b1024.md.
 # Traffic grows with the rows of a launch.
-STAGE_TRAFFIC_PER_ROW = {"fc1": (38_987_776 + 101_157_632) / 201_728,
-                         "fc2": (193_862_656 + 23_533_568) / 201_728,
-                         "ln1": (38_791_424 + 1_806_336) / 201_728}
+STAGE_TRAFFIC_PER_ROW = {"fc1": (38_966_016 + 100_830_720) / 201_728,
+                         "fc2": (193_862_912 + 24_387_584) / 201_728,
+                         "ln1": (38_798_848 + 1_535_744) / 201_728}
 
 
 def algorithmic_macs(counts):
