@@ -60,6 +60,15 @@ struct PLayout {
     static constexpr int SMEM = USED > 116 * 1024 ? USED : 116 * 1024;
 };
 
+// 32 contiguous bytes in one 256-bit store: whole 32-byte sectors, half the store
+// instructions of two 16-byte stores.  The address must be 32-byte aligned (row
+// strides of 192, 576 and 768 bytes, 32-column pieces).
+__device__ __forceinline__ void st_global_32B(void *p, const uint32_t (&w)[8]) {
+    asm volatile("st.global.v8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};\n" ::"l"(p), "r"(w[0]), "r"(w[1]),
+                 "r"(w[2]), "r"(w[3]), "r"(w[4]), "r"(w[5]), "r"(w[6]), "r"(w[7])
+                 : "memory");
+}
+
 __device__ __forceinline__ void cp_async16(uint32_t saddr, const void *g, int src_bytes) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(saddr), "l"(g), "r"(src_bytes) : "memory");
 }
@@ -395,11 +404,7 @@ __global__ void __launch_bounds__(PT_THREADS, 1) tcp_gemm_kernel(GemmArgs g, int
                             pk[w] = pack_sat8(o[0], o[1], o[2], o[3]);
                         }
                     }
-                    if (valid) {
-                        uint4 *dst = (uint4 *)((int8_t *)g.out + orow * g.ldo + gcol0);
-                        dst[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-                        dst[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
-                    }
+                    if (valid) st_global_32B((int8_t *)g.out + orow * g.ldo + gcol0, pk);
                 }
                 tc05::fence_before();
                 __syncwarp();
