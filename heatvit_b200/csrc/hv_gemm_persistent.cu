@@ -69,6 +69,13 @@ __device__ __forceinline__ void st_global_32B(void *p, const uint32_t (&w)[8]) {
                  : "memory");
 }
 
+// 32 contiguous bytes in one 256-bit read-only load (32-byte aligned address).
+__device__ __forceinline__ void ld_global_32B(const void *p, uint32_t (&w)[8]) {
+    asm volatile("ld.global.nc.v8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];\n"
+                 : "=r"(w[0]), "=r"(w[1]), "=r"(w[2]), "=r"(w[3]), "=r"(w[4]), "=r"(w[5]), "=r"(w[6]), "=r"(w[7])
+                 : "l"(p));
+}
+
 __device__ __forceinline__ void cp_async16(uint32_t saddr, const void *g, int src_bytes) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(saddr), "l"(g), "r"(src_bytes) : "memory");
 }
@@ -295,12 +302,15 @@ __global__ void __launch_bounds__(PT_THREADS, 1) tcp_gemm_kernel(GemmArgs g, int
             bool stop = false;
             // Residual rows (N = 192: one chunk per tile): this thread's 96 bytes are
             // requested before the accumulator wait, so their latency overlaps the MMA.
-            uint4 rpre[6];
+            uint32_t rpre[BN / 64][8];
             if (EPI == EPI_I8_RES && L::NCH == 1) {
 #pragma unroll
-                for (int i = 0; i < 6; ++i)
-                    rpre[i] = valid ? ((const uint4 *)(g.epi.res + orow * g.ldo + half * (BN / 2)))[i]
-                                    : make_uint4(0, 0, 0, 0);
+                for (int i = 0; i < BN / 64; ++i) {
+                    if (valid) ld_global_32B(g.epi.res + orow * g.ldo + half * (BN / 2) + 32 * i, rpre[i]);
+                    else
+#pragma unroll
+                        for (int j = 0; j < 8; ++j) rpre[i][j] = 0;
+                }
             }
             for (int c = 0; c < L::NCH; ++c, ++a) {
                 const int tb = a & 1;
@@ -317,20 +327,14 @@ __global__ void __launch_bounds__(PT_THREADS, 1) tcp_gemm_kernel(GemmArgs g, int
                     const int col0 = half * (BN / 2) + cc * 32;  // chunk-local column of v[0]
                     const int gcol0 = c * BN + col0;
                     // residual / positional bytes first, so their latency overlaps the TMEM read
-                    uint4 r0 = make_uint4(0, 0, 0, 0), r1 = r0;
+                    uint32_t aux[8] = {0, 0, 0, 0, 0, 0, 0, 0};
                     if (EPI == EPI_I8_RES && L::NCH == 1) {
-                        r0 = rpre[2 * cc];
-                        r1 = rpre[2 * cc + 1];
+#pragma unroll
+                        for (int j = 0; j < 8; ++j) aux[j] = rpre[cc][j];
                     } else if (EPI == EPI_I8_RES && valid) {
-                        const uint4 *r = (const uint4 *)(g.epi.res + orow * g.ldo + gcol0);
-                        r0 = r[0];
-                        r1 = r[1];
+                        ld_global_32B(g.epi.res + orow * g.ldo + gcol0, aux);
                     }
-                    if (EPI == EPI_PATCH) {
-                        const uint4 *r = (const uint4 *)(g.epi.pos + (pidx + 1) * 192 + gcol0);
-                        r0 = r[0];
-                        r1 = r[1];
-                    }
+                    if (EPI == EPI_PATCH) ld_global_32B(g.epi.pos + (pidx + 1) * 192 + gcol0, aux);
                     uint32_t v[32];
                     tc05::ld32(lane_addr + tb * 256 + col0, v);
                     int32_t bv[32];
@@ -343,7 +347,6 @@ __global__ void __launch_bounds__(PT_THREADS, 1) tcp_gemm_kernel(GemmArgs g, int
                         bv[4 * q4 + 3] = b4.w;
                     }
                     tc05::wait_ld();
-                    const uint32_t aux[8] = {r0.x, r0.y, r0.z, r0.w, r1.x, r1.y, r1.z, r1.w};
                     uint32_t pk[8];
                     bool slow = true;
                     if (EPI == EPI_GELU && FAST && L::TABB > 0 && g.epi.gtab_mode == 2) {

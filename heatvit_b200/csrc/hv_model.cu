@@ -351,8 +351,10 @@ GemmArgs gemm_args(const void *a, int lda, int patch_mode, const int8_t *bt, int
 // A layer GEMM of the model: the persistent kernel for the layer shapes it covers.
 cudaError_t model_gemm(const hv_model *m, GemmArgs &g, int epi, int m_max, cudaStream_t st) {
     g.epi.fast = gemm_epi_fast(epi, g.epi);
-    // (the persistent epilogue stores 32-byte pieces: 32-byte aligned rows)
-    if (m->persistent && gemm_persistent_supported(epi, g.n, g.k) && (uintptr_t)g.out % 32 == 0 && g.ldo % 32 == 0) {
+    // (the persistent epilogue stores and reads 32-byte pieces: 32-byte aligned rows)
+    const bool al32 = (uintptr_t)g.out % 32 == 0 && g.ldo % 32 == 0 && (uintptr_t)g.epi.res % 32 == 0 &&
+                      (uintptr_t)g.epi.pos % 32 == 0;
+    if (m->persistent && gemm_persistent_supported(epi, g.n, g.k) && al32) {
         if (epi == EPI_GELU) g.epi.fast = g.epi.gelu_k2 || g.epi.gtab_n > 0;  // the persistent kernel's fast forms
         return launch_gemm_persistent(g, epi, m_max, m->err, m->sms, st);
     }
