@@ -309,7 +309,7 @@ def main():
     # End-to-end through the public host API: pinned host images in, host logits out.
     pinned = torch.empty((b, 150528), dtype=torch.int8, pin_memory=True)
     pinned.numpy()[:] = host_imgs
-    host_logits = np.empty((b, 1000), np.int32)
+    host_logits = torch.empty((b, 1000), dtype=torch.int32, pin_memory=True).numpy()
     for _ in range(2):
         eng.infer_host(pinned.numpy(), logits=host_logits)
     if world > 1:

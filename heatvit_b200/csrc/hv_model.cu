@@ -1224,6 +1224,9 @@ int hv_infer_host(hv_model *m, const int8_t *h_images, int batch, int32_t *h_log
     cudaPointerAttributes pa;
     const bool pinned_in = cudaPointerGetAttributes(&pa, h_images) == cudaSuccess && pa.type == cudaMemoryTypeHost;
     cudaGetLastError();  // clear a possible error from the query
+    // Page-locked logits take the device copies directly (no staging copy at the end).
+    const bool pinned_out = cudaPointerGetAttributes(&pa, h_logits) == cudaSuccess && pa.type == cudaMemoryTypeHost;
+    cudaGetLastError();
     if (!pinned_in && chunk > m->pin_in_cap) {
         for (int i = 0; i < 2; ++i) {
             if (m->pin_in[i]) cudaFreeHost(m->pin_in[i]);
@@ -1265,8 +1268,9 @@ int hv_infer_host(hv_model *m, const int8_t *h_images, int batch, int32_t *h_log
                             h_warnings ? dw : nullptr, nullptr, nullptr, cst, buf);
         if (rc) return rc;
         CUDA_TRY(cudaEventRecord(m->ev_done[buf], cst));
-        CUDA_TRY(cudaMemcpyAsync(m->pin_out + o_log + (size_t)first * HV_CLASSES * 4, dl, (size_t)cnt * HV_CLASSES * 4,
-                                 cudaMemcpyDeviceToHost, cst));
+        CUDA_TRY(cudaMemcpyAsync(pinned_out ? (uint8_t *)(h_logits + (size_t)first * HV_CLASSES)
+                                            : m->pin_out + o_log + (size_t)first * HV_CLASSES * 4,
+                                 dl, (size_t)cnt * HV_CLASSES * 4, cudaMemcpyDeviceToHost, cst));
         if (h_token_counts)
             CUDA_TRY(cudaMemcpyAsync(m->pin_out + o_tc + (size_t)first * (ns + 1) * 4, dtc, (size_t)cnt * (ns + 1) * 4,
                                      cudaMemcpyDeviceToHost, cst));
@@ -1279,7 +1283,7 @@ int hv_infer_host(hv_model *m, const int8_t *h_images, int batch, int32_t *h_log
     }
     for (int i = 0; i < 2; ++i) CUDA_TRY(cudaStreamSynchronize(m->compute_stream[i]));
     use_workspace(m, 0);
-    memcpy(h_logits, m->pin_out + o_log, (size_t)batch * HV_CLASSES * 4);
+    if (!pinned_out) memcpy(h_logits, m->pin_out + o_log, (size_t)batch * HV_CLASSES * 4);
     if (h_token_counts) memcpy(h_token_counts, m->pin_out + o_tc, (size_t)batch * (ns + 1) * 4);
     if (h_summary && ns) memcpy(h_summary, m->pin_out + o_sum, (size_t)batch * ns * sizeof(hv_selector_summary));
     if (h_warnings) memcpy(h_warnings, m->pin_out + o_warn, (size_t)batch);

@@ -149,10 +149,14 @@ def test_host_entry_matches_device_entry(cuda):
     ns = eng.num_selectors
     pinned = torch.empty(imgs.shape, dtype=torch.int8, pin_memory=True)
     pinned.numpy()[:] = imgs
-    for src in (imgs, pinned.numpy()):                         # pageable (staged) and pinned input
+    pinned_logits = torch.empty((n, 1000), dtype=torch.int32, pin_memory=True).numpy()
+    # pageable (staged) and pinned input; pageable (staged) and pinned (direct) logits
+    for src, out in ((imgs, None), (pinned.numpy(), None), (pinned.numpy(), pinned_logits)):
         tc = np.empty((n, ns + 1), np.int32)
         warn = np.empty(n, np.uint8)
-        host = eng.infer_host(src, token_counts=tc, warnings=warn)
+        if out is not None:
+            out[:] = -1
+        host = eng.infer_host(src, logits=out, token_counts=tc, warnings=warn)
         np.testing.assert_array_equal(host, dev["logits"].cpu().numpy())
         np.testing.assert_array_equal(tc, dev["token_counts"].cpu().numpy())
         np.testing.assert_array_equal(warn, dev["warnings"].cpu().numpy())
