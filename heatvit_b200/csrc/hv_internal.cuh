@@ -115,6 +115,7 @@ struct SelDebug {
     int8_t *local;          // [B][3][196][32]
     int8_t *global_;        // [B][3][32]
     int8_t *stats;          // [B][196][3]
+    int8_t *h2;             // [B][3][196][16] score layer-2 outputs
 };
 
 // Selector over a ragged batch: x rows offsets[i]..offsets[i+1], pkg_in[i] ->

@@ -1537,11 +1537,28 @@ int hv_token_selector(hv_model *m, int selector_index, const int8_t *d_x, const 
     if (rc) return rc;
     cudaStream_t st = (cudaStream_t)stream;
     CUDA_TRY(cudaMemsetAsync(m->warn, 0, ((size_t)images + 3) & ~(size_t)3, st));
-    SelDebug dbg{d_fused, d_head_scores, d_head_weights, d_local, d_global, d_stats};
+    SelDebug dbg{d_fused, d_head_scores, d_head_weights, d_local, d_global, d_stats, nullptr};
     SelParams sp = bind_sel(m, m->sels[selector_index]);
     CUDA_TRY(launch_selector(d_x, d_offsets, d_pkg_in, images, sp, m->STAGE, m->counts, d_pkg_out, d_summary, 1,
                              m->warn, nullptr, 0, 0, &dbg, st));
     CUDA_TRY(launch_pack(m->STAGE, m->counts, images, d_y, d_offsets_out, st));
+    return HV_OK;
+}
+
+int hv_selector_h2(hv_model *m, int selector_index, const int8_t *d_x, const int32_t *d_offsets, int images,
+                   int8_t *d_h2, void *stream) {
+    if (!m || !d_x || !d_offsets || !d_h2) return fail(HV_ERR_VALUE, "null argument");
+    if (selector_index < 0 || selector_index >= m->num_sel) return fail(HV_ERR_VALUE, "selector index out of range");
+    if (images <= 0) return fail(HV_ERR_VALUE, "images must be positive");
+    CUDA_TRY(cudaSetDevice(m->device));
+    int rc = ensure_capacity(m, images);
+    if (rc) return rc;
+    cudaStream_t st = (cudaStream_t)stream;
+    CUDA_TRY(cudaMemsetAsync(m->warn, 0, ((size_t)images + 3) & ~(size_t)3, st));
+    SelDebug dbg{nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, d_h2};
+    SelParams sp = bind_sel(m, m->sels[selector_index]);
+    CUDA_TRY(launch_selector(d_x, d_offsets, nullptr, images, sp, m->STAGE, m->counts, nullptr, nullptr, 1, m->warn,
+                             nullptr, 0, 0, &dbg, st));
     return HV_OK;
 }
 

@@ -270,6 +270,13 @@ __global__ void __launch_bounds__(THREADS) selector_kernel(
                                    : sel_gelu((int64_t)acc + b2, p.h2_k2, p.h2_k, p.h2_fast, p.h2_sh_in, p.h2_sh_out));
     }
     __syncthreads();
+    if (dbg.h2)
+        for (int i = tid; i < 3 * C * 16; i += THREADS) {
+            const int m = i & 15;
+            int h, c;
+            split_hc(i >> 4, C, h, c);
+            dbg.h2[(((size_t)img * 3 + h) * MAXC + c) * 16 + m] = h2s[(h * MAXC + c) * 16 + m];
+        }
     // the token rows come back for the compaction (their copies overlap the phases below)
     if (p.tab_h1.mode || p.tab_h2.mode) {
         for (int c = tid; c < n * 12; c += THREADS) {
@@ -461,7 +468,7 @@ cudaError_t launch_selector(const int8_t *x, const int32_t *offsets, const uint8
     if (images <= 0) return cudaSuccess;
     cudaError_t e = cudaFuncSetAttribute(selector_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
     if (e != cudaSuccess) return e;
-    SelDebug d = dbg ? *dbg : SelDebug{nullptr, nullptr, nullptr, nullptr, nullptr, nullptr};
+    SelDebug d = dbg ? *dbg : SelDebug{nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr};
     return launch_pdl(selector_kernel, dim3(images), dim3(THREADS), SMEM_BYTES, st, x, offsets, pkg_in, p, stage,
                       counts_out, pkg_out, summary, sum_stride, warn, token_counts, tc_stride, tc_col, d);
 }

@@ -340,6 +340,14 @@ HV_API int hv_token_selector(hv_model *model, int selector_index, const int8_t *
                       int32_t *d_head_scores, int32_t *d_head_weights, int8_t *d_local,
                       int8_t *d_global, int8_t *d_stats, void *stream);
 
+/* Score layer-2 outputs h2 of selector `selector_index` over a ragged batch (rows
+ * d_offsets[i]..d_offsets[i+1] of d_x): d_h2 [images][3][196][16] int8, candidate c of
+ * head h at [i][h][c]; entries past an image's candidates are left untouched.
+ * Replaces weights._selector_h2 (weights.py:143-155), the feature the reference's
+ * selector calibration (weights.py:158-204) reads. */
+HV_API int hv_selector_h2(hv_model *model, int selector_index, const int8_t *d_x,
+                          const int32_t *d_offsets, int images, int8_t *d_h2, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

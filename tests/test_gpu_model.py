@@ -122,7 +122,8 @@ def test_batch_invariance_full_size(cuda):
 
 
 def test_full_size_sample_vs_oracle(cuda, oracle):
-    """Batch 1024 on the device; a seeded sample of 64 of its images against the oracle."""
+    """Batch 1024 on the device (the benchmark's per-GPU batch); a seeded sample of
+    256 of its images plus every zero-package-denominator image against the oracle."""
     import torch
     from heatvit_b200 import synth
     from heatvit_b200.engine import Engine
@@ -131,10 +132,14 @@ def test_full_size_sample_vs_oracle(cuda, oracle):
     eng = Engine(params)
     out = eng.infer(torch.from_numpy(imgs).cuda())
     assert eng.device_error() == 0
-    idx = np.random.default_rng(1).choice(1024, 64, replace=False)
+    warn = out["warnings"].cpu().numpy()
+    zero_den = np.nonzero(warn & 2)[0]
+    assert zero_den.size >= 10                                  # >= 1% of the batch
+    idx = np.union1d(np.random.default_rng(1).choice(1024, 256, replace=False), zero_den)
     ref = oracle.infer_batch(params, imgs[idx])
     np.testing.assert_array_equal(out["logits"].cpu().numpy()[idx], ref["logits"])
     np.testing.assert_array_equal(out["token_counts"].cpu().numpy()[idx], ref["counts"])
+    np.testing.assert_array_equal(warn[idx], ref["warnings"])
 
 
 def test_host_entry_matches_device_entry(cuda):
