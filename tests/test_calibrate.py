@@ -77,3 +77,32 @@ def test_calibration_on_gpu(cuda, oracle):
     base = synth.reference_seeded_base()
     x, _ = _run_to_selector(oracle, params, image, 1)
     np.testing.assert_array_equal(calibrate.selector_h2(x, base["bases"][0]), _h2_oracle(oracle, base["bases"][0], x))
+
+
+# What synth.calibrate_keep_bias returns over the current seeded images (the oracle
+# as backend, about a minute on 8 host threads); the committed BASELINE_KEEP_BIAS
+# came from the first image generator.
+KEEP_BIAS_SEARCH = (-23305, -895, 10084)
+
+
+@pytest.mark.slow
+def test_keep_bias_calibration_with_oracle_backend(oracle):
+    """The benchmark generator's per-stage keep-bias search (bisection on the mean
+    selector output counts of 64 images) with the oracle as the backend."""
+    from heatvit_b200 import synth
+    got = synth.calibrate_keep_bias(synth.SEED, lambda p, imgs: oracle.infer_batch(p, imgs, threads=0)["counts"])
+    assert got == KEEP_BIAS_SEARCH
+
+
+@pytest.mark.gpu
+def test_keep_bias_calibration_on_gpu(cuda):
+    """The same search with the CUDA engine as the backend (78 model builds and
+    inferences, a few seconds)."""
+    import torch
+    from heatvit_b200 import synth
+    from heatvit_b200.engine import Engine
+
+    def counts(params, imgs):
+        return Engine(params).infer(torch.from_numpy(imgs).cuda())["token_counts"].cpu().numpy()
+
+    assert synth.calibrate_keep_bias(synth.SEED, counts) == KEEP_BIAS_SEARCH
