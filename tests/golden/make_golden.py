@@ -313,6 +313,40 @@ def golden_config3(R, seed, indices):
     return out
 
 
+def golden_memimage(R, seed):
+    """Digests of the reference's weight image (serialize_weights at
+    build_memory_map's weight offsets, and its .mem text) for the seeded model and
+    the config-3 model, and the reference ScaleTable's saved text for config 3."""
+    import tempfile
+    from pathlib import Path
+    from heatvit_b200 import synth
+    from heatvit_b200 import memimage
+    from heatvit_b200.params import to_reference
+    from tools.generate_descriptors import build_memory_map
+    from tools.generate_e2e_vectors import serialize_weights, write_mem_lines
+    from tools.p2.scale_table import ScaleTable
+    from verification.heatvit_ref import weights as W
+    rng = random.Random(W.SEED)
+    image = [rng.randint(-128, 127) for _ in range(224 * 224 * 3)]
+    seeded, _, _ = W.build_params(image)
+    mm = build_memory_map()[0]["weight"]
+    out = {"memimage_seed": np.array(seed)}
+    with tempfile.TemporaryDirectory() as td:
+        for tag, gp in (("seeded", seeded), ("config3", to_reference(synth.config3_params(seed), ref_namespace()))):
+            raw = serialize_weights(gp, mm)
+            out[f"memimage_{tag}_bytes"] = np.array(len(raw))
+            out[f"memimage_{tag}_sha256"] = np.array(hashlib.sha256(raw).hexdigest())
+            path = Path(td) / f"{tag}.mem"
+            write_mem_lines(path, raw)
+            out[f"memimage_{tag}_mem_sha256"] = np.array(hashlib.sha256(path.read_bytes()).hexdigest())
+        table = memimage.scale_table(synth.config3_params(seed))
+        st = ScaleTable(weights=table["weights"], activations=table["activations"]).validate()
+        path = Path(td) / "scales.json"
+        st.save(path)
+        out["memimage_config3_scales_json"] = np.array(path.read_text())
+    return out
+
+
 def golden_units(R, seed):
     """Per-operator golden outputs on seeded random inputs."""
     from verification.heatvit_ref import fixed as F
@@ -462,6 +496,8 @@ def main():
         save("golden_seeded.npz", golden_seeded(ref))
     if on("baseline"):
         save("golden_baseline.npz", golden_baseline(ref, 20260815, 2, True, "pruned"))
+    if on("memimage"):
+        save("golden_memimage.npz", golden_memimage(ref, 20260815))
     if on("config3"):
         save("golden_config3.npz", golden_config3(ref, 20260815, (2, 0)))
     if on("unpruned"):
