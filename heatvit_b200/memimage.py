@@ -93,17 +93,17 @@ def write_weights(params):
 def mem_lines(raw):
     """.mem text: one 64-bit little-endian beat per line (16 hex digits)."""
     raw = bytes(raw) + b"\0" * ((-len(raw)) % 8)
-    return "".join(f"{int.from_bytes(raw[i:i + 8], 'little'):016x}\n" for i in range(0, len(raw), 8))
+    beats = np.frombuffer(raw, np.uint8).reshape(-1, 8)[:, ::-1]  # most significant byte first
+    digits = np.frombuffer(beats.tobytes().hex().encode(), np.uint8).reshape(-1, 16)
+    return np.concatenate([digits, np.full((digits.shape[0], 1), ord("\n"), np.uint8)], 1).tobytes().decode()
 
 
 def parse_mem(text):
     """Bytes of a .mem text (inverse of mem_lines; the padding stays)."""
-    out = bytearray()
-    for line in text.splitlines():
-        line = line.strip()
-        if line:
-            out += int(line, 16).to_bytes(8, "little")
-    return bytes(out)
+    lines = text.split()
+    if all(len(v) == 16 for v in lines):
+        return np.frombuffer(bytes.fromhex("".join(lines)), np.uint8).reshape(-1, 8)[:, ::-1].tobytes()
+    return b"".join(int(v, 16).to_bytes(8, "little") for v in lines)
 
 
 def _arrays(raw):

@@ -347,6 +347,38 @@ def golden_memimage(R, seed):
     return out
 
 
+def golden_e2evectors(R):
+    """The reference's end-to-end vector set for its seeded model and image
+    (tools/generate_e2e_vectors.py ``generate``), written into a temporary
+    folder: the SHA-256 of every region image and checkpoint file, and the full
+    text of manifest.json and e2e_tb_config.sv.  The testbench package, which
+    ``generate`` writes into the reference's sim/generated/, is redirected to the
+    temporary folder and compared with the committed copy there."""
+    import tempfile
+    from pathlib import Path
+    import tools.generate_e2e_vectors as G
+    from verification.heatvit_ref import weights as W
+    orig = G.write_e2e_tb_config
+    with tempfile.TemporaryDirectory() as td:
+        sv = Path(td) / "e2e_tb_config.sv"
+        G.write_e2e_tb_config = lambda mm, manifest, layout, tc, cfg_path=None: orig(mm, manifest, layout, tc, sv)
+        try:
+            G.generate(W.SEED, Path(td) / "e2e")
+        finally:
+            G.write_e2e_tb_config = orig
+        base = Path(td) / "e2e"
+        names = ["input.mem", "weights.mem", "scratch_init.mem", "output_init.mem"]
+        names += sorted(f"checkpoints/{p.name}" for p in (base / "checkpoints").iterdir())
+        committed = (Path(R) / "sim" / "generated" / "e2e_tb_config.sv").read_text()
+        return {
+            "e2e_files": np.array(names),
+            "e2e_sha256": np.array([hashlib.sha256((base / n).read_bytes()).hexdigest() for n in names]),
+            "e2e_manifest": np.array((base / "manifest.json").read_text()),
+            "e2e_tb_config_sv": np.array(sv.read_text()),
+            "e2e_tb_config_matches_committed": np.array(sv.read_text() == committed),
+        }
+
+
 def golden_units(R, seed):
     """Per-operator golden outputs on seeded random inputs."""
     from verification.heatvit_ref import fixed as F
@@ -498,6 +530,8 @@ def main():
         save("golden_baseline.npz", golden_baseline(ref, 20260815, 2, True, "pruned"))
     if on("memimage"):
         save("golden_memimage.npz", golden_memimage(ref, 20260815))
+    if on("e2evectors"):
+        save("golden_e2evectors.npz", golden_e2evectors(ref))
     if on("config3"):
         save("golden_config3.npz", golden_config3(ref, 20260815, (2, 0)))
     if on("unpruned"):
