@@ -32,6 +32,7 @@ _SIGNATURES = {
     "hv_gemm_i8": (I, [P, P, P, I, I, I, I, I, I, I, I, P, P]),
     "hv_gemm_i8_acc": (I, [P, P, P, I, I, I, I, I, P, P]),
     "hv_gemm_i8_acc_noalloc": (I, [P, P, P, I, I, I, I, I, P, P]),
+    "hv_quantize_images": (I, [P, I, I, P, P]),
     "hv_layernorm_i8": (I, [P, P, P, I, I, I, I, I, P, P, P]),
     "hv_softmax_rows": (I, [P, P, I, I, P, P]),
     "hv_shiftgelu": (I, [P, I64, P, P]),

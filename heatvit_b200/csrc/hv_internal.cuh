@@ -139,6 +139,7 @@ cudaError_t launch_gelu_requant(const int32_t *acc, int64_t n, int sh_in, int sh
                                 cudaStream_t st);
 cudaError_t launch_softmax_rows(const int32_t *x, const int32_t *offsets, int rows, int mode, void *out,
                                 cudaStream_t st);
+cudaError_t launch_quantize_images(const float *src, int batch, int input_exp, int8_t *dst, cudaStream_t st);
 cudaError_t launch_align_add(const int8_t *a, const int8_t *b, AlignAdd k, int64_t n, int8_t *out, cudaStream_t st);
 cudaError_t launch_writeback(const int64_t *acc, int64_t n, int shift, int bits, void *out, cudaStream_t st);
 

@@ -616,6 +616,34 @@ cudaError_t launch_layernorm_cls(const int8_t *x, const int32_t *offsets, int im
     return launch_pdl(kern, dim3((images + 31) / 32), dim3(256), 0, st, x, offsets, images, out, p, warn);
 }
 
+// Image quantisation of the P2 tooling (tools/p2/p2_sim.py:536-545): one CTA per
+// image row.  Each thread takes one pixel's three channel values from the CHW
+// float planes (coalesced per plane), q = clamp(round_half_even(x * 2^-e),
+// -128, 127) (the division by a power of two is exact in fp32, so the product
+// equals the quotient), and the row's 672 HWC bytes leave shared memory as words.
+__global__ void __launch_bounds__(224) quantize_images_kernel(const float *__restrict__ src, float scale,
+                                                              int8_t *__restrict__ dst) {
+    __shared__ uint32_t row[168];
+    const int h = blockIdx.x, b = blockIdx.y, w = threadIdx.x;
+    const float *img = src + (size_t)b * 3 * 224 * 224 + h * 224 + w;
+    int8_t *srow = (int8_t *)row;
+#pragma unroll
+    for (int c = 0; c < 3; ++c) {
+        const float v = rintf(img[(size_t)c * 224 * 224] * scale);
+        // NaN maps to 0; fminf/fmaxf return the non-NaN operand
+        srow[3 * w + c] = (int8_t)(v != v ? 0 : (int)fminf(fmaxf(v, -128.0f), 127.0f));
+    }
+    __syncthreads();
+    if (w < 168) ((uint32_t *)(dst + (size_t)b * 150528 + h * 672))[w] = row[w];
+}
+
+cudaError_t launch_quantize_images(const float *src, int batch, int input_exp, int8_t *dst, cudaStream_t st) {
+    if (batch <= 0) return cudaSuccess;
+    const float scale = ldexpf(1.0f, -input_exp);
+    quantize_images_kernel<<<dim3(224, batch), 224, 0, st>>>(src, scale, dst);
+    return cudaGetLastError();
+}
+
 cudaError_t launch_softmax_rows(const int32_t *x, const int32_t *offsets, int rows, int mode, void *out,
                                 cudaStream_t st) {
     if (rows <= 0) return cudaSuccess;

@@ -166,7 +166,24 @@ def load_scale_table(text):
 def read_weights(raw, table):
     """A pruned HeatViTParams from a weight image and its scale table
     (p2_export_weights.golden_params_from_real with integer tensors)."""
-    t = _arrays(raw)
+    return params_from_tensors(_arrays(raw), table)
+
+
+def params_from_tensors(tensors, table, selectors=3):
+    """HeatViTParams from named integer tensors (the weight layout's names:
+    patch_w, b<n>_wqkv, s<s>_local_w, ...) and a scale table; ``selectors=0``
+    gives the unpruned model and needs no selector tensors or exponents."""
+    t = {}
+    for name, off, shape, esz in weight_layout():
+        if name.startswith("s") and name[1].isdigit() and int(name[1]) > selectors:
+            continue
+        a = np.asarray(tensors[name])
+        if a.size != int(np.prod(shape)):
+            raise ValueError(f"{name}: {a.size} values, the layout holds {int(np.prod(shape))}")
+        lo, hi = (-(1 << 31), (1 << 31) - 1) if esz == 4 else (-128, 127)
+        if a.size and (int(a.min()) < lo or int(a.max()) > hi):
+            raise ValueError(f"{name}: values outside the int{8 * esz} range")
+        t[name] = a.reshape(shape).astype(np.int32 if esz == 4 else np.int8)
     wt, act = table["weights"], table["activations"]
 
     def block_in(n):
@@ -193,9 +210,9 @@ def read_weights(raw, table):
                         hidden_out_scale_exp=act[f"b{n}_hidden"], w2_scale_exp=wt[f"b{n}_w2"],
                         ffn_out_scale_exp=act[f"b{n}_ffn_out"], out_scale_exp=act[f"b{n}_out"])
         blocks.append(BlockParams(mhsa=mhsa, ffn=ffn))
-    selectors = []
-    for s in range(1, 4):
-        selectors.append(SelectorParams(
+    sels = []
+    for s in range(1, selectors + 1):
+        sels.append(SelectorParams(
             local=SelectorLocalParams(w=t[f"s{s}_local_w"], b=t[f"s{s}_local_b"]),
             score=SelectorScoreParams(w1=t[f"s{s}_score_w1"], b1=t[f"s{s}_score_b1"], w2=t[f"s{s}_score_w2"],
                                       b2=t[f"s{s}_score_b2"], w3=t[f"s{s}_score_w3"], b3=t[f"s{s}_score_b3"]),
@@ -208,7 +225,8 @@ def read_weights(raw, table):
             h2_out_scale_exp=act[f"s{s}_h2_out"], logits_out_scale_exp=act[f"s{s}_logits_out"],
             stats_out_scale_exp=act[f"s{s}_stats_out"], hw_w1_scale_exp=wt[f"s{s}_hw_w1"],
             hw_hidden_out_scale_exp=act[f"s{s}_hw_hidden_out"], hw_w2_scale_exp=wt[f"s{s}_hw_w2"]))
-    return HeatViTParams(patch=patch, blocks=tuple(blocks), selectors=tuple(selectors),
+    return HeatViTParams(patch=patch, blocks=tuple(blocks), selectors=tuple(sels),
+                         selector_blocks=(4, 7, 10)[:selectors],
                          final_gamma=t["final_gamma"], final_beta=t["final_beta"], head_w=t["head_w"],
                          head_b=t["head_b"], final_gamma_scale_exp=wt["final_gamma"],
                          final_beta_scale_exp=wt["final_beta"], final_ln_out_scale_exp=act["final_ln_out"],

@@ -327,6 +327,27 @@ def baseline_images(seed, count, first=0):
     return out
 
 
+def p2_float_images(seed, count, input_exp, first=0):
+    """Seeded float32 images [count, 3, 224, 224] (CHW, the layout of the P2
+    tooling's normalised image tensors) for a model whose input exponent is
+    ``input_exp``: values mostly inside the int8 range after scaling by
+    2^-input_exp, with about 1% exact half-way values (rounding ties) and 0.2%
+    values far outside the range (saturation).  Image i depends only on
+    (seed, i)."""
+    out = np.empty((count, 3, 224, 224), np.float32)
+    step = np.float32(2.0 ** input_exp)
+    for j in range(count):
+        rng = np.random.default_rng([seed, 7, first + j])
+        x = rng.normal(0.0, 40.0, (3, 224, 224))
+        flat = x.reshape(-1)
+        ties = rng.choice(flat.size, flat.size // 100, replace=False)
+        flat[ties] = rng.integers(-140, 140, ties.size) + 0.5
+        far = rng.choice(flat.size, flat.size // 500, replace=False)
+        flat[far] = rng.choice([-1.0, 1.0], far.size) * rng.uniform(130.0, 4000.0, far.size)
+        out[j] = (x * step).astype(np.float32)
+    return out
+
+
 # Calibrated per-stage keep-logit biases of ``baseline_params`` (seed ->
 # keep_bias): chosen by ``calibrate_keep_bias`` so the mean output token counts
 # of the three selectors over ``baseline_images(seed, 64)`` sit at the target

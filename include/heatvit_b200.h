@@ -285,6 +285,13 @@ HV_API int hv_writeback_i64(const int64_t *d_acc, int64_t count, int src_exp, in
 HV_API int hv_align_add_i8(const int8_t *d_a, int a_exp, const int8_t *d_b, int b_exp, int out_exp,
                            int64_t count, int8_t *d_out, void *stream);
 
+/* Image quantisation of the P2 accuracy tooling: d_images [batch][3][224][224]
+ * float (CHW planes) -> d_out [batch][150528] int8 in the HWC order of the golden
+ * image, q = clamp(round_half_even(x / 2^input_exp), -128, 127); NaN gives 0.
+ * Replaces the first lines of tools/p2/p2_sim.py forward_image (p2_sim.py:536-541:
+ * torch.round, clamp, permute to NHWC). */
+HV_API int hv_quantize_images(const float *d_images, int batch, int input_exp, int8_t *d_out, void *stream);
+
 /* Row LayerNorm over D = 192: replaces nonlinear.layernorm (nonlinear.py:136-186).
  *   d_x [rows][192] int8, d_gamma/d_beta [192] int8 -> d_out [rows][192] int8,
  *   d_negvar [rows] uint8 (1 = variance clamped), may be NULL. */

@@ -379,6 +379,46 @@ def golden_e2evectors(R):
         }
 
 
+def _quant_deit(params, table, pruned):
+    """The reference P2 simulator's QuantDeiT holding a model's integer tensors."""
+    import torch
+    from heatvit_b200 import memimage
+    from tools.p2 import p2_sim as P
+    from tools.p2.scale_table import ScaleTable
+    t = {k: torch.from_numpy(np.ascontiguousarray(v)) for k, v in memimage._tensors(params).items()}
+    blocks = [P.BlockP(**{f: t[f"b{n}_{f}"] for f in P.BlockP.__dataclass_fields__}) for n in range(1, 13)]
+    sels = [P.SelectorP(**{f: t[f"s{s}_{f}"] for f in P.SelectorP.__dataclass_fields__})
+            for s in range(1, 4)] if pruned else []
+    return P.QuantDeiT(scales=ScaleTable(weights=dict(table["weights"]), activations=dict(table["activations"])),
+                       patch_w=t["patch_w"], patch_b=t["patch_b"], cls=t["cls"], pos=t["pos"], blocks=blocks,
+                       selectors=sels, final_gamma=t["final_gamma"], final_beta=t["final_beta"],
+                       head_w=t["head_w"], head_b=t["head_b"])
+
+
+def golden_p2sim(R, seed, count=6):
+    """The reference P2 simulator (tools/p2/p2_sim.py forward_image, pruned and
+    unpruned) on the config-3 model and seeded float images
+    (synth.p2_float_images): logits and token counts."""
+    import torch
+    from heatvit_b200 import memimage, synth
+    from tools.p2 import p2_sim as P
+    params = synth.config3_params(seed)
+    table = memimage.scale_table(params)
+    imgs = synth.p2_float_images(seed, count, params.patch.image_scale_exp)
+    out = {"p2_seed": np.array(seed), "p2_count": np.array(count)}
+    for tag, pruned in (("pruned", True), ("unpruned", False)):
+        model = _quant_deit(params, table, pruned)
+        logits, counts = [], []
+        for i in range(count):
+            lg, tc, e = P.forward_image(model, torch.from_numpy(imgs[i]), prune=pruned)
+            assert e == -14
+            logits.append(lg.numpy().astype(np.int32))
+            counts.append(tc)
+        out[f"p2_{tag}_logits"] = np.stack(logits)
+        out[f"p2_{tag}_counts"] = np.array(counts, np.int32)
+    return out
+
+
 def golden_units(R, seed):
     """Per-operator golden outputs on seeded random inputs."""
     from verification.heatvit_ref import fixed as F
@@ -532,6 +572,8 @@ def main():
         save("golden_memimage.npz", golden_memimage(ref, 20260815))
     if on("e2evectors"):
         save("golden_e2evectors.npz", golden_e2evectors(ref))
+    if on("p2sim"):
+        save("golden_p2sim.npz", golden_p2sim(ref, 20260815))
     if on("config3"):
         save("golden_config3.npz", golden_config3(ref, 20260815, (2, 0)))
     if on("unpruned"):
