@@ -29,6 +29,8 @@ _SIGNATURES = {
     "hv_infer_batch": (I, [P, P, I, P, P, P, P, P]),
     "hv_infer_batch_checkpoints": (I, [P, P, I, P, P, P, P, P, P, P]),
     "hv_infer_host": (I, [P, P, I, P, P, P, P]),
+    "hv_infer_host_submit": (I, [P, P, I, P, P, P, P]),
+    "hv_infer_host_wait": (I, [P]),
     "hv_gemm_i8": (I, [P, P, P, I, I, I, I, I, I, I, I, P, P]),
     "hv_gemm_i8_acc": (I, [P, P, P, I, I, I, I, I, P, P]),
     "hv_gemm_i8_acc_noalloc": (I, [P, P, P, I, I, I, I, I, P, P]),

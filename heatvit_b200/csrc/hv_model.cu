@@ -39,6 +39,14 @@ int fail(int code, const char *fmt, ...) {
         if (_e != cudaSuccess) return fail(HV_ERR_CUDA, "%s: %s", #expr, cudaGetErrorString(_e)); \
     } while (0)
 
+// Entry points that use the model's workspaces refuse to run while host calls are
+// in flight (their kernels would share the buffers).
+#define HOST_IDLE(m)                                                                              \
+    do {                                                                                          \
+        if ((m)->host_pending)                                                                    \
+            return fail(HV_ERR_STATE, "host calls in flight: call hv_infer_host_wait first");     \
+    } while (0)
+
 constexpr int64_t kNarrowLimit = (int64_t)1 << 30;
 
 // Largest |bias| of a vector.
@@ -168,13 +176,25 @@ struct hv_model {
     const CUtensorMap *tm_ln = nullptr, *tm_ctx = nullptr, *tm_hid = nullptr;  // nullptr: cp.async loads
     // host-pipeline staging
     int host_cap = 0;
-    int8_t *himg[2] = {nullptr, nullptr};
-    // pinned host staging of hv_infer_host: outputs of a whole call, and two image
-    // chunks for callers whose image buffer is pageable
-    uint8_t *pin_out = nullptr;
-    size_t pin_out_cap = 0;
+    int8_t *himg[4] = {nullptr, nullptr, nullptr, nullptr};  // device image chunks (chunk g uses g % 4)
+    // pinned host staging of the host entry: the outputs of each call in flight
+    // (one slot per call), and two image chunks for pageable image buffers
+    uint8_t *pin_out[2] = {nullptr, nullptr};
+    size_t pin_out_cap[2] = {0, 0};
     int8_t *pin_in[2] = {nullptr, nullptr};
     int pin_in_cap = 0;
+    // host calls in flight (hv_infer_host_submit), a ring of two slots
+    struct HostCall {
+        int batch = 0, ns = 0;
+        int32_t *logits = nullptr, *tc = nullptr;
+        hv_selector_summary *sum = nullptr;
+        uint8_t *warn = nullptr;
+        bool pinned_out = false;
+        size_t o_tc = 0, o_sum = 0, o_warn = 0;
+        cudaEvent_t done[2] = {nullptr, nullptr};  // recorded on both compute streams
+    } host_calls[2];
+    int host_head = 0, host_pending = 0;
+    unsigned long long host_chunks = 0;  // chunks enqueued so far: chunk g uses buffer g & 1
     int32_t *hlogits = nullptr, *htc = nullptr;
     hv_selector_summary *hsum = nullptr;
     uint8_t *hwarn = nullptr;
@@ -185,7 +205,9 @@ struct hv_model {
     unsigned long long graph_clock = 0;
     cudaStream_t graph_stream = nullptr;
     cudaEvent_t ev_fork = nullptr, ev_join = nullptr;
-    cudaEvent_t ev_in[2] = {nullptr, nullptr}, ev_done[2] = {nullptr, nullptr};
+    // per device image chunk: upload finished / compute on it finished; per pinned
+    // staging buffer: the upload out of it finished
+    cudaEvent_t ev_in[4] = {}, ev_done[4] = {}, ev_pin[2] = {};
 
     // kernel timing (hv_profile_*)
     int prof_stage = 0, prof_max = 0, prof_n = 0;
@@ -252,6 +274,14 @@ int ensure_capacity(hv_model *m, int images, int i = 0) {
     Workspace &w = m->ws[i];
     if (images > w.cap) {
         if (w.scratch) {
+            // Captured graphs hold this workspace's addresses: wait for the device,
+            // then drop them with the buffers.
+            CUDA_TRY(cudaDeviceSynchronize());
+            for (GraphEntry &g : m->graphs)
+                if (g.exec && g.ws == i) {
+                    cudaGraphExecDestroy(g.exec);
+                    g = GraphEntry();
+                }
             cudaFree(w.scratch);
             w = Workspace();
         }
@@ -1090,6 +1120,12 @@ int hv_model_create(const hv_params *params, int device, hv_model **out) {
 int hv_model_destroy(hv_model *m) {
     if (!m) return HV_OK;
     cudaSetDevice(m->device);
+    for (int i = 0; i < 2; ++i)
+        for (int k = 0; k < 2; ++k)
+            if (m->host_calls[i].done[k]) {
+                cudaEventSynchronize(m->host_calls[i].done[k]);  // calls never waited for
+                cudaEventDestroy(m->host_calls[i].done[k]);
+            }
     for (GraphEntry &g : m->graphs)
         if (g.exec) cudaGraphExecDestroy(g.exec);
     if (m->graph_stream) cudaStreamDestroy(m->graph_stream);
@@ -1099,6 +1135,9 @@ int hv_model_destroy(hv_model *m) {
     for (int i = 0; i < 2; ++i)
         if (m->ws[i].scratch) cudaFree(m->ws[i].scratch);
     for (int i = 0; i < 2; ++i) {
+        if (m->ev_pin[i]) cudaEventDestroy(m->ev_pin[i]);
+    }
+    for (int i = 0; i < 4; ++i) {
         if (m->himg[i]) cudaFree(m->himg[i]);
         if (m->ev_in[i]) cudaEventDestroy(m->ev_in[i]);
         if (m->ev_done[i]) cudaEventDestroy(m->ev_done[i]);
@@ -1107,9 +1146,10 @@ int hv_model_destroy(hv_model *m) {
     if (m->htc) cudaFree(m->htc);
     if (m->hsum) cudaFree(m->hsum);
     if (m->hwarn) cudaFree(m->hwarn);
-    if (m->pin_out) cudaFreeHost(m->pin_out);
-    for (int i = 0; i < 2; ++i)
+    for (int i = 0; i < 2; ++i) {
+        if (m->pin_out[i]) cudaFreeHost(m->pin_out[i]);
         if (m->pin_in[i]) cudaFreeHost(m->pin_in[i]);
+    }
     for (auto e : m->prof_ev) cudaEventDestroy(e);
     if (m->prof_rows) cudaFree(m->prof_rows);
     if (m->copy_stream) cudaStreamDestroy(m->copy_stream);
@@ -1122,6 +1162,7 @@ int hv_model_destroy(hv_model *m) {
 int hv_infer_batch(hv_model *m, const int8_t *d_images, int batch, int32_t *d_logits, int32_t *d_token_counts,
                    hv_selector_summary *d_summary, uint8_t *d_warnings, void *stream) {
     if (!m) return fail(HV_ERR_VALUE, "null model");
+    HOST_IDLE(m);
     cudaStream_t st = (cudaStream_t)stream;
     if (!m->use_graphs || batch <= 0 || !d_images || !d_logits)
         return infer_impl(m, d_images, batch, d_logits, d_token_counts, d_summary, d_warnings, nullptr, nullptr, st);
@@ -1158,16 +1199,56 @@ int hv_infer_batch_checkpoints(hv_model *m, const int8_t *d_images, int batch, i
                                int32_t *d_token_counts, hv_selector_summary *d_summary, uint8_t *d_warnings,
                                int8_t *d_ckpt, int32_t *d_ckpt_rows, void *stream) {
     if (!m) return fail(HV_ERR_VALUE, "null model");
+    HOST_IDLE(m);
     if (!d_ckpt || !d_ckpt_rows) return fail(HV_ERR_VALUE, "checkpoint buffers are required");
     return infer_impl(m, d_images, batch, d_logits, d_token_counts, d_summary, d_warnings, d_ckpt, d_ckpt_rows,
                       (cudaStream_t)stream);
 }
 
-int hv_infer_host(hv_model *m, const int8_t *h_images, int batch, int32_t *h_logits, int32_t *h_token_counts,
-                  hv_selector_summary *h_summary, uint8_t *h_warnings) {
+namespace {
+
+int host_wait_oldest(hv_model *m) {
+    hv_model::HostCall &c = m->host_calls[m->host_head];
+    const int slot = m->host_head;
+    for (int k = 0; k < 2; ++k) CUDA_TRY(cudaEventSynchronize(c.done[k]));
+    m->host_head = (m->host_head + 1) % 2;
+    m->host_pending -= 1;
+    const uint8_t *st = m->pin_out[slot];
+    if (!c.pinned_out) memcpy(c.logits, st, (size_t)c.batch * HV_CLASSES * 4);
+    if (c.tc) memcpy(c.tc, st + c.o_tc, (size_t)c.batch * (c.ns + 1) * 4);
+    if (c.sum && c.ns) memcpy(c.sum, st + c.o_sum, (size_t)c.batch * c.ns * sizeof(hv_selector_summary));
+    if (c.warn) memcpy(c.warn, st + c.o_warn, (size_t)c.batch);
+    for (int i = 0; i < 2; ++i) {
+        if (!m->ws[i].err) continue;
+        int code = 0;
+        CUDA_TRY(cudaMemcpy(&code, m->ws[i].err, sizeof(int), cudaMemcpyDeviceToHost));
+        if (code) return fail(HV_ERR_STATE, "a device-side bounded wait gave up (code %d)", code);
+    }
+    return HV_OK;
+}
+
+// Let the device work of every call in flight finish; the calls stay pending
+// (their outputs reach the caller at their waits).
+int host_quiesce(hv_model *m) {
+    for (int k = 0; k < m->host_pending; ++k) {
+        const hv_model::HostCall &c = m->host_calls[(m->host_head + k) % 2];
+        for (int j = 0; j < 2; ++j) CUDA_TRY(cudaEventSynchronize(c.done[j]));
+    }
+    return HV_OK;
+}
+
+}  // namespace
+
+int hv_infer_host_submit(hv_model *m, const int8_t *h_images, int batch, int32_t *h_logits, int32_t *h_token_counts,
+                         hv_selector_summary *h_summary, uint8_t *h_warnings) {
     if (!m) return fail(HV_ERR_VALUE, "null model");
     if (batch <= 0 || !h_images || !h_logits) return fail(HV_ERR_VALUE, "bad arguments");
     CUDA_TRY(cudaSetDevice(m->device));
+    if (m->host_pending == 2) {
+        const int rc = host_wait_oldest(m);
+        if (rc) return rc;
+    }
+    if (!m->host_pending) m->host_chunks = 0;  // every earlier chunk has finished
     // Chunk schedule.  Consecutive chunks run on two streams and every upload but
     // the first overlaps compute; a tail of less than a quarter chunk joins the
     // chunk before it.  The first chunk stays as large as the others: measured on
@@ -1194,44 +1275,62 @@ int hv_infer_host(hv_model *m, const int8_t *h_images, int batch, int32_t *h_log
     if (!m->copy_stream) {
         CUDA_TRY(cudaStreamCreateWithFlags(&m->copy_stream, cudaStreamNonBlocking));
         for (int i = 0; i < 2; ++i) CUDA_TRY(cudaStreamCreateWithFlags(&m->compute_stream[i], cudaStreamNonBlocking));
-        for (int i = 0; i < 2; ++i) {
+        for (int i = 0; i < 4; ++i) {
             CUDA_TRY(cudaEventCreateWithFlags(&m->ev_in[i], cudaEventDisableTiming));
             CUDA_TRY(cudaEventCreateWithFlags(&m->ev_done[i], cudaEventDisableTiming));
         }
+        for (int i = 0; i < 2; ++i) {
+            CUDA_TRY(cudaEventCreateWithFlags(&m->ev_pin[i], cudaEventDisableTiming));
+            for (int k = 0; k < 2; ++k)
+                CUDA_TRY(cudaEventCreateWithFlags(&m->host_calls[i].done[k], cudaEventDisableTiming));
+        }
+    }
+    // Workspaces this call uses (chunk g takes g & 1).  Growing a device buffer
+    // frees the old one, which calls in flight may still use: finish them first.
+    bool use_ws[2] = {false, false};
+    for (size_t c = 0; c + 1 < starts.size(); ++c) use_ws[(m->host_chunks + c) & 1] = true;
+    if ((chunk > m->host_cap || (use_ws[0] && chunk > m->ws[0].cap) || (use_ws[1] && chunk > m->ws[1].cap)) &&
+        m->host_pending) {
+        const int rc = host_quiesce(m);
+        if (rc) return rc;
     }
     if (chunk > m->host_cap) {
-        for (int i = 0; i < 2; ++i)
+        for (int i = 0; i < 4; ++i)
             if (m->himg[i]) cudaFree(m->himg[i]);
         if (m->hlogits) cudaFree(m->hlogits);
         if (m->htc) cudaFree(m->htc);
         if (m->hsum) cudaFree(m->hsum);
         if (m->hwarn) cudaFree(m->hwarn);
-        for (int i = 0; i < 2; ++i) CUDA_TRY(cudaMalloc(&m->himg[i], (size_t)chunk * HV_IMAGE_BYTES));
+        m->host_cap = 0;
+        for (int i = 0; i < 4; ++i) CUDA_TRY(cudaMalloc(&m->himg[i], (size_t)chunk * HV_IMAGE_BYTES));
         CUDA_TRY(cudaMalloc(&m->hlogits, (size_t)chunk * HV_CLASSES * 4 * 2));
         CUDA_TRY(cudaMalloc(&m->htc, (size_t)chunk * (HV_MAX_SELECTORS + 1) * 4 * 2));
         CUDA_TRY(cudaMalloc(&m->hsum, (size_t)chunk * HV_MAX_SELECTORS * sizeof(hv_selector_summary) * 2));
         CUDA_TRY(cudaMalloc(&m->hwarn, (size_t)chunk * 2));
         m->host_cap = chunk;
     }
-    // Consecutive chunks alternate between two workspaces and two compute streams,
-    // so one chunk's kernels fill the idle tails of the other's.
-    int rc = ensure_capacity(m, chunk, 0);
-    if (rc) return rc;
-    if (starts.size() > 2 && (rc = ensure_capacity(m, chunk, 1)) != 0) return rc;
-    // Outputs land in pinned staging (an asynchronous copy into pageable memory
-    // would block this thread until the chunk's compute finished, serialising the
-    // pipeline) and are copied to the caller's arrays once at the end.
+    // Chunks alternate between two workspaces and two compute streams, so one
+    // chunk's kernels fill the idle tails of the other's (also across calls).
+    int rc = HV_OK;
+    for (int i = 0; i < 2; ++i)
+        if (use_ws[i] && (rc = ensure_capacity(m, chunk, i)) != 0) return rc;
+    // Outputs land in the call's pinned staging slot (an asynchronous copy into
+    // pageable memory would block this thread until the chunk's compute finished)
+    // and reach the caller's arrays at the wait.
+    const int slot = (m->host_head + m->host_pending) % 2;
+    hv_model::HostCall &call = m->host_calls[slot];
     const size_t o_log = 0, o_tc = o_log + (size_t)batch * HV_CLASSES * 4,
                  o_sum = o_tc + (size_t)batch * (ns + 1) * 4,
                  o_warn = o_sum + (size_t)batch * ns * sizeof(hv_selector_summary),
                  o_end = o_warn + (size_t)batch;
-    if (o_end > m->pin_out_cap) {
-        if (m->pin_out) cudaFreeHost(m->pin_out);
-        m->pin_out = nullptr;
-        m->pin_out_cap = 0;
-        CUDA_TRY(cudaHostAlloc((void **)&m->pin_out, o_end, cudaHostAllocDefault));
-        m->pin_out_cap = o_end;
+    if (o_end > m->pin_out_cap[slot]) {
+        if (m->pin_out[slot]) cudaFreeHost(m->pin_out[slot]);
+        m->pin_out[slot] = nullptr;
+        m->pin_out_cap[slot] = 0;
+        CUDA_TRY(cudaHostAlloc((void **)&m->pin_out[slot], o_end, cudaHostAllocDefault));
+        m->pin_out_cap[slot] = o_end;
     }
+    uint8_t *stage = m->pin_out[slot];
     // Pageable images are staged through two pinned chunk buffers; the host copy of
     // chunk c + 1 overlaps the device work on chunk c.
     cudaPointerAttributes pa;
@@ -1242,7 +1341,10 @@ int hv_infer_host(hv_model *m, const int8_t *h_images, int batch, int32_t *h_log
     cudaGetLastError();
     if (!pinned_in && chunk > m->pin_in_cap) {
         for (int i = 0; i < 2; ++i) {
-            if (m->pin_in[i]) cudaFreeHost(m->pin_in[i]);
+            if (m->pin_in[i]) {
+                CUDA_TRY(cudaEventSynchronize(m->ev_pin[i]));  // its last upload has finished
+                cudaFreeHost(m->pin_in[i]);
+            }
             m->pin_in[i] = nullptr;
         }
         m->pin_in_cap = 0;
@@ -1252,61 +1354,86 @@ int hv_infer_host(hv_model *m, const int8_t *h_images, int batch, int32_t *h_log
     }
     const int nchunks = (int)starts.size() - 1;
     for (int c = 0; c < nchunks; ++c) {
-        const int buf = c & 1;
+        // chunk g: device images g % 4, workspace, compute stream and outputs g % 2,
+        // pinned staging g % 2
+        const unsigned long long g = m->host_chunks++;
+        const int buf = (int)(g & 1), ib = (int)(g & 3);
         const int first = starts[c], cnt = starts[c + 1] - starts[c];
         const int8_t *src = h_images + (size_t)first * HV_IMAGE_BYTES;
         if (!pinned_in) {
-            // the copy out of pin_in[buf] issued two chunks back must have finished
-            if (c >= 2) CUDA_TRY(cudaEventSynchronize(m->ev_in[buf]));
+            // the upload out of pin_in[buf] issued two chunks back must have finished
+            CUDA_TRY(cudaEventSynchronize(m->ev_pin[buf]));
             memcpy(m->pin_in[buf], src, (size_t)cnt * HV_IMAGE_BYTES);
             src = m->pin_in[buf];
         }
-        // The copy into buffer `buf` must wait until the compute two chunks back released it.
-        if (c >= 2) CUDA_TRY(cudaStreamWaitEvent(m->copy_stream, m->ev_done[buf], 0));
-        CUDA_TRY(cudaMemcpyAsync(m->himg[buf], src, (size_t)cnt * HV_IMAGE_BYTES, cudaMemcpyHostToDevice,
+        // The upload into himg[ib] waits until the chunk four back has computed on it
+        // (an event never recorded is complete), so uploads run up to three chunks
+        // ahead of the compute.
+        CUDA_TRY(cudaStreamWaitEvent(m->copy_stream, m->ev_done[ib], 0));
+        CUDA_TRY(cudaMemcpyAsync(m->himg[ib], src, (size_t)cnt * HV_IMAGE_BYTES, cudaMemcpyHostToDevice,
                                  m->copy_stream));
-        CUDA_TRY(cudaEventRecord(m->ev_in[buf], m->copy_stream));
+        CUDA_TRY(cudaEventRecord(m->ev_in[ib], m->copy_stream));
+        if (!pinned_in) CUDA_TRY(cudaEventRecord(m->ev_pin[buf], m->copy_stream));
         cudaStream_t cst = m->compute_stream[buf];
         use_workspace(m, buf);
-        CUDA_TRY(cudaStreamWaitEvent(cst, m->ev_in[buf], 0));
+        CUDA_TRY(cudaStreamWaitEvent(cst, m->ev_in[ib], 0));
         int32_t *dl = m->hlogits + (size_t)buf * m->host_cap * HV_CLASSES;
         int32_t *dtc = m->htc + (size_t)buf * m->host_cap * (HV_MAX_SELECTORS + 1);
         hv_selector_summary *dsum = m->hsum + (size_t)buf * m->host_cap * HV_MAX_SELECTORS;
         uint8_t *dw = m->hwarn + (size_t)buf * m->host_cap;
         if (m->use_graphs && !m->prof_stage)
-            rc = run_graph(m, m->himg[buf], cnt, dl, h_token_counts ? dtc : nullptr, h_summary ? dsum : nullptr,
+            rc = run_graph(m, m->himg[ib], cnt, dl, h_token_counts ? dtc : nullptr, h_summary ? dsum : nullptr,
                            h_warnings ? dw : nullptr, buf, cst);
         else
-            rc = infer_impl(m, m->himg[buf], cnt, dl, h_token_counts ? dtc : nullptr, h_summary ? dsum : nullptr,
+            rc = infer_impl(m, m->himg[ib], cnt, dl, h_token_counts ? dtc : nullptr, h_summary ? dsum : nullptr,
                             h_warnings ? dw : nullptr, nullptr, nullptr, cst, buf);
-        if (rc) return rc;
-        CUDA_TRY(cudaEventRecord(m->ev_done[buf], cst));
+        if (rc) {
+            use_workspace(m, 0);
+            return rc;
+        }
+        CUDA_TRY(cudaEventRecord(m->ev_done[ib], cst));
         CUDA_TRY(cudaMemcpyAsync(pinned_out ? (uint8_t *)(h_logits + (size_t)first * HV_CLASSES)
-                                            : m->pin_out + o_log + (size_t)first * HV_CLASSES * 4,
+                                            : stage + o_log + (size_t)first * HV_CLASSES * 4,
                                  dl, (size_t)cnt * HV_CLASSES * 4, cudaMemcpyDeviceToHost, cst));
         if (h_token_counts)
-            CUDA_TRY(cudaMemcpyAsync(m->pin_out + o_tc + (size_t)first * (ns + 1) * 4, dtc, (size_t)cnt * (ns + 1) * 4,
+            CUDA_TRY(cudaMemcpyAsync(stage + o_tc + (size_t)first * (ns + 1) * 4, dtc, (size_t)cnt * (ns + 1) * 4,
                                      cudaMemcpyDeviceToHost, cst));
         if (h_summary && ns)
-            CUDA_TRY(cudaMemcpyAsync(m->pin_out + o_sum + (size_t)first * ns * sizeof(hv_selector_summary), dsum,
-                                     (size_t)cnt * ns * sizeof(hv_selector_summary), cudaMemcpyDeviceToHost,
-                                     cst));
-        if (h_warnings)
-            CUDA_TRY(cudaMemcpyAsync(m->pin_out + o_warn + first, dw, cnt, cudaMemcpyDeviceToHost, cst));
+            CUDA_TRY(cudaMemcpyAsync(stage + o_sum + (size_t)first * ns * sizeof(hv_selector_summary), dsum,
+                                     (size_t)cnt * ns * sizeof(hv_selector_summary), cudaMemcpyDeviceToHost, cst));
+        if (h_warnings) CUDA_TRY(cudaMemcpyAsync(stage + o_warn + first, dw, cnt, cudaMemcpyDeviceToHost, cst));
     }
-    for (int i = 0; i < 2; ++i) CUDA_TRY(cudaStreamSynchronize(m->compute_stream[i]));
     use_workspace(m, 0);
-    if (!pinned_out) memcpy(h_logits, m->pin_out + o_log, (size_t)batch * HV_CLASSES * 4);
-    if (h_token_counts) memcpy(h_token_counts, m->pin_out + o_tc, (size_t)batch * (ns + 1) * 4);
-    if (h_summary && ns) memcpy(h_summary, m->pin_out + o_sum, (size_t)batch * ns * sizeof(hv_selector_summary));
-    if (h_warnings) memcpy(h_warnings, m->pin_out + o_warn, (size_t)batch);
-    for (int i = 0; i < 2; ++i) {
-        if (!m->ws[i].err) continue;
-        int code = 0;
-        CUDA_TRY(cudaMemcpy(&code, m->ws[i].err, sizeof(int), cudaMemcpyDeviceToHost));
-        if (code) return fail(HV_ERR_STATE, "a device-side bounded wait gave up (code %d)", code);
-    }
+    for (int k = 0; k < 2; ++k) CUDA_TRY(cudaEventRecord(call.done[k], m->compute_stream[k]));
+    call.batch = batch;
+    call.ns = ns;
+    call.logits = h_logits;
+    call.tc = h_token_counts;
+    call.sum = h_summary;
+    call.warn = h_warnings;
+    call.pinned_out = pinned_out;
+    call.o_tc = o_tc;
+    call.o_sum = o_sum;
+    call.o_warn = o_warn;
+    m->host_pending += 1;
     return HV_OK;
+}
+
+int hv_infer_host_wait(hv_model *m) {
+    if (!m) return fail(HV_ERR_VALUE, "null model");
+    if (!m->host_pending) return fail(HV_ERR_STATE, "no host call in flight");
+    CUDA_TRY(cudaSetDevice(m->device));
+    return host_wait_oldest(m);
+}
+
+int hv_infer_host(hv_model *m, const int8_t *h_images, int batch, int32_t *h_logits, int32_t *h_token_counts,
+                  hv_selector_summary *h_summary, uint8_t *h_warnings) {
+    if (!m) return fail(HV_ERR_VALUE, "null model");
+    HOST_IDLE(m);
+    CUDA_TRY(cudaSetDevice(m->device));
+    const int rc = hv_infer_host_submit(m, h_images, batch, h_logits, h_token_counts, h_summary, h_warnings);
+    if (rc) return rc;
+    return host_wait_oldest(m);
 }
 
 int hv_device_error(hv_model *m, int *code) {
@@ -1327,6 +1454,7 @@ int hv_device_error(hv_model *m, int *code) {
 
 int hv_profile_start(hv_model *m, int stage, int max_launches) {
     if (!m) return fail(HV_ERR_VALUE, "null model");
+    HOST_IDLE(m);
     if (max_launches < 0) return fail(HV_ERR_VALUE, "negative launch count");
     CUDA_TRY(cudaSetDevice(m->device));
     if ((int)m->prof_ev.size() < 2 * max_launches) {
@@ -1518,6 +1646,7 @@ int hv_gelu_requant(const int32_t *d_acc, int64_t count, int src_exp, int dst_ex
 int hv_transformer_block(hv_model *m, int block_index, const int8_t *d_x, const int32_t *d_offsets, int images,
                          int total_rows, int8_t *d_z, void *stream) {
     if (!m) return fail(HV_ERR_VALUE, "null model");
+    HOST_IDLE(m);
     if (block_index < 0 || block_index >= HV_BLOCKS) return fail(HV_ERR_VALUE, "block index out of range");
     if (!m->has_block[block_index]) return fail(HV_ERR_STATE, "model has no block %d", block_index + 1);
     if (images <= 0 || total_rows < 0 || total_rows > images * HV_TOKENS)
@@ -1536,6 +1665,7 @@ int hv_transformer_block(hv_model *m, int block_index, const int8_t *d_x, const 
 
 int hv_patch_embedding(hv_model *m, const int8_t *d_images, int batch, int8_t *d_tokens, void *stream) {
     if (!m) return fail(HV_ERR_VALUE, "null model");
+    HOST_IDLE(m);
     if (batch <= 0) return fail(HV_ERR_VALUE, "batch must be positive");
     if (!m->has_patch) return fail(HV_ERR_STATE, "model has no patch embedding");
     CUDA_TRY(cudaSetDevice(m->device));
@@ -1553,6 +1683,7 @@ int hv_token_selector(hv_model *m, int selector_index, const int8_t *d_x, const 
                       hv_selector_summary *d_summary, int32_t *d_fused, int32_t *d_head_scores,
                       int32_t *d_head_weights, int8_t *d_local, int8_t *d_global, int8_t *d_stats, void *stream) {
     if (!m) return fail(HV_ERR_VALUE, "null model");
+    HOST_IDLE(m);
     if (selector_index < 0 || selector_index >= m->num_sel) return fail(HV_ERR_VALUE, "selector index out of range");
     if (images <= 0) return fail(HV_ERR_VALUE, "images must be positive");
     CUDA_TRY(cudaSetDevice(m->device));
@@ -1570,6 +1701,8 @@ int hv_token_selector(hv_model *m, int selector_index, const int8_t *d_x, const 
 
 int hv_selector_h2(hv_model *m, int selector_index, const int8_t *d_x, const int32_t *d_offsets, int images,
                    int8_t *d_h2, void *stream) {
+    if (!m) return fail(HV_ERR_VALUE, "null model");
+    HOST_IDLE(m);
     if (!m || !d_x || !d_offsets || !d_h2) return fail(HV_ERR_VALUE, "null argument");
     if (selector_index < 0 || selector_index >= m->num_sel) return fail(HV_ERR_VALUE, "selector index out of range");
     if (images <= 0) return fail(HV_ERR_VALUE, "images must be positive");

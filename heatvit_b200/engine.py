@@ -66,6 +66,7 @@ class Engine:
         with torch.cuda.device(dev):
             self._h = _Handle(self.packed.struct, dev.index, self.packed)
         self.num_selectors = self.packed.used_selectors
+        self._inflight = []  # arrays of submitted host calls, oldest first
 
     @property
     def handle(self):
@@ -136,6 +137,32 @@ class Engine:
             check(lib().hv_infer_host(self.handle, pl(images), b, pl(logits), pl(token_counts), pl(summary),
                                       pl(warnings)))
         return logits
+
+    def infer_host_submit(self, images, logits, token_counts=None, summary=None, warnings=None):
+        """Asynchronous host entry (serving loops): enqueue one call and return;
+        ``infer_host_wait()`` finishes the oldest call and returns its logits.
+        The arrays stay referenced (and must stay untouched) until then."""
+        images = np.ascontiguousarray(images).reshape(-1, abi.IMAGE_BYTES)
+        if images.dtype != np.int8:
+            raise TypeError("images must be int8")
+        if logits.dtype != np.int32 or logits.shape != (images.shape[0], abi.CLASSES) or \
+                not logits.flags.c_contiguous:
+            raise ValueError("logits must be a contiguous int32 [B, 1000] array")
+        if len(self._inflight) == 2:
+            self.infer_host_wait()  # the library would wait for the oldest call itself
+        pl = lambda a: None if a is None else a.ctypes.data_as(C.c_void_p)
+        torch = _torch()
+        with torch.cuda.device(self.device):
+            check(lib().hv_infer_host_submit(self.handle, pl(images), images.shape[0], pl(logits),
+                                             pl(token_counts), pl(summary), pl(warnings)))
+        self._inflight.append((images, logits, token_counts, summary, warnings))
+
+    def infer_host_wait(self):
+        torch = _torch()
+        done = self._inflight.pop(0) if self._inflight else None
+        with torch.cuda.device(self.device):
+            check(lib().hv_infer_host_wait(self.handle))
+        return None if done is None else done[1]
 
     def transformer_block(self, block_index, x, offsets):
         """Fused block over a ragged batch: x [T, 192] int8, offsets [B+1] int32 (CUDA)."""

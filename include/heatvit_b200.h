@@ -186,10 +186,25 @@ HV_API int hv_infer_batch_checkpoints(hv_model *model, const int8_t *d_images, i
 
 /* Host-buffer convenience: copies h_images (pinned or pageable) to the device in
  * chunks on two streams overlapped with compute, runs the batch, copies logits
- * (and the optional outputs) back.  Blocks until the results are on the host. */
+ * (and the optional outputs) back.  Blocks until the results are on the host.
+ * The host-side counterpart of model.HeatViTModel.infer over a batch
+ * (verification/heatvit_ref/model.py:70-123). */
 HV_API int hv_infer_host(hv_model *model, const int8_t *h_images, int batch,
                   int32_t *h_logits, int32_t *h_token_counts,
                   hv_selector_summary *h_summary, uint8_t *h_warnings);
+
+/* Asynchronous form of hv_infer_host for serving loops: enqueues one call's
+ * uploads, inference and downloads and returns.  hv_infer_host_wait blocks until
+ * the oldest submitted call has finished and its outputs are in the caller's
+ * arrays, which (and h_images) must stay untouched until then.  Two calls may be
+ * in flight (a third submit first waits for the oldest); the next call's uploads
+ * run during this call's compute.  While calls are in flight the model's other
+ * entry points return HV_ERR_STATE.  No counterpart in the reference (its model
+ * runs one image per call). */
+HV_API int hv_infer_host_submit(hv_model *model, const int8_t *h_images, int batch,
+                  int32_t *h_logits, int32_t *h_token_counts,
+                  hv_selector_summary *h_summary, uint8_t *h_warnings);
+HV_API int hv_infer_host_wait(hv_model *model);
 
 /* Read and clear the model's device error word (synchronises with the device).
  * *code != 0 means a kernel's bounded wait on a tensor-core completion gave up

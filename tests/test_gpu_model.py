@@ -167,6 +167,69 @@ def test_host_entry_matches_device_entry(cuda):
         np.testing.assert_array_equal(warn, dev["warnings"].cpu().numpy())
 
 
+def test_host_submit_wait_pipeline(cuda):
+    """Asynchronous host calls: up to two in flight, buffers alternating across
+    calls, single- and multi-chunk calls, pageable and pinned arrays; every call's
+    outputs equal the device entry's.  Other entry points refuse to run while a
+    call is in flight."""
+    import torch
+    from heatvit_b200 import synth
+    from heatvit_b200.engine import Engine
+    params = synth.config3_params(synth.SEED)
+    eng = Engine(params)
+    ns = eng.num_selectors
+    sizes = [700, 300, 1024, 5, 513]                           # 512+188, 300, 512+512, 5, 513 images
+    calls = []
+    for i, n in enumerate(sizes):
+        imgs = synth.baseline_images(synth.SEED, n, first=3000 + 1000 * i)
+        dev = eng.infer(torch.from_numpy(imgs).cuda())
+        if i % 2:
+            src = torch.empty(imgs.shape, dtype=torch.int8, pin_memory=True).numpy()
+            src[:] = imgs
+            lg = torch.empty((n, 1000), dtype=torch.int32, pin_memory=True).numpy()
+        else:
+            src, lg = imgs, np.empty((n, 1000), np.int32)
+        calls.append(dict(src=src, logits=lg, tc=np.empty((n, ns + 1), np.int32), warn=np.empty(n, np.uint8),
+                          summ=np.empty((n, ns, 6), np.int32), dev=dev))
+    def check(c):
+        np.testing.assert_array_equal(c["logits"], c["dev"]["logits"].cpu().numpy())
+        np.testing.assert_array_equal(c["tc"], c["dev"]["token_counts"].cpu().numpy())
+        np.testing.assert_array_equal(c["summ"], c["dev"]["summary"].cpu().numpy())
+        np.testing.assert_array_equal(c["warn"], c["dev"]["warnings"].cpu().numpy())
+
+    def submit(c):
+        for k in ("logits", "tc", "summ"):
+            c[k].fill(-1)
+        c["warn"].fill(255)
+        eng.infer_host_submit(c["src"], c["logits"], token_counts=c["tc"], summary=c["summ"], warnings=c["warn"])
+
+    # two calls in flight at every submit after the first; waits return in order
+    done = []
+    for i, c in enumerate(calls):
+        submit(c)
+        if i == 1:
+            with pytest.raises(RuntimeError, match="in flight"):
+                eng.infer(torch.zeros((1, 150528), dtype=torch.int8, device="cuda"))
+            with pytest.raises(RuntimeError, match="in flight"):
+                eng.infer_host(c["src"])
+        if len(eng._inflight) == 2:
+            done.append(eng.infer_host_wait())
+    done.append(eng.infer_host_wait())
+    assert [id(a) for a in done] == [id(c["logits"]) for c in calls]
+    for c in calls:
+        check(c)
+    # a third submit waits for the oldest call itself
+    for c in calls[:4]:
+        submit(c)
+    while eng._inflight:
+        eng.infer_host_wait()
+    for c in calls[:4]:
+        check(c)
+    eng.infer(torch.zeros((1, 150528), dtype=torch.int8, device="cuda"))  # idle again
+    with pytest.raises(RuntimeError, match="no host call"):
+        eng.infer_host_wait()
+
+
 def test_engine_input_errors(cuda):
     import torch
     from heatvit_b200 import synth
