@@ -19,6 +19,7 @@ struct LnParams {
     int fast;                      // 1: sh_g <= 16 and sh_b <= 40 (int64 output stage)
     int split;                     // 1: x_scale <= -4, so |x_q32 - mean| <= 2^36 (64-bit split product)
     int out32;                     // 1: sh_g == 0, sh_b <= 22, sh_out in [1, 30] (32-bit output stage)
+    int one;                       // a runtime 1: multiply-adds by it stay on the FMA pipe
 };
 
 LnParams make_ln(const int8_t *gamma, const int8_t *beta, int x_scale, int gamma_scale, int beta_scale,

@@ -26,6 +26,7 @@ LnParams make_ln(const int8_t *gamma, const int8_t *beta, int x_scale, int gamma
     p.fast = (p.sh_g <= 16 && p.sh_b <= 40) ? 1 : 0;
     p.split = x_scale <= -4 ? 1 : 0;
     p.out32 = (p.sh_g == 0 && p.sh_b <= 22 && p.sh_out >= 1 && p.sh_out <= 30) ? 1 : 0;
+    p.one = 1;
     return p;
 }
 
@@ -317,13 +318,21 @@ __global__ void __launch_bounds__(256, 3) ln_kernel(const int8_t *x, int8_t *out
     // gamma and the aligned beta term per channel, in shared memory (lane stride 25
     // words: the 8 lanes of a row group hit distinct banks)
     __shared__ int32_t s_gam[8 * 25], s_bet[8 * 25];
+    // the same as {gamma, beta} pairs of consecutive channels, one 16-byte load per
+    // two channels (lane stride 13 x 16 bytes: the 8 row-group lanes hit distinct
+    // bank quads)
+    __shared__ int4 s_gb[8 * 13];
     for (int c = threadIdx.x; c < 192; c += blockDim.x) {
         const int slot = (c / 24) * 25 + c % 24;
         s_gam[slot] = p.gamma[c];
         const int32_t b = p.beta[c];
         s_bet[slot] = OUT32 ? b * (1 << p.sh_b) : b;
+        int32_t *pair = (int32_t *)&s_gb[(c / 24) * 13 + (c % 24) / 2] + 2 * (c & 1);
+        pair[0] = p.gamma[c];
+        pair[1] = OUT32 ? b * (1 << p.sh_b) : b;
     }
     __syncthreads();
+    const int4 *gb = s_gb + sub * 13;
     const int32_t *gam = s_gam + sub * 25, *bet = s_bet + sub * 25;
     griddep_wait();  // rows and their count come from earlier kernels
     griddep_launch();
@@ -336,16 +345,25 @@ __global__ void __launch_bounds__(256, 3) ln_kernel(const int8_t *x, int8_t *out
     for (int base = warp * R; base < rows; base += warps * R) {
         int32_t my_s = 0;
         int64_t my_s2 = 0;
-#pragma unroll 1
-        for (int k = 0; k < g; ++k) {
+        // this lane's 24 bytes of sub-pass k's row (zeros past the rows); each
+        // sub-pass loads the next one's words before its own arithmetic
+        auto load_words = [&](int k, uint2 (&w)[3]) {
             const int r = base + 4 * k + grp;
-            uint2 w[3] = {make_uint2(0, 0), make_uint2(0, 0), make_uint2(0, 0)};
-            if (r < rows) {
+            w[0] = w[1] = w[2] = make_uint2(0, 0);
+            if (k < g && r < rows) {
                 const uint2 *src = (const uint2 *)(x + (size_t)r * 192 + 24 * sub);
                 w[0] = src[0];
                 w[1] = src[1];
                 w[2] = src[2];
             }
+        };
+        uint2 wn[3];
+        load_words(0, wn);
+#pragma unroll 1
+        for (int k = 0; k < g; ++k) {
+            const int r = base + 4 * k + grp;
+            const uint2 w[3] = {wn[0], wn[1], wn[2]};
+            load_words(k + 1, wn);
             // Σx and Σx² of the 24 bytes with 4-way byte dot products (|Σx²| < 2^21)
             int32_t s = 0, q = 0;
 #pragma unroll
@@ -392,6 +410,7 @@ __global__ void __launch_bounds__(256, 3) ln_kernel(const int8_t *x, int8_t *out
             }
         }
         const bool all_safe = __all_sync(0xffffffffu, af.safe || myrow >= rows);
+        if (OUT32 && all_safe) load_words(0, wn);
 #pragma unroll 1
         for (int k = 0; k < g; ++k) {
             const int r = base + 4 * k + grp;
@@ -401,6 +420,73 @@ __global__ void __launch_bounds__(256, 3) ln_kernel(const int8_t *x, int8_t *out
             rs.mean = shfl64(st.mean, owner);
             rs.inv = (uint64_t)shfl64((int64_t)st.inv, owner);
             rs.neg = false;
+            if (OUT32 && all_safe) {
+                // Short form with the output stage on the FMA pipe, per element:
+                //   t  = vp*ahh + (khh + 255)        (vp = v + 128, 64-bit)
+                //   nr = vp*aq + kq + hi32(t)
+                //   o  = (x + 2^(sh-1) + [x < 0]*-1) >> sh,  x = nr*gamma + beta'
+                // The +255 keeps hi32(t) equal to the short form's term exactly when the
+                // low word of vp*ahh + khh lies in [1, 2^32 - 256] (no carry) and then
+                // lifts it to [256, 2^32 - 1]; every other case leaves a low word below
+                // 256.  The lanes track the smallest low word, and a pass with one below
+                // 256 is redone with the exact per-element form.
+                const uint32_t aq = __shfl_sync(0xffffffffu, af.aq, owner);
+                const uint32_t ahh = __shfl_sync(0xffffffffu, af.ahh, owner);
+                const uint64_t kh = (uint64_t)__shfl_sync(0xffffffffu, af.khh, owner) + 255u;
+                const int32_t kq = __shfl_sync(0xffffffffu, af.kq, owner);
+                const int32_t one = p.one, half = 1 << (p.sh_out - 1);
+                const uint32_t words[6] = {wn[0].x, wn[0].y, wn[1].x, wn[1].y, wn[2].x, wn[2].y};
+                load_words(k + 1, wn);
+                uint32_t lo_min = 0xFFFFFFFFu, ow[6];
+#pragma unroll
+                for (int q = 0; q < 6; ++q) {
+                    const uint32_t xb = words[q] ^ 0x80808080u;  // bytes v + 128
+                    const int4 g01 = gb[2 * q], g23 = gb[2 * q + 1];
+                    const int32_t gg[4] = {g01.x, g01.z, g23.x, g23.z}, bb[4] = {g01.y, g01.w, g23.y, g23.w};
+                    int32_t o4[4];
+#pragma unroll
+                    for (int b = 0; b < 4; ++b) {
+                        const uint32_t vp = __byte_perm(xb, 0u, 0x4440u + b);
+                        const uint64_t t = (uint64_t)vp * ahh + kh;
+                        lo_min = min(lo_min, (uint32_t)t);
+                        const int32_t nr = (int32_t)(vp * aq) + kq + (int32_t)(t >> 32);
+                        const int32_t xv = nr * gg[b] + bb[b];
+                        const int32_t xh = xv * one + half;
+                        o4[b] = (__mulhi(xv, one) + xh) >> p.sh_out;
+                    }
+                    ow[q] = pack_sat8(o4[0], o4[1], o4[2], o4[3]);
+                }
+                if (!active) lo_min = 0xFFFFFFFFu;
+                if (__any_sync(0xffffffffu, lo_min < 256u)) {
+                    LnAff f;
+                    f.aq = aq;
+                    f.ahh = ahh;
+                    f.khh = (uint32_t)(kh - 255u);
+                    f.kq = kq;
+                    int32_t v[24];
+                    ln_load24(x + (size_t)(active ? r : 0) * 192, sub, active, v);
+#pragma unroll
+                    for (int q = 0; q < 6; ++q) {
+                        int32_t o4[4];
+#pragma unroll
+                        for (int b = 0; b < 4; ++b) {
+                            const int i = 4 * q + b;
+                            bool ok;
+                            int32_t nr = ln_norm_short(v[i], f, ok);
+                            if (!ok) nr = ln_norm<SPLIT>(v[i], rs, p);
+                            o4[b] = rsa32(nr * gam[i] + bet[i], p.sh_out);
+                        }
+                        ow[q] = pack_sat8(o4[0], o4[1], o4[2], o4[3]);
+                    }
+                }
+                if (active) {
+                    uint2 *dst = (uint2 *)(out + (size_t)r * 192 + 24 * sub);
+                    dst[0] = make_uint2(ow[0], ow[1]);
+                    dst[1] = make_uint2(ow[2], ow[3]);
+                    dst[2] = make_uint2(ow[4], ow[5]);
+                }
+                continue;
+            }
             int32_t v[24];
             ln_load24(x + (size_t)(active ? r : 0) * 192, sub, active, v);
             int32_t o[24];
