@@ -1,6 +1,7 @@
 // hv_gemm.cu — int8 GEMM on tcgen05 tensor cores with fused integer epilogues.
 //
-// One CTA computes a 128 x BN output tile (BN = 64, 192 or 256 columns):
+// One CTA computes a 128 x BN output tile (BN = 64 columns; the ragged last tile of
+// N is masked in the epilogue):
 //   * 256 threads stream A [128 x 64] and B [BN x 64] k-tiles with cp.async into
 //     a 4-stage ring, each stage in the no-swizzle K-major canonical layout
 //     (hv_tc05.cuh); 8 consecutive threads fill one 128-byte core matrix, so
@@ -293,15 +294,17 @@ cudaError_t launch_t(const GemmArgs &g, int m_max, int *err, cudaStream_t st) {
     return launch_pdl(kern, grid, dim3(THREADS), smem, st, g, err);
 }
 
+// 64-column tiles for every N: a ragged last tile costs only its own columns, and
+// narrow tiles spread small-M GEMMs over more SMs (the 192 -> 1000 head over 1024
+// CLS rows runs as 128 CTAs instead of 32 with 256-column tiles).
 template <int EPI, bool U8, bool FAST>
 cudaError_t launch_bn(const GemmArgs &g, int m_max, int *err, cudaStream_t st) {
-    if (g.n % 64 == 0) return launch_t<EPI, U8, FAST, 64>(g, m_max, err, st);
-    return launch_t<EPI, U8, FAST, 256>(g, m_max, err, st);
+    return launch_t<EPI, U8, FAST, 64>(g, m_max, err, st);
 }
 
 }  // namespace
 
-int gemm_tile_n(int n) { return n % 64 == 0 ? 64 : 256; }
+int gemm_tile_n(int) { return 64; }
 
 cudaError_t launch_gemm(const GemmArgs &g, int epi, int a_unsigned, int m_max, int *err, cudaStream_t st) {
     const bool fast = g.epi.fast != 0;

@@ -4,6 +4,8 @@
 // owns 6 channels (bytes 4l..4l+3 and 128+2l..129+2l, so every load and
 // store is aligned and the warp touches the row with two coalesced accesses).
 // The 81-bit product (x_q32 - mean) * inv_std_q32 is formed in 128 bits.
+#include <algorithm>
+
 #include "hv_internal.cuh"
 
 namespace hv {
@@ -337,12 +339,19 @@ __global__ void __launch_bounds__(256, 3) ln_kernel(const int8_t *x, int8_t *out
     griddep_wait();  // rows and their count come from earlier kernels
     griddep_launch();
     const int rows = rows_dev ? *rows_dev : rows_max;
-    // Rows per warp pass: 4 * g for g 4-row sub-passes.  Few rows spread over all
-    // warps with short passes (the pass latency bounds small launches); many rows use
-    // full 32-row passes, which amortise the per-row statistics best.
-    const int g = max(1, min(8, (rows + 4 * warps - 1) / (4 * warps)));
+    // Rounds of one pass per warp (the grid is one wave of resident CTAs).  Each
+    // round's rows per pass, 4 * g for g 4-row sub-passes, spread the remaining rows
+    // over every warp: full 32-row passes while more than one round's worth remain
+    // (they amortise the per-row statistics best), then one shorter balanced round,
+    // so no warp runs a pass more than the others need (the pass latency bounds the
+    // launch).
+    for (int done = 0; done < rows;) {
+    const int g = max(1, min(8, (rows - done + 4 * warps - 1) / (4 * warps)));
     const int R = 4 * g;
-    for (int base = warp * R; base < rows; base += warps * R) {
+    const int base = done + warp * R;
+    done += warps * R;
+    if (base >= rows) break;  // warp-uniform; every later round starts past the rows
+    {
         int32_t my_s = 0;
         int64_t my_s2 = 0;
         // this lane's 24 bytes of sub-pass k's row (zeros past the rows); each
@@ -530,6 +539,7 @@ __global__ void __launch_bounds__(256, 3) ln_kernel(const int8_t *x, int8_t *out
             }
         }
     }
+    }  // rounds
 }
 
 template <bool SPLIT, bool OUT32>
@@ -685,11 +695,28 @@ cudaError_t launch_layernorm(const int8_t *x, int8_t *out, int rows_max, const i
                              const LnParams &p, uint8_t *negvar_row, const int32_t *offsets, int images,
                              uint8_t *warn, cudaStream_t st) {
     if (rows_max <= 0) return cudaSuccess;
-    const int rows_per_block = 8 * 32;  // 8 warps x 32 rows
-    int blocks = (rows_max + rows_per_block - 1) / rows_per_block;
-    if (blocks > 148 * 16) blocks = 148 * 16;
     auto kern = p.split ? (p.out32 ? ln_kernel<true, true> : ln_kernel<true, false>)
                         : (p.out32 ? ln_kernel<false, true> : ln_kernel<false, false>);
+    // One wave: as many CTAs as the GPU holds at once (3 per SM by the launch
+    // bounds), fewer when the worst-case rows need fewer 32-row passes.  The live
+    // row count is read on the device, which sizes each round's passes to it.
+    const int variant = (p.split ? 2 : 0) + (p.out32 ? 1 : 0);
+    static int s_wave[16][4];  // per device and variant; 0 = not yet queried
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    int wave = dev < 16 ? s_wave[dev][variant] : 0;
+    if (wave <= 0) {
+        int sms = 0, per_sm = 0;
+        e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        if (e != cudaSuccess) return e;
+        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, 256, 0);
+        if (e != cudaSuccess) return e;
+        wave = std::max(1, sms * per_sm);
+        if (dev < 16) s_wave[dev][variant] = wave;
+    }
+    const int rows_per_block = 8 * 32;  // 8 warps x 32 rows
+    const int blocks = std::min((rows_max + rows_per_block - 1) / rows_per_block, wave);
     return launch_pdl(kern, dim3(blocks), dim3(256), 0, st, x, out, rows_max, rows_dev, p, negvar_row, offsets, images,
                       warn);
 }
