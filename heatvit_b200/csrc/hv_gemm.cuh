@@ -109,6 +109,11 @@ bool gemm_persistent_supported(int epi, int n, int k);
 // Tensor map of a row-major int8 A operand [rows][k] (k a multiple of 16) read as
 // 16-byte x 128-row boxes; rows past `rows` read as zero.  Returns 0 on success.
 int make_tmap_a(CUtensorMap *map, const void *base, int k, int rows);
+// Tensor map of NHWC images [images_n][224][224][3] for the patch GEMM's TMA
+// gather: 5-D boxes of one 16-byte K strip for 7 x 14 patches.  Returns 0 on
+// success, non-zero when the driver entry point is missing or `images` is not
+// 16-byte aligned (the caller then keeps the cp.async gather).
+int make_tmap_patch(CUtensorMap *map, const void *images, int images_n);
 cudaError_t launch_gemm_persistent(const GemmArgs &g, int epi, int m_max, int *err, int sms, cudaStream_t st);
 
 }  // namespace hv

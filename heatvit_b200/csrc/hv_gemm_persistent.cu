@@ -91,6 +91,17 @@ __device__ __forceinline__ void tma_load_a(uint32_t dst, const CUtensorMap *map,
         : "memory");
 }
 
+// One 16-byte K strip of 7 patch rows x 14 patches (98 A rows, 1568 bytes) from the
+// NHWC images (5-D map [img][pr][ir][pc][48 bytes], see make_tmap_patch), no multicast.
+__device__ __forceinline__ void tma_load_patch(uint32_t dst, const CUtensorMap *map, int w0, int ir, int pr0, int img,
+                                               uint64_t *mbar) {
+    asm volatile(
+        "cp.async.bulk.tensor.5d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5, "
+        "%6}], [%7];\n" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(w0), "r"(0), "r"(ir), "r"(pr0), "r"(img), "r"(tc05::smem_u32(mbar))
+        : "memory");
+}
+
 __device__ __forceinline__ void cp_arrive_noinc(uint64_t *mbar) {
     asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];\n" ::"r"(tc05::smem_u32(mbar)) : "memory");
 }
@@ -174,7 +185,10 @@ __global__ void __launch_bounds__(PT_THREADS, 1) tcp_gemm_kernel(GemmArgs g, int
     griddep_wait();
     griddep_launch();
     const int m_lim = g.m_dev ? *g.m_dev : g.m_host;
-    const int mtiles = (m_lim + 127) / 128;
+    // Patch GEMM with TMA: tile mt holds image mt / 2's patch rows 7 * (mt & 1) ..
+    // + 6, i.e. 98 A rows (TMEM lanes 98..127 hold unused rows).
+    const bool ptma = EPI == EPI_PATCH && use_tma;
+    const int mtiles = ptma ? 2 * (m_lim / 196) : (m_lim + 127) / 128;
     tc05::fence_proxy_async();
     tc05::fence_before();
     __syncthreads();
@@ -196,10 +210,18 @@ __global__ void __launch_bounds__(PT_THREADS, 1) tcp_gemm_kernel(GemmArgs g, int
                         break;
                     }
                     const uint32_t dst = tc05::smem_u32(sA + s * L::A_STAGE);
-                    mbar_expect_tx(&full[s], 128u * L::AK);
+                    mbar_expect_tx(&full[s], (ptma ? 98u : 128u) * L::AK);
 #pragma unroll
-                    for (int kc = 0; kc < L::AK / 16; ++kc)
-                        tma_load_a(dst + kc * 2048, &tmA, ks * L::AK + kc * 16, mt * 128, &full[s]);
+                    for (int kc = 0; kc < L::AK / 16; ++kc) {
+                        if (ptma) {
+                            // K byte k = ir * 48 + w (layout.py:31-72): strip kg = k / 16
+                            const int kg = ks * (L::AK / 16) + kc, ir = kg / 3;
+                            tma_load_patch(dst + kc * 2048, &tmA, (kg - 3 * ir) * 16, ir, 7 * (mt & 1), mt >> 1,
+                                           &full[s]);
+                        } else {
+                            tma_load_a(dst + kc * 2048, &tmA, ks * L::AK + kc * 16, mt * 128, &full[s]);
+                        }
+                    }
                 }
             }
             if (!ok) *abortf = 1;
@@ -291,12 +313,12 @@ __global__ void __launch_bounds__(PT_THREADS, 1) tcp_gemm_kernel(GemmArgs g, int
         uint32_t a = 0;
         for (int mt = blockIdx.x; mt < mtiles; mt += gridDim.x) {
             const int grow = mt * 128 + row;
-            const bool valid = grow < m_lim;
+            const bool valid = ptma ? row < 98 : grow < m_lim;
             size_t orow = (size_t)grow;
             int pidx = 0;
             if (EPI == EPI_PATCH) {
-                const int img = valid ? grow / 196 : 0;
-                pidx = valid ? grow - img * 196 : 0;
+                const int img = ptma ? mt >> 1 : (valid ? grow / 196 : 0);
+                pidx = !valid ? 0 : (ptma ? 98 * (mt & 1) + row : grow - img * 196);
                 orow = (size_t)img * 197 + 1 + pidx;
             }
             bool stop = false;
@@ -434,7 +456,8 @@ cudaError_t launch_p(const GemmArgs &g, int m_max, int *err, int sms, cudaStream
     static_assert(smem <= 227 * 1024, "persistent GEMM shared memory");
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
-    const int tiles = (m_max + 127) / 128;
+    // (the patch GEMM with TMA runs two 98-row tiles per image)
+    const int tiles = EPI == EPI_PATCH && g.tma ? 2 * (m_max / 196) : (m_max + 127) / 128;
     const int grid = tiles < sms ? tiles : sms;
     if (grid <= 0) return cudaSuccess;
     CUtensorMap tm;
@@ -489,16 +512,45 @@ cudaError_t launch_gemm_persistent(const GemmArgs &g, int epi, int m_max, int *e
     }
 }
 
-int make_tmap_a(CUtensorMap *map, const void *base, int k, int rows) {
+namespace {
+
+PFN_cuTensorMapEncodeTiled tmap_encoder() {
     static PFN_cuTensorMapEncodeTiled encode = nullptr;
     if (!encode) {
         void *fn = nullptr;
         cudaDriverEntryPointQueryResult q;
         if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) != cudaSuccess ||
             q != cudaDriverEntryPointSuccess || !fn)
-            return 1;
+            return nullptr;
         encode = (PFN_cuTensorMapEncodeTiled)fn;
     }
+    return encode;
+}
+
+}  // namespace
+
+// NHWC images [images][224][224][3] viewed as [img][pr][ir][pc][w]: patch row pr and
+// column pc (14 each), pixel row ir inside the patch (16), byte w = in_col * 3 + ch
+// of the patch's 48-byte row segment (layout.py:31-72).  Box: one 16-byte strip of
+// w, all 14 patch columns, one ir, 7 patch rows, one image = 98 A rows of 16 bytes
+// in tile-row order (row = 14 * pr + pc), the K-major strip layout of tma_load_a.
+int make_tmap_patch(CUtensorMap *map, const void *images, int images_n) {
+    PFN_cuTensorMapEncodeTiled encode = tmap_encoder();
+    if (!encode) return 1;
+    if ((uintptr_t)images % 16 != 0 || images_n <= 0) return 3;
+    const cuuint64_t dims[5] = {48, 14, 16, 14, (cuuint64_t)images_n};
+    const cuuint64_t strides[4] = {48, 672, 10752, 150528};
+    const cuuint32_t box[5] = {16, 14, 1, 7, 1};
+    const cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+    const CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 5, const_cast<void *>(images), dims, strides, box,
+                              estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                              CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? 0 : 2;
+}
+
+int make_tmap_a(CUtensorMap *map, const void *base, int k, int rows) {
+    PFN_cuTensorMapEncodeTiled encode = tmap_encoder();
+    if (!encode) return 1;
     const cuuint64_t dims[2] = {(cuuint64_t)k, (cuuint64_t)rows};
     const cuuint64_t strides[1] = {(cuuint64_t)k};
     const cuuint32_t box[2] = {16, 128};

@@ -514,6 +514,9 @@ int run_patch(hv_model *m, const int8_t *images, int count, int8_t *out, cudaStr
     g.epi.bits_wide = m->patch_wide;
     g.epi.pos = m->w<int8_t>(m->pos);
     g.epi.add = m->patch_add;
+    // TMA gather of the patches (two 98-row tiles per image) when the map can be made
+    CUtensorMap tm;
+    if (make_tmap_patch(&tm, images, count) == 0) g.tma = &tm;
     CUDA_TRY(model_gemm(m, g, EPI_PATCH, count * HV_PATCHES, st));
     return HV_OK;
 }
