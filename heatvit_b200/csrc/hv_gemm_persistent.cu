@@ -322,13 +322,16 @@ __global__ void __launch_bounds__(PT_THREADS, 1) tcp_gemm_kernel(GemmArgs g, int
                 orow = (size_t)img * 197 + 1 + pidx;
             }
             bool stop = false;
-            // Residual rows (N = 192: one chunk per tile): this thread's 96 bytes are
-            // requested before the accumulator wait, so their latency overlaps the MMA.
+            // Residual or positional rows (N = 192: one chunk per tile): this thread's
+            // 96 bytes are requested before the accumulator wait, so their latency
+            // overlaps the MMA.
+            constexpr bool PRE = (EPI == EPI_I8_RES || EPI == EPI_PATCH) && L::NCH == 1;
             uint32_t rpre[BN / 64][8];
-            if (EPI == EPI_I8_RES && L::NCH == 1) {
+            if (PRE) {
+                const int8_t *src = EPI == EPI_PATCH ? g.epi.pos + (pidx + 1) * 192 : g.epi.res + orow * g.ldo;
 #pragma unroll
                 for (int i = 0; i < BN / 64; ++i) {
-                    if (valid) ld_global_32B(g.epi.res + orow * g.ldo + half * (BN / 2) + 32 * i, rpre[i]);
+                    if (valid) ld_global_32B(src + half * (BN / 2) + 32 * i, rpre[i]);
                     else
 #pragma unroll
                         for (int j = 0; j < 8; ++j) rpre[i][j] = 0;
@@ -342,21 +345,22 @@ __global__ void __launch_bounds__(PT_THREADS, 1) tcp_gemm_kernel(GemmArgs g, int
                     break;
                 }
                 tc05::fence_after();
-                // unrolled for the residual epilogue only (its prefetched registers need
-                // compile-time indices); the others stay rolled to keep registers low
-#pragma unroll (EPI == EPI_I8_RES ? BN / 64 : 1)
+                // unrolled for the prefetching epilogues only (their prefetched registers
+                // need compile-time indices); the others stay rolled to keep registers low
+#pragma unroll (PRE ? BN / 64 : 1)
                 for (int cc = 0; cc < BN / 64; ++cc) {
                     const int col0 = half * (BN / 2) + cc * 32;  // chunk-local column of v[0]
                     const int gcol0 = c * BN + col0;
                     // residual / positional bytes first, so their latency overlaps the TMEM read
                     uint32_t aux[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-                    if (EPI == EPI_I8_RES && L::NCH == 1) {
+                    if (PRE) {
 #pragma unroll
                         for (int j = 0; j < 8; ++j) aux[j] = rpre[cc][j];
                     } else if (EPI == EPI_I8_RES && valid) {
                         ld_global_32B(g.epi.res + orow * g.ldo + gcol0, aux);
+                    } else if (EPI == EPI_PATCH) {
+                        ld_global_32B(g.epi.pos + (pidx + 1) * 192 + gcol0, aux);
                     }
-                    if (EPI == EPI_PATCH) ld_global_32B(g.epi.pos + (pidx + 1) * 192 + gcol0, aux);
                     uint32_t v[32];
                     tc05::ld32(lane_addr + tb * 256 + col0, v);
                     int32_t bv[32];
