@@ -1259,12 +1259,15 @@ int hv_infer_host_submit(hv_model *m, const int8_t *h_images, int batch, int32_t
     // 1.10 ms, 512 images 2.53 ms, 1024 images 4.19 ms), so a smaller first chunk
     // adds more fixed cost than the 2.7 us per image of upload it hides (1024
     // images: first chunk 512 -> 6.16 ms, 256 -> 6.75 ms, 128 -> 6.93 ms).
+    // A call submitted behind another has its upload hidden behind that call's
+    // compute already, so it runs as 1024-image chunks, all on one compute stream:
+    // inferences on two streams at once compete for the SMs and the L2 (measured
+    // pipelined at 1024 images per call: 1024-image chunks alternating between two
+    // streams 4.97 ms per call, 512-image chunks on two streams 4.40 ms).
     // HV_HOST_CHUNK_FIRST / HV_HOST_CHUNK_MAX override the sizes; later chunks
-    // grow by at most 1.5x.  Calls submitted behind another keep 512-image chunks
-    // too: two chunks on two streams fill each other's kernel tails, which beats one
-    // 1024-image chunk (measured pipelined at 1024 images per call: 229k against
-    // 201k images/s).
-    int first_chunk = 512, max_chunk = 512;
+    // grow by at most 1.5x.
+    const bool behind = m->host_pending > 0;
+    int first_chunk = behind ? 1024 : 512, max_chunk = first_chunk;
     if (const char *e = getenv("HV_HOST_CHUNK_FIRST")) first_chunk = std::max(1, atoi(e));
     if (const char *e = getenv("HV_HOST_CHUNK_MAX")) max_chunk = std::max(1, atoi(e));
     std::vector<int> starts(1, 0);
@@ -1315,8 +1318,9 @@ int hv_infer_host_submit(hv_model *m, const int8_t *h_images, int batch, int32_t
         CUDA_TRY(cudaMalloc(&m->hwarn, (size_t)chunk * 2));
         m->host_cap = chunk;
     }
-    // Chunks alternate between two workspaces and two compute streams, so one
-    // chunk's kernels fill the idle tails of the other's (also across calls).
+    // Chunks alternate between two workspaces.  The chunks of a call with nothing in
+    // flight also alternate between two compute streams, so one chunk's kernels fill
+    // the idle tails of the other's while the later uploads land.
     int rc = HV_OK;
     for (int i = 0; i < 2; ++i)
         if (use_ws[i] && (rc = ensure_capacity(m, chunk, i)) != 0) return rc;
@@ -1360,8 +1364,8 @@ int hv_infer_host_submit(hv_model *m, const int8_t *h_images, int batch, int32_t
     }
     const int nchunks = (int)starts.size() - 1;
     for (int c = 0; c < nchunks; ++c) {
-        // chunk g: device images g % 4, workspace, compute stream and outputs g % 2,
-        // pinned staging g % 2
+        // chunk g: device images g % 4, workspace and outputs g % 2, compute stream
+        // g % 2 (stream 0 for a call behind another), pinned staging g % 2
         const unsigned long long g = m->host_chunks++;
         const int buf = (int)(g & 1), ib = (int)(g & 3);
         const int first = starts[c], cnt = starts[c + 1] - starts[c];
@@ -1380,7 +1384,7 @@ int hv_infer_host_submit(hv_model *m, const int8_t *h_images, int batch, int32_t
                                  m->copy_stream));
         CUDA_TRY(cudaEventRecord(m->ev_in[ib], m->copy_stream));
         if (!pinned_in) CUDA_TRY(cudaEventRecord(m->ev_pin[buf], m->copy_stream));
-        cudaStream_t cst = m->compute_stream[buf];
+        cudaStream_t cst = m->compute_stream[behind ? 0 : buf];
         use_workspace(m, buf);
         CUDA_TRY(cudaStreamWaitEvent(cst, m->ev_in[ib], 0));
         int32_t *dl = m->hlogits + (size_t)buf * m->host_cap * HV_CLASSES;
