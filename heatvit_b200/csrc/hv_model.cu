@@ -1297,7 +1297,7 @@ int hv_infer_host_submit(hv_model *m, const int8_t *h_images, int batch, int32_t
     // Workspaces this call uses (chunk g takes g & 1).  Growing a device buffer
     // frees the old one, which calls in flight may still use: finish them first.
     bool use_ws[2] = {false, false};
-    for (size_t c = 0; c + 1 < starts.size(); ++c) use_ws[(m->host_chunks + c) & 1] = true;
+    for (size_t c = 0; c + 1 < starts.size(); ++c) use_ws[behind ? 0 : (m->host_chunks + c) & 1] = true;
     if ((chunk > m->host_cap || (use_ws[0] && chunk > m->ws[0].cap) || (use_ws[1] && chunk > m->ws[1].cap)) &&
         m->host_pending) {
         const int rc = host_quiesce(m);
@@ -1364,10 +1364,12 @@ int hv_infer_host_submit(hv_model *m, const int8_t *h_images, int batch, int32_t
     }
     const int nchunks = (int)starts.size() - 1;
     for (int c = 0; c < nchunks; ++c) {
-        // chunk g: device images g % 4, workspace and outputs g % 2, compute stream
-        // g % 2 (stream 0 for a call behind another), pinned staging g % 2
+        // chunk g: device images g % 4, pinned staging g % 2; workspace, device outputs
+        // and compute stream g % 2, or all 0 for a call behind another (stream order
+        // then follows every earlier user of workspace 0 and its outputs, and the
+        // earlier call's chunks on workspace 1 / stream 1 are left alone)
         const unsigned long long g = m->host_chunks++;
-        const int buf = (int)(g & 1), ib = (int)(g & 3);
+        const int buf = (int)(g & 1), ib = (int)(g & 3), wsb = behind ? 0 : buf;
         const int first = starts[c], cnt = starts[c + 1] - starts[c];
         const int8_t *src = h_images + (size_t)first * HV_IMAGE_BYTES;
         if (!pinned_in) {
@@ -1384,19 +1386,19 @@ int hv_infer_host_submit(hv_model *m, const int8_t *h_images, int batch, int32_t
                                  m->copy_stream));
         CUDA_TRY(cudaEventRecord(m->ev_in[ib], m->copy_stream));
         if (!pinned_in) CUDA_TRY(cudaEventRecord(m->ev_pin[buf], m->copy_stream));
-        cudaStream_t cst = m->compute_stream[behind ? 0 : buf];
-        use_workspace(m, buf);
+        cudaStream_t cst = m->compute_stream[wsb];
+        use_workspace(m, wsb);
         CUDA_TRY(cudaStreamWaitEvent(cst, m->ev_in[ib], 0));
-        int32_t *dl = m->hlogits + (size_t)buf * m->host_cap * HV_CLASSES;
-        int32_t *dtc = m->htc + (size_t)buf * m->host_cap * (HV_MAX_SELECTORS + 1);
-        hv_selector_summary *dsum = m->hsum + (size_t)buf * m->host_cap * HV_MAX_SELECTORS;
-        uint8_t *dw = m->hwarn + (size_t)buf * m->host_cap;
+        int32_t *dl = m->hlogits + (size_t)wsb * m->host_cap * HV_CLASSES;
+        int32_t *dtc = m->htc + (size_t)wsb * m->host_cap * (HV_MAX_SELECTORS + 1);
+        hv_selector_summary *dsum = m->hsum + (size_t)wsb * m->host_cap * HV_MAX_SELECTORS;
+        uint8_t *dw = m->hwarn + (size_t)wsb * m->host_cap;
         if (m->use_graphs && !m->prof_stage)
             rc = run_graph(m, m->himg[ib], cnt, dl, h_token_counts ? dtc : nullptr, h_summary ? dsum : nullptr,
-                           h_warnings ? dw : nullptr, buf, cst);
+                           h_warnings ? dw : nullptr, wsb, cst);
         else
             rc = infer_impl(m, m->himg[ib], cnt, dl, h_token_counts ? dtc : nullptr, h_summary ? dsum : nullptr,
-                            h_warnings ? dw : nullptr, nullptr, nullptr, cst, buf);
+                            h_warnings ? dw : nullptr, nullptr, nullptr, cst, wsb);
         if (rc) {
             use_workspace(m, 0);
             return rc;

@@ -198,7 +198,9 @@ HV_API int hv_infer_host(hv_model *model, const int8_t *h_images, int batch,
  * the oldest submitted call has finished and its outputs are in the caller's
  * arrays, which (and h_images) must stay untouched until then.  Two calls may be
  * in flight (a third submit first waits for the oldest); the next call's uploads
- * run during this call's compute.  While calls are in flight the model's other
+ * run during this call's compute, so a call submitted behind another runs as
+ * whole 1024-image chunks on one compute stream instead of the two-stream chunks
+ * of hv_infer_host.  While calls are in flight the model's other
  * entry points return HV_ERR_STATE.  No counterpart in the reference (its model
  * runs one image per call). */
 HV_API int hv_infer_host_submit(hv_model *model, const int8_t *h_images, int batch,

@@ -178,7 +178,11 @@ def test_host_submit_wait_pipeline(cuda):
     params = synth.config3_params(synth.SEED)
     eng = Engine(params)
     ns = eng.num_selectors
-    sizes = [700, 300, 1024, 5, 513]                           # 512+188, 300, 512+512, 5, 513 images
+    # the first call (nothing in flight) runs 512 + 188 images on two streams; the
+    # calls behind it run as 1024-image chunks on one stream: 1024 + 476, 300, 1024,
+    # 5 and 513 images (the 1500-image call reuses a workspace that the first call's
+    # second chunk may still be using on the other stream)
+    sizes = [700, 1500, 300, 1024, 5, 513]
     calls = []
     for i, n in enumerate(sizes):
         imgs = synth.baseline_images(synth.SEED, n, first=3000 + 1000 * i)
@@ -219,11 +223,11 @@ def test_host_submit_wait_pipeline(cuda):
     for c in calls:
         check(c)
     # a third submit waits for the oldest call itself
-    for c in calls[:4]:
+    for c in calls[:5]:
         submit(c)
     while eng._inflight:
         eng.infer_host_wait()
-    for c in calls[:4]:
+    for c in calls[:5]:
         check(c)
     eng.infer(torch.zeros((1, 150528), dtype=torch.int8, device="cuda"))  # idle again
     with pytest.raises(RuntimeError, match="no host call"):
