@@ -5,20 +5,24 @@
 // (N x K int8, at most 147 KB) stays resident in shared memory for the CTA's
 // lifetime, so A (read once) and the output (written once) are the only DRAM
 // traffic.  Roles:
-//   warp 0      producer: cp.async of A into a ring of S stages in the
-//               no-swizzle K-major canonical layout; each of its 32 threads
-//               arrives on the stage's `full` mbarrier when its copies land
-//               (cp.async.mbarrier.arrive.noinc).
-//   warp 1      MMA issuer (one thread): tcgen05.mma kind::i8 into one of two
+//   warps 0-3   producer.  With a tensor map, one thread issues TMA copies of A
+//               into a ring of S stages, completing on the stage's `full`
+//               mbarrier (expect_tx): one 2-D box of 16 bytes x 128 rows per K
+//               strip for row-major A, or one 5-D box of 14 x 7 patches per K
+//               strip for the patch GEMM (two 98-row tiles per image).  Without
+//               one, the 128 threads gather A with cp.async in the no-swizzle
+//               K-major canonical layout and arrive with
+//               cp.async.mbarrier.arrive.noinc.
+//   warp 4      MMA issuer (one thread): tcgen05.mma kind::i8 into one of two
 //               TMEM accumulators (192 columns each, 256 apart); commits free
 //               the A stage (`empty`) and hand the accumulator to the epilogue
 //               (`acc_full`).
-//   warps 2-9   epilogue: thread = (TMEM lane, column half); reads its
+//   warps 5-12  epilogue: thread = (TMEM lane, column half); reads its
 //               accumulator row with tcgen05.ld, applies the fused golden
 //               writeback, stores 32 contiguous bytes per step, then releases
 //               the accumulator (`acc_empty`).
 // For K = 192 one stage holds the whole A tile and feeds every 192-column
-// chunk of N; for K = 768 (N = 192) A streams through 4 stages of 64 columns.
+// chunk of N; for K = 768 (N = 192) A streams through 8 stages of 64 columns.
 // Every mbarrier wait is bounded; a timeout sets the model's error word.
 #include <cudaTypedefs.h>
 #include <string.h>
