@@ -45,7 +45,7 @@ STAGE_BYTES_PER_ROW = {"ln1": 384, "ln2": 384}
 # Traffic grows with the rows of a launch.
 STAGE_TRAFFIC_PER_ROW = {"fc1": (38_966_016 + 100_830_720) / 201_728,
                          "fc2": (193_862_912 + 24_387_584) / 201_728,
-                         "ln1": (38_798_848 + 1_535_744) / 201_728}
+                         "ln1": (38_799_616 + 1_387_776) / 201_728}
 
 
 def algorithmic_macs(counts):
