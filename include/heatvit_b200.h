@@ -273,15 +273,17 @@ HV_API int hv_gemm_i8_acc(const void *d_a, const int8_t *d_b, const int32_t *d_b
  * The padded operands and the device error word live in one fixed per-device
  * array of HV_NOALLOC_SCRATCH_BYTES inside the library.  The call needs
  *   256 + roundup256(m * kp) + np * kp  bytes of it,
- * with kp = max(64, roundup64(k)) and np = n rounded up to 64 (n % 64 == 0)
- * or to 256 (otherwise); larger problems are rejected with HV_ERR_VALUE and a
- * message naming the limit, before any work is enqueued.
+ * with kp = max(64, roundup64(k)) and np = roundup64(n) (the GEMM's 64-column
+ * tiles); larger problems are rejected with HV_ERR_VALUE and a message naming
+ * the limit, before any work is enqueued.
  *
  * The first call on each device resolves the array's device address
  * (cudaGetSymbolAddress, with that device current); make that first call
  * before any stream capture starts on the device.  Each call clears the error
- * word on `stream` before use, rewrites every padded byte it reads, and waits
- * for `stream` before returning so it can report a bounded-wait timeout.
+ * word on `stream` before use and rewrites every padded byte it reads.  Before
+ * it returns, every call copies the error word to a host variable and
+ * synchronises `stream` (cudaStreamSynchronize), as hv_gemm_i8_acc does, so
+ * that it can report a bounded-wait timeout.
  * The array is shared by all callers on a device: calls that overlap in time
  * (two host threads, or work on another stream still reading the array) race
  * and may return wrong results.  Serialise them. */
