@@ -48,6 +48,7 @@ _SIGNATURES = {
     "hv_device_error": (I, [P, C.POINTER(C.c_int)]),
     "hv_profile_stop": (I, [P, C.POINTER(C.c_int), C.POINTER(C.c_double), C.POINTER(C.c_longlong)]),
     "hv_graph_kernels": (I, [P, C.POINTER(C.c_int)]),
+    "hv_test_gemm_stall": (I, [P, C.c_uint, I]),
     "hv_selector_h2": (I, [P, I, P, P, I, P, P]),
     "hv_align_add_i8": (I, [P, I, P, I, I, I64, P, P]),
 }

@@ -81,6 +81,12 @@ struct GemmArgs {
     void *out;                // int8 / int32 / int64 [M][ldo]
     int ldo;
     EpiParams epi;
+    // Test hooks of the persistent kernel (zero-initialised = off): the pipeline's
+    // bounded waits give up after wait_iters polls (0 = the default limit), and with
+    // skip_tile > 0 the A tile of index skip_tile - 1 is never loaded, so the waits
+    // on it run out and the launch takes its abort path (error word 3).
+    uint32_t wait_iters;
+    int skip_tile;
 };
 
 // Launch helpers (defined in hv_gemm.cu).  `bt` must hold

@@ -199,6 +199,7 @@ __global__ void __launch_bounds__(PT_THREADS, 1) tcp_gemm_kernel(GemmArgs g, int
     tc05::fence_after();
     const uint32_t tbase = *tslot;
     const uint8_t *abase = (const uint8_t *)g.a.ptr;
+    const uint32_t wl = g.wait_iters ? g.wait_iters : PT_WAIT;  // pipeline waits; drains use PT_WAIT
 
     if (warp < PT_PROD && use_tma) {
         // ---- producer (TMA): one thread; stage = AK/16 boxes of [128 rows][16 bytes],
@@ -206,13 +207,19 @@ __global__ void __launch_bounds__(PT_THREADS, 1) tcp_gemm_kernel(GemmArgs g, int
         if (tid == 0) {
             uint32_t q = 0;
             bool ok = true;
+            // last ring slot whose copies were issued into each stage (-1: none)
+            int last_q[L::S];
+#pragma unroll
+            for (int s = 0; s < L::S; ++s) last_q[s] = -1;
             for (int mt = blockIdx.x; mt < mtiles && ok && !*abortf; mt += gridDim.x) {
                 for (int ks = 0; ks < L::KST; ++ks, ++q) {
                     const int s = q % L::S;
-                    if (q >= (uint32_t)L::S && !tc05::mbar_wait(&empty[s], ((q / L::S) - 1) & 1u, PT_WAIT)) {
+                    if (q >= (uint32_t)L::S && !tc05::mbar_wait(&empty[s], ((q / L::S) - 1) & 1u, wl)) {
                         ok = false;
                         break;
                     }
+                    if (mt == g.skip_tile - 1) continue;  // test hook: this tile never arrives
+                    last_q[s] = (int)q;
                     const uint32_t dst = tc05::smem_u32(sA + s * L::A_STAGE);
                     mbar_expect_tx(&full[s], (ptma ? 98u : 128u) * L::AK);
 #pragma unroll
@@ -229,6 +236,14 @@ __global__ void __launch_bounds__(PT_THREADS, 1) tcp_gemm_kernel(GemmArgs g, int
                 }
             }
             if (!ok) *abortf = 1;
+            // After an abort the consumer may have stopped before some stages: wait
+            // (bounded) until every box issued into them has landed, so no bulk copy
+            // still writes this CTA's shared memory when it exits.
+            if (*abortf) {
+#pragma unroll
+                for (int s = 0; s < L::S; ++s)
+                    if (last_q[s] >= 0) tc05::mbar_wait(&full[s], ((uint32_t)last_q[s] / L::S) & 1u, PT_WAIT);
+            }
         }
     } else if (warp < PT_PROD) {
         // ---- producer ------------------------------------------------------------
@@ -237,10 +252,11 @@ __global__ void __launch_bounds__(PT_THREADS, 1) tcp_gemm_kernel(GemmArgs g, int
             const int m0 = mt * 128;
             for (int ks = 0; ks < L::KST; ++ks, ++q) {
                 const int s = q % L::S;
-                if (q >= (uint32_t)L::S && !tc05::mbar_wait(&empty[s], ((q / L::S) - 1) & 1u, PT_WAIT)) {
+                if (q >= (uint32_t)L::S && !tc05::mbar_wait(&empty[s], ((q / L::S) - 1) & 1u, wl)) {
                     *abortf = 1;
                     break;
                 }
+                if (mt == g.skip_tile - 1) continue;  // test hook: this tile never arrives
                 uint8_t *dst = sA + s * L::A_STAGE;
                 constexpr int AKC = L::AK / 16;
                 for (int c = tid; c < 128 * AKC; c += 32 * PT_PROD) {
@@ -276,14 +292,14 @@ __global__ void __launch_bounds__(PT_THREADS, 1) tcp_gemm_kernel(GemmArgs g, int
             for (int mt = blockIdx.x; mt < mtiles && ok && !*abortf; mt += gridDim.x) {
                 for (int c = 0; c < L::NCH && ok; ++c, ++a) {
                     const int tb = a & 1;
-                    if (a >= 2 && !tc05::mbar_wait(&acce[tb], ((a >> 1) - 1) & 1u, PT_WAIT)) { ok = false; break; }
+                    if (a >= 2 && !tc05::mbar_wait(&acce[tb], ((a >> 1) - 1) & 1u, wl)) { ok = false; break; }
                     tc05::fence_after();
                     const uint32_t d = tbase + tb * 256;
                     for (int ks = 0; ks < L::KST; ++ks) {
                         const uint32_t qq = q + ks;
                         const int s = qq % L::S;
                         if (c == 0 || L::KST > 1) {
-                            if (!tc05::mbar_wait(&full[s], (qq / L::S) & 1u, PT_WAIT)) { ok = false; break; }
+                            if (!tc05::mbar_wait(&full[s], (qq / L::S) & 1u, wl)) { ok = false; break; }
                             tc05::fence_proxy_async();
                             tc05::fence_after();
                         }
@@ -343,7 +359,7 @@ __global__ void __launch_bounds__(PT_THREADS, 1) tcp_gemm_kernel(GemmArgs g, int
             }
             for (int c = 0; c < L::NCH; ++c, ++a) {
                 const int tb = a & 1;
-                if (!tc05::mbar_wait(&accf[tb], (a >> 1) & 1u, PT_WAIT)) {
+                if (!tc05::mbar_wait(&accf[tb], (a >> 1) & 1u, wl)) {
                     *abortf = 1;
                     stop = true;
                     break;
@@ -475,10 +491,12 @@ cudaError_t launch_p(const GemmArgs &g, int m_max, int *err, int sms, cudaStream
 }
 
 // The (epilogue, K, N) combinations the model uses: QKV (I8, 192 -> 576), proj and
-// FC2 (I8_RES, 192 -> 192 and 768 -> 192), FC1 (GELU, 192 -> 768), patch (768 -> 192).
+// FC2 (I8_RES, 192 -> 192 and 768 -> 192), FC1 (GELU, 192 -> 768), patch (768 -> 192);
+// plus the plain int8 writeback for every layer shape (unit API, hv_gemm_i8).
 constexpr bool shape_used(int epi, int k, int n) {
-    return (epi == EPI_I8 && k == 192 && n == 576) || (epi == EPI_I8_RES && n == 192 && (k == 192 || k == 768)) ||
-           (epi == EPI_GELU && k == 192 && n == 768) || (epi == EPI_PATCH && k == 768 && n == 192);
+    return (epi == EPI_I8 && ((k == 192 && (n == 192 || n == 576 || n == 768)) || (k == 768 && n == 192))) ||
+           (epi == EPI_I8_RES && n == 192 && (k == 192 || k == 768)) || (epi == EPI_GELU && k == 192 && n == 768) ||
+           (epi == EPI_PATCH && k == 768 && n == 192);
 }
 
 template <int EPI, bool FAST, int KDIM, int N>

@@ -145,6 +145,7 @@ struct GraphEntry {
     int prof_stage = 0;  // stage whose launches the graph brackets with profiling events
     int prof_n = 0;      // profiling event pairs recorded by one replay
     int kernels = 0;     // kernel nodes in the graph
+    int prof_max = 0;    // launch limit of the profiling bracket it was captured with
 };
 
 struct hv_model {
@@ -212,6 +213,9 @@ struct hv_model {
     // kernel timing (hv_profile_*)
     int prof_stage = 0, prof_max = 0, prof_n = 0;
     int last_graph_kernels = 0;  // kernel nodes of the last replayed graph
+    // test hook of the layer GEMMs (hv_test_gemm_stall): wait limit and skipped tile
+    uint32_t test_wait_iters = 0;
+    int test_skip_tile = 0;
     std::vector<cudaEvent_t> prof_ev;
     int32_t *prof_rows = nullptr;  // device [prof_max] live row counts
 
@@ -386,6 +390,8 @@ cudaError_t model_gemm(const hv_model *m, GemmArgs &g, int epi, int m_max, cudaS
                       (uintptr_t)g.epi.pos % 32 == 0;
     if (m->persistent && gemm_persistent_supported(epi, g.n, g.k) && al32) {
         if (epi == EPI_GELU) g.epi.fast = g.epi.gelu_k2 || g.epi.gtab_n > 0;  // the persistent kernel's fast forms
+        g.wait_iters = m->test_wait_iters;
+        g.skip_tile = m->test_skip_tile;
         return launch_gemm_persistent(g, epi, m_max, m->err, m->sms, st);
     }
     return launch_gemm(g, epi, 0, m_max, m->err, st);
@@ -1042,7 +1048,7 @@ int run_graph(hv_model *m, const int8_t *img, int batch, int32_t *lg, int32_t *t
     GraphEntry *hit = nullptr, *victim = &m->graphs[0];
     for (GraphEntry &g : m->graphs) {
         if (g.exec && g.img == img && g.batch == batch && g.ws == wsi && g.lg == lg && g.tc == tc && g.sum == sum &&
-            g.warn == warn && g.prof_stage == m->prof_stage)
+            g.warn == warn && g.prof_stage == m->prof_stage && (!m->prof_stage || g.prof_max == m->prof_max))
             hit = &g;
         if (!g.exec || g.stamp < victim->stamp) victim = &g;
     }
@@ -1076,7 +1082,7 @@ int run_graph(hv_model *m, const int8_t *img, int batch, int32_t *lg, int32_t *t
         cudaGraphDestroy(graph);
         if (ie != cudaSuccess) return fail(HV_ERR_CUDA, "graph instantiate: %s", cudaGetErrorString(ie));
         if (victim->exec) cudaGraphExecDestroy(victim->exec);
-        *victim = GraphEntry{exec, img, batch, wsi, lg, tc, sum, warn, 0, m->prof_stage, m->prof_n, kernels};
+        *victim = GraphEntry{exec, img, batch, wsi, lg, tc, sum, warn, 0, m->prof_stage, m->prof_n, kernels, m->prof_max};
         hit = victim;
     }
     hit->stamp = ++m->graph_clock;
@@ -1511,6 +1517,24 @@ int hv_profile_stop(hv_model *m, int *launches, double *total_ms, long long *row
     return HV_OK;
 }
 
+int hv_test_gemm_stall(hv_model *m, unsigned wait_iters, int skip_tile) {
+    if (!m) return fail(HV_ERR_VALUE, "null model");
+    HOST_IDLE(m);
+    if (skip_tile < -1) return fail(HV_ERR_VALUE, "skip_tile must be -1 (off) or a tile index");
+    CUDA_TRY(cudaSetDevice(m->device));
+    // Captured graphs hold the launch arguments: drop them so the next calls capture
+    // (or launch) with the new settings.
+    CUDA_TRY(cudaDeviceSynchronize());
+    for (GraphEntry &g : m->graphs)
+        if (g.exec) {
+            cudaGraphExecDestroy(g.exec);
+            g = GraphEntry();
+        }
+    m->test_wait_iters = wait_iters;
+    m->test_skip_tile = skip_tile + 1;  // GemmArgs: 0 = off, t + 1 = tile t
+    return HV_OK;
+}
+
 int hv_graph_kernels(hv_model *m, int *kernels) {
     if (!m || !kernels) return fail(HV_ERR_VALUE, "null argument");
     *kernels = m->last_graph_kernels;
@@ -1583,16 +1607,88 @@ int hv_gemm_i8_acc(const void *d_a, const int8_t *d_b, const int32_t *d_bias, in
 int hv_gemm_i8(const void *d_a, const int8_t *d_b, const int32_t *d_bias, int m, int n, int k, int transpose_b,
                int a_unsigned, int src_exp, int dst_exp, int out_bits, void *d_out, void *stream) {
     if (out_bits != 8 && out_bits != 32) return fail(HV_ERR_VALUE, "output_bits must be 8 or 32");
+    if (m < 0 || n < 0 || k < 0) return fail(HV_ERR_VALUE, "negative dimension");
     if (m == 0 || n == 0) return HV_OK;
-    int64_t *acc = nullptr;
-    CUDA_TRY(cudaMalloc(&acc, (size_t)m * n * 8));
-    int rc = hv_gemm_i8_acc(d_a, d_b, d_bias, m, n, k, transpose_b, a_unsigned, acc, stream);
-    if (!rc) {
-        cudaError_t e = launch_writeback(acc, (int64_t)m * n, dst_exp - src_exp, out_bits, d_out, (cudaStream_t)stream);
-        if (e != cudaSuccess) rc = fail(HV_ERR_CUDA, "writeback: %s", cudaGetErrorString(e));
-        cudaStreamSynchronize((cudaStream_t)stream);
+    if (!d_a || !d_b || !d_out) return fail(HV_ERR_VALUE, "null buffer");
+    if (k > (a_unsigned ? 65793 : 131071))
+        return fail(HV_ERR_VALUE, "k=%d can overflow the int32 accumulator; not supported", k);
+    cudaStream_t st = (cudaStream_t)stream;
+    if (k == 0 || (a_unsigned && out_bits == 8)) {
+        // the raw accumulator, then the element-wise writeback
+        int64_t *acc = nullptr;
+        CUDA_TRY(cudaMalloc(&acc, (size_t)m * n * 8));
+        int rc = HV_OK;
+        if (k == 0) {
+            cudaMemsetAsync(acc, 0, (size_t)m * n * 8, st);
+            if (d_bias) rc = fail(HV_ERR_VALUE, "k = 0 with a bias: use hv_gemm_i8_acc");
+        } else {
+            rc = hv_gemm_i8_acc(d_a, d_b, d_bias, m, n, k, transpose_b, a_unsigned, acc, stream);
+        }
+        if (!rc) {
+            cudaError_t e = launch_writeback(acc, (int64_t)m * n, dst_exp - src_exp, out_bits, d_out, st);
+            if (e != cudaSuccess) rc = fail(HV_ERR_CUDA, "writeback: %s", cudaGetErrorString(e));
+            cudaStreamSynchronize(st);
+        }
+        cudaFree(acc);
+        return rc;
     }
-    cudaFree(acc);
+    // Fused writeback in the GEMM epilogue (gemm.py:123-139): EPI_I8 requantises
+    // acc + bias to int8, EPI_I32 to int32.  The 32-bit epilogue form needs the
+    // host-side bias bound (|acc| <= k * 2^14 plus |bias| below 2^30).
+    std::vector<int32_t> hb(n, 0);
+    if (d_bias) CUDA_TRY(cudaMemcpy(hb.data(), d_bias, sizeof(int32_t) * (size_t)n, cudaMemcpyDeviceToHost));
+    int dev = 0, sms = 148;
+    CUDA_TRY(cudaGetDevice(&dev));
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int epi = out_bits == 8 ? EPI_I8 : EPI_I32;
+    // The model's layer shapes (signed A, K in {192, 768}) run on the persistent
+    // kernel: weights resident in shared memory, A by TMA, 32-byte output stores.
+    const bool persistent = epi == EPI_I8 && gemm_persistent_supported(EPI_I8, n, k) &&
+                            (uintptr_t)d_a % 16 == 0 && (uintptr_t)d_out % 32 == 0;
+    const int tn = gemm_tile_n(n);
+    const int kp = persistent ? k : std::max(64, (k + 63) / 64 * 64);
+    const int np = persistent ? n : (n + tn - 1) / tn * tn;
+    const bool pad_a = !persistent && (kp != k || (uintptr_t)d_a % 16 != 0);
+    uint8_t *ap = nullptr;
+    int8_t *bp = nullptr;
+    int *err = nullptr;
+    if ((pad_a && cudaMalloc(&ap, (size_t)m * kp + 16) != cudaSuccess) ||
+        cudaMalloc(&bp, (size_t)np * kp) != cudaSuccess || cudaMalloc(&err, 16) != cudaSuccess) {
+        cudaFree(ap);
+        cudaFree(bp);
+        cudaFree(err);
+        return fail(HV_ERR_NOMEM, "cannot allocate padded operands");
+    }
+    int rc = HV_OK;
+    cudaMemsetAsync(err, 0, 16, st);
+    if (pad_a) pad_a_kernel<<<148 * 4, 256, 0, st>>>((const uint8_t *)d_a, m, k, kp, ap);
+    pad_b_kernel<<<148 * 4, 256, 0, st>>>(d_b, n, k, transpose_b, np, kp, bp);
+    GemmArgs g = gemm_args(pad_a ? (const void *)ap : d_a, kp, 0, bp, n, kp, m, nullptr, d_out, n);
+    g.epi.bias = d_bias;
+    g.epi.shift = dst_exp - src_exp;
+    g.epi.bits_wide = needs_wide(hb.data(), n, k);
+    g.epi.fast = gemm_epi_fast(epi, g.epi);
+    cudaError_t e;
+    if (persistent) {
+        CUtensorMap tm;
+        if (make_tmap_a(&tm, d_a, k, m) != 0) {
+            rc = fail(HV_ERR_CUDA, "cannot encode the tensor map of A");
+            e = cudaSuccess;
+        } else {
+            g.tma = &tm;
+            e = launch_gemm_persistent(g, EPI_I8, m, err, sms, st);
+        }
+    } else {
+        e = launch_gemm(g, epi, a_unsigned, m, err, st);
+    }
+    if (!rc && e != cudaSuccess) rc = fail(HV_ERR_CUDA, "gemm launch: %s", cudaGetErrorString(e));
+    cudaStreamSynchronize(st);
+    int code = 0;
+    cudaMemcpy(&code, err, sizeof(int), cudaMemcpyDeviceToHost);
+    if (!rc && code) rc = fail(HV_ERR_STATE, "a device-side bounded wait gave up (code %d)", code);
+    cudaFree(ap);
+    cudaFree(bp);
+    cudaFree(err);
     return rc;
 }
 

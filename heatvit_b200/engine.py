@@ -86,16 +86,46 @@ class Engine:
             raise ValueError("each image must hold 224*224*3 int8 values")
         return images.contiguous()
 
-    def infer(self, images, checkpoints=False):
+    def alloc_outputs(self, batch):
+        """Output buffers for ``infer(..., out=...)``: logits, token counts and
+        warnings are views of ONE contiguous int32 buffer (``packed``), so a
+        single collective can move all three; the summaries sit beside it."""
+        torch = _torch()
+        b, ns = batch, self.num_selectors
+        n_lg, n_tc, n_w = b * abi.CLASSES, b * (ns + 1), (b + 3) // 4
+        packed = torch.zeros(n_lg + n_tc + n_w, dtype=torch.int32, device=self.device)
+        return dict(packed=packed,
+                    logits=packed[:n_lg].view(b, abi.CLASSES),
+                    token_counts=packed[n_lg:n_lg + n_tc].view(b, ns + 1),
+                    warnings=packed[n_lg + n_tc:].view(torch.uint8)[:b],
+                    summary=torch.zeros((b, max(ns, 1), 6), dtype=torch.int32, device=self.device))
+
+    @staticmethod
+    def unpack_outputs(packed, batch, num_selectors):
+        """Split one rank's ``packed`` buffer of ``alloc_outputs``, as a host
+        numpy int32 array, into logits [batch, 1000], token counts [batch, S+1]
+        and warnings [batch] uint8."""
+        b, ns = batch, num_selectors
+        n_lg, n_tc = b * abi.CLASSES, b * (ns + 1)
+        packed = np.ascontiguousarray(packed, dtype=np.int32)
+        warn = packed[n_lg + n_tc:n_lg + n_tc + (b + 3) // 4].view(np.uint8)[:b]
+        return packed[:n_lg].reshape(b, abi.CLASSES), packed[n_lg:n_lg + n_tc].reshape(b, ns + 1), warn
+
+    def infer(self, images, checkpoints=False, out=None):
         torch = _torch()
         images = self._images(images)
         b = images.shape[0]
         ns = self.num_selectors
         dev = self.device
-        logits = torch.empty((b, abi.CLASSES), dtype=torch.int32, device=dev)
-        counts = torch.empty((b, ns + 1), dtype=torch.int32, device=dev)
-        summary = torch.zeros((b, max(ns, 1), 6), dtype=torch.int32, device=dev)
-        warnings = torch.empty(b, dtype=torch.uint8, device=dev)
+        if out is not None:
+            if out["logits"].shape[0] != b or out["token_counts"].shape[1] != ns + 1:
+                raise ValueError("output buffers were allocated for another batch or model")
+            logits, counts, summary, warnings = out["logits"], out["token_counts"], out["summary"], out["warnings"]
+        else:
+            logits = torch.empty((b, abi.CLASSES), dtype=torch.int32, device=dev)
+            counts = torch.empty((b, ns + 1), dtype=torch.int32, device=dev)
+            summary = torch.zeros((b, max(ns, 1), 6), dtype=torch.int32, device=dev)
+            warnings = torch.empty(b, dtype=torch.uint8, device=dev)
         with torch.cuda.device(dev):
             st = _stream(torch)
             if checkpoints:

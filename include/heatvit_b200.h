@@ -242,6 +242,20 @@ HV_API int hv_profile_stop(hv_model *model, int *launches, double *total_ms, lon
  * No counterpart in the reference. */
 HV_API int hv_graph_kernels(hv_model *model, int *kernels);
 
+/* Test hook for the bounded-wait error path of the layer GEMMs (QKV, proj, FC1,
+ * FC2, patch).  In later calls on this model their pipeline waits give up after
+ * `wait_iters` polls (0 = the default limit, about a second), and with
+ * skip_tile >= 0 every such launch leaves the A tile of that index unloaded, so
+ * the waits on it run out: the launch stops issuing work, waits (with the default
+ * limit) for the copies and tensor-core operations it already issued, releases
+ * its TMEM and sets the model's device error word to 3, which hv_device_error
+ * reports.  Nothing faults and the context stays usable.  skip_tile = -1 with
+ * wait_iters = 0 restores normal operation.  Drops the model's captured graphs.
+ * No counterpart in the reference (its RTL testbench injects stalls through the
+ * behavioural memory model, sim/common/behavioral_memory.sv:13, and reports a
+ * watchdog timeout as a fatal error code, rtl/include/heatvit_pkg.sv:109-118). */
+HV_API int hv_test_gemm_stall(hv_model *model, unsigned wait_iters, int skip_tile);
+
 /* ---- per-operator entry points (unit configs; device buffers) --------------------- */
 
 /* GEMM + writeback: out = requant(A·B + bias, src_exp, dst_exp, out_bits).

@@ -5,6 +5,7 @@ tests/golden/make_golden.py (golden_memimage.npz)."""
 import hashlib
 
 import numpy as np
+import pytest
 
 from conftest import load_golden
 
@@ -61,3 +62,27 @@ def test_layout_is_eight_byte_aligned_and_ordered():
         assert off % 8 == 0 and off >= end, name
         end = off + int(np.prod(shape)) * esz
     assert memimage.weight_bytes() == (end + 7) & ~7
+
+
+@pytest.mark.gpu
+def test_engine_from_reference_memory_image_matches_oracle(cuda, oracle):
+    """The engine loaded from the reference's weight memory image (.mem text,
+    tools/generate_e2e_vectors.py:87-155) and its ScaleTable JSON
+    (tools/p2/scale_table.py:82-98) runs a config-3 batch bit-exactly like the
+    oracle on the original parameters.  The image text is the reference
+    serializer's, byte for byte (its SHA-256 is the golden one)."""
+    import torch
+    from heatvit_b200 import memimage, synth
+    from heatvit_b200.engine import Engine
+    g = load_golden("golden_memimage.npz")
+    params = synth.config3_params(synth.SEED)
+    text = memimage.mem_lines(memimage.write_weights(params))
+    assert hashlib.sha256(text.encode()).hexdigest() == str(g["memimage_config3_mem_sha256"])
+    table = memimage.load_scale_table(memimage.scale_table_json(memimage.scale_table(params)))
+    loaded = memimage.read_weights(memimage.parse_mem(text), table)
+    imgs = synth.baseline_images(synth.SEED, 48)
+    got = Engine(loaded).infer(torch.from_numpy(imgs).cuda())
+    ref = oracle.infer_batch(params, imgs)
+    np.testing.assert_array_equal(got["logits"].cpu().numpy(), ref["logits"])
+    np.testing.assert_array_equal(got["token_counts"].cpu().numpy(), ref["counts"])
+    np.testing.assert_array_equal(got["warnings"].cpu().numpy(), ref["warnings"])
