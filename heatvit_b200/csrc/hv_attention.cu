@@ -1,30 +1,39 @@
 // hv_attention.cu — per-(image, head) attention on tcgen05 tensor cores and TMEM.
 //
-// Restates transformer.py:233-268 for one image and head:
+// Restates transformer.py:230-268 for one image and head:
 //   score = requant(Q·Kᵀ, 2q, score_scale, 32)            (int32 writeback)
 //   q16   = sat24(rsa(score, -(score_scale + 13)))         (Q8.16)
 //   prob  = softmax_attention(q16 row)                     (UQ0.8, nonlinear.py:98-133)
 //   ctx   = requant(prob(uint8)·V, prob_scale + q, context_out, 8)
 // written straight into the head-concatenated layout (layout.py:132-155).
 //
-// Persistent CTAs (16 warps) walk (image, head) items, query rows in tiles of 128:
-//   1. K, V and each Q tile are staged in shared memory with 16-byte copies in
-//      the no-swizzle canonical layout (hv_tc05.cuh).  K and Q are K-major
-//      operands; V is the same byte layout read as an MN-major B operand
-//      (tokens along K, head dims along N), so no transpose is needed.
-//   2. One thread issues S = Q·Kᵀ as tcgen05.mma kind::i8 (M=128, N=np, K=64)
-//      into TMEM columns [0, np); completion arrives on an mbarrier.
-//   3. Query row r of the tile is TMEM lane r.  Warps w, w+4, w+8, w+12 own
-//      lanes 32*(w%4)..+31 and split the row's 16-column chunks round-robin;
-//      each reads its chunks with tcgen05.ld, and the four parts combine the
-//      row max and the exp sum through shared memory.  Exp terms are written back to
-//      TMEM, then turned into UQ0.8 probabilities stored to shared memory as
-//      the A operand of the next MMA.  Warps whose 32 rows all lie past the
-//      image's token count skip the softmax.
-//   4. ctx = P·V as tcgen05.mma kind::i8 with unsigned A (M=128, N=64, K=np)
-//      into TMEM columns [0, 64), then requantised in 16-column pieces per part
-//      and written out.
-// TMEM: 256 columns per CTA; shared memory is padded so two CTAs share an SM.
+// Work units.  attn_plan_kernel lists the batch's work once per token layout (after
+// the batch is set up and after every selector): a unit is one 128-row tile of query
+// rows.
+//   * n > 128 tokens (list B): one unit per (head, 128-row half): 6 per image.
+//   * 64 < n <= 128 (list A): one unit per head.
+//   * 32 < n <= 64 (list A): heads {0, 1} packed in one tile (64 rows each), head 2
+//     alone.
+//   * n <= 32 (list A): the three heads packed in one tile (32 rows each).
+// A packed tile stacks the heads' Q rows, K rows and V rows in slots of R = 64 or
+// 32 rows; S = Q·Kᵀ then holds every head's scores in its diagonal R x R block,
+// and P is written block-diagonal (zero outside the row's own block), so one
+// P·V over all 128 stacked V rows gives each row its own head's context.
+//
+// Per unit (CTA of 4 warps, persistent over its units):
+//   1. K, V and Q are staged in shared memory with 16-byte cp.async copies in the
+//      no-swizzle canonical layout (hv_tc05.cuh); K and Q are K-major operands, V is
+//      the same byte layout read as an MN-major B operand (tokens along K).  The next
+//      unit's K/V load into the second buffer while this unit computes; its Q loads
+//      once this unit's P·V has consumed P (Q and P share a buffer).
+//   2. One thread issues S = Q·Kᵀ (tcgen05.mma kind::i8, M = 128) into TMEM.
+//   3. Query row r is TMEM lane r and belongs to thread r: warp w owns lanes
+//      32w..32w+31 and reads its rows in 32-column pieces.  Each thread takes its
+//      row's max, exp terms and sum by itself (no cross-warp exchange), writes the
+//      exp terms back to TMEM, then its UQ0.8 probabilities to shared memory as the
+//      A operand of the next MMA.
+//   4. ctx = P·V (unsigned A) into TMEM columns [0, 64), requantised and stored.
+// TMEM: 128 columns per CTA for list A (4 CTAs per SM), 256 for list B (2 per SM).
 #include <algorithm>
 
 #include "hv_internal.cuh"
@@ -36,31 +45,153 @@ namespace {
 
 constexpr uint32_t WAIT_ITERS = 1u << 24;
 
-// Two CTA shapes.  Images of up to 128 tokens use the small one (128 TMEM
-// columns, 8 warps, about 46 KB of shared memory: four CTAs per SM); longer
-// images use the large one (256 TMEM columns, 16 warps, 80 KB: two per SM).
-// Shared memory is padded so that TMEM is never oversubscribed.
-template <int NPM, int SPL>
+// Unit encoding: image << 7 | mtile << 6 | log2(G) << 4 | first head << 2 | heads.
+__host__ __device__ __forceinline__ uint32_t unit_code(int img, int mt, int glog, int h0, int nh) {
+    return ((uint32_t)img << 7) | ((uint32_t)mt << 6) | ((uint32_t)glog << 4) | ((uint32_t)h0 << 2) | (uint32_t)nh;
+}
+
+// Units of an image of n tokens on list A (n <= 128) and list B (n > 128).
+__device__ __forceinline__ int units_a(int n) { return n <= 0 || n > 128 ? 0 : (n <= 32 ? 1 : (n <= 64 ? 2 : 3)); }
+// (an image longer than 224 tokens has no units: the model never makes one, and the
+// kernel's buffers hold 224 rows)
+__device__ __forceinline__ int units_b(int n) { return n > 128 && n <= 224 ? 6 : 0; }
+
+// One CTA (1024 threads) lists every unit of the batch, image-major.  cnt[0], cnt[1]
+// = lengths of list A and list B.
+__global__ void __launch_bounds__(1024) attn_plan_kernel(const int32_t *__restrict__ offsets, int images,
+                                                          uint32_t *__restrict__ list_a,
+                                                          uint32_t *__restrict__ list_b, int32_t *__restrict__ cnt) {
+    griddep_wait();
+    griddep_launch();
+    __shared__ int wsum[2][32];
+    __shared__ int base[2];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    if (tid == 0) base[0] = base[1] = 0;
+    __syncthreads();
+    for (int i0 = 0; i0 < images; i0 += 1024) {
+        const int img = i0 + tid;
+        const int n = img < images ? offsets[img + 1] - offsets[img] : 0;
+        const int ca = units_a(n), cb = units_b(n);
+        int sa = ca, sb = cb;  // inclusive warp scans
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int ta = __shfl_up_sync(0xffffffffu, sa, o), tb = __shfl_up_sync(0xffffffffu, sb, o);
+            if (lane >= o) {
+                sa += ta;
+                sb += tb;
+            }
+        }
+        if (lane == 31) {
+            wsum[0][warp] = sa;
+            wsum[1][warp] = sb;
+        }
+        __syncthreads();
+        int pa = base[0], pb = base[1];
+        for (int w = 0; w < warp; ++w) {
+            pa += wsum[0][w];
+            pb += wsum[1][w];
+        }
+        pa += sa - ca;  // exclusive position of this image's first unit
+        pb += sb - cb;
+        if (ca == 1) {
+            list_a[pa] = unit_code(img, 0, 2, 0, 3);
+        } else if (ca == 2) {
+            list_a[pa] = unit_code(img, 0, 1, 0, 2);
+            list_a[pa + 1] = unit_code(img, 0, 1, 2, 1);
+        } else if (ca == 3) {
+            for (int h = 0; h < 3; ++h) list_a[pa + h] = unit_code(img, 0, 0, h, 1);
+        }
+        for (int u = 0; u < cb; ++u) list_b[pb + u] = unit_code(img, u / 3, 0, u % 3, 1);
+        __syncthreads();
+        if (tid == 0) {
+            int ta = 0, tb = 0;
+            for (int w = 0; w < 32; ++w) {
+                ta += wsum[0][w];
+                tb += wsum[1][w];
+            }
+            base[0] += ta;
+            base[1] += tb;
+        }
+        __syncthreads();
+    }
+    if (tid == 0) {
+        cnt[0] = base[0];
+        cnt[1] = base[1];
+    }
+}
+
+// Two CTA shapes: list A units need at most 128 S columns (TMEM 128, four CTAs per
+// SM), list B units at most 224 (TMEM 256, two per SM).  SPL warps share each TMEM
+// lane quadrant: a row's 32-column pieces are dealt round-robin to them, and they
+// combine the row max and sum through shared memory.  Shared memory is padded so
+// that the resident CTAs never ask for more than the SM's 512 TMEM columns.
+// Arguments n = max - q16 below kSmallN (a quarter of ln2 in Q8.16, so z = 0) read
+// their exp term from a table in shared memory: softmax_exp_q16_n(n) = tab[n].
+constexpr int kSmallN = 2048;
+
+template <int NPM, int SPL, bool DBUF>
 struct AttnCfg {
-    static constexpr int NPMAX = NPM;                 // longest image rounded up to 32
-    static constexpr int SPLIT = SPL;                 // warps per TMEM lane quadrant (column parts)
+    static constexpr int SPLIT = SPL;
+    static constexpr bool DB = DBUF;
     static constexpr int THREADS = 128 * SPL;
+    static constexpr int PER_SM = NPM <= 128 ? 4 : 2;   // resident CTAs (TMEM-limited)
     static constexpr uint32_t TMEM_COLS = NPM <= 128 ? 128 : 256;
-    static constexpr int KV = NPM * 64;                        // one [NPMAX][64] K-major operand
-    static constexpr int OFF_KV = 0;                           // two (K, V) buffers: item j uses j & 1
-    static constexpr int OFF_P = OFF_KV + 4 * KV;              // [128][NPMAX] uint8
-    static constexpr int OFF_Q = OFF_P;                        // [128][64]; Q is dead before P is written
-    static constexpr int OFF_RED = OFF_P + 128 * NPM;          // [2][SPLIT][128] int32 row partials
+    static constexpr int KV = NPM * 64;                 // one [NPMAX][64] operand
+    static constexpr int OFF_K = 0;                     // K [NPMAX][64]
+    static constexpr int OFF_V = OFF_K + KV;            // V [NPMAX][64]
+    static constexpr int OFF_Q = OFF_V + KV;            // Q [128][64]
+    static constexpr int OFF_P = OFF_Q + 128 * 64;      // P [128][NPMAX] uint8
+    static constexpr int OFF_TAB = OFF_P + 128 * NPM;   // exp terms of small arguments [kSmallN] uint32
+    static constexpr int OFF_RED = OFF_TAB + kSmallN * 4;  // [2][SPL][128] int32 row partials
     static constexpr int OFF_BAR = OFF_RED + 2 * SPL * 128 * 4;  // mbarrier, TMEM base, abort flag
-    static constexpr int SMEM = (OFF_BAR + 64 + 1023) / 1024 * 1024;
-    // Shared memory alone keeps the resident CTAs within the 512 TMEM columns, so
-    // tcgen05.alloc never waits: at most 4 small (128 columns) or 2 large (256) per SM.
-    static_assert(NPM <= 128 ? (5 * SMEM > 228 * 1024 && 4 * (SMEM + 2048) <= 228 * 1024)
-                             : (3 * SMEM > 228 * 1024 && 2 * (SMEM + 3072) <= 228 * 1024),
+    static constexpr int USED = (OFF_BAR + 64 + 1023) / 1024 * 1024;
+    // padded so that no more CTAs fit an SM than its 512 TMEM columns hold
+    static constexpr int MIN = NPM <= 128 ? 46 * 1024 : 77 * 1024;
+    static constexpr int SMEM = USED > MIN ? USED : MIN;
+    static_assert(NPM <= 128 ? (5 * SMEM > 228 * 1024 && 4 * (SMEM + 1024) <= 228 * 1024)
+                             : (3 * SMEM > 228 * 1024 && 2 * (SMEM + 1024) <= 228 * 1024),
                   "attention shared memory sizing");
 };
-using AttnSmall = AttnCfg<128, 2>;
-using AttnLarge = AttnCfg<224, 4>;
+
+// Runs f(v, c) over the 16-column pieces c = c0, c0 + step, ... < cend of a TMEM row
+// (address addr + 16c).  DB: double-buffered, the next piece's tcgen05.ld is in
+// flight while f works on the current one (16 more registers).  All arguments are
+// warp-uniform.
+template <bool DB, class F>
+__device__ __forceinline__ void for_pieces(uint32_t addr, int c0, int step, int cend, F &&f) {
+    if (c0 >= cend) return;
+    if (!DB) {
+        for (int c = c0; c < cend; c += step) {
+            uint32_t a[16];
+            tc05::ld16(addr + c * 16, a);
+            tc05::wait_ld_regs(a);
+            f(a, c);
+        }
+        return;
+    }
+    uint32_t a[16], b[16];
+    int c = c0;
+    tc05::ld16(addr + c * 16, a);
+    while (true) {
+        tc05::wait_ld_regs(a);
+        const int c1 = c + step;
+        if (c1 < cend) tc05::ld16(addr + c1 * 16, b);
+        f(a, c);
+        if (c1 >= cend) break;
+        tc05::wait_ld_regs(b);
+        const int c2 = c1 + step;
+        if (c2 < cend) tc05::ld16(addr + c2 * 16, a);
+        f(b, c1);
+        if (c2 >= cend) break;
+        c = c2;
+    }
+}
+
+// Barrier of the SPLIT warps that share TMEM lane quadrant `quad` (ids 1..4).
+template <class CFG>
+__device__ __forceinline__ void quad_sync(int quad) {
+    if (CFG::SPLIT > 1) asm volatile("bar.sync %0, %1;\n" ::"r"(1 + quad), "r"(32 * CFG::SPLIT) : "memory");
+}
 
 // q16 of one score accumulator.  FAST: host-proven that the int32 score
 // writeback and the sat24 cannot clip, so q16 = rsa(acc, fast_shift), written
@@ -78,74 +209,131 @@ __device__ __forceinline__ int32_t q16_of(int32_t acc, const AttnParams &p) {
 // once per row.  |acc| <= 2^20 and |mx*2^s| <= 2^30 + 2^20 keep the sum inside int32.
 template <bool FAST>
 __device__ __forceinline__ uint32_t negxt_of(int32_t acc, int32_t mx, int32_t cmn, const AttnParams &p) {
+    // (with fast_shift = 0 the mask is 0 and cmn = mx: mx - acc)
     if (FAST) return (uint32_t)((cmn - acc - ((acc >> 31) & p.fast_negmask)) >> p.fast_shift);
     return (uint32_t)(mx - q16_of<false>(acc, p));
 }
 
+// Exp terms of one 16-column piece (columns >= valid give 0 when MASK); returns their
+// sum.  When every argument of the warp's piece is below kSmallN (one vote), the terms
+// come from the table `tab` instead of the arithmetic; both are exact.
 template <bool FAST, bool MASK>
-__device__ __forceinline__ uint32_t chunk_exp(uint32_t (&v)[16], int valid, int32_t mx, int32_t cmn,
-                                              const AttnParams &p) {
-    uint32_t sum = 0;
+__device__ __forceinline__ uint32_t piece_exp(uint32_t (&v)[16], int valid, int32_t mx, int32_t cmn,
+                                              const AttnParams &p, const uint32_t *tab) {
+    uint32_t orv = 0;
 #pragma unroll
     for (int j = 0; j < 16; ++j) {
-        uint32_t e = softmax_exp_q16_n(negxt_of<FAST>((int32_t)v[j], mx, cmn, p));
-        if (MASK && j >= valid) e = 0u;
-        v[j] = e;
-        sum += e;
+        uint32_t nn = negxt_of<FAST>((int32_t)v[j], mx, cmn, p);
+        if (MASK && j >= valid) nn = 0u;  // (its term is zeroed below)
+        v[j] = nn;
+        orv |= nn;
     }
-    return sum;
+    if (__all_sync(0xffffffffu, orv < (uint32_t)kSmallN)) {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) v[j] = tab[v[j]];
+    } else {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) v[j] = softmax_exp_q16_n(v[j]);
+    }
+    if (MASK) {
+#pragma unroll
+        for (int j = 0; j < 16; ++j)
+            if (j >= valid) v[j] = 0u;
+    }
+    // pairwise tree: a dependency depth of 4 instead of a chain of 16 adds
+    uint32_t s8[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) s8[j] = v[2 * j] + v[2 * j + 1];
+#pragma unroll
+    for (int w = 4; w >= 1; w >>= 1)
+#pragma unroll
+        for (int j = 0; j < w; ++j) s8[j] += s8[j + w];
+    return s8[0];
 }
 
-// Asynchronous copy of item `item`'s K and V rows into a (K, V) buffer pair, both in
-// the K-major byte layout; rows n..np-1 are zero-filled (src-size 0).
-template <class CFG>
-__device__ __forceinline__ void attn_load_kv(const int8_t *qkv, const int32_t *offsets, int item, uint8_t *kv,
-                                             int tid) {
-    const int img = item / 3, head = item - img * 3;
-    const int row0 = offsets[img], n = offsets[img + 1] - row0, np = (n + 31) & ~31;
-    for (int c = tid; c < np * 8; c += CFG::THREADS) {
-        const int r = c >> 3, ch = c & 3, isv = (c >> 2) & 1;
-        const int8_t *src = qkv + (size_t)(row0 + (r < n ? r : 0)) * 576 + 192 * (1 + isv) + head * 64 + ch * 16;
-        const uint32_t dst = tc05::smem_u32(kv + isv * CFG::KV + tc05::kmajor_offset(r, ch * 16, 64));
-        asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(dst), "l"(src), "r"(r < n ? 16 : 0)
+// Largest of 16 values (the first `valid` when MASK), as a pairwise tree.
+template <bool MASK>
+__device__ __forceinline__ int32_t piece_max(const uint32_t (&v)[16], int valid) {
+    int32_t m[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        const int32_t a = (MASK && 2 * j >= valid) ? INT32_MIN : (int32_t)v[2 * j];
+        const int32_t b = (MASK && 2 * j + 1 >= valid) ? INT32_MIN : (int32_t)v[2 * j + 1];
+        m[j] = max(a, b);
+    }
+#pragma unroll
+    for (int w = 4; w >= 1; w >>= 1)
+#pragma unroll
+        for (int j = 0; j < w; ++j) m[j] = max(m[j], m[j + w]);
+    return m[0];
+}
+
+struct Unit {
+    int img, mt, glog, h0, nh;
+    int row0, n;
+};
+
+__device__ __forceinline__ Unit decode_unit(uint32_t code, const int32_t *offsets) {
+    Unit u;
+    u.img = (int)(code >> 7);
+    u.mt = (code >> 6) & 1;
+    u.glog = (code >> 4) & 3;
+    u.h0 = (code >> 2) & 3;
+    u.nh = code & 3;
+    u.row0 = offsets[u.img];
+    u.n = offsets[u.img + 1] - u.row0;
+    return u;
+}
+
+// K (V = 0) or V (V = 1) rows of a unit, K-major bytes, as one cp.async group.  Slot
+// j (head h0 + j) occupies rows [j*R, j*R + R) with R = 128 >> glog (G = 1: R = np);
+// rows past the image are zero-filled (src-size 0).
+template <class CFG, int V>
+__device__ __forceinline__ void load_kv(const int8_t *qkv, const Unit &u, uint8_t *dst_buf, int tid) {
+    const int R = u.glog ? (128 >> u.glog) : ((u.n + 31) & ~31);
+    const int rows = R * u.nh;
+    for (int c = tid; c < rows * 4; c += CFG::THREADS) {
+        const int r = c >> 2, ch = c & 3;
+        const int j = u.glog ? r / R : 0, t = r - j * R;
+        const int8_t *src = qkv + (size_t)(u.row0 + (t < u.n ? t : 0)) * 576 + 192 * (1 + V) + (u.h0 + j) * 64 + ch * 16;
+        const uint32_t dst = tc05::smem_u32(dst_buf + tc05::kmajor_offset(r, ch * 16, 64));
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(dst), "l"(src), "r"(t < u.n ? 16 : 0)
                      : "memory");
     }
-    asm volatile("cp.async.commit_group;\n" ::: "memory");
 }
 
-// Asynchronous copy of the 128-row Q tile t of item `item` (rows past the image are
-// zero-filled) into the K-major Q buffer.
+// The unit's 128 query rows into the K-major Q buffer (rows past the image zero-filled).
 template <class CFG>
-__device__ __forceinline__ void attn_load_q(const int8_t *qkv, const int32_t *offsets, int item, int t, uint8_t *sq,
-                                            int tid) {
-    const int img = item / 3, head = item - img * 3;
-    const int row0 = offsets[img], n = offsets[img + 1] - row0;
+__device__ __forceinline__ void load_q(const int8_t *qkv, const Unit &u, uint8_t *sq, int tid) {
+    const int R = u.glog ? (128 >> u.glog) : 128;
     for (int c = tid; c < 128 * 4; c += CFG::THREADS) {
-        const int r = c >> 2, ch = c & 3, gr = t * 128 + r;
-        const int8_t *src = qkv + (size_t)(row0 + (gr < n ? gr : 0)) * 576 + head * 64 + ch * 16;
+        const int r = c >> 2, ch = c & 3;
+        const int j = r / R;
+        const int t = u.glog ? r - j * R : u.mt * 128 + r;
+        const bool ok = j < u.nh && t < u.n;
+        const int8_t *src = qkv + (size_t)(u.row0 + (ok ? t : 0)) * 576 + (u.h0 + (ok ? j : 0)) * 64 + ch * 16;
         const uint32_t dst = tc05::smem_u32(sq + tc05::kmajor_offset(r, ch * 16, 64));
-        asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(dst), "l"(src), "r"(gr < n ? 16 : 0)
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(dst), "l"(src), "r"(ok ? 16 : 0)
                      : "memory");
     }
-    asm volatile("cp.async.commit_group;\n" ::: "memory");
 }
 
-// Barrier of the SPLIT warps that share TMEM lane quadrant `quad` (ids 1..4).
-template <class CFG>
-__device__ __forceinline__ void quad_sync(int quad) {
-    asm volatile("bar.sync %0, %1;\n" ::"r"(1 + quad), "r"(32 * CFG::SPLIT) : "memory");
-}
+__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+// Wait until at most one (the newest) cp.async group of this thread is pending.
+__device__ __forceinline__ void cp_wait_all_but_newest() { asm volatile("cp.async.wait_group 1;\n" ::: "memory"); }
 
 template <bool FAST, class CFG>
-__global__ void __launch_bounds__(CFG::THREADS) attention_tc_kernel(const int8_t *__restrict__ qkv,
+__global__ void __launch_bounds__(CFG::THREADS, CFG::PER_SM) attention_tc_kernel(const int8_t *__restrict__ qkv,
                                                                const int32_t *__restrict__ offsets,
                                                                int8_t *__restrict__ ctx, AttnParams p,
-                                                               int *__restrict__ err, int items, int np_lo,
-                                                               int np_hi) {
+                                                               int *__restrict__ err,
+                                                               const uint32_t *__restrict__ list,
+                                                               const int32_t *__restrict__ count) {
     extern __shared__ __align__(1024) uint8_t smem[];
-    uint8_t *sQ = smem + CFG::OFF_Q;
     uint8_t *sP = smem + CFG::OFF_P;
-    int32_t *sred = (int32_t *)(smem + CFG::OFF_RED);
+    uint8_t *sQ = smem + CFG::OFF_Q;
+    uint8_t *sK = smem + CFG::OFF_K;
+    uint8_t *sV = smem + CFG::OFF_V;
     uint64_t *bar = (uint64_t *)(smem + CFG::OFF_BAR);
     uint32_t *tmem_slot = (uint32_t *)(smem + CFG::OFF_BAR + 8);
     volatile int *abort_flag = (volatile int *)(smem + CFG::OFF_BAR + 12);
@@ -153,6 +341,9 @@ __global__ void __launch_bounds__(CFG::THREADS) attention_tc_kernel(const int8_t
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int quad = warp & 3, part = warp >> 2;
     const int lrow = quad * 32 + lane;  // tile row = TMEM lane
+    int32_t *sred = (int32_t *)(smem + CFG::OFF_RED);
+    uint32_t *stab = (uint32_t *)(smem + CFG::OFF_TAB);
+    for (int i = tid; i < kSmallN; i += CFG::THREADS) stab[i] = softmax_exp_q16_n((uint32_t)i);
 
     if (warp == 0) {
         tc05::tmem_alloc(tmem_slot, CFG::TMEM_COLS);
@@ -163,7 +354,7 @@ __global__ void __launch_bounds__(CFG::THREADS) attention_tc_kernel(const int8_t
         *abort_flag = 0;
         tc05::fence_mbar_init();
     }
-    griddep_wait();  // QKV and the offsets come from earlier kernels
+    griddep_wait();  // QKV, the offsets and the unit list come from earlier kernels
     griddep_launch();
     tc05::fence_before();
     __syncthreads();
@@ -171,58 +362,33 @@ __global__ void __launch_bounds__(CFG::THREADS) attention_tc_kernel(const int8_t
     const uint32_t tbase = *tmem_slot;
     const uint32_t lane_addr = tbase + ((uint32_t)(quad * 32) << 16);
     uint32_t phase = 0;
+    const int units = *count;
+    const int stride = gridDim.x;
 
-    // Persistent: the CTA's items are blockIdx.x + j * gridDim.x.  Its threads test a
-    // batch of THREADS candidates at once (one offsets read each) and list the items
-    // of this CTA shape; the CTA then processes the list.
-    __shared__ int s_items[CFG::THREADS];
-    __shared__ int s_nitems;
-    for (int jb = 0; blockIdx.x + jb * gridDim.x < items && !*abort_flag; jb += CFG::THREADS) {
-    if (tid == 0) s_nitems = 0;
-    __syncthreads();
-    {
-        const int it = blockIdx.x + (jb + tid) * gridDim.x;
-        if (it < items) {
-            const int im = it / 3;
-            const int nn = offsets[im + 1] - offsets[im];
-            const int npp = (nn + 31) & ~31;
-            if (nn > 0 && npp > np_lo && npp <= np_hi) s_items[atomicAdd(&s_nitems, 1)] = it;
-        }
+    // cp.async groups, oldest first: [K, Q] of a unit (issued once the previous unit's
+    // S = Q.K^T has completed), then [V] of it (once the previous unit's P.V has).
+    Unit cur;
+    if ((int)blockIdx.x < units) {
+        cur = decode_unit(list[blockIdx.x], offsets);
+        load_kv<CFG, 0>(qkv, cur, sK, tid);
+        load_q<CFG>(qkv, cur, sQ, tid);
+        cp_commit();
+        load_kv<CFG, 1>(qkv, cur, sV, tid);
+        cp_commit();
     }
-    __syncthreads();
-    const int nlist = s_nitems;
-    if (nlist > 0) {
-        attn_load_kv<CFG>(qkv, offsets, s_items[0], smem + CFG::OFF_KV, tid);
-        attn_load_q<CFG>(qkv, offsets, s_items[0], 0, sQ, tid);
-    }
-    for (int li = 0; li < nlist && !*abort_flag; ++li) {
-    const int item = s_items[li];
-    const int img = item / 3, head = item - img * 3;
-    const int row0 = offsets[img];
-    const int n = offsets[img + 1] - row0;
-    const int np = (n + 31) & ~31;
-    // This item's K/V copies (issued during the previous item) land; then the next
-    // item's copies go to the other buffer, whose last reader (that item's P.V) has
-    // completed.
-    asm volatile("cp.async.wait_all;\n" ::: "memory");
-    __syncthreads();
-    uint8_t *sK = smem + CFG::OFF_KV + (li & 1) * 2 * CFG::KV;
-    uint8_t *sV = sK + CFG::KV;
-    if (li + 1 < nlist)
-        attn_load_kv<CFG>(qkv, offsets, s_items[li + 1], smem + CFG::OFF_KV + ((li + 1) & 1) * 2 * CFG::KV, tid);
-    const uint32_t sbo_np = (uint32_t)(np / 16) * 128;
-    const int nchunks = np >> 4;       // 16-column chunks of P
-    const int nvalid = (n + 15) >> 4;  // chunks holding at least one real column
-
-    for (int t = 0; t * 128 < n; ++t) {
-        // ---- Q tile: its copies were issued when the previous P.V completed --------
-        asm volatile("cp.async.wait_all;\n" ::: "memory");
+    for (int ui = blockIdx.x; ui < units && !*abort_flag; ui += stride) {
+        const Unit u = cur;
+        cp_wait_all_but_newest();  // this unit's K and Q have landed (its V may not have)
         tc05::fence_proxy_async();
         tc05::fence_before();
         __syncthreads();
+        const bool more = ui + stride < units;
+        const int np = (u.n + 31) & ~31;
+        const int scols = u.glog ? 128 : np;  // S columns = K rows = P columns
+        // ---- S = Q.K^T ----------------------------------------------------------------
         if (tid == 0) {
             tc05::fence_after();
-            const uint32_t idesc = tc05::idesc_i8(128, np, true, true);
+            const uint32_t idesc = tc05::idesc_i8(128, scols, true, true);
 #pragma unroll
             for (int s = 0; s < 2; ++s)
                 tc05::mma_i8_ss(tbase, tc05::smem_desc(tc05::smem_u32(sQ) + s * 256, 128, 512),
@@ -234,62 +400,60 @@ __global__ void __launch_bounds__(CFG::THREADS) attention_tc_kernel(const int8_t
         __syncthreads();
         if (*abort_flag) break;
         tc05::fence_after();
+        // K and Q are consumed: the next unit's copies overlap this unit's softmax
+        if (more) {
+            cur = decode_unit(list[ui + stride], offsets);
+            load_kv<CFG, 0>(qkv, cur, sK, tid);
+            load_q<CFG>(qkv, cur, sQ, tid);
+        }
+        cp_commit();  // (an empty group when there is no next unit)
 
-        // ---- softmax straight from TMEM: this warp's rows, 16-column chunks c = part + CFG::SPLIT*i
-        // q16 is monotone in the accumulator, so the row max is taken on raw
-        // accumulators and converted once.
-        const bool live = t * 128 + quad * 32 < n;  // warp-uniform
-        const int nfull = n & ~15;
+        // ---- this thread's row: slot j (head h0 + j), local row t, S columns [cb, cb + np);
+        // this part's pieces are c = part, part + SPLIT, ...
+        const int R = u.glog ? (128 >> u.glog) : 128;
+        const int j = lrow / R;  // quadrant-uniform (R >= 32)
+        const int t = u.glog ? lrow - j * R : u.mt * 128 + lrow;
+        const int cb = u.glog ? j * R : 0;
+        const int t0 = u.glog ? quad * 32 - j * R : u.mt * 128 + quad * 32;  // the quadrant's first row
+        const bool live = j < u.nh && t0 < u.n;                            // quadrant-uniform
+        const uint32_t row_addr = lane_addr + cb;
+        const int nv = (u.n + 15) >> 4, nfull = u.n >> 4;  // 16-column pieces: with a column / all full
+        constexpr int SP = CFG::SPLIT;
         if (live) {
+            // q16 is monotone in the accumulator: the row max is taken on raw values
             int32_t mxa = INT32_MIN;
-            for (int c = part; c < nvalid; c += CFG::SPLIT) {
-                const int c0 = c * 16;
-                uint32_t v[16];
-                tc05::ld16(lane_addr + c0, v);
-                tc05::wait_ld();
-                if (c0 < nfull) {
+            for_pieces<CFG::DB>(row_addr, part, SP, nv, [&](uint32_t (&v)[16], int c) {
+                mxa = max(mxa, c < nfull ? piece_max<false>(v, 16) : piece_max<true>(v, u.n - c * 16));
+            });
+            if (SP > 1) {
+                sred[part * 128 + lrow] = mxa;
+                quad_sync<CFG>(quad);
 #pragma unroll
-                    for (int j = 0; j < 16; ++j) mxa = max(mxa, (int32_t)v[j]);
-                } else {
-#pragma unroll
-                    for (int j = 0; j < 16; ++j)
-                        if (c0 + j < n) mxa = max(mxa, (int32_t)v[j]);
-                }
+                for (int q = 0; q < SP; ++q) mxa = max(mxa, sred[q * 128 + lrow]);
             }
-            sred[part * 128 + lrow] = mxa;
-            quad_sync<CFG>(quad);  // the SPLIT warps of this lane quadrant (live is quad-uniform)
-            int32_t mraw = sred[lrow];
-#pragma unroll
-            for (int q = 1; q < CFG::SPLIT; ++q) mraw = max(mraw, sred[q * 128 + lrow]);
-            const int32_t mx = q16_of<FAST>(mraw, p);
+            const int32_t mx = q16_of<FAST>(mxa, p);
             const int32_t cmn =
                 (int32_t)(((int64_t)1 << p.fast_shift) - 1 - p.fast_half + ((int64_t)mx << p.fast_shift));
             uint32_t sum = 0;
-            for (int c = part; c < nvalid; c += CFG::SPLIT) {
-                const int c0 = c * 16;
-                uint32_t v[16];
-                tc05::ld16(lane_addr + c0, v);
-                tc05::wait_ld();
-                if (c0 < nfull) sum += chunk_exp<FAST, false>(v, 16, mx, cmn, p);
-                else sum += chunk_exp<FAST, true>(v, n - c0, mx, cmn, p);
-                tc05::st16(lane_addr + c0, v);
-            }
+            for_pieces<CFG::DB>(row_addr, part, SP, nv, [&](uint32_t (&v)[16], int c) {
+                if (c < nfull) sum += piece_exp<FAST, false>(v, 16, mx, cmn, p, stab);
+                else sum += piece_exp<FAST, true>(v, u.n - c * 16, mx, cmn, p, stab);
+                tc05::st16(row_addr + c * 16, v);
+            });
             tc05::wait_st();
-            sred[(CFG::SPLIT + part) * 128 + lrow] = (int32_t)sum;
-            quad_sync<CFG>(quad);
-            uint32_t tot = 0;
+            if (SP > 1) {
+                sred[(SP + part) * 128 + lrow] = (int32_t)sum;
+                quad_sync<CFG>(quad);
+                sum = 0;
 #pragma unroll
-            for (int q = 0; q < CFG::SPLIT; ++q) tot += (uint32_t)sred[(CFG::SPLIT + q) * 128 + lrow];
-            const uint64_t rc = softmax_recip(tot ? tot : 1u);
-            for (int c = part; c < nchunks; c += CFG::SPLIT) {
-                const int c0 = c * 16;
-                if (c >= nvalid) {  // padding columns: zero probabilities
-                    *(uint4 *)(sP + tc05::kmajor_offset(lrow, c0, np)) = make_uint4(0, 0, 0, 0);
-                    continue;
-                }
-                uint32_t v[16];
-                tc05::ld16(lane_addr + c0, v);
-                tc05::wait_ld();
+                for (int q = 0; q < SP; ++q) sum += (uint32_t)sred[(SP + q) * 128 + lrow];
+            }
+            // S >= exp(0) = 65554 (the max element), so rc = round_div(2^32, S) <= 65519
+            // and the products below fit a 32 x 32 -> 64-bit multiply
+            const uint32_t rc = (uint32_t)softmax_recip(sum ? sum : 1u);
+            // P row: the own block's probabilities, zeros in every other column
+            const int cb16 = cb >> 4;
+            for_pieces<CFG::DB>(row_addr, part, SP, nv, [&](uint32_t (&v)[16], int c) {
                 uint32_t pk[4];
 #pragma unroll
                 for (int w = 0; w < 4; ++w) {
@@ -303,19 +467,25 @@ __global__ void __launch_bounds__(CFG::THREADS) attention_tc_kernel(const int8_t
                     }
                     pk[w] = pack_satu8(pr[0], pr[1], pr[2], pr[3]);
                 }
-                *(uint4 *)(sP + tc05::kmajor_offset(lrow, c0, np)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-            }
+                *(uint4 *)(sP + tc05::kmajor_offset(lrow, (cb16 + c) * 16, scols)) =
+                    make_uint4(pk[0], pk[1], pk[2], pk[3]);
+            });
+            for (int c = part; c < scols / 16; c += SP)
+                if (c < cb16 || c >= cb16 + nv)
+                    *(uint4 *)(sP + tc05::kmajor_offset(lrow, c * 16, scols)) = make_uint4(0, 0, 0, 0);
         }
 
-        // ---- ctx = P·V (rows of dead warps hold stale probabilities; their ctx rows are not stored)
+        // ---- ctx = P.V (rows of dead warps hold stale probabilities; their ctx rows are not stored)
+        cp_wait_all_but_newest();  // this unit's V has landed (the next unit's K/Q may not have)
         tc05::fence_proxy_async();
         tc05::fence_before();
         __syncthreads();
         if (tid == 0) {
             tc05::fence_after();
             const uint32_t idesc = tc05::idesc_i8(128, 64, false, true, true);
-            for (int s = 0; s < np / 32; ++s)
-                tc05::mma_i8_ss(tbase, tc05::smem_desc(tc05::smem_u32(sP) + s * 256, 128, sbo_np),
+            const uint32_t sbo = (uint32_t)(scols / 16) * 128;
+            for (int s = 0; s < scols / 32; ++s)
+                tc05::mma_i8_ss(tbase, tc05::smem_desc(tc05::smem_u32(sP) + s * 256, 128, sbo),
                                 tc05::smem_desc(tc05::smem_u32(sV) + s * 2048, 512, 128), idesc, s);
             tc05::commit(bar);
         }
@@ -324,19 +494,18 @@ __global__ void __launch_bounds__(CFG::THREADS) attention_tc_kernel(const int8_t
         __syncthreads();
         if (*abort_flag) break;
         tc05::fence_after();
-        // P (and with it the Q buffer it overlays) is free: the next tile's Q copies
-        // overlap this tile's context epilogue
-        if ((t + 1) * 128 < n) attn_load_q<CFG>(qkv, offsets, item, t + 1, sQ, tid);
-        else if (li + 1 < nlist) attn_load_q<CFG>(qkv, offsets, s_items[li + 1], 0, sQ, tid);
-        const int r = t * 128 + lrow;
+        // V is consumed: the next unit's V copies overlap the rest of this unit
+        if (more) load_kv<CFG, 1>(qkv, cur, sV, tid);
+        cp_commit();
         if (live) {
-            for (int pc = part; pc < 4; pc += CFG::SPLIT) {  // 16-column pieces of the 64 head dims
-                uint32_t o[16];
-                tc05::ld16(lane_addr + pc * 16, o);
+            const int h = u.h0 + j;
+            for (int half = part; half < 2; half += CFG::SPLIT) {
+                uint32_t o[32];
+                tc05::ld32(lane_addr + half * 32, o);
                 tc05::wait_ld();
-                uint32_t pk[4];
+                uint32_t pk[8];
 #pragma unroll
-                for (int w = 0; w < 4; ++w) {
+                for (int w = 0; w < 8; ++w) {
                     int32_t q[4];
 #pragma unroll
                     for (int b = 0; b < 4; ++b) {
@@ -345,17 +514,16 @@ __global__ void __launch_bounds__(CFG::THREADS) attention_tc_kernel(const int8_t
                     }
                     pk[w] = pack_sat8(q[0], q[1], q[2], q[3]);
                 }
-                if (r < n)
-                    *(uint4 *)(ctx + (size_t)(row0 + r) * 192 + head * 64 + pc * 16) =
-                        make_uint4(pk[0], pk[1], pk[2], pk[3]);
+                if (t < u.n) {
+                    uint4 *dst = (uint4 *)(ctx + (size_t)(u.row0 + t) * 192 + h * 64 + half * 32);
+                    dst[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+                    dst[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+                }
             }
         }
         tc05::fence_before();
         __syncthreads();
     }
-    }  // listed items
-    __syncthreads();  // s_items is rewritten by the next batch
-    }  // candidate batches
 
     asm volatile("cp.async.wait_all;\n" ::: "memory");  // a prefetch may be left after an abort
     if (*abort_flag) {
@@ -386,24 +554,37 @@ AttnParams make_attn(int qkv_out_scale, int score_scale, int prob_scale, int con
     return a;
 }
 
-cudaError_t launch_attention(const int8_t *qkv, const int32_t *offsets, int images, int8_t *ctx,
-                             const AttnParams &p, int may_be_short, int sms, int *err, cudaStream_t st) {
+cudaError_t launch_attn_plan(const int32_t *offsets, int images, const AttnPlan &plan, cudaStream_t st) {
     if (images <= 0) return cudaSuccess;
-    const int items = images * 3;
-    // Images of up to 128 tokens (np <= 128) go to the small shape when any may exist.
+    return launch_pdl(attn_plan_kernel, dim3(1), dim3(1024), 0, st, offsets, images, plan.list_a, plan.list_b,
+                      plan.cnt);
+}
+
+template <class CFG>
+cudaError_t launch_one(const int8_t *qkv, const int32_t *offsets, int8_t *ctx, const AttnParams &p, int *err,
+                       const uint32_t *list, const int32_t *count, int grid, cudaStream_t st) {
+    auto k = p.fast ? attention_tc_kernel<true, CFG> : attention_tc_kernel<false, CFG>;
+    cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, CFG::SMEM);
+    if (e != cudaSuccess) return e;
+    return launch_pdl(k, dim3(grid), dim3(CFG::THREADS), CFG::SMEM, st, qkv, offsets, ctx, p, err, list, count);
+}
+
+cudaError_t launch_attention(const int8_t *qkv, const int32_t *offsets, int images, int8_t *ctx,
+                             const AttnParams &p, int may_be_short, int sms, int *err, const AttnPlan &plan,
+                             cudaStream_t st) {
+    if (images <= 0) return cudaSuccess;
+    // List A: one warp per TMEM lane quadrant, double-buffered TMEM reads (four
+    // CTAs of 4 warps per SM); list B: four warps per quadrant splitting each row's
+    // pieces, single-buffered (two CTAs of 16 warps per SM, 64 registers).
+    const uint32_t *la = plan.list_a, *lb = plan.list_b;
+    const int32_t *ca = plan.cnt, *cb = plan.cnt + 1;
     if (may_be_short) {
-        auto ks = p.fast ? attention_tc_kernel<true, AttnSmall> : attention_tc_kernel<false, AttnSmall>;
-        cudaError_t e = cudaFuncSetAttribute(ks, cudaFuncAttributeMaxDynamicSharedMemorySize, AttnSmall::SMEM);
-        if (e != cudaSuccess) return e;
-        e = launch_pdl(ks, dim3(std::min(items, sms * 4)), dim3(AttnSmall::THREADS), AttnSmall::SMEM, st, qkv, offsets,
-                       ctx, p, err, items, 0, 128);
+        const int ga = std::min(images * 3, sms * 4);
+        cudaError_t e = launch_one<AttnCfg<128, 1, true>>(qkv, offsets, ctx, p, err, la, ca, ga, st);
         if (e != cudaSuccess) return e;
     }
-    auto kl = p.fast ? attention_tc_kernel<true, AttnLarge> : attention_tc_kernel<false, AttnLarge>;
-    cudaError_t e = cudaFuncSetAttribute(kl, cudaFuncAttributeMaxDynamicSharedMemorySize, AttnLarge::SMEM);
-    if (e != cudaSuccess) return e;
-    return launch_pdl(kl, dim3(std::min(items, sms * 2)), dim3(AttnLarge::THREADS), AttnLarge::SMEM, st, qkv, offsets,
-                      ctx, p, err, items, may_be_short ? 128 : 0, AttnLarge::NPMAX);
+    const int gb = std::min(images * 6, sms * 2);
+    return launch_one<AttnCfg<224, 4, false>>(qkv, offsets, ctx, p, err, lb, cb, gb, st);
 }
 
 }  // namespace hv

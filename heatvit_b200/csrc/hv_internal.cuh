@@ -58,8 +58,18 @@ AttnParams make_attn(int qkv_out_scale, int score_scale, int prob_scale, int con
 cudaError_t gelu_table_window(int32_t qmax, int sh_out, int *d_mm, int32_t *wlo, int32_t *wn, cudaStream_t st);
 cudaError_t launch_gelu_table_fill(int8_t *tab, int32_t wlo, int32_t wn, int sh_out, cudaStream_t st);
 
+// Work-unit lists of the attention kernel for one token layout (attn_plan_kernel in
+// hv_attention.cu): list_a [3 * images] (images of at most 128 tokens), list_b
+// [6 * images] (longer images), cnt [2] their lengths.  Rebuilt whenever the
+// offsets change (batch set-up, every selector).
+struct AttnPlan {
+    uint32_t *list_a, *list_b;
+    int32_t *cnt;
+};
+cudaError_t launch_attn_plan(const int32_t *offsets, int images, const AttnPlan &plan, cudaStream_t st);
 cudaError_t launch_attention(const int8_t *qkv, const int32_t *offsets, int images, int8_t *ctx,
-                             const AttnParams &p, int may_be_short, int sms, int *err, cudaStream_t st);
+                             const AttnParams &p, int may_be_short, int sms, int *err, const AttnPlan &plan,
+                             cudaStream_t st);
 
 // Device-resident selector weights and constants.
 // Exact output table of one GELU chain over the Q8.16 inputs q = rsa(v, sh_in) its

@@ -123,6 +123,7 @@ struct Workspace {
     int32_t *off[2] = {nullptr, nullptr}, *counts = nullptr;
     uint8_t *pkg[2] = {nullptr, nullptr}, *warn = nullptr;
     int *err = nullptr;
+    AttnPlan plan{};  // attention work units of the current token layout
     // TMA descriptors of the GEMM A operands LN, CTX ([rows][192]) and HID ([rows][768])
     CUtensorMap tm_ln, tm_ctx, tm_hid;
     int tm_ok = 0;
@@ -174,6 +175,7 @@ struct hv_model {
     int32_t *off[2] = {nullptr, nullptr}, *counts = nullptr;
     uint8_t *pkg[2] = {nullptr, nullptr}, *warn = nullptr;
     int *err = nullptr;  // device error word (bounded waits that gave up)
+    AttnPlan plan{};
     const CUtensorMap *tm_ln = nullptr, *tm_ctx = nullptr, *tm_hid = nullptr;  // nullptr: cp.async loads
     // host-pipeline staging
     int host_cap = 0;
@@ -268,6 +270,7 @@ void use_workspace(hv_model *m, int i) {
     m->pkg[1] = w.pkg[1];
     m->warn = w.warn;
     m->err = w.err;
+    m->plan = w.plan;
     m->tm_ln = w.tm_ok ? &w.tm_ln : nullptr;
     m->tm_ctx = w.tm_ok ? &w.tm_ctx : nullptr;
     m->tm_hid = w.tm_ok ? &w.tm_hid : nullptr;
@@ -302,7 +305,8 @@ int ensure_capacity(hv_model *m, int images, int i = 0) {
                      oOff1 = take((size_t)(images + 1) * 4), oCnt = take((size_t)images * 4), oPkg0 = take(images),
                      oPkg1 = take(images), oWarn = take(((size_t)images + 3) & ~(size_t)3), oErr = take(16),
                      oOL = take((size_t)images * HV_CLASSES * 4), oOT = take((size_t)images * (HV_MAX_SELECTORS + 1) * 4),
-                     oOS = take((size_t)images * HV_MAX_SELECTORS * sizeof(hv_selector_summary)), oOW = take(images);
+                     oOS = take((size_t)images * HV_MAX_SELECTORS * sizeof(hv_selector_summary)), oOW = take(images),
+                     oLA = take((size_t)images * 3 * 4), oLB = take((size_t)images * 6 * 4), oPC = take(16);
         uint8_t *base = nullptr;
         if (cudaMalloc(&base, total) != cudaSuccess)
             return fail(HV_ERR_NOMEM, "cannot allocate %zu bytes of scratch", total);
@@ -326,6 +330,9 @@ int ensure_capacity(hv_model *m, int images, int i = 0) {
         w.o_tc = (int32_t *)(base + oOT);
         w.o_sum = (hv_selector_summary *)(base + oOS);
         w.o_warn = base + oOW;
+        w.plan.list_a = (uint32_t *)(base + oLA);
+        w.plan.list_b = (uint32_t *)(base + oLB);
+        w.plan.cnt = (int32_t *)(base + oPC);
         if (cudaMemset(w.err, 0, 16) != cudaSuccess) return fail(HV_ERR_CUDA, "cannot clear the error word");
         const int r = (int)rows;
         w.tm_ok = make_tmap_a(&w.tm_ln, w.LN, 192, r) == 0 && make_tmap_a(&w.tm_ctx, w.CTX, 192, r) == 0 &&
@@ -454,7 +461,7 @@ int run_block(hv_model *m, int b, int images, const int32_t *off, int may_be_sho
     }
     {
         Prof pr(m, HV_STAGE_ATTN, st);
-        CUDA_TRY(launch_attention(m->QKV, off, images, m->CTX, d.attn, may_be_short, m->sms, m->err, st));
+        CUDA_TRY(launch_attention(m->QKV, off, images, m->CTX, d.attn, may_be_short, m->sms, m->err, m->plan, st));
         pr.end(st, rows_dev, 0);
     }
     {
@@ -555,6 +562,7 @@ int infer_impl(hv_model *m, const int8_t *d_images, int batch, int32_t *d_logits
         ckpt_copy_kernel<<<batch, 256, 0, st>>>(m->X, m->off[cur], d_ckpt, d_ckpt_rows, HV_CKPT_PATCH);
         CUDA_TRY(cudaGetLastError());
     }
+    CUDA_TRY(launch_attn_plan(m->off[cur], batch, m->plan, st));
     int sel_no = 0;
     for (int b = 0; b < HV_BLOCKS; ++b) {
         const int si = m->sel_before[b];
@@ -567,6 +575,7 @@ int infer_impl(hv_model *m, const int8_t *d_images, int batch, int32_t *d_logits
             pr.end(st, m->off[cur] + batch, 0);
             CUDA_TRY(launch_pack(m->STAGE, m->counts, batch, m->X, m->off[cur ^ 1], st));
             cur ^= 1;
+            CUDA_TRY(launch_attn_plan(m->off[cur], batch, m->plan, st));
             ++sel_no;
             if (d_ckpt) {
                 ckpt_copy_kernel<<<batch, 256, 0, st>>>(m->X, m->off[cur], d_ckpt, d_ckpt_rows,
@@ -1613,7 +1622,10 @@ int hv_gemm_i8(const void *d_a, const int8_t *d_b, const int32_t *d_bias, int m,
     if (k > (a_unsigned ? 65793 : 131071))
         return fail(HV_ERR_VALUE, "k=%d can overflow the int32 accumulator; not supported", k);
     cudaStream_t st = (cudaStream_t)stream;
-    if (k == 0 || (a_unsigned && out_bits == 8)) {
+    // The tiled kernel's int8 epilogue stores 16-byte pieces of a row: it needs
+    // 16-byte aligned output rows (n a multiple of 16, d_out 16-byte aligned).
+    const bool i8_rows_ok = n % 16 == 0 && (uintptr_t)d_out % 16 == 0;
+    if (k == 0 || (out_bits == 8 && (a_unsigned || !i8_rows_ok))) {
         // the raw accumulator, then the element-wise writeback
         int64_t *acc = nullptr;
         CUDA_TRY(cudaMalloc(&acc, (size_t)m * n * 8));
@@ -1765,6 +1777,7 @@ int hv_transformer_block(hv_model *m, int block_index, const int8_t *d_x, const 
     cudaStream_t st = (cudaStream_t)stream;
     CUDA_TRY(cudaMemcpyAsync(m->X, d_x, (size_t)total_rows * 192, cudaMemcpyDeviceToDevice, st));
     CUDA_TRY(cudaMemsetAsync(m->warn, 0, ((size_t)images + 3) & ~(size_t)3, st));
+    CUDA_TRY(launch_attn_plan(d_offsets, images, m->plan, st));
     rc = run_block(m, block_index, images, d_offsets, 1, st);
     if (rc) return rc;
     CUDA_TRY(cudaMemcpyAsync(d_z, m->X, (size_t)total_rows * 192, cudaMemcpyDeviceToDevice, st));

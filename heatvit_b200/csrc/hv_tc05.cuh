@@ -87,6 +87,29 @@ HV_DEV bool mbar_wait(uint64_t *mbar, uint32_t parity, uint32_t max_iters) {
     return false;
 }
 
+// Wait for this thread's tcgen05.ld operations, with the destination registers of
+// the load being waited for as operands: the compiler cannot move a use of them
+// above the wait (a plain wait::ld has no data dependence on them).
+HV_DEV void wait_ld_regs(uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.wait::ld.sync.aligned;\n"
+        : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+          "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15]),
+          "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]), "+r"(r[22]), "+r"(r[23]),
+          "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]), "+r"(r[29]), "+r"(r[30]), "+r"(r[31])
+        :
+        : "memory");
+}
+
+HV_DEV void wait_ld_regs(uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.wait::ld.sync.aligned;\n"
+        : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+          "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15])
+        :
+        : "memory");
+}
+
 HV_DEV void fence_before() { asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory"); }
 HV_DEV void fence_after() { asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory"); }
 HV_DEV void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory"); }

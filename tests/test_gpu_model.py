@@ -272,6 +272,31 @@ def test_transformer_block_fused_ragged_vs_oracle(cuda, oracle):
             np.testing.assert_array_equal(z, want)
 
 
+@pytest.mark.parametrize("q,k", [(-8, 9), (-5, 12), (-10, 7)])
+def test_attention_wide_scores_vs_oracle(cuda, oracle, q, k):
+    """Attention rows with wide Q8.16 spreads: qkv_out_scale_exp q (score_scale 2q - 3)
+    with the QKV weight exponent raised by k so the scores stay large.  (-8, 9): most
+    arguments above the small-argument table, none past ln2; (-5, 12): arguments far
+    past ln2 (zero exp terms) through the general (non-FAST) q16 form; (-10, 7): small
+    arguments only.  The benchmark model's rows are nearly flat, so these cases carry
+    the general exp path of the attention kernel."""
+    import dataclasses
+    from heatvit_b200 import synth
+    from heatvit_b200.transformer import transformer_block_batch
+    params = synth.config_params(synth.SEED, pruned=True)
+    bp = params.blocks[5]
+    m = dataclasses.replace(bp.mhsa, qkv_out_scale_exp=q, score_scale_exp=2 * q - 3,
+                            wqkv_scale_exp=bp.mhsa.wqkv_scale_exp + k)
+    blk = dataclasses.replace(bp, mhsa=m)
+    rng = np.random.default_rng([-q, k])
+    counts = [197, 1, 2, 31, 32, 33, 64, 65, 88, 128, 129, 150, 196, 17]
+    xs = [rng.integers(-128, 128, (n, 192)) for n in counts]
+    zs = transformer_block_batch(xs, blk)
+    for x, z in zip(xs, zs):
+        want, _, _ = oracle.transformer_block(x, blk)
+        np.testing.assert_array_equal(z, want)
+
+
 def test_patch_embedding_vs_oracle(cuda, oracle):
     from heatvit_b200 import synth
     from heatvit_b200.transformer import patch_embedding
