@@ -49,7 +49,9 @@ class RootGather:
     def __init__(self, world, rank, numel, dtype, device, slots=2, group=None):
         import torch
         self.world, self.rank, self.group = world, rank, group
-        self.side = torch.cuda.Stream(device=device) if world > 1 else None
+        device = torch.device(device)
+        # CPU tensors (gloo) gather synchronously; CUDA tensors on a side stream
+        self.side = torch.cuda.Stream(device=device) if world > 1 and device.type == "cuda" else None
         self.recv = []
         if world > 1 and rank == 0:
             self.recv = [torch.empty((world, numel), dtype=dtype, device=device) for _ in range(slots)]
@@ -64,11 +66,14 @@ class RootGather:
             return buf
         slot = self.n % max(1, len(self.recv) or 2)
         self.n += 1
+        out = self.recv[slot] if self.rank == 0 else None
+        lst = list(out.unbind(0)) if out is not None else None
+        if self.side is None:
+            dist.gather(buf, lst, dst=0, group=self.group)
+            return out
         cur = torch.cuda.current_stream(buf.device)
         self.side.wait_stream(cur)
         with torch.cuda.stream(self.side):
-            out = self.recv[slot] if self.rank == 0 else None
-            lst = list(out.unbind(0)) if out is not None else None
             work = dist.gather(buf, lst, dst=0, group=self.group, async_op=True)
         buf.record_stream(self.side)
         self.pending[buf.data_ptr()] = work
