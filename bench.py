@@ -566,6 +566,7 @@ def main():
         steps3 = max(args.steps, 20)
         ms3 = time_steps(torch, step3, steps3, 1) / steps3
         c3 = out3["token_counts"].cpu().numpy()
+        stages3 = stage_breakdown(torch, eng, step3, c3, int8_tops, hbm, launches_of)
         macs3 = algorithmic_macs(c3)
         t3 = 2 * float(macs3.sum()) / (int8_tops * 1e12)
         e2e3, _ = e2e_rates_for(b3, max(args.e2e_steps, 20))
@@ -578,6 +579,7 @@ def main():
             "e2e": {"value": e2e3["pipelined"], "unit": "images/s", "h2d_bytes_per_step": b3 * 150528,
                     "d2h_bytes_per_step": b3 * 4000, "mode": "pipelined host calls",
                     "blocking_value": e2e3["blocking"]},
+            "stages": stages3,
             "_logits": out3["logits"].cpu().numpy(), "_counts": c3,
             "_warn": out3["warnings"].cpu().numpy(),
         }

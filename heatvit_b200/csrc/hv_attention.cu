@@ -251,6 +251,19 @@ __device__ __forceinline__ uint32_t piece_exp(uint32_t (&v)[16], int valid, int3
     return s8[0];
 }
 
+// round_div(2^32, S) for a row sum S in [65554, 2^25) (every term <= 65554 and at
+// least one equal to it, at most 224 columns): q0 from a single-precision quotient
+// (relative error below 2^-21, so within 1 of the true quotient, which is < 65520),
+// then the exact remainder r = 2^32 - q*S fixes q to floor(2^32 / S) and the
+// ties-away rounding adds one when 2r >= S.
+__device__ __forceinline__ uint32_t softmax_recip32(uint32_t S) {
+    int32_t q = (int32_t)__fdividef(4294967296.0f, __uint2float_rn(S));
+    int64_t r = ((int64_t)1 << 32) - (int64_t)q * S;
+    if (r < 0) { q -= 1; r += S; }
+    if (r >= (int64_t)S) { q += 1; r -= S; }
+    return (uint32_t)(2 * r >= (int64_t)S ? q + 1 : q);
+}
+
 // Largest of 16 values (the first `valid` when MASK), as a pairwise tree.
 template <bool MASK>
 __device__ __forceinline__ int32_t piece_max(const uint32_t (&v)[16], int valid) {
@@ -292,9 +305,10 @@ template <class CFG, int V>
 __device__ __forceinline__ void load_kv(const int8_t *qkv, const Unit &u, uint8_t *dst_buf, int tid) {
     const int R = u.glog ? (128 >> u.glog) : ((u.n + 31) & ~31);
     const int rows = R * u.nh;
+    const int rsh = 7 - u.glog;  // packed slots: R = 2^rsh
     for (int c = tid; c < rows * 4; c += CFG::THREADS) {
         const int r = c >> 2, ch = c & 3;
-        const int j = u.glog ? r / R : 0, t = r - j * R;
+        const int j = u.glog ? r >> rsh : 0, t = r - j * R;
         const int8_t *src = qkv + (size_t)(u.row0 + (t < u.n ? t : 0)) * 576 + 192 * (1 + V) + (u.h0 + j) * 64 + ch * 16;
         const uint32_t dst = tc05::smem_u32(dst_buf + tc05::kmajor_offset(r, ch * 16, 64));
         asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(dst), "l"(src), "r"(t < u.n ? 16 : 0)
@@ -305,10 +319,11 @@ __device__ __forceinline__ void load_kv(const int8_t *qkv, const Unit &u, uint8_
 // The unit's 128 query rows into the K-major Q buffer (rows past the image zero-filled).
 template <class CFG>
 __device__ __forceinline__ void load_q(const int8_t *qkv, const Unit &u, uint8_t *sq, int tid) {
-    const int R = u.glog ? (128 >> u.glog) : 128;
+    const int rsh = 7 - u.glog;  // slot rows R = 2^rsh (128 when unpacked)
+    const int R = 1 << rsh;
     for (int c = tid; c < 128 * 4; c += CFG::THREADS) {
         const int r = c >> 2, ch = c & 3;
-        const int j = r / R;
+        const int j = r >> rsh;
         const int t = u.glog ? r - j * R : u.mt * 128 + r;
         const bool ok = j < u.nh && t < u.n;
         const int8_t *src = qkv + (size_t)(u.row0 + (ok ? t : 0)) * 576 + (u.h0 + (ok ? j : 0)) * 64 + ch * 16;
@@ -450,7 +465,7 @@ __global__ void __launch_bounds__(CFG::THREADS, CFG::PER_SM) attention_tc_kernel
             }
             // S >= exp(0) = 65554 (the max element), so rc = round_div(2^32, S) <= 65519
             // and the products below fit a 32 x 32 -> 64-bit multiply
-            const uint32_t rc = (uint32_t)softmax_recip(sum ? sum : 1u);
+            const uint32_t rc = softmax_recip32(sum);
             // P row: the own block's probabilities, zeros in every other column
             const int cb16 = cb >> 4;
             for_pieces<CFG::DB>(row_addr, part, SP, nv, [&](uint32_t (&v)[16], int c) {

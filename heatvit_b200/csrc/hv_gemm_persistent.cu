@@ -193,6 +193,13 @@ __global__ void __launch_bounds__(PT_THREADS, 1) tcp_gemm_kernel(GemmArgs g, int
     // + 6, i.e. 98 A rows (TMEM lanes 98..127 hold unused rows).
     const bool ptma = EPI == EPI_PATCH && use_tma;
     const int mtiles = ptma ? 2 * (m_lim / 196) : (m_lim + 127) / 128;
+    // Work units are (tile, 192-column chunk) pairs, unit u = mt * NCH + c.  Each CTA
+    // takes one contiguous range of equal size (within one unit), so a tile's chunks
+    // mostly stay in one CTA and share its A stage, and no CTA runs more than one
+    // chunk past the others.
+    const int units = mtiles * L::NCH;
+    const int u_begin = (int)(((long long)blockIdx.x * units) / gridDim.x);
+    const int u_end = (int)(((long long)(blockIdx.x + 1) * units) / gridDim.x);
     tc05::fence_proxy_async();
     tc05::fence_before();
     __syncthreads();
@@ -211,7 +218,9 @@ __global__ void __launch_bounds__(PT_THREADS, 1) tcp_gemm_kernel(GemmArgs g, int
             int last_q[L::S];
 #pragma unroll
             for (int s = 0; s < L::S; ++s) last_q[s] = -1;
-            for (int mt = blockIdx.x; mt < mtiles && ok && !*abortf; mt += gridDim.x) {
+            for (int u = u_begin; u < u_end && ok && !*abortf; ++u) {
+                const int mt = u / L::NCH;
+                if (u != u_begin && u - mt * L::NCH != 0) continue;  // the tile's A is staged already
                 for (int ks = 0; ks < L::KST; ++ks, ++q) {
                     const int s = q % L::S;
                     if (q >= (uint32_t)L::S && !tc05::mbar_wait(&empty[s], ((q / L::S) - 1) & 1u, wl)) {
@@ -248,7 +257,9 @@ __global__ void __launch_bounds__(PT_THREADS, 1) tcp_gemm_kernel(GemmArgs g, int
     } else if (warp < PT_PROD) {
         // ---- producer ------------------------------------------------------------
         uint32_t q = 0;
-        for (int mt = blockIdx.x; mt < mtiles && !*abortf; mt += gridDim.x) {
+        for (int u = u_begin; u < u_end && !*abortf; ++u) {
+            const int mt = u / L::NCH;
+            if (u != u_begin && u - mt * L::NCH != 0) continue;  // the tile's A is staged already
             const int m0 = mt * 128;
             for (int ks = 0; ks < L::KST; ++ks, ++q) {
                 const int s = q % L::S;
@@ -289,8 +300,11 @@ __global__ void __launch_bounds__(PT_THREADS, 1) tcp_gemm_kernel(GemmArgs g, int
             const uint32_t idesc = tc05::idesc_i8(128, BN, true, true);
             uint32_t q = 0, a = 0;
             bool ok = true;
-            for (int mt = blockIdx.x; mt < mtiles && ok && !*abortf; mt += gridDim.x) {
-                for (int c = 0; c < L::NCH && ok; ++c, ++a) {
+            for (int u = u_begin; u < u_end && ok && !*abortf; ++u, ++a) {
+                const int mt = u / L::NCH, c = u - mt * L::NCH;
+                const bool first = u == u_begin || c == 0;           // the tile's stage arrives now
+                const bool last = u == u_end - 1 || c == L::NCH - 1;  // and is released after this unit
+                {
                     const int tb = a & 1;
                     if (a >= 2 && !tc05::mbar_wait(&acce[tb], ((a >> 1) - 1) & 1u, wl)) { ok = false; break; }
                     tc05::fence_after();
@@ -298,7 +312,7 @@ __global__ void __launch_bounds__(PT_THREADS, 1) tcp_gemm_kernel(GemmArgs g, int
                     for (int ks = 0; ks < L::KST; ++ks) {
                         const uint32_t qq = q + ks;
                         const int s = qq % L::S;
-                        if (c == 0 || L::KST > 1) {
+                        if (first || L::KST > 1) {
                             if (!tc05::mbar_wait(&full[s], (qq / L::S) & 1u, wl)) { ok = false; break; }
                             tc05::fence_proxy_async();
                             tc05::fence_after();
@@ -315,10 +329,10 @@ __global__ void __launch_bounds__(PT_THREADS, 1) tcp_gemm_kernel(GemmArgs g, int
                         if (L::KST > 1) tc05::commit(&empty[s]);
                     }
                     if (!ok) break;
-                    if (L::KST == 1 && c == L::NCH - 1) tc05::commit(&empty[q % L::S]);
+                    if (L::KST == 1 && last) tc05::commit(&empty[q % L::S]);
                     tc05::commit(&accf[tb]);
                 }
-                q += L::KST;
+                if (last) q += L::KST;
             }
             if (!ok) *abortf = 1;
             // Every MMA this thread issued has completed once `drain` flips.
@@ -331,7 +345,8 @@ __global__ void __launch_bounds__(PT_THREADS, 1) tcp_gemm_kernel(GemmArgs g, int
         const int row = quad * 32 + lane;
         const uint32_t lane_addr = tbase + ((uint32_t)(quad * 32) << 16);
         uint32_t a = 0;
-        for (int mt = blockIdx.x; mt < mtiles; mt += gridDim.x) {
+        for (int u = u_begin; u < u_end; ++u) {
+            const int mt = u / L::NCH, c = u - mt * L::NCH;
             const int grow = mt * 128 + row;
             const bool valid = ptma ? row < 98 : grow < m_lim;
             size_t orow = (size_t)grow;
@@ -357,7 +372,7 @@ __global__ void __launch_bounds__(PT_THREADS, 1) tcp_gemm_kernel(GemmArgs g, int
                         for (int j = 0; j < 8; ++j) rpre[i][j] = 0;
                 }
             }
-            for (int c = 0; c < L::NCH; ++c, ++a) {
+            {
                 const int tb = a & 1;
                 if (!tc05::mbar_wait(&accf[tb], (a >> 1) & 1u, wl)) {
                     *abortf = 1;
@@ -458,6 +473,7 @@ __global__ void __launch_bounds__(PT_THREADS, 1) tcp_gemm_kernel(GemmArgs g, int
                 tc05::fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&acce[tb]);
+                ++a;
             }
             if (stop || *abortf) break;
         }
@@ -482,7 +498,8 @@ cudaError_t launch_p(const GemmArgs &g, int m_max, int *err, int sms, cudaStream
     if (e != cudaSuccess) return e;
     // (the patch GEMM with TMA runs two 98-row tiles per image)
     const int tiles = EPI == EPI_PATCH && g.tma ? 2 * (m_max / 196) : (m_max + 127) / 128;
-    const int grid = tiles < sms ? tiles : sms;
+    const int units = tiles * PLayout<KDIM, N>::NCH;
+    const int grid = units < sms ? units : sms;
     if (grid <= 0) return cudaSuccess;
     CUtensorMap tm;
     if (g.tma) tm = *g.tma;
