@@ -40,7 +40,7 @@ INT8_SPEC_TOPS = 4500.0      # B200 dense int8 (NVIDIA datasheet, non-sparse)
 HBM_SPEC_GBS = 8000.0
 WEIGHT_BYTES = 5_830_000     # int8 weights + biases + LN + pos + selectors
 STAGES = {"ln1": 1, "qkv": 2, "attn": 3, "proj": 4, "ln2": 5, "fc1": 6, "fc2": 7, "selector": 8, "patch": 9,
-          "head": 10}
+          "head": 10, "ffn": 11}
 # GEMM stages: (K, N, residual bytes per row).  Algorithmic ops per row 2*K*N; HBM
 # bytes per row K (A) + N (output) + residual, plus the weights once per launch.
 GEMM_SHAPES = {"qkv": (192, 576, 0), "proj": (192, 192, 192), "fc1": (192, 768, 0), "fc2": (768, 192, 192),
@@ -105,6 +105,9 @@ def stage_work(stage, counts, launches_per_step):
             k, nn, r = GEMM_SHAPES[stage]
             ops += 2.0 * rows * k * nn
             byt += rows * (k + nn + r) + k * nn
+        elif stage == "ffn":  # FC1 + FC2 fused: LN2 rows and the residual in, block output out
+            ops += 2.0 * rows * 2 * 192 * 768
+            byt += rows * (192 + 192 + 192) + 2 * 192 * 768
         elif stage == "attn":
             ops += float((3 * 4 * 64 * n * n).sum())   # QK^T and P.V per head
             byt += rows * (576 + 192)                   # Q, K, V in; context out
@@ -489,7 +492,7 @@ def main():
     # Per-kernel breakdown of a step (every rank runs the same steps; no collective).
     stages = None
     launches_of = {"patch": 1, "head": 1, "selector": ns}
-    for k in ("ln1", "qkv", "attn", "proj", "ln2", "fc1", "fc2"):
+    for k in ("ln1", "qkv", "attn", "proj", "ln2", "fc1", "fc2", "ffn"):
         launches_of[k] = 12
 
     def local_step():

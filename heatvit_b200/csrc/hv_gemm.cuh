@@ -115,6 +115,8 @@ bool gemm_persistent_supported(int epi, int n, int k);
 // Tensor map of a row-major int8 A operand [rows][k] (k a multiple of 16) read as
 // 16-byte x 128-row boxes; rows past `rows` read as zero.  Returns 0 on success.
 int make_tmap_a(CUtensorMap *map, const void *base, int k, int rows);
+// The same with boxes of 16 bytes x box_rows rows (box_rows <= 256).
+int make_tmap_box(CUtensorMap *map, const void *base, int k, int rows, int box_rows);
 // Tensor map of NHWC images [images_n][224][224][3] for the patch GEMM's TMA
 // gather: 5-D boxes of one 16-byte K strip for 7 x 14 patches.  Returns 0 on
 // success, non-zero when the driver entry point is missing or `images` is not

@@ -27,12 +27,15 @@
 #include <cudaTypedefs.h>
 #include <string.h>
 
+#include "hv_epi.cuh"
 #include "hv_gemm.cuh"
 #include "hv_tc05.cuh"
 
 namespace hv {
 
 namespace {
+
+using namespace pg;
 
 constexpr int PT_PROD = 4;                       // producer warps
 constexpr int PT_MMA_WARP = PT_PROD;
@@ -63,75 +66,6 @@ struct PLayout {
     // At least 116 KB so that two CTAs never share an SM: each takes all 512 TMEM columns.
     static constexpr int SMEM = USED > 116 * 1024 ? USED : 116 * 1024;
 };
-
-// 32 contiguous bytes in one 256-bit store: whole 32-byte sectors, half the store
-// instructions of two 16-byte stores.  The address must be 32-byte aligned (row
-// strides of 192, 576 and 768 bytes, 32-column pieces).
-__device__ __forceinline__ void st_global_32B(void *p, const uint32_t (&w)[8]) {
-    asm volatile("st.global.v8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};\n" ::"l"(p), "r"(w[0]), "r"(w[1]),
-                 "r"(w[2]), "r"(w[3]), "r"(w[4]), "r"(w[5]), "r"(w[6]), "r"(w[7])
-                 : "memory");
-}
-
-// 32 contiguous bytes in one 256-bit read-only load (32-byte aligned address).
-__device__ __forceinline__ void ld_global_32B(const void *p, uint32_t (&w)[8]) {
-    asm volatile("ld.global.nc.v8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];\n"
-                 : "=r"(w[0]), "=r"(w[1]), "=r"(w[2]), "=r"(w[3]), "=r"(w[4]), "=r"(w[5]), "=r"(w[6]), "=r"(w[7])
-                 : "l"(p));
-}
-
-__device__ __forceinline__ void cp_async16(uint32_t saddr, const void *g, int src_bytes) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(saddr), "l"(g), "r"(src_bytes) : "memory");
-}
-__device__ __forceinline__ void mbar_expect_tx(uint64_t *mbar, uint32_t bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(tc05::smem_u32(mbar)), "r"(bytes)
-                 : "memory");
-}
-// One 16-byte x 128-row box of A at (x = k byte, y = row) into shared memory (no multicast).
-__device__ __forceinline__ void tma_load_a(uint32_t dst, const CUtensorMap *map, int x, int y, uint64_t *mbar) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];\n" ::
-            "r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(tc05::smem_u32(mbar))
-        : "memory");
-}
-
-// One 16-byte K strip of 7 patch rows x 14 patches (98 A rows, 1568 bytes) from the
-// NHWC images (5-D map [img][pr][ir][pc][48 bytes], see make_tmap_patch), no multicast.
-__device__ __forceinline__ void tma_load_patch(uint32_t dst, const CUtensorMap *map, int w0, int ir, int pr0, int img,
-                                               uint64_t *mbar) {
-    asm volatile(
-        "cp.async.bulk.tensor.5d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5, "
-        "%6}], [%7];\n" ::"r"(dst),
-        "l"(reinterpret_cast<uint64_t>(map)), "r"(w0), "r"(0), "r"(ir), "r"(pr0), "r"(img), "r"(tc05::smem_u32(mbar))
-        : "memory");
-}
-
-__device__ __forceinline__ void cp_arrive_noinc(uint64_t *mbar) {
-    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];\n" ::"r"(tc05::smem_u32(mbar)) : "memory");
-}
-__device__ __forceinline__ void mbar_arrive(uint64_t *mbar) {
-    asm volatile("{\n.reg .b64 st;\nmbarrier.arrive.shared::cta.b64 st, [%0];\n}\n" ::"r"(tc05::smem_u32(mbar))
-                 : "memory");
-}
-
-// One output element before the final int8 saturation (pack_sat8 applies it).
-// FAST: the 32-bit forms (gemm_epi_fast; for EPI_GELU, gelu_chain_fast2).
-template <int EPI, bool FAST>
-__device__ __forceinline__ int32_t epi_elem(int32_t acc, int32_t bb, int32_t ax, const EpiParams &e) {
-    if (EPI == EPI_GELU)
-        return FAST ? gelu_chain_fast2(acc + bb, e.gk) : gelu_chain((int64_t)acc + bb, e.gelu_sh_in, e.gelu_sh_out);
-    if (FAST) {
-        const int32_t y = rsa32(acc + bb, e.shift);
-        if (EPI == EPI_I8) return y;
-        const int32_t ys = sat8(y);
-        if (EPI == EPI_I8_RES) return rsa32(ax * (1 << e.add.sa) + ys * (1 << e.add.sb), e.add.sh);
-        return rsa32(ys * (1 << e.add.sa) + ax * (1 << e.add.sb), e.add.sh);  // patch: a = embedding, b = pos
-    }
-    const int32_t y = (int32_t)requant64((int64_t)acc + bb, e.shift, 8);
-    if (EPI == EPI_I8) return y;
-    if (EPI == EPI_I8_RES) return (int32_t)requant64(((int64_t)ax << e.add.sa) + ((int64_t)y << e.add.sb), e.add.sh, 8);
-    return (int32_t)requant64(((int64_t)y << e.add.sa) + ((int64_t)ax << e.add.sb), e.add.sh, 8);
-}
 
 template <int EPI, bool FAST, int KDIM, int N>
 __global__ void __launch_bounds__(PT_THREADS, 1) tcp_gemm_kernel(GemmArgs g, int *err,
@@ -409,65 +343,7 @@ __global__ void __launch_bounds__(PT_THREADS, 1) tcp_gemm_kernel(GemmArgs g, int
                     }
                     tc05::wait_ld();
                     uint32_t pk[8];
-                    bool slow = true;
-                    if (EPI == EPI_GELU && FAST && L::TABB > 0 && g.epi.gtab_mode == 2) {
-                        // exact bucket table over the whole window (see EpiParams)
-                        const GeluK &k = g.epi.gk;
-                        const int lo = g.epi.gtab_lo, last = g.epi.gtab_n - 1, kb = g.epi.gtab_k;
-                        const int msk = (1 << kb) - 1;
-                        const uint32_t *coarse = (const uint32_t *)stab;
-                        const int8_t *fine = stab + g.epi.gtab_fine;
-#pragma unroll
-                        for (int w = 0; w < 8; ++w) {
-                            int32_t o[4];
-#pragma unroll
-                            for (int b = 0; b < 4; ++b) {
-                                const int32_t x = (int32_t)v[w * 4 + b] + bv[w * 4 + b];
-                                const int32_t q = (x + k.hin + mulhi_s(x, k.ksgn)) >> k.sh_in;
-                                const int u = min(max(q - lo, 0), last);
-                                const uint32_t e = coarse[u >> kb];
-                                const int off = u & msk;
-                                const uint32_t pcut = e >> 16;
-                                o[b] = off >= (int)pcut ? (int32_t)(int8_t)(e >> 8) : (int32_t)(int8_t)e;
-                                if (pcut == 0xFFFFu) o[b] = fine[(int)((e & 0xFFFFu) << kb) + off];
-                            }
-                            pk[w] = pack_sat8(o[0], o[1], o[2], o[3]);
-                        }
-                        slow = false;
-                    } else if (EPI == EPI_GELU && FAST && L::TABB > 0 && g.epi.gtab_mode == 1) {
-                        // exact table of the GELU chain, valid for q in [elo, ehi)
-                        const GeluK &k = g.epi.gk;
-                        const int lo = g.epi.gtab_lo, last = g.epi.gtab_n - 1;
-                        const int elo = g.epi.gtab_elo, ehi = g.epi.gtab_ehi;
-                        bool esc = false;
-#pragma unroll
-                        for (int w = 0; w < 8; ++w) {
-                            int32_t o[4];
-#pragma unroll
-                            for (int b = 0; b < 4; ++b) {
-                                const int32_t x = (int32_t)v[w * 4 + b] + bv[w * 4 + b];
-                                const int32_t q = (x + k.hin + mulhi_s(x, k.ksgn)) >> k.sh_in;
-                                esc |= (q < elo) | (q >= ehi);
-                                o[b] = stab[min(max(q - lo, 0), last)];
-                            }
-                            pk[w] = pack_sat8(o[0], o[1], o[2], o[3]);
-                        }
-                        // every lane of an epilogue warp runs this loop (stores are guarded by valid)
-                        slow = __any_sync(0xffffffffu, esc);
-                    }
-                    if (slow) {
-#pragma unroll
-                        for (int w = 0; w < 8; ++w) {
-                            int32_t o[4];
-#pragma unroll
-                            for (int b = 0; b < 4; ++b) {
-                                const int j = w * 4 + b;
-                                const int32_t ax = (int8_t)((aux[w] >> (8 * b)) & 0xffu);
-                                o[b] = epi_elem<EPI, FAST>((int32_t)v[j], bv[j], ax, g.epi);
-                            }
-                            pk[w] = pack_sat8(o[0], o[1], o[2], o[3]);
-                        }
-                    }
+                    epi_piece32<EPI, FAST, (L::TABB > 0)>(v, bv, aux, g.epi, stab, pk);
                     if (valid) st_global_32B((int8_t *)g.out + orow * g.ldo + gcol0, pk);
                 }
                 tc05::fence_before();
@@ -591,12 +467,15 @@ int make_tmap_patch(CUtensorMap *map, const void *images, int images_n) {
     return r == CUDA_SUCCESS ? 0 : 2;
 }
 
-int make_tmap_a(CUtensorMap *map, const void *base, int k, int rows) {
+int make_tmap_a(CUtensorMap *map, const void *base, int k, int rows) { return make_tmap_box(map, base, k, rows, 128); }
+
+int make_tmap_box(CUtensorMap *map, const void *base, int k, int rows, int box_rows) {
     PFN_cuTensorMapEncodeTiled encode = tmap_encoder();
     if (!encode) return 1;
+    if ((uintptr_t)base % 16 != 0 || k % 16 != 0 || box_rows < 1 || box_rows > 256) return 3;
     const cuuint64_t dims[2] = {(cuuint64_t)k, (cuuint64_t)rows};
     const cuuint64_t strides[1] = {(cuuint64_t)k};
-    const cuuint32_t box[2] = {16, 128};
+    const cuuint32_t box[2] = {16, (cuuint32_t)box_rows};
     const cuuint32_t estr[2] = {1, 1};
     const CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(base), dims, strides, box, estr,
                               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,

@@ -71,6 +71,23 @@ cudaError_t launch_attention(const int8_t *qkv, const int32_t *offsets, int imag
                              const AttnParams &p, int may_be_short, int sms, int *err, const AttnPlan &plan,
                              cudaStream_t st);
 
+// The fused FFN (hv_ffn.cu): A = LN2 output [rows][192] (tensor map, 16 x 128
+// boxes), W1 = the K-major FC1 weights [768][192] (16 x 128 boxes), W2 = the
+// K-major FC2 weights [192][768] (16 x 192 boxes).  e1: FC1 bias and GELU chain
+// (fast: the persistent kernel's fast forms, gelu_chain_fast2 or the tables); e2:
+// FC2 bias, writeback shift and residual 2 (res = the block's y, add).  out
+// [rows][192] must not alias A or the residual.
+struct FfnArgs {
+    int m_host;
+    const int32_t *m_dev;
+    EpiParams e1, e2;
+    int8_t *out;
+    uint32_t wait_iters;  // test hooks, as in GemmArgs
+    int skip_tile;
+};
+cudaError_t launch_ffn(const FfnArgs &f, const CUtensorMap &tmA, const CUtensorMap &tmW1, const CUtensorMap &tmW2,
+                       int m_max, int *err, int sms, cudaStream_t st);
+
 // Device-resident selector weights and constants.
 // Exact output table of one GELU chain over the Q8.16 inputs q = rsa(v, sh_in) its
 // layer can reach; outside [lo, lo + n) the output is constant (clamped index):

@@ -102,6 +102,9 @@ struct BlockDev {
     int fc1_tab_mode, fc1_tab_k, fc1_tab_fine, fc1_tab_bytes;  // EpiParams gtab_* fields
     AlignAdd res1, res2;
     AttnParams attn;
+    // tensor maps of the K-major FC1 / FC2 weights for the fused FFN (ffn_ok)
+    CUtensorMap tm_w1, tm_w2;
+    int ffn_ok;
 };
 
 struct SelDev {
@@ -153,6 +156,7 @@ struct hv_model {
     int device = 0;
     int sms = 148;         // SM count: one persistent GEMM CTA per SM
     int persistent = 1;    // layer GEMMs on the persistent kernel (HV_GEMM_TILED=1 selects the per-tile one)
+    int fused_ffn = 1;     // FC1 + FC2 in one kernel (HV_FFN_UNFUSED=1: two persistent GEMMs)
     int has_patch = 0, has_head = 0, has_block[HV_BLOCKS] = {0};
     int used_sel = 0;  // selectors that actually run (strides of token counts / summaries)
     uint8_t *weights = nullptr;
@@ -480,6 +484,42 @@ int run_block(hv_model *m, int b, int images, const int32_t *off, int may_be_sho
         Prof pr(m, HV_STAGE_LN2, st);
         CUDA_TRY(launch_layernorm(m->Y, m->LN, rows_max, rows_dev, ln2, nullptr, off, images, m->warn, st));
         pr.end(st, rows_dev, 0);
+    }
+    if (m->fused_ffn && d.ffn_ok && m->tm_ln) {
+        // FC1 + GELU + FC2 + residual 2 in one kernel (hv_ffn.cu); HID stays on chip
+        Prof pr(m, HV_STAGE_FFN, st);
+        FfnArgs f;
+        memset(&f, 0, sizeof(f));
+        f.m_dev = rows_dev;
+        f.e1.bias = m->w<int32_t>(d.b1);
+        f.e1.bits_wide = d.fc1_wide;
+        f.e1.gelu_sh_in = d.fc1_sh_in;
+        f.e1.gelu_sh_out = d.fc1_sh_out;
+        f.e1.gelu_fast = d.fc1_fast;
+        f.e1.gelu_k2 = d.fc1_k2;
+        f.e1.gk = d.fc1_gk;
+        f.e1.gtab = d.fc1_tab_n > 0 ? m->w<int8_t>(d.fc1_tab) : nullptr;
+        f.e1.gtab_lo = d.fc1_tab_lo;
+        f.e1.gtab_n = d.fc1_tab_n;
+        f.e1.gtab_elo = d.fc1_tab_elo;
+        f.e1.gtab_ehi = d.fc1_tab_ehi;
+        f.e1.gtab_mode = d.fc1_tab_n > 0 ? d.fc1_tab_mode : 0;
+        f.e1.gtab_k = d.fc1_tab_k;
+        f.e1.gtab_fine = d.fc1_tab_fine;
+        f.e1.gtab_bytes = d.fc1_tab_bytes;
+        f.e1.fast = d.fc1_k2 || d.fc1_tab_n > 0;  // the persistent kernels' fast GELU forms
+        f.e2.bias = m->w<int32_t>(d.b2);
+        f.e2.shift = d.fc2_shift;
+        f.e2.bits_wide = d.fc2_wide;
+        f.e2.res = m->Y;
+        f.e2.add = d.res2;
+        f.e2.fast = gemm_epi_fast(EPI_I8_RES, f.e2);
+        f.out = m->X;
+        f.wait_iters = m->test_wait_iters;
+        f.skip_tile = m->test_skip_tile;
+        CUDA_TRY(launch_ffn(f, *m->tm_ln, d.tm_w1, d.tm_w2, rows_max, m->err, m->sms, st));
+        pr.end(st, rows_dev, 0);
+        return HV_OK;
     }
     {
         Prof pr(m, HV_STAGE_FC1, st);
@@ -1036,6 +1076,11 @@ int pack_model(hv_model *m, const hv_params *P) {
     m->weights_bytes = A.host.size();
     CUDA_TRY(cudaMemcpy(m->weights, A.host.data(), A.host.size(), cudaMemcpyHostToDevice));
     for (int b = 0; b < HV_BLOCKS; ++b) {
+        BlockDev &d = m->blocks[b];
+        d.ffn_ok = m->has_block[b] && make_tmap_box(&d.tm_w1, m->weights + d.w1, 192, HV_FFN, 128) == 0 &&
+                   make_tmap_box(&d.tm_w2, m->weights + d.w2, HV_FFN, 192, 192) == 0;
+    }
+    for (int b = 0; b < HV_BLOCKS; ++b) {
         const BlockDev &d = m->blocks[b];
         if (m->has_block[b] && d.fc1_tab_n > 0 && d.fc1_tab_mode == 1)
             CUDA_TRY(launch_gelu_table_fill((int8_t *)(m->weights + d.fc1_tab), d.fc1_tab_lo, d.fc1_tab_n, d.fc1_sh_out,
@@ -1123,6 +1168,8 @@ int hv_model_create(const hv_params *params, int device, hv_model **out) {
     {
         const char *t = getenv("HV_GEMM_TILED");
         m->persistent = (t && t[0] == '1') ? 0 : 1;
+        const char *u = getenv("HV_FFN_UNFUSED");
+        m->fused_ffn = (m->persistent && !(u && u[0] == '1')) ? 1 : 0;
         const char *g = getenv("HV_NO_GRAPH");
         m->use_graphs = (g && g[0] == '1') ? 0 : 1;
     }

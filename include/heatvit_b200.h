@@ -226,6 +226,7 @@ HV_API int hv_device_error(hv_model *model, int *code);
 #define HV_STAGE_SELECTOR 8
 #define HV_STAGE_PATCH 9
 #define HV_STAGE_HEAD 10
+#define HV_STAGE_FFN 11   /* FC1 + GELU + FC2 + residual 2 in one kernel (replaces FC1 / FC2) */
 
 /* Record a CUDA event pair around every launch of `stage` (0 disables) in the
  * following hv_infer_* calls; at most `max_launches` launches are recorded.
