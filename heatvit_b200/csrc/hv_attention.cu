@@ -251,19 +251,6 @@ __device__ __forceinline__ uint32_t piece_exp(uint32_t (&v)[16], int valid, int3
     return s8[0];
 }
 
-// round_div(2^32, S) for a row sum S in [65554, 2^25) (every term <= 65554 and at
-// least one equal to it, at most 224 columns): q0 from a single-precision quotient
-// (relative error below 2^-21, so within 1 of the true quotient, which is < 65520),
-// then the exact remainder r = 2^32 - q*S fixes q to floor(2^32 / S) and the
-// ties-away rounding adds one when 2r >= S.
-__device__ __forceinline__ uint32_t softmax_recip32(uint32_t S) {
-    int32_t q = (int32_t)__fdividef(4294967296.0f, __uint2float_rn(S));
-    int64_t r = ((int64_t)1 << 32) - (int64_t)q * S;
-    if (r < 0) { q -= 1; r += S; }
-    if (r >= (int64_t)S) { q += 1; r -= S; }
-    return (uint32_t)(2 * r >= (int64_t)S ? q + 1 : q);
-}
-
 // Largest of 16 values (the first `valid` when MASK), as a pairwise tree.
 template <bool MASK>
 __device__ __forceinline__ int32_t piece_max(const uint32_t (&v)[16], int valid) {

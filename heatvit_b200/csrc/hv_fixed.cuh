@@ -337,6 +337,19 @@ HV_DEV uint64_t softmax_recip(uint64_t s) {
     return q;
 }
 
+// round_div(2^32, S) for a softmax row sum S in [65554, 2^25) (every term <= 65554
+// and the row maximum's term equal to it, at most 224 columns): q0 from a single-precision quotient
+// (relative error below 2^-21, so within 1 of the true quotient, which is < 65520),
+// then the exact remainder r = 2^32 - q*S fixes q to floor(2^32 / S) and the
+// ties-away rounding adds one when 2r >= S.
+__device__ __forceinline__ uint32_t softmax_recip32(uint32_t S) {
+    int32_t q = (int32_t)__fdividef(4294967296.0f, __uint2float_rn(S));
+    int64_t r = ((int64_t)1 << 32) - (int64_t)q * S;
+    if (r < 0) { q -= 1; r += S; }
+    if (r >= (int64_t)S) { q += 1; r -= S; }
+    return (uint32_t)(2 * r >= (int64_t)S ? q + 1 : q);
+}
+
 // ratio = rsa(E * recip, 16); scaled = rsa(ratio * 65536, 16) == ratio.
 HV_DEV uint32_t softmax_ratio(uint32_t e, uint64_t recip) {
     return (uint32_t)(((uint64_t)e * recip + 32768u) >> 16);

@@ -124,7 +124,7 @@ __device__ __forceinline__ int32_t sel_gelu(int64_t v, int k2, const GeluK &k, i
 __device__ __forceinline__ int32_t keep_score(int32_t q0, int32_t q1) {
     const int32_t mx = max(q0, q1);
     const uint32_t e0 = softmax_exp_q16(q0 - mx), e1 = softmax_exp_q16(q1 - mx);
-    const uint64_t rc = softmax_recip((uint64_t)e0 + e1);
+    const uint64_t rc = softmax_recip32(e0 + e1);  // one term is exp(0): S in [65554, 131108]
     const uint32_t r1 = softmax_ratio(e1, rc);
     return (int32_t)(r1 < 65536u ? r1 : 65536u);
 }
@@ -211,11 +211,22 @@ __global__ void __launch_bounds__(THREADS) selector_kernel(
 
     // ---- global mean (selector.py:273-289) and head stats (358-367), the last reads
     // of the token rows before the score-layer tables take their place ----------------
-    if (tid < 96) {
-        const int h = tid >> 5, j = tid & 31;
-        int32_t t = 0;
-        for (int c = 0; c < C; ++c) t += local[(h * MAXC + c) * LSTR + j];
-        glob[h * 32 + j] = (int8_t)sat8((int32_t)round_div64(t, C));
+    {
+        // four threads per (head, lane) sum interleaved candidates, then one of them adds
+        // the four partial sums (shorter dependent chains than one thread over C)
+        int32_t *gpart = hs;  // head-score rows are free until the score MLP
+        if (tid < 384) {
+            const int q = tid / 96, hj = tid - q * 96;
+            const int h = hj >> 5, j = hj & 31;
+            int32_t t = 0;
+            for (int c = q; c < C; c += 4) t += local[(h * MAXC + c) * LSTR + j];
+            gpart[q * 96 + hj] = t;
+        }
+        __syncthreads();
+        if (tid < 96) {
+            const int32_t t = gpart[tid] + gpart[96 + tid] + gpart[192 + tid] + gpart[288 + tid];
+            glob[tid] = (int8_t)sat8((int32_t)round_div64(t, C));
+        }
     }
     for (int c = tid; c < C; c += THREADS) {
 #pragma unroll
@@ -387,17 +398,27 @@ __global__ void __launch_bounds__(THREADS) selector_kernel(
         if (flags[c] & 1) ((int4 *)(out + (size_t)(1 + kidx[c]) * 192))[ch] = ((const int4 *)(tok + (1 + c) * 192))[ch];
     }
     if (parts > 0) {
+        // Σ s·x[d] (or Σ x[d]) over the participants: thread (d, q) of 2 x 192 sums every
+        // other candidate (s <= 65536, |x| <= 128, at most 98 terms: int32 is exact), the
+        // two halves meet in shared memory (over the score layer-1 rows, dead by now)
         int8_t *prow = out + (size_t)(1 + kept) * 192;
-        for (int d = tid; d < 192; d += THREADS) {
-            long long num = 0;
+        int32_t *ppart = (int32_t *)(smem + OFF_H1);
+        if (tid < 384) {
+            const int q = tid / 192, d = tid - q * 192;
+            int32_t num = 0;
             if (pden == 0) {
-                for (int c = 0; c < C; ++c)
+                for (int c = q; c < C; c += 2)
                     if (flags[c] & 2) num += tok[(1 + c) * 192 + d];
             } else {
-                for (int c = 0; c < C; ++c)
-                    if (flags[c] & 2) num += (long long)fused[c] * tok[(1 + c) * 192 + d];
+                for (int c = q; c < C; c += 2)
+                    if (flags[c] & 2) num += fused[c] * (int32_t)tok[(1 + c) * 192 + d];
             }
-            prow[d] = (int8_t)sat8((int32_t)round_div64(num, pden == 0 ? parts : pden));
+            ppart[tid] = num;
+        }
+        __syncthreads();
+        if (tid < 192) {
+            const long long num = (long long)ppart[tid] + ppart[192 + tid];
+            prow[tid] = (int8_t)sat8((int32_t)round_div64(num, pden == 0 ? parts : pden));
         }
     }
     if (tid == 0) {
