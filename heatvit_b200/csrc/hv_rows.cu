@@ -698,8 +698,8 @@ cudaError_t launch_layernorm(const int8_t *x, int8_t *out, int rows_max, const i
     auto kern = p.split ? (p.out32 ? ln_kernel<true, true> : ln_kernel<true, false>)
                         : (p.out32 ? ln_kernel<false, true> : ln_kernel<false, false>);
     // One wave: as many CTAs as the GPU holds at once (3 per SM by the launch
-    // bounds), fewer when the worst-case rows need fewer 32-row passes.  The live
-    // row count is read on the device, which sizes each round's passes to it.
+    // bounds).  The live row count is read on the device, which sizes each round's
+    // passes to it.
     const int variant = (p.split ? 2 : 0) + (p.out32 ? 1 : 0);
     static int s_wave[16][4];  // per device and variant; 0 = not yet queried
     int dev = 0;
@@ -715,8 +715,11 @@ cudaError_t launch_layernorm(const int8_t *x, int8_t *out, int rows_max, const i
         wave = std::max(1, sms * per_sm);
         if (dev < 16) s_wave[dev][variant] = wave;
     }
-    const int rows_per_block = 8 * 32;  // 8 warps x 32 rows
-    const int blocks = std::min((rows_max + rows_per_block - 1) / rows_per_block, wave);
+    // The whole wave even when fewer 32-row passes would cover the rows: the kernel
+    // then picks shorter passes (4 rows per sub-pass, fewer sub-passes per warp), so a
+    // small batch finishes in the latency of a shorter pass; CTAs beyond the live rows
+    // exit at once.  Tiny calls (unit API) keep one CTA per 8 x 4 rows.
+    const int blocks = std::min((rows_max + 31) / 32, wave);
     return launch_pdl(kern, dim3(blocks), dim3(256), 0, st, x, out, rows_max, rows_dev, p, negvar_row, offsets, images,
                       warn);
 }
