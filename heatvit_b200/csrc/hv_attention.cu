@@ -20,18 +20,22 @@
 // and P is written block-diagonal (zero outside the row's own block), so one
 // P·V over all 128 stacked V rows gives each row its own head's context.
 //
-// Per unit (CTA of 4 warps, persistent over its units):
+// Per unit (CTA of 4 x SPL warps, persistent over its units; SPL = 1 for list A,
+// 4 for list B):
 //   1. K, V and Q are staged in shared memory with 16-byte cp.async copies in the
 //      no-swizzle canonical layout (hv_tc05.cuh); K and Q are K-major operands, V is
-//      the same byte layout read as an MN-major B operand (tokens along K).  The next
-//      unit's K/V load into the second buffer while this unit computes; its Q loads
-//      once this unit's P·V has consumed P (Q and P share a buffer).
+//      the same byte layout read as an MN-major B operand (tokens along K).  Each
+//      has one buffer: the next unit's K and Q are copied as soon as this unit's
+//      S = Q·Kᵀ has completed (during the softmax), its V as soon as this unit's
+//      P·V has (during the context writeback).
 //   2. One thread issues S = Q·Kᵀ (tcgen05.mma kind::i8, M = 128) into TMEM.
-//   3. Query row r is TMEM lane r and belongs to thread r: warp w owns lanes
-//      32w..32w+31 and reads its rows in 32-column pieces.  Each thread takes its
-//      row's max, exp terms and sum by itself (no cross-warp exchange), writes the
-//      exp terms back to TMEM, then its UQ0.8 probabilities to shared memory as the
-//      A operand of the next MMA.
+//   3. Query row r is TMEM lane r.  The SPL warps of lane quadrant r / 32 read the
+//      row in 16-column pieces dealt round-robin among them; each thread takes the
+//      max, exp terms and sum of its share of its row, the SPL partials of a row
+//      are combined through shared memory behind a named barrier of the quadrant's
+//      warps (with SPL = 1 the thread owns the whole row and nothing is exchanged),
+//      the exp terms go back to TMEM, then the UQ0.8 probabilities to shared memory
+//      as the A operand of the next MMA.
 //   4. ctx = P·V (unsigned A) into TMEM columns [0, 64), requantised and stored.
 // TMEM: 128 columns per CTA for list A (4 CTAs per SM), 256 for list B (2 per SM).
 #include <algorithm>

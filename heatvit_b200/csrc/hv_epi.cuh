@@ -55,6 +55,15 @@ __device__ __forceinline__ void tma_load_patch(uint32_t dst, const CUtensorMap *
         : "memory");
 }
 
+// One contiguous run of `bytes` (a multiple of 16; both addresses 16-byte aligned)
+// from global into shared memory by the bulk-copy engine, completing on `mbar` (no
+// multicast).
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void *src, uint32_t bytes, uint64_t *mbar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(dst),
+                 "l"(src), "r"(bytes), "r"(tc05::smem_u32(mbar))
+                 : "memory");
+}
+
 __device__ __forceinline__ void cp_arrive_noinc(uint64_t *mbar) {
     asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];\n" ::"r"(tc05::smem_u32(mbar)) : "memory");
 }
@@ -91,7 +100,23 @@ template <int EPI, bool FAST, bool TAB>
 __device__ __forceinline__ void epi_piece32(const uint32_t (&v)[32], const int32_t (&bv)[32], const uint32_t (&aux)[8],
                                             const EpiParams &e, const int8_t *stab, uint32_t (&pk)[8]) {
     bool slow = true;
-    if (EPI == EPI_GELU && FAST && TAB && e.gtab_mode == 2) {
+    if (EPI == EPI_GELU && FAST && TAB && e.gtab_mode == 3) {
+        // whole-window table (see EpiParams): five integer operations and one byte load
+        const GeluK &k = e.gk;
+        const int last = e.gtab_n - 1, c = e.gtab_c;
+#pragma unroll
+        for (int w = 0; w < 8; ++w) {
+            int32_t o[4];
+#pragma unroll
+            for (int b = 0; b < 4; ++b) {
+                const int32_t x = (int32_t)v[w * 4 + b] + bv[w * 4 + b];
+                const int32_t u = (x + c + mulhi_s(x, k.ksgn)) >> k.sh_in;
+                o[b] = stab[min(max(u, 0), last)];
+            }
+            pk[w] = pack_sat8(o[0], o[1], o[2], o[3]);
+        }
+        slow = false;
+    } else if (EPI == EPI_GELU && FAST && TAB && e.gtab_mode == 2) {
         // exact bucket table over the whole window (see EpiParams)
         const GeluK &k = e.gk;
         const int lo = e.gtab_lo, last = e.gtab_n - 1, kb = e.gtab_k;

@@ -10,9 +10,12 @@
 //     D2        += H · W2[128j : 128j + 128, :]        (TMEM columns 256..447)
 //   out = align_add(Y, requant(D2 + b2))               (residual 2)
 // so the 768 hidden bytes of a row never reach HBM.  Neither weight matrix fits in
-// shared memory beside the other, so both stream from L2 by TMA in 24 KB chunks
-// (W1: 128 hidden rows x 192; W2: 192 output rows x 128 hidden columns), each in a
-// two-slot ring.
+// shared memory beside the other, so both stream from L2 in 24 KB chunks (W1: 128
+// hidden rows x 192; W2: 192 output rows x 128 hidden columns), each in a two-slot
+// ring.  The model stores every chunk as the exact bytes of its shared-memory image
+// (FfnArgs::w1img / w2img), so one bulk copy moves a chunk: 16-byte-wide tensor
+// boxes would cost one copy request per row and 16-byte strip.  The tile's residual
+// rows (contiguous, 24 KB) arrive the same way, ahead of the FC2 epilogue.
 //
 // Roles (576 threads): warp 0 lane 0 issues every TMA load (A tiles, W1 and W2
 // chunks, in consumption order); warp 1 lane 0 issues the MMAs, FC1 of chunk j + 1
@@ -44,6 +47,7 @@ struct FLayout {
     static constexpr int W1_BYTES = CH * 192;   // W1 chunk: 12 strips of 16 B x 128 rows
     static constexpr int W2_BYTES = 192 * CH;   // W2 chunk: 8 strips of 16 B x 192 rows
     static constexpr int H_BYTES = 128 * CH;    // hidden chunk: 8 strips of 16 B x 128 rows
+    static constexpr int R_BYTES = 128 * 192;   // residual rows of the tile, row-major
     static constexpr int OFF_A = 0;
     static constexpr int OFF_W1 = OFF_A + 2 * A_BYTES;
     static constexpr int OFF_W2 = OFF_W1 + 2 * W1_BYTES;
@@ -51,26 +55,27 @@ struct FLayout {
     static constexpr int OFF_B1 = OFF_H + 2 * H_BYTES;
     static constexpr int OFF_B2 = OFF_B1 + 768 * 4;
     static constexpr int OFF_TAB = OFF_B2 + 192 * 4;
-    static constexpr int OFF_BAR = OFF_TAB + kGeluTableMax;
-    static constexpr int NBAR = 23;
+    static constexpr int OFF_R = OFF_TAB + kGeluTableMax;
+    static constexpr int OFF_BAR = OFF_R + R_BYTES;
+    static constexpr int NBAR = 25;
     static constexpr int SMEM = OFF_BAR + NBAR * 8 + 16;
 };
 static_assert(FLayout::SMEM <= 227 * 1024, "fused FFN shared memory");
 
 template <bool F1, bool F2, bool TAB>
 __global__ void __launch_bounds__(FF_THREADS, 1)
-    ffn_kernel(FfnArgs f, int *err, const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW1,
-               const __grid_constant__ CUtensorMap tmW2) {
+    ffn_kernel(FfnArgs f, int *err, const __grid_constant__ CUtensorMap tmA) {
     using L = FLayout;
     extern __shared__ __align__(1024) uint8_t smem[];
     uint8_t *sA = smem + L::OFF_A, *sW1 = smem + L::OFF_W1, *sW2 = smem + L::OFF_W2, *sH = smem + L::OFF_H;
     int32_t *sb1 = (int32_t *)(smem + L::OFF_B1), *sb2 = (int32_t *)(smem + L::OFF_B2);
     int8_t *stab = (int8_t *)(smem + L::OFF_TAB);
+    const uint8_t *sR = smem + L::OFF_R;
     uint64_t *bars = (uint64_t *)(smem + L::OFF_BAR);
     uint64_t *a_full = bars, *a_empty = bars + 2, *w1_full = bars + 4, *w1_empty = bars + 6;
     uint64_t *w2_full = bars + 8, *w2_empty = bars + 10, *acc1_full = bars + 12, *acc1_empty = bars + 14;
     uint64_t *hid_full = bars + 16, *hid_empty = bars + 18, *acc2_full = bars + 20, *acc2_empty = bars + 21;
-    uint64_t *drain = bars + 22;
+    uint64_t *drain = bars + 22, *r_full = bars + 23, *r_empty = bars + 24;
     uint32_t *tslot = (uint32_t *)(bars + L::NBAR);
     volatile int *abortf = (volatile int *)(tslot + 1);
 
@@ -97,6 +102,8 @@ __global__ void __launch_bounds__(FF_THREADS, 1)
         tc05::mbar_init(acc2_full, 1);
         tc05::mbar_init(acc2_empty, FF_EPI_WARPS);
         tc05::mbar_init(drain, 1);
+        tc05::mbar_init(r_full, 1);
+        tc05::mbar_init(r_empty, FF_EPI_WARPS);
         *abortf = 0;
         tc05::fence_mbar_init();
     }
@@ -121,8 +128,8 @@ __global__ void __launch_bounds__(FF_THREADS, 1)
     if (warp == 0) {
         // ---- producer: one thread issues every TMA load (no multicast) ------------------
         if (lane == 0) {
-            uint32_t qa = 0, q1 = 0, q2 = 0;
-            int la[2] = {-1, -1}, l1[2] = {-1, -1}, l2[2] = {-1, -1};  // last slot issued per stage
+            uint32_t qa = 0, q1 = 0, q2 = 0, qr = 0;
+            int la[2] = {-1, -1}, l1[2] = {-1, -1}, l2[2] = {-1, -1}, lr = -1;  // last slot issued per stage
             bool ok = true;
             for (int t = t_begin; t < t_end && ok && !*abortf; ++t) {
                 {
@@ -149,10 +156,8 @@ __global__ void __launch_bounds__(FF_THREADS, 1)
                     }
                     l1[s1] = (int)q1;
                     mbar_expect_tx(&w1_full[s1], L::W1_BYTES);
-#pragma unroll
-                    for (int kc = 0; kc < 12; ++kc)
-                        tma_load_a(tc05::smem_u32(sW1 + s1 * L::W1_BYTES + kc * (CH * 16)), &tmW1, kc * 16, j * CH,
-                                   &w1_full[s1]);
+                    bulk_load(tc05::smem_u32(sW1 + s1 * L::W1_BYTES), f.w1img + (size_t)j * L::W1_BYTES, L::W1_BYTES,
+                              &w1_full[s1]);
                     ++q1;
                     const int s2 = q2 & 1;
                     if (q2 >= 2 && !tc05::mbar_wait(&w2_empty[s2], ((q2 >> 1) - 1) & 1u, wl)) {
@@ -161,11 +166,22 @@ __global__ void __launch_bounds__(FF_THREADS, 1)
                     }
                     l2[s2] = (int)q2;
                     mbar_expect_tx(&w2_full[s2], L::W2_BYTES);
-#pragma unroll
-                    for (int kc = 0; kc < CH / 16; ++kc)
-                        tma_load_a(tc05::smem_u32(sW2 + s2 * L::W2_BYTES + kc * (192 * 16)), &tmW2, j * CH + kc * 16,
-                                   0, &w2_full[s2]);
+                    bulk_load(tc05::smem_u32(sW2 + s2 * L::W2_BYTES), f.w2img + (size_t)j * L::W2_BYTES, L::W2_BYTES,
+                              &w2_full[s2]);
                     ++q2;
+                    if (j == 1) {
+                        // the tile's residual rows, once the previous tile's FC2 epilogue
+                        // has read its own (by now long done: it precedes chunk 0's GELU)
+                        if (qr >= 1 && !tc05::mbar_wait(r_empty, (qr - 1) & 1u, wl)) {
+                            ok = false;
+                            break;
+                        }
+                        const uint32_t bytes = (uint32_t)min(128, m_lim - t * 128) * 192u;
+                        lr = (int)qr;
+                        mbar_expect_tx(r_full, bytes);
+                        bulk_load(tc05::smem_u32(sR), f.e2.res + (size_t)t * L::R_BYTES, bytes, r_full);
+                        ++qr;
+                    }
                 }
             }
             if (!ok) *abortf = 1;
@@ -177,6 +193,7 @@ __global__ void __launch_bounds__(FF_THREADS, 1)
                     if (l1[s] >= 0) tc05::mbar_wait(&w1_full[s], ((uint32_t)l1[s] >> 1) & 1u, FF_WAIT);
                     if (l2[s] >= 0) tc05::mbar_wait(&w2_full[s], ((uint32_t)l2[s] >> 1) & 1u, FF_WAIT);
                 }
+                if (lr >= 0) tc05::mbar_wait(r_full, (uint32_t)lr & 1u, FF_WAIT);
             }
         }
     } else if (warp == FF_MMA_WARP) {
@@ -295,21 +312,15 @@ __global__ void __launch_bounds__(FF_THREADS, 1)
                 ++h;
             }
             if (stop) break;
-            // residual bytes of this thread's pieces, requested before the accumulator wait
-            const int np = sub < 2 ? 2 : 1;  // pieces sub, sub + 4 (< 6)
-            uint32_t rpre[2][8];
-#pragma unroll
-            for (int i = 0; i < 2; ++i) {
-                if (valid && i < np) ld_global_32B(f.e2.res + (size_t)grow * 192 + (sub + 4 * i) * 32, rpre[i]);
-                else
-#pragma unroll
-                    for (int q = 0; q < 8; ++q) rpre[i][q] = 0;
-            }
-            if (!tc05::mbar_wait(acc2_full, tl & 1u, wl)) {
+            if (!tc05::mbar_wait(acc2_full, tl & 1u, wl) || !tc05::mbar_wait(r_full, tl & 1u, wl)) {
                 stop = true;
                 break;
             }
             tc05::fence_after();
+            // 32-column pieces sub and sub + 4 (< 6) of the 192 output columns: 32-byte
+            // stores fill whole sectors, which beats an even three-way split into
+            // 16-column pieces with 16-byte stores
+            const int np = sub < 2 ? 2 : 1;
 #pragma unroll
             for (int i = 0; i < 2; ++i) {
                 if (i < np) {
@@ -325,15 +336,21 @@ __global__ void __launch_bounds__(FF_THREADS, 1)
                         bv[4 * q4 + 2] = b4.z;
                         bv[4 * q4 + 3] = b4.w;
                     }
+                    const uint4 ra = *(const uint4 *)(sR + row * 192 + col0);
+                    const uint4 rb = *(const uint4 *)(sR + row * 192 + col0 + 16);
+                    const uint32_t aux[8] = {ra.x, ra.y, ra.z, ra.w, rb.x, rb.y, rb.z, rb.w};
                     tc05::wait_ld();
                     uint32_t p8[8];
-                    epi_piece32<EPI_I8_RES, F2, false>(v, bv, rpre[i], f.e2, stab, p8);
+                    epi_piece32<EPI_I8_RES, F2, false>(v, bv, aux, f.e2, stab, p8);
                     if (valid) st_global_32B(f.out + (size_t)grow * 192 + col0, p8);
                 }
             }
             tc05::fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(acc2_empty);
+            if (lane == 0) {
+                mbar_arrive(acc2_empty);  // D2 is read: FC2 of the next tile may start
+                mbar_arrive(r_empty);     // and the residual rows: the next tile's may land
+            }
         }
         if (stop) *abortf = 1;
     }
@@ -348,28 +365,26 @@ __global__ void __launch_bounds__(FF_THREADS, 1)
 }
 
 template <bool F1, bool F2, bool TAB>
-cudaError_t launch_t(const FfnArgs &f, const CUtensorMap &tmA, const CUtensorMap &tmW1, const CUtensorMap &tmW2,
-                     int grid, int *err, cudaStream_t st) {
+cudaError_t launch_t(const FfnArgs &f, const CUtensorMap &tmA, int grid, int *err, cudaStream_t st) {
     auto k = ffn_kernel<F1, F2, TAB>;
     cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, FLayout::SMEM);
     if (e != cudaSuccess) return e;
-    return launch_pdl(k, dim3(grid), dim3(FF_THREADS), FLayout::SMEM, st, f, err, tmA, tmW1, tmW2);
+    return launch_pdl(k, dim3(grid), dim3(FF_THREADS), FLayout::SMEM, st, f, err, tmA);
 }
 
 }  // namespace
 
-cudaError_t launch_ffn(const FfnArgs &f, const CUtensorMap &tmA, const CUtensorMap &tmW1, const CUtensorMap &tmW2,
-                       int m_max, int *err, int sms, cudaStream_t st) {
+cudaError_t launch_ffn(const FfnArgs &f, const CUtensorMap &tmA, int m_max, int *err, int sms, cudaStream_t st) {
     const int tiles = (m_max + 127) / 128;
     const int grid = tiles < sms ? tiles : sms;
     if (grid <= 0) return cudaSuccess;
     const bool f1 = f.e1.fast != 0, f2 = f.e2.fast != 0, tab = f1 && f.e1.gtab_n > 0;
-    if (f1 && f2) return tab ? launch_t<true, true, true>(f, tmA, tmW1, tmW2, grid, err, st)
-                             : launch_t<true, true, false>(f, tmA, tmW1, tmW2, grid, err, st);
-    if (f1) return tab ? launch_t<true, false, true>(f, tmA, tmW1, tmW2, grid, err, st)
-                       : launch_t<true, false, false>(f, tmA, tmW1, tmW2, grid, err, st);
-    return f2 ? launch_t<false, true, false>(f, tmA, tmW1, tmW2, grid, err, st)
-              : launch_t<false, false, false>(f, tmA, tmW1, tmW2, grid, err, st);
+    if (f1 && f2) return tab ? launch_t<true, true, true>(f, tmA, grid, err, st)
+                             : launch_t<true, true, false>(f, tmA, grid, err, st);
+    if (f1) return tab ? launch_t<true, false, true>(f, tmA, grid, err, st)
+                       : launch_t<true, false, false>(f, tmA, grid, err, st);
+    return f2 ? launch_t<false, true, false>(f, tmA, grid, err, st)
+              : launch_t<false, false, false>(f, tmA, grid, err, st);
 }
 
 }  // namespace hv

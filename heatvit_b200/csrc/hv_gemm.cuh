@@ -53,10 +53,16 @@ struct EpiParams {
     //  gtab_mode 2 (buckets of 2^gtab_k inputs): e = coarse[u >> k] (uint32 at gtab),
     //    p = e >> 16; p == 0xFFFF: out = fine[(e & 0xFFFF) * 2^k + (u & (2^k - 1))]
     //    (bytes at gtab + gtab_fine), else out = (int8)(u & (2^k - 1) >= p ? e >> 8 : e)
+    //  gtab_mode 3 (the table covers the whole window, so it is exact everywhere):
+    //    out = gtab[clamp((x + gtab_c + sgn(x)) >> sh_in, 0, gtab_n - 1)], x = acc + bias,
+    //    gtab_c = 2^(sh_in - 1) - gtab_lo * 2^sh_in, sgn(x) = -1 for x < 0 else 0: the
+    //    rounding shift and the offset by gtab_lo in one add (the host checks that
+    //    |x| + |gtab_c| + 1 stays below 2^31)
     const int8_t *gtab;
     int gtab_lo, gtab_n;      // gtab_n = input span; 0 = no table
     int gtab_elo, gtab_ehi;
     int gtab_mode, gtab_k, gtab_fine;
+    int gtab_c;
     int gtab_bytes;           // bytes to stage in shared memory, at most kGeluTableMax
     // patch (EPI_PATCH): pos [197][192], add = (a = embed, b = pos)
     const int8_t *pos;

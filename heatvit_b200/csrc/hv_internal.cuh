@@ -82,11 +82,13 @@ struct FfnArgs {
     const int32_t *m_dev;
     EpiParams e1, e2;
     int8_t *out;
+    // FC1 / FC2 weights in the kernel's shared-memory chunk layout: six 24,576-byte
+    // chunks each (w1img[j][kc 12][row 128][16 B], w2img[j][kc 8][row 192][16 B])
+    const int8_t *w1img, *w2img;
     uint32_t wait_iters;  // test hooks, as in GemmArgs
     int skip_tile;
 };
-cudaError_t launch_ffn(const FfnArgs &f, const CUtensorMap &tmA, const CUtensorMap &tmW1, const CUtensorMap &tmW2,
-                       int m_max, int *err, int sms, cudaStream_t st);
+cudaError_t launch_ffn(const FfnArgs &f, const CUtensorMap &tmA, int m_max, int *err, int sms, cudaStream_t st);
 
 // Device-resident selector weights and constants.
 // Exact output table of one GELU chain over the Q8.16 inputs q = rsa(v, sh_in) its

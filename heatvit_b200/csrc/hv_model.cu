@@ -102,9 +102,12 @@ struct BlockDev {
     int fc1_tab_mode, fc1_tab_k, fc1_tab_fine, fc1_tab_bytes;  // EpiParams gtab_* fields
     AlignAdd res1, res2;
     AttnParams attn;
-    // tensor maps of the K-major FC1 / FC2 weights for the fused FFN (ffn_ok)
-    CUtensorMap tm_w1, tm_w2;
-    int ffn_ok;
+    int fc1_tab_c;             // EpiParams gtab_c (table mode 3)
+    // FC1 / FC2 weights in the fused FFN's shared-memory chunk layout (hv_ffn.cu): per
+    // 128-column hidden chunk j, 24,576 contiguous bytes that one bulk copy moves
+    //   w1img[j][kc][r][b] = w1[16 kc + b][128 j + r]   (kc < 12, r < 128)
+    //   w2img[j][kc][r][b] = w2[128 j + 16 kc + b][r]   (kc < 8, r < 192)
+    size_t w1img, w2img;
 };
 
 struct SelDev {
@@ -485,7 +488,7 @@ int run_block(hv_model *m, int b, int images, const int32_t *off, int may_be_sho
         CUDA_TRY(launch_layernorm(m->Y, m->LN, rows_max, rows_dev, ln2, nullptr, off, images, m->warn, st));
         pr.end(st, rows_dev, 0);
     }
-    if (m->fused_ffn && d.ffn_ok && m->tm_ln) {
+    if (m->fused_ffn && m->tm_ln) {
         // FC1 + GELU + FC2 + residual 2 in one kernel (hv_ffn.cu); HID stays on chip
         Prof pr(m, HV_STAGE_FFN, st);
         FfnArgs f;
@@ -507,6 +510,7 @@ int run_block(hv_model *m, int b, int images, const int32_t *off, int may_be_sho
         f.e1.gtab_k = d.fc1_tab_k;
         f.e1.gtab_fine = d.fc1_tab_fine;
         f.e1.gtab_bytes = d.fc1_tab_bytes;
+        f.e1.gtab_c = d.fc1_tab_c;
         f.e1.fast = d.fc1_k2 || d.fc1_tab_n > 0;  // the persistent kernels' fast GELU forms
         f.e2.bias = m->w<int32_t>(d.b2);
         f.e2.shift = d.fc2_shift;
@@ -515,9 +519,11 @@ int run_block(hv_model *m, int b, int images, const int32_t *off, int may_be_sho
         f.e2.add = d.res2;
         f.e2.fast = gemm_epi_fast(EPI_I8_RES, f.e2);
         f.out = m->X;
+        f.w1img = m->w<int8_t>(d.w1img);
+        f.w2img = m->w<int8_t>(d.w2img);
         f.wait_iters = m->test_wait_iters;
         f.skip_tile = m->test_skip_tile;
-        CUDA_TRY(launch_ffn(f, *m->tm_ln, d.tm_w1, d.tm_w2, rows_max, m->err, m->sms, st));
+        CUDA_TRY(launch_ffn(f, *m->tm_ln, rows_max, m->err, m->sms, st));
         pr.end(st, rows_dev, 0);
         return HV_OK;
     }
@@ -541,6 +547,7 @@ int run_block(hv_model *m, int b, int images, const int32_t *off, int may_be_sho
         g.epi.gtab_k = d.fc1_tab_k;
         g.epi.gtab_fine = d.fc1_tab_fine;
         g.epi.gtab_bytes = d.fc1_tab_bytes;
+        g.epi.gtab_c = d.fc1_tab_c;
         CUDA_TRY(model_gemm(m, g, EPI_GELU, rows_max, st));
         pr.end(st, rows_dev, 0);
     }
@@ -886,6 +893,22 @@ int pack_model(hv_model *m, const hv_params *P) {
         d.w1 = A.add_t(q.w1, 192, HV_FFN, HV_FFN);
         d.b1 = A.add(q.b1, HV_FFN * 4);
         d.w2 = A.add_t(q.w2, HV_FFN, 192, 192);
+        {
+            std::vector<int8_t> i1((size_t)192 * HV_FFN), i2((size_t)192 * HV_FFN);
+            for (int j = 0; j < HV_FFN / 128; ++j) {
+                int8_t *c1 = i1.data() + (size_t)j * 24576, *c2 = i2.data() + (size_t)j * 24576;
+                for (int kc = 0; kc < 12; ++kc)
+                    for (int r = 0; r < 128; ++r)
+                        for (int b = 0; b < 16; ++b)
+                            c1[kc * 2048 + r * 16 + b] = q.w1[(size_t)(16 * kc + b) * HV_FFN + 128 * j + r];
+                for (int kc = 0; kc < 8; ++kc)
+                    for (int r = 0; r < 192; ++r)
+                        for (int b = 0; b < 16; ++b)
+                            c2[kc * 3072 + r * 16 + b] = q.w2[(size_t)(128 * j + 16 * kc + b) * 192 + r];
+            }
+            d.w1img = A.add(i1.data(), i1.size());
+            d.w2img = A.add(i2.data(), i2.size());
+        }
         d.b2 = A.add(q.b2, 192 * 4);
         d.ln1_xs = q.x_scale_exp;
         d.ln1_gs = q.gamma1_scale_exp;
@@ -915,7 +938,7 @@ int pack_model(hv_model *m, const hv_params *P) {
             d.fc1_tab_n = 0;
             d.fc1_tab_elo = INT32_MIN;
             d.fc1_tab_ehi = INT32_MAX;
-            d.fc1_tab_mode = d.fc1_tab_k = d.fc1_tab_fine = d.fc1_tab_bytes = 0;
+            d.fc1_tab_mode = d.fc1_tab_k = d.fc1_tab_fine = d.fc1_tab_bytes = d.fc1_tab_c = 0;
             if (!d.fc1_wide && d.fc1_sh_in >= 0 && d.fc1_sh_in <= 30 && vmax < ((int64_t)1 << 30)) {
                 const int64_t hin = d.fc1_sh_in > 0 ? (int64_t)1 << (d.fc1_sh_in - 1) : 0;
                 const int64_t qmax = (vmax + hin) >> d.fc1_sh_in;
@@ -946,6 +969,14 @@ int pack_model(hv_model *m, const hv_params *P) {
                         d.fc1_tab_ehi = tw.ehi;
                         d.fc1_tab_bytes = tw.n;
                         d.fc1_gk = make_gelu_k(d.fc1_sh_in, d.fc1_k2 ? d.fc1_sh_out : 0);
+                        // a table over the whole window is exact everywhere: fold the
+                        // offset into the rounding add when that stays in int32
+                        const int64_t c = hin - ((int64_t)tw.lo << d.fc1_sh_in);
+                        if (tw.elo == INT32_MIN && tw.ehi == INT32_MAX &&
+                            vmax + (c < 0 ? -c : c) + 1 < ((int64_t)1 << 31)) {
+                            d.fc1_tab_mode = 3;
+                            d.fc1_tab_c = (int32_t)c;
+                        }
                     } else if (bucket) {
                         bt.blob.resize((bt.blob.size() + 15) & ~(size_t)15, 0);
                         d.fc1_tab_mode = 2;
@@ -1076,13 +1107,8 @@ int pack_model(hv_model *m, const hv_params *P) {
     m->weights_bytes = A.host.size();
     CUDA_TRY(cudaMemcpy(m->weights, A.host.data(), A.host.size(), cudaMemcpyHostToDevice));
     for (int b = 0; b < HV_BLOCKS; ++b) {
-        BlockDev &d = m->blocks[b];
-        d.ffn_ok = m->has_block[b] && make_tmap_box(&d.tm_w1, m->weights + d.w1, 192, HV_FFN, 128) == 0 &&
-                   make_tmap_box(&d.tm_w2, m->weights + d.w2, HV_FFN, 192, 192) == 0;
-    }
-    for (int b = 0; b < HV_BLOCKS; ++b) {
         const BlockDev &d = m->blocks[b];
-        if (m->has_block[b] && d.fc1_tab_n > 0 && d.fc1_tab_mode == 1)
+        if (m->has_block[b] && d.fc1_tab_n > 0 && (d.fc1_tab_mode == 1 || d.fc1_tab_mode == 3))
             CUDA_TRY(launch_gelu_table_fill((int8_t *)(m->weights + d.fc1_tab), d.fc1_tab_lo, d.fc1_tab_n, d.fc1_sh_out,
                                             nullptr));
     }
