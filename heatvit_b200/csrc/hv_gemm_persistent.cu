@@ -45,7 +45,7 @@ constexpr int BN = 192;
 constexpr uint32_t PT_TMEM_COLS = 512;
 constexpr uint32_t PT_WAIT = 1u << 24;
 
-template <int KDIM, int N>
+template <int KDIM, int N, bool RES = false>
 struct PLayout {
     static constexpr int NCH = N / BN;                 // n-chunks per tile
     static constexpr int AK = KDIM == 192 ? 192 : 64;  // A stage width (bytes of K)
@@ -54,23 +54,35 @@ struct PLayout {
     static constexpr int S = KDIM == 192 ? (N == 768 ? 2 : 3) : 8;
     static constexpr int TABB = N == 768 ? kGeluTableMax : 0;  // exact GELU-chain table (EPI_GELU)
     static constexpr int A_STAGE = 128 * AK;
+    // residual rows staged beside each A stage (set by the kernel for EPI_I8_RES, K = 192)
+    static constexpr int R_STAGE = 128 * N;
     // An A stage is released after its tile's last n-chunk, or after its own k-step.
     static_assert(KST == 1 || NCH == 1, "streamed K with several n-chunks is not pipelined");
     static constexpr int OFF_B = 0;
     static constexpr int OFF_A = OFF_B + N * KDIM;
     static constexpr int OFF_BIAS = OFF_A + S * A_STAGE;
     static constexpr int OFF_TAB = OFF_BIAS + N * 4;
-    static constexpr int OFF_BAR = OFF_TAB + TABB;
-    static constexpr int NBAR = 2 * S + 5;
+    static constexpr int OFF_R = OFF_TAB + TABB;
+    static constexpr int OFF_BAR = OFF_R + (RES ? S * R_STAGE : 0);
+    static constexpr int NBAR = 3 * S + 5;
     static constexpr int USED = OFF_BAR + NBAR * 8 + 16;
     // At least 116 KB so that two CTAs never share an SM: each takes all 512 TMEM columns.
     static constexpr int SMEM = USED > 116 * 1024 ? USED : 116 * 1024;
 };
 
+// Residual rows through shared memory: the proj GEMM (one 192-column chunk, K = 192)
+// with a tensor-mapped A.  The producer copies a tile's 128 residual rows (contiguous,
+// 24 KB) with one bulk copy into the stage beside its A, completing on the same
+// `full` barrier, so they are on chip long before the epilogue needs them; the
+// epilogue warps release them (`rempty`).
+template <int EPI, int KDIM, int N>
+constexpr bool kResStaged = EPI == EPI_I8_RES && KDIM == 192 && N == 192;
+
 template <int EPI, bool FAST, int KDIM, int N>
 __global__ void __launch_bounds__(PT_THREADS, 1) tcp_gemm_kernel(GemmArgs g, int *err,
                                                                   const __grid_constant__ CUtensorMap tmA, int use_tma) {
-    using L = PLayout<KDIM, N>;
+    constexpr bool RS = kResStaged<EPI, KDIM, N>;
+    using L = PLayout<KDIM, N, RS>;
     extern __shared__ __align__(1024) uint8_t smem[];
     uint8_t *sB = smem + L::OFF_B;
     uint8_t *sA = smem + L::OFF_A;
@@ -80,7 +92,9 @@ __global__ void __launch_bounds__(PT_THREADS, 1) tcp_gemm_kernel(GemmArgs g, int
     uint64_t *accf = empty + L::S;
     uint64_t *acce = accf + 2;
     uint64_t *drain = acce + 2;
-    uint32_t *tslot = (uint32_t *)(drain + 1);
+    uint64_t *rempty = drain + 1;  // [S]: the epilogue has read the stage's residual rows
+    const uint8_t *sR = smem + L::OFF_R;
+    uint32_t *tslot = (uint32_t *)(rempty + L::S);
     volatile int *abortf = (volatile int *)(tslot + 1);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -100,6 +114,7 @@ __global__ void __launch_bounds__(PT_THREADS, 1) tcp_gemm_kernel(GemmArgs g, int
             tc05::mbar_init(&acce[b], 8);
         }
         tc05::mbar_init(drain, 1);
+        for (int s = 0; s < L::S; ++s) tc05::mbar_init(&rempty[s], 8);
         *abortf = 0;
         tc05::fence_mbar_init();
     }
@@ -140,6 +155,8 @@ __global__ void __launch_bounds__(PT_THREADS, 1) tcp_gemm_kernel(GemmArgs g, int
     tc05::fence_after();
     const uint32_t tbase = *tslot;
     const uint8_t *abase = (const uint8_t *)g.a.ptr;
+    // residual rows staged in shared memory (contiguous 16-byte-aligned rows needed)
+    const bool rs_on = RS && use_tma && g.ldo == N && (((uintptr_t)g.epi.res) & 15) == 0;
     const uint32_t wl = g.wait_iters ? g.wait_iters : PT_WAIT;  // pipeline waits; drains use PT_WAIT
 
     if (warp < PT_PROD && use_tma) {
@@ -161,10 +178,19 @@ __global__ void __launch_bounds__(PT_THREADS, 1) tcp_gemm_kernel(GemmArgs g, int
                         ok = false;
                         break;
                     }
+                    const bool rs = rs_on;
+                    if (rs && q >= (uint32_t)L::S && !tc05::mbar_wait(&rempty[s], ((q / L::S) - 1) & 1u, wl)) {
+                        ok = false;
+                        break;
+                    }
                     if (mt == g.skip_tile - 1) continue;  // test hook: this tile never arrives
                     last_q[s] = (int)q;
                     const uint32_t dst = tc05::smem_u32(sA + s * L::A_STAGE);
-                    mbar_expect_tx(&full[s], (ptma ? 98u : 128u) * L::AK);
+                    const uint32_t rbytes = rs ? (uint32_t)min(128, m_lim - mt * 128) * (uint32_t)g.ldo : 0u;
+                    mbar_expect_tx(&full[s], (ptma ? 98u : 128u) * L::AK + rbytes);
+                    if (rs)
+                        bulk_load(tc05::smem_u32(sR + s * L::R_STAGE), g.epi.res + (size_t)mt * 128 * g.ldo, rbytes,
+                                  &full[s]);
 #pragma unroll
                     for (int kc = 0; kc < L::AK / 16; ++kc) {
                         if (ptma) {
@@ -296,7 +322,7 @@ __global__ void __launch_bounds__(PT_THREADS, 1) tcp_gemm_kernel(GemmArgs g, int
             // overlaps the MMA.
             constexpr bool PRE = (EPI == EPI_I8_RES || EPI == EPI_PATCH) && L::NCH == 1;
             uint32_t rpre[BN / 64][8];
-            if (PRE) {
+            if (PRE && !rs_on) {
                 const int8_t *src = EPI == EPI_PATCH ? g.epi.pos + (pidx + 1) * 192 : g.epi.res + orow * g.ldo;
 #pragma unroll
                 for (int i = 0; i < BN / 64; ++i) {
@@ -308,7 +334,9 @@ __global__ void __launch_bounds__(PT_THREADS, 1) tcp_gemm_kernel(GemmArgs g, int
             }
             {
                 const int tb = a & 1;
-                if (!tc05::mbar_wait(&accf[tb], (a >> 1) & 1u, wl)) {
+                const int rsl = RS ? (int)(a % L::S) : 0;  // stage of this tile's residual rows
+                if (!tc05::mbar_wait(&accf[tb], (a >> 1) & 1u, wl) ||
+                    (rs_on && !tc05::mbar_wait(&full[rsl], (a / L::S) & 1u, wl))) {
                     *abortf = 1;
                     stop = true;
                     break;
@@ -322,7 +350,12 @@ __global__ void __launch_bounds__(PT_THREADS, 1) tcp_gemm_kernel(GemmArgs g, int
                     const int gcol0 = c * BN + col0;
                     // residual / positional bytes first, so their latency overlaps the TMEM read
                     uint32_t aux[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-                    if (PRE) {
+                    if (RS && rs_on) {
+                        const uint8_t *rr = sR + rsl * L::R_STAGE + row * N + gcol0;
+                        const uint4 ra = *(const uint4 *)rr, rb = *(const uint4 *)(rr + 16);
+                        aux[0] = ra.x; aux[1] = ra.y; aux[2] = ra.z; aux[3] = ra.w;
+                        aux[4] = rb.x; aux[5] = rb.y; aux[6] = rb.z; aux[7] = rb.w;
+                    } else if (PRE) {
 #pragma unroll
                         for (int j = 0; j < 8; ++j) aux[j] = rpre[cc][j];
                     } else if (EPI == EPI_I8_RES && valid) {
@@ -348,7 +381,10 @@ __global__ void __launch_bounds__(PT_THREADS, 1) tcp_gemm_kernel(GemmArgs g, int
                 }
                 tc05::fence_before();
                 __syncwarp();
-                if (lane == 0) mbar_arrive(&acce[tb]);
+                if (lane == 0) {
+                    mbar_arrive(&acce[tb]);
+                    if (rs_on) mbar_arrive(&rempty[rsl]);
+                }
                 ++a;
             }
             if (stop || *abortf) break;
@@ -368,7 +404,7 @@ __global__ void __launch_bounds__(PT_THREADS, 1) tcp_gemm_kernel(GemmArgs g, int
 template <int EPI, bool FAST, int KDIM, int N>
 cudaError_t launch_p(const GemmArgs &g, int m_max, int *err, int sms, cudaStream_t st) {
     auto kern = tcp_gemm_kernel<EPI, FAST, KDIM, N>;
-    constexpr int smem = PLayout<KDIM, N>::SMEM;
+    constexpr int smem = PLayout<KDIM, N, kResStaged<EPI, KDIM, N>>::SMEM;
     static_assert(smem <= 227 * 1024, "persistent GEMM shared memory");
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
