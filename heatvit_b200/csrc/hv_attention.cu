@@ -63,8 +63,8 @@ __device__ __forceinline__ int units_b(int n) { return n > 128 && n <= 224 ? 6 :
 // One CTA (1024 threads) lists every unit of the batch, image-major.  cnt[0], cnt[1]
 // = lengths of list A and list B.
 __global__ void __launch_bounds__(1024) attn_plan_kernel(const int32_t *__restrict__ offsets, int images,
-                                                          uint32_t *__restrict__ list_a,
-                                                          uint32_t *__restrict__ list_b, int32_t *__restrict__ cnt) {
+                                                          uint2 *__restrict__ list_a,
+                                                          uint2 *__restrict__ list_b, int32_t *__restrict__ cnt) {
     griddep_wait();
     griddep_launch();
     __shared__ int wsum[2][32];
@@ -97,15 +97,17 @@ __global__ void __launch_bounds__(1024) attn_plan_kernel(const int32_t *__restri
         }
         pa += sa - ca;  // exclusive position of this image's first unit
         pb += sb - cb;
+        // the image's first row and token count ride with every unit (row0 < 2^24)
+        const uint32_t rn = img < images ? ((uint32_t)offsets[img] << 8) | (uint32_t)n : 0u;
         if (ca == 1) {
-            list_a[pa] = unit_code(img, 0, 2, 0, 3);
+            list_a[pa] = make_uint2(unit_code(img, 0, 2, 0, 3), rn);
         } else if (ca == 2) {
-            list_a[pa] = unit_code(img, 0, 1, 0, 2);
-            list_a[pa + 1] = unit_code(img, 0, 1, 2, 1);
+            list_a[pa] = make_uint2(unit_code(img, 0, 1, 0, 2), rn);
+            list_a[pa + 1] = make_uint2(unit_code(img, 0, 1, 2, 1), rn);
         } else if (ca == 3) {
-            for (int h = 0; h < 3; ++h) list_a[pa + h] = unit_code(img, 0, 0, h, 1);
+            for (int h = 0; h < 3; ++h) list_a[pa + h] = make_uint2(unit_code(img, 0, 0, h, 1), rn);
         }
-        for (int u = 0; u < cb; ++u) list_b[pb + u] = unit_code(img, u / 3, 0, u % 3, 1);
+        for (int u = 0; u < cb; ++u) list_b[pb + u] = make_uint2(unit_code(img, u / 3, 0, u % 3, 1), rn);
         __syncthreads();
         if (tid == 0) {
             int ta = 0, tb = 0;
@@ -277,15 +279,17 @@ struct Unit {
     int row0, n;
 };
 
-__device__ __forceinline__ Unit decode_unit(uint32_t code, const int32_t *offsets) {
+// A list entry: {unit code, row0 << 8 | n} (attn_plan_kernel).
+__device__ __forceinline__ Unit decode_unit(uint2 e) {
+    const uint32_t code = e.x;
     Unit u;
     u.img = (int)(code >> 7);
     u.mt = (code >> 6) & 1;
     u.glog = (code >> 4) & 3;
     u.h0 = (code >> 2) & 3;
     u.nh = code & 3;
-    u.row0 = offsets[u.img];
-    u.n = offsets[u.img + 1] - u.row0;
+    u.row0 = (int)(e.y >> 8);
+    u.n = (int)(e.y & 0xffu);
     return u;
 }
 
@@ -330,10 +334,9 @@ __device__ __forceinline__ void cp_wait_all_but_newest() { asm volatile("cp.asyn
 
 template <bool FAST, class CFG>
 __global__ void __launch_bounds__(CFG::THREADS, CFG::PER_SM) attention_tc_kernel(const int8_t *__restrict__ qkv,
-                                                               const int32_t *__restrict__ offsets,
                                                                int8_t *__restrict__ ctx, AttnParams p,
                                                                int *__restrict__ err,
-                                                               const uint32_t *__restrict__ list,
+                                                               const uint2 *__restrict__ list,
                                                                const int32_t *__restrict__ count) {
     extern __shared__ __align__(1024) uint8_t smem[];
     uint8_t *sP = smem + CFG::OFF_P;
@@ -373,9 +376,13 @@ __global__ void __launch_bounds__(CFG::THREADS, CFG::PER_SM) attention_tc_kernel
 
     // cp.async groups, oldest first: [K, Q] of a unit (issued once the previous unit's
     // S = Q.K^T has completed), then [V] of it (once the previous unit's P.V has).
+    // The entry of the unit after the next is loaded one unit ahead, so that its
+    // latency hides behind a whole unit's work.
     Unit cur;
+    uint2 ahead = make_uint2(0, 0);
+    if ((int)blockIdx.x + stride < units) ahead = list[blockIdx.x + stride];
     if ((int)blockIdx.x < units) {
-        cur = decode_unit(list[blockIdx.x], offsets);
+        cur = decode_unit(list[blockIdx.x]);
         load_kv<CFG, 0>(qkv, cur, sK, tid);
         load_q<CFG>(qkv, cur, sQ, tid);
         cp_commit();
@@ -408,7 +415,8 @@ __global__ void __launch_bounds__(CFG::THREADS, CFG::PER_SM) attention_tc_kernel
         tc05::fence_after();
         // K and Q are consumed: the next unit's copies overlap this unit's softmax
         if (more) {
-            cur = decode_unit(list[ui + stride], offsets);
+            cur = decode_unit(ahead);
+            if (ui + 2 * stride < units) ahead = list[ui + 2 * stride];
             load_kv<CFG, 0>(qkv, cur, sK, tid);
             load_q<CFG>(qkv, cur, sQ, tid);
         }
@@ -567,12 +575,12 @@ cudaError_t launch_attn_plan(const int32_t *offsets, int images, const AttnPlan 
 }
 
 template <class CFG>
-cudaError_t launch_one(const int8_t *qkv, const int32_t *offsets, int8_t *ctx, const AttnParams &p, int *err,
-                       const uint32_t *list, const int32_t *count, int grid, cudaStream_t st) {
+cudaError_t launch_one(const int8_t *qkv, int8_t *ctx, const AttnParams &p, int *err,
+                       const uint2 *list, const int32_t *count, int grid, cudaStream_t st) {
     auto k = p.fast ? attention_tc_kernel<true, CFG> : attention_tc_kernel<false, CFG>;
     cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, CFG::SMEM);
     if (e != cudaSuccess) return e;
-    return launch_pdl(k, dim3(grid), dim3(CFG::THREADS), CFG::SMEM, st, qkv, offsets, ctx, p, err, list, count);
+    return launch_pdl(k, dim3(grid), dim3(CFG::THREADS), CFG::SMEM, st, qkv, ctx, p, err, list, count);
 }
 
 cudaError_t launch_attention(const int8_t *qkv, const int32_t *offsets, int images, int8_t *ctx,
@@ -582,15 +590,15 @@ cudaError_t launch_attention(const int8_t *qkv, const int32_t *offsets, int imag
     // List A: one warp per TMEM lane quadrant, double-buffered TMEM reads (four
     // CTAs of 4 warps per SM); list B: four warps per quadrant splitting each row's
     // pieces, single-buffered (two CTAs of 16 warps per SM, 64 registers).
-    const uint32_t *la = plan.list_a, *lb = plan.list_b;
+    const uint2 *la = plan.list_a, *lb = plan.list_b;
     const int32_t *ca = plan.cnt, *cb = plan.cnt + 1;
     if (may_be_short) {
         const int ga = std::min(images * 3, sms * 4);
-        cudaError_t e = launch_one<AttnCfg<128, 1, true>>(qkv, offsets, ctx, p, err, la, ca, ga, st);
+        cudaError_t e = launch_one<AttnCfg<128, 1, true>>(qkv, ctx, p, err, la, ca, ga, st);
         if (e != cudaSuccess) return e;
     }
     const int gb = std::min(images * 6, sms * 2);
-    return launch_one<AttnCfg<224, 4, false>>(qkv, offsets, ctx, p, err, lb, cb, gb, st);
+    return launch_one<AttnCfg<224, 4, false>>(qkv, ctx, p, err, lb, cb, gb, st);
 }
 
 }  // namespace hv

@@ -60,10 +60,11 @@ cudaError_t launch_gelu_table_fill(int8_t *tab, int32_t wlo, int32_t wn, int sh_
 
 // Work-unit lists of the attention kernel for one token layout (attn_plan_kernel in
 // hv_attention.cu): list_a [3 * images] (images of at most 128 tokens), list_b
-// [6 * images] (longer images), cnt [2] their lengths.  Rebuilt whenever the
-// offsets change (batch set-up, every selector).
+// [6 * images] (longer images), cnt [2] their lengths.  An entry is {unit code, the
+// image's first row << 8 | its token count}.  Rebuilt whenever the offsets change
+// (batch set-up, every selector).
 struct AttnPlan {
-    uint32_t *list_a, *list_b;
+    uint2 *list_a, *list_b;
     int32_t *cnt;
 };
 cudaError_t launch_attn_plan(const int32_t *offsets, int images, const AttnPlan &plan, cudaStream_t st);

@@ -313,7 +313,7 @@ int ensure_capacity(hv_model *m, int images, int i = 0) {
                      oPkg1 = take(images), oWarn = take(((size_t)images + 3) & ~(size_t)3), oErr = take(16),
                      oOL = take((size_t)images * HV_CLASSES * 4), oOT = take((size_t)images * (HV_MAX_SELECTORS + 1) * 4),
                      oOS = take((size_t)images * HV_MAX_SELECTORS * sizeof(hv_selector_summary)), oOW = take(images),
-                     oLA = take((size_t)images * 3 * 4), oLB = take((size_t)images * 6 * 4), oPC = take(16);
+                     oLA = take((size_t)images * 3 * 8), oLB = take((size_t)images * 6 * 8), oPC = take(16);
         uint8_t *base = nullptr;
         if (cudaMalloc(&base, total) != cudaSuccess)
             return fail(HV_ERR_NOMEM, "cannot allocate %zu bytes of scratch", total);
@@ -337,8 +337,8 @@ int ensure_capacity(hv_model *m, int images, int i = 0) {
         w.o_tc = (int32_t *)(base + oOT);
         w.o_sum = (hv_selector_summary *)(base + oOS);
         w.o_warn = base + oOW;
-        w.plan.list_a = (uint32_t *)(base + oLA);
-        w.plan.list_b = (uint32_t *)(base + oLB);
+        w.plan.list_a = (uint2 *)(base + oLA);
+        w.plan.list_b = (uint2 *)(base + oLB);
         w.plan.cnt = (int32_t *)(base + oPC);
         if (cudaMemset(w.err, 0, 16) != cudaSuccess) return fail(HV_ERR_CUDA, "cannot clear the error word");
         const int r = (int)rows;
