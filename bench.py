@@ -45,13 +45,12 @@ STAGES = {"ln1": 1, "qkv": 2, "attn": 3, "proj": 4, "ln2": 5, "fc1": 6, "fc2": 7
 # bytes per row K (A) + N (output) + residual, plus the weights once per launch.
 GEMM_SHAPES = {"qkv": (192, 576, 0), "proj": (192, 192, 192), "fc1": (192, 768, 0), "fc2": (768, 192, 192),
                "patch": (768, 192, 192), "head": (192, 1000, 0)}
-# DRAM bytes (read + write) per live row of one launch from the committed ncu
-# captures (profiles/): block 1 of a 1024-image step, 201,728 rows.  Traffic grows
-# with the rows of a launch.
-STAGE_TRAFFIC_PER_ROW = {"fc1": (38_966_016 + 100_830_720) / 201_728,
-                         "fc2": (193_862_912 + 24_387_584) / 201_728,
-                         "ln1": (38_799_616 + 1_387_776) / 201_728,
-                         "attn": (116_252_928 + 16_623_360) / 201_728}
+# DRAM bytes (read + write) per live row of one launch, from full-size ncu captures
+# (profiles/): block 1 of a 1024-image step, 201,728 rows (dram__bytes_read.sum +
+# dram__bytes_write.sum).  Traffic grows with the rows of a launch.
+STAGE_TRAFFIC_PER_ROW = {"ffn": (77_869_824 + 11_407_360) / 201_728,
+                         "attn": (116_340_992 + 20_178_688) / 201_728,
+                         "ln1": (38_799_616 + 1_387_776) / 201_728}
 
 
 def algorithmic_macs(counts):
@@ -399,7 +398,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--batch", type=int, default=1024, help="images per GPU per step")
     ap.add_argument("--variant", default="pruned", choices=["pruned", "unpruned"])
-    ap.add_argument("--profile-stage", default="attn", choices=sorted(STAGES))
+    ap.add_argument("--profile-stage", default="ffn", choices=sorted(STAGES))
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extras", action="store_true",
                     help="skip the config-3 leg, the stage breakdown and the parity check")

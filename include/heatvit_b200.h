@@ -243,8 +243,9 @@ HV_API int hv_profile_stop(hv_model *model, int *launches, double *total_ms, lon
  * No counterpart in the reference. */
 HV_API int hv_graph_kernels(hv_model *model, int *kernels);
 
-/* Test hook for the bounded-wait error path of the layer GEMMs (QKV, proj, FC1,
- * FC2, patch).  In later calls on this model their pipeline waits give up after
+/* Test hook for the bounded-wait error path of the layer GEMMs (QKV, proj, patch,
+ * and the fused FFN, or FC1 and FC2 when it is unfused).  In later calls on this
+ * model their pipeline waits give up after
  * `wait_iters` polls (0 = the default limit, about a second), and with
  * skip_tile >= 0 every such launch leaves the A tile of that index unloaded, so
  * the waits on it run out: the launch stops issuing work, waits (with the default
