@@ -136,6 +136,7 @@ struct SelParams {
     GeluK local_k, h1_k, h2_k, hw_k;
     // exact tables of the local, score layer-1 and layer-2 chains (mode 0: none)
     GeluTab tab_local, tab_h1, tab_h2;
+    int *err;                 // device error word: 3 when a bounded wait gave up
 };
 
 // Optional selector intermediates (token_selector API), image stride 196.

@@ -255,6 +255,7 @@ SelParams bind_sel(const hv_model *m, const SelDev &s) {
     p.tab_local.tab = p.tab_local.mode ? m->w<int8_t>(s.tab_local) : nullptr;
     p.tab_h1.tab = p.tab_h1.mode ? m->w<int8_t>(s.tab_h1) : nullptr;
     p.tab_h2.tab = p.tab_h2.mode ? m->w<int8_t>(s.tab_h2) : nullptr;
+    p.err = m->err;
     return p;
 }
 

@@ -14,6 +14,7 @@
 // kernel then prefix-sums the new counts and writes the packed ragged layout
 // that every later kernel consumes.
 #include "hv_internal.cuh"
+#include "hv_tc05.cuh"
 
 namespace hv {
 
@@ -21,20 +22,24 @@ namespace {
 
 constexpr int THREADS = 512;
 constexpr int MAXC = 196;
-constexpr int LSTR = 32;   // local / layer-1 row stride (read as two 16-byte words)
-constexpr int WSTR = 80;   // transposed 64-wide weight row stride: 16-byte rows, conflict-free per 8 lanes
-constexpr int W2STR = 48;  // transposed 32-wide weight row stride (same property)
+// Token rows and the two MLP activations live in the strip layout the tensor cores
+// read: byte k of row r at (k / 16) * STRIP + r * 16 + k % 16, 197 rows per strip
+// (no-swizzle K-major core matrices: LBO = STRIP, SBO = 128).
+constexpr int STRIP = 197 * 16;
+// Weights as B operands, per head, strip layout with 32 (16) rows per strip:
+// local [h][4 strips][32][16], layer 1 (its local half) [h][2][32][16], layer 2 [h][2][16][16].
+constexpr int LW_HEAD = 4 * 32 * 16, W1_HEAD = 2 * 32 * 16, W2_HEAD = 2 * 16 * 16;
 
 constexpr int OFF_TOK = 0;
-constexpr int SZ_TOK = 197 * 192;
-constexpr int OFF_LOCAL = OFF_TOK + SZ_TOK;
-constexpr int SZ_LOCAL = 3 * MAXC * LSTR;
+constexpr int SZ_TOK = 12 * STRIP;
+constexpr int OFF_LOCAL = OFF_TOK + SZ_TOK;     // local features [6 strips][197][16]
+constexpr int SZ_LOCAL = 6 * STRIP;
 constexpr int OFF_LWT = OFF_LOCAL + SZ_LOCAL;
-constexpr int SZ_LWT = 3 * 32 * WSTR;
+constexpr int SZ_LWT = 3 * LW_HEAD;
 constexpr int OFF_W1T = OFF_LWT + SZ_LWT;
-constexpr int SZ_W1T = 3 * 32 * WSTR;
+constexpr int SZ_W1T = 3 * W1_HEAD;
 constexpr int OFF_W2T = OFF_W1T + SZ_W1T;
-constexpr int SZ_W2T = 3 * 16 * W2STR;
+constexpr int SZ_W2T = 3 * W2_HEAD;
 constexpr int OFF_W3T = OFF_W2T + SZ_W2T;
 constexpr int SZ_W3T = 3 * 2 * 16;
 constexpr int OFF_G1 = (OFF_W3T + SZ_W3T + 15) & ~15;
@@ -54,9 +59,10 @@ constexpr int SZ_FLAGS = MAXC;  // bit0 keep, bit1 participant
 constexpr int OFF_STATS = (OFF_FLAGS + SZ_FLAGS + 15) & ~15;
 constexpr int SZ_STATS = MAXC * 3;
 constexpr int OFF_MISC = (OFF_STATS + SZ_STATS + 15) & ~15;
-constexpr int SZ_MISC = 128;  // [0] warn, [1] kept, [2] participants, [4..4+THREADS/32) scan
-constexpr int OFF_H1 = OFF_MISC + SZ_MISC;  // score layer-1 outputs [3][MAXC][LSTR]
-constexpr int SZ_H1 = 3 * MAXC * LSTR;
+constexpr int SZ_MISC = 128;  // [0] warn, [1] kept, [2] participants, [4..4+THREADS/32) scan,
+                              // [24] wait status, byte 112: mbarrier, byte 120: TMEM base
+constexpr int OFF_H1 = OFF_MISC + SZ_MISC;  // score layer-1 outputs [6 strips][197][16]
+constexpr int SZ_H1 = 6 * STRIP;
 constexpr int OFF_H2 = OFF_LOCAL;           // score layer-2 outputs [3][MAXC][16], over the dead local rows
 constexpr int SZ_H2 = 3 * MAXC * 16;
 static_assert(SZ_H2 <= SZ_LOCAL, "layer-2 outputs overlay the local features");
@@ -69,6 +75,22 @@ constexpr int OFF_TAB2 = OFF_TOK + kSelTabH1Bytes;
 static_assert(kSelTabH1Bytes + kSelTabH2Bytes <= SZ_TOK, "score-layer tables fit the token rows");
 static_assert(OFF_TABL % 16 == 0 && OFF_TAB2 % 16 == 0, "16-byte table staging");
 static_assert(2 * (SMEM_BYTES + 1024) <= 228 * 1024, "two selector CTAs per SM");
+static_assert(OFF_LOCAL % 16 == 0 && OFF_LWT % 16 == 0 && OFF_W1T % 16 == 0 && OFF_W2T % 16 == 0 &&
+                  OFF_H1 % 16 == 0 && OFF_MISC % 16 == 0,
+              "16-byte aligned tensor-core operands");
+// An M = 128 tile that starts at row 128 reads strip rows up to 255: past row 196 of
+// the last strip it reads the next region (garbage rows whose results are dropped),
+// which must stay inside the CTA's shared memory.
+static_assert(OFF_TOK + SZ_TOK + 59 * 16 <= SMEM_BYTES && OFF_LOCAL + SZ_LOCAL + 59 * 16 <= SMEM_BYTES &&
+                  OFF_H1 + SZ_H1 + 59 * 16 <= SMEM_BYTES,
+              "tile overrun stays in shared memory");
+constexpr uint32_t SEL_WAIT = 1u << 24;
+constexpr uint32_t SEL_TMEM_COLS = 256;  // two CTAs per SM
+
+// Address of byte k of row r in a strip-layout array.
+__device__ __forceinline__ int8_t *strip_at(int8_t *base, int r, int k) {
+    return base + (k >> 4) * STRIP + r * 16 + (k & 15);
+}
 
 __device__ __forceinline__ int32_t sat_q016(int64_t v) { return (int32_t)(v < 0 ? 0 : (v > 65536 ? 65536 : v)); }
 
@@ -76,20 +98,6 @@ __device__ __forceinline__ int32_t sat_q016(int64_t v) { return (int32_t)(v < 0 
 __device__ __forceinline__ void stage_tab(const GeluTab &t, int8_t *dst, int tid) {
     if (!t.mode) return;
     for (int i = tid; i < t.bytes / 16; i += THREADS) ((int4 *)dst)[i] = ((const int4 *)t.tab)[i];
-}
-
-// GELU chain output from its exact table (GeluTab) staged at s; v = acc + bias with
-// |v| + 2^(sh_in-1) < 2^31 (host-checked).
-__device__ __forceinline__ int32_t tab_gelu(int32_t v, const GeluTab &t, const int8_t *s) {
-    const int32_t q = t.sh_in ? rsa32(v, t.sh_in) : v;
-    const int u = min(max(q - t.lo, 0), t.n - 1);
-    if (t.mode == 1) return s[u];
-    const uint32_t e = ((const uint32_t *)s)[u >> t.k];
-    const int off = u & ((1 << t.k) - 1);
-    const uint32_t pc = e >> 16;
-    int32_t o = off >= (int)pc ? (int32_t)(int8_t)(e >> 8) : (int32_t)(int8_t)e;
-    if (pc == 0xFFFFu) o = s[t.fine + (int)((e & 0xFFFFu) << t.k) + off];
-    return o;
 }
 
 // acc + a · b over W 16-byte words of packed int8 (shared memory, 16-byte aligned).
@@ -129,6 +137,49 @@ __device__ __forceinline__ int32_t keep_score(int32_t q0, int32_t q1) {
     return (int32_t)(r1 < 65536u ? r1 : 65536u);
 }
 
+// One selector activation in a form fixed per layer (A = 1, 2: exact table of that
+// mode; 0: the GELU chain), so an epilogue's 16 unrolled elements are one short
+// straight-line path rather than every form inlined per element.
+struct SelAct {
+    const GeluTab *tab;
+    const int8_t *s;  // staged table
+    int k2, fast, sh_in, sh_out;
+    const GeluK *k;
+};
+template <int A>
+__device__ __forceinline__ int32_t sel_act(int64_t v, const SelAct &a) {
+    if (A == 0) return sel_gelu(v, a.k2, *a.k, a.fast, a.sh_in, a.sh_out);
+    const GeluTab &t = *a.tab;
+    const int32_t q = t.sh_in ? rsa32((int32_t)v, t.sh_in) : (int32_t)v;
+    const int u = min(max(q - t.lo, 0), t.n - 1);
+    if (A == 1) return a.s[u];
+    const uint32_t e = ((const uint32_t *)a.s)[u >> t.k];
+    const int off = u & ((1 << t.k) - 1);
+    const uint32_t pc = e >> 16;
+    int32_t o = off >= (int)pc ? (int32_t)(int8_t)(e >> 8) : (int32_t)(int8_t)e;
+    if (pc == 0xFFFFu) o = a.s[t.fine + (int)((e & 0xFFFFu) << t.k) + off];
+    return o;
+}
+// 16 outputs of one TMEM piece: act(acc + bias) packed as 16 int8 bytes.
+template <int A, class B>
+__device__ __forceinline__ uint4 sel_piece(const uint32_t (&v)[16], B &&bias, const SelAct &a) {
+    uint32_t pk[4];
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+        int32_t o[4];
+#pragma unroll
+        for (int b = 0; b < 4; ++b) o[b] = sel_act<A>((int64_t)(int32_t)v[4 * w + b] + bias(4 * w + b), a);
+        pk[w] = pack_sat8(o[0], o[1], o[2], o[3]);
+    }
+    return make_uint4(pk[0], pk[1], pk[2], pk[3]);
+}
+template <class B>
+__device__ __forceinline__ uint4 sel_piece_any(int mode, const uint32_t (&v)[16], B &&bias, const SelAct &a) {
+    if (mode == 1) return sel_piece<1>(v, bias, a);
+    if (mode == 2) return sel_piece<2>(v, bias, a);
+    return sel_piece<0>(v, bias, a);
+}
+
 __global__ void __launch_bounds__(THREADS) selector_kernel(
     const int8_t *__restrict__ x, const int32_t *__restrict__ offsets, const uint8_t *__restrict__ pkg_in,
     SelParams p, int8_t *__restrict__ stage, int32_t *__restrict__ counts_out, uint8_t *__restrict__ pkg_out,
@@ -163,7 +214,7 @@ __global__ void __launch_bounds__(THREADS) selector_kernel(
     const int pkg = pkg_in ? (pkg_in[img] != 0) : 0;
     int8_t *out = stage + (size_t)img * 197 * 192;
 
-    if (tid < 16) misc[tid] = 0;
+    if (tid < 26) misc[tid] = 0;
     if (C < 1) {  // selector.py:513-514 needs CLS plus a candidate; pass the row through
         if (tid < 12) ((int4 *)out)[tid] = ((const int4 *)(x + (size_t)row0 * 192))[tid];
         if (tid == 0) {
@@ -173,40 +224,107 @@ __global__ void __launch_bounds__(THREADS) selector_kernel(
         return;
     }
 
-    // ---- load tokens and weights ------------------------------------------------
-    for (int c = tid; c < n * 12; c += THREADS) ((int4 *)tok)[c] = ((const int4 *)(x + (size_t)row0 * 192))[c];
-    for (int c = tid; c < 3 * 32 * 16; c += THREADS) {
-        const int row = c >> 4, w = c & 15;
-        *(int32_t *)(lwt + row * WSTR + 4 * w) = ((const int32_t *)p.local_wt)[c];
-        *(int32_t *)(w1t + row * WSTR + 4 * w) = ((const int32_t *)p.w1t)[c];
+    // ---- load tokens (strip layout) and weights (per-head B operands) --------------
+    for (int c = tid; c < n * 12; c += THREADS)
+        *(int4 *)(tok + (c % 12) * STRIP + (c / 12) * 16) = ((const int4 *)(x + (size_t)row0 * 192))[c];
+    for (int c = tid; c < 3 * 32 * 4; c += THREADS) {  // local_wt [h][j][64]: 4 chunks per row
+        const int hj = c >> 2, k4 = c & 3, h = hj >> 5, j = hj & 31;
+        *(int4 *)(lwt + h * LW_HEAD + k4 * 512 + j * 16) = ((const int4 *)p.local_wt)[c];
     }
-    for (int c = tid; c < 3 * 16 * 8; c += THREADS) {
-        const int row = c >> 3, w = c & 7;
-        *(int32_t *)(w2t + row * W2STR + 4 * w) = ((const int32_t *)p.w2t)[c];
+    for (int c = tid; c < 3 * 32 * 2; c += THREADS) {  // w1t [h][j][0..31]: the local half
+        const int hj = c >> 1, k2 = c & 1, h = hj >> 5, j = hj & 31;
+        *(int4 *)(w1t + h * W1_HEAD + k2 * 512 + j * 16) = ((const int4 *)p.w1t)[hj * 4 + k2];
+    }
+    for (int c = tid; c < 3 * 16 * 2; c += THREADS) {  // w2t [h][m][32]
+        const int hm = c >> 1, k2 = c & 1, h = hm >> 4, m = hm & 15;
+        *(int4 *)(w2t + h * W2_HEAD + k2 * 256 + m * 16) = ((const int4 *)p.w2t)[c];
     }
     if (tid < 24) ((int32_t *)w3t)[tid] = ((const int32_t *)p.w3t)[tid];
     stage_tab(p.tab_local, tabl, tid);
-    __syncthreads();
-
-    // ---- local MLP: local[h][c][j] ------------------------------------------------
-    for (int idx = tid; idx < 3 * C * 32; idx += THREADS) {
-        const int j = idx & 31;
-        int h, c;
-        split_hc(idx >> 5, C, h, c);
-        const int32_t acc = dot16<4>(tok + (1 + c) * 192 + 64 * h, lwt + (h * 32 + j) * WSTR, 0);
-        const int32_t lb = p.local_b[h * 32 + j];
-        local[(h * MAXC + c) * LSTR + j] =
-            (int8_t)(p.tab_local.mode ? tab_gelu(acc + lb, p.tab_local, tabl)
-                                      : sel_gelu((int64_t)acc + lb, p.local_k2, p.local_k, p.local_fast, p.local_sh_in,
-                                                 p.local_sh_out));
+    uint64_t *bar = (uint64_t *)((uint8_t *)misc + 112);
+    uint32_t *tslot = (uint32_t *)((uint8_t *)misc + 120);
+    volatile int *wstat = (volatile int *)(misc + 24);
+    if (tid < 32) {
+        tc05::tmem_alloc(tslot, SEL_TMEM_COLS);
+        tc05::tmem_relinquish();
     }
+    if (tid == 0) {
+        tc05::mbar_init(bar, 1);
+        tc05::fence_mbar_init();
+    }
+    tc05::fence_proxy_async();  // the operands written above are read by the tensor cores
+    tc05::fence_before();
+    __syncthreads();
+    tc05::fence_after();
+    const uint32_t tbase = *tslot;
+    const int lane = tid & 31, warp = tid >> 5, quad = warp & 3, part = warp >> 2;
+    const int tiles = (n + 127) >> 7;  // M = 128 tiles of token rows (row 0 = CLS, dropped)
+    const uint32_t lane_base = tbase + ((uint32_t)(quad * 32) << 16);
+    uint32_t phase = 0;
+    // One layer: thread 0 issues `issue` (the tensor-core work) and commits; every
+    // thread learns whether it completed in time (bounded wait, then a barrier).
+    auto mma_layer = [&](auto &&issue) -> bool {
+        if (tid == 0) {
+            tc05::fence_after();
+            issue();
+            tc05::commit(bar);
+            const bool ok = tc05::mbar_wait(bar, phase, SEL_WAIT);
+            *wstat = ok ? 0 : 1;
+            if (!ok) {
+                misc[25] = (int)phase;  // the parity to drain before TMEM is released
+                if (p.err) atomicExch(p.err, 3);
+            }
+        }
+        phase ^= 1;
+        __syncthreads();
+        tc05::fence_after();
+        return *wstat == 0;
+    };
+    const uint32_t id32 = tc05::idesc_i8(128, 32, true, true), id16 = tc05::idesc_i8(128, 16, true, true);
+    const uint32_t tok_u = tc05::smem_u32(tok), loc_u = tc05::smem_u32(local), lwt_u = tc05::smem_u32(lwt);
+    const uint32_t w1t_u = tc05::smem_u32(w1t), w2t_u = tc05::smem_u32(w2t);
+    int8_t *h1s = (int8_t *)(smem + OFF_H1);
+    int8_t *h2s = (int8_t *)(smem + OFF_H2);
+    const uint32_t h1_u = tc05::smem_u32(h1s);
+    bool ok = true;
+    const SelAct act_l{&p.tab_local, tabl, p.local_k2, p.local_fast, p.local_sh_in, p.local_sh_out, &p.local_k};
+    const SelAct act_1{&p.tab_h1, tab1, p.h1_k2, p.h1_fast, p.h1_sh_in, p.h1_sh_out, &p.h1_k};
+    const SelAct act_2{&p.tab_h2, tab2, p.h2_k2, p.h2_fast, p.h2_sh_in, p.h2_sh_out, &p.h2_k};
+
+    // ---- local MLP (selector.py:253-270): per head [n x 64] . [64 x 32] on tcgen05 ------
+    ok = mma_layer([&] {
+        for (int t = 0; t < tiles; ++t)
+            for (int h = 0; h < 3; ++h)
+                for (int k = 0; k < 2; ++k)
+                    tc05::mma_i8_ss(tbase + t * 96 + h * 32,
+                                    tc05::smem_desc(tok_u + (4 * h + 2 * k) * STRIP + t * 2048, STRIP, 128),
+                                    tc05::smem_desc(lwt_u + h * LW_HEAD + 2 * k * 512, 512, 128), id32, k);
+    });
+    // epilogue: thread = token row (TMEM lane), pieces of 16 columns (head pc / 2,
+    // outputs 16 (pc % 2) ..) dealt to the quadrant's four warps
+    if (ok)
+        for (int t = 0; t < tiles; ++t) {
+            const int r = t * 128 + quad * 32 + lane;
+            for (int pc = part; pc < 6; pc += 4) {
+                uint32_t v[16];
+                tc05::ld16(lane_base + t * 96 + pc * 16, v);
+                tc05::wait_ld_regs(v);
+                if (r >= 1 && r < n) {
+                    const int32_t *lb = p.local_b + pc * 16;  // head pc / 2, outputs 16 (pc % 2) ..
+                    *(uint4 *)(local + pc * STRIP + r * 16) =
+                        sel_piece_any(p.tab_local.mode, v, [&](int i) { return (int64_t)lb[i]; }, act_l);
+                }
+            }
+        }
+    tc05::fence_proxy_async();
+    tc05::fence_before();
     __syncthreads();
     if (dbg.local)  // exported now: the layer-2 outputs overwrite these rows later
         for (int i = tid; i < 3 * C * 32; i += THREADS) {
             const int j = i & 31;
             int h, c;
             split_hc(i >> 5, C, h, c);
-            dbg.local[(((size_t)img * 3 + h) * MAXC + c) * 32 + j] = local[(h * MAXC + c) * LSTR + j];
+            dbg.local[(((size_t)img * 3 + h) * MAXC + c) * 32 + j] = *strip_at(local, 1 + c, h * 32 + j);
         }
 
     // ---- global mean (selector.py:273-289) and head stats (358-367), the last reads
@@ -217,9 +335,9 @@ __global__ void __launch_bounds__(THREADS) selector_kernel(
         int32_t *gpart = hs;  // head-score rows are free until the score MLP
         if (tid < 384) {
             const int q = tid / 96, hj = tid - q * 96;
-            const int h = hj >> 5, j = hj & 31;
             int32_t t = 0;
-            for (int c = q; c < C; c += 4) t += local[(h * MAXC + c) * LSTR + j];
+            const int8_t *col = strip_at(local, 0, hj);
+            for (int c = q; c < C; c += 4) t += col[(1 + c) * 16];
             gpart[q * 96 + hj] = t;
         }
         __syncthreads();
@@ -231,11 +349,10 @@ __global__ void __launch_bounds__(THREADS) selector_kernel(
     for (int c = tid; c < C; c += THREADS) {
 #pragma unroll
         for (int h = 0; h < 3; ++h) {
-            const int4 *trow = (const int4 *)(tok + (1 + c) * 192 + 64 * h);
             int32_t t = 0;
 #pragma unroll
             for (int w = 0; w < 4; ++w) {
-                const int4 x4 = trow[w];
+                const int4 x4 = *(const int4 *)(tok + (4 * h + w) * STRIP + (1 + c) * 16);
                 t = __dp4a(x4.x, 0x01010101, t);
                 t = __dp4a(x4.y, 0x01010101, t);
                 t = __dp4a(x4.z, 0x01010101, t);
@@ -248,38 +365,65 @@ __global__ void __launch_bounds__(THREADS) selector_kernel(
     stage_tab(p.tab_h1, tab1, tid);
     stage_tab(p.tab_h2, tab2, tid);
     if (tid < 96) {
+        // the global half of layer 1, once per image (W1 rows read from global memory)
         const int h = tid >> 5, j = tid & 31;
         int32_t acc = 0;
-        const int8_t *wrow = w1t + (h * 32 + j) * WSTR + 32;
+        const int8_t *wrow = p.w1t + (h * 32 + j) * 64 + 32;
         for (int k = 0; k < 32; ++k) acc += (int32_t)glob[h * 32 + k] * wrow[k];
         g1[h * 32 + j] = (int64_t)acc + p.b1[h * 32 + j];
     }
     __syncthreads();
 
-    // ---- score MLP (selector.py:307-355), one thread per (head, candidate, output) ---
-    int8_t *h1s = (int8_t *)(smem + OFF_H1);
-    int8_t *h2s = (int8_t *)(smem + OFF_H2);
-    for (int idx = tid; idx < 3 * C * 32; idx += THREADS) {
-        const int j = idx & 31;
-        int h, c;
-        split_hc(idx >> 5, C, h, c);
-        const int32_t acc = dot16<2>(local + (h * MAXC + c) * LSTR, w1t + (h * 32 + j) * WSTR, 0);
-        h1s[(h * MAXC + c) * LSTR + j] =
-            (int8_t)(p.tab_h1.mode ? tab_gelu((int32_t)(acc + g1[h * 32 + j]), p.tab_h1, tab1)
-                                   : sel_gelu(acc + g1[h * 32 + j], p.h1_k2, p.h1_k, p.h1_fast, p.h1_sh_in,
-                                              p.h1_sh_out));
-    }
+    // ---- score MLP layer 1 (selector.py:307-330): per head [n x 32] . [32 x 32] -------
+    ok = ok && mma_layer([&] {
+        for (int t = 0; t < tiles; ++t)
+            for (int h = 0; h < 3; ++h)
+                tc05::mma_i8_ss(tbase + t * 96 + h * 32, tc05::smem_desc(loc_u + 2 * h * STRIP + t * 2048, STRIP, 128),
+                                tc05::smem_desc(w1t_u + h * W1_HEAD, 512, 128), id32, 0);
+    });
+    if (ok)
+        for (int t = 0; t < tiles; ++t) {
+            const int r = t * 128 + quad * 32 + lane;
+            for (int pc = part; pc < 6; pc += 4) {
+                uint32_t v[16];
+                tc05::ld16(lane_base + t * 96 + pc * 16, v);
+                tc05::wait_ld_regs(v);
+                if (r >= 1 && r < n) {
+                    const int64_t *gb = g1 + pc * 16;  // global half of layer 1 plus its bias
+                    *(uint4 *)(h1s + pc * STRIP + r * 16) =
+                        sel_piece_any(p.tab_h1.mode, v, [&](int i) { return gb[i]; }, act_1);
+                }
+            }
+        }
+    tc05::fence_proxy_async();
+    tc05::fence_before();
     __syncthreads();
-    for (int idx = tid; idx < 3 * C * 16; idx += THREADS) {
-        const int m = idx & 15;
-        int h, c;
-        split_hc(idx >> 4, C, h, c);
-        const int32_t acc = dot16<2>(h1s + (h * MAXC + c) * LSTR, w2t + (h * 16 + m) * W2STR, 0);
-        const int32_t b2 = p.b2[h * 16 + m];
-        h2s[(h * MAXC + c) * 16 + m] =
-            (int8_t)(p.tab_h2.mode ? tab_gelu(acc + b2, p.tab_h2, tab2)
-                                   : sel_gelu((int64_t)acc + b2, p.h2_k2, p.h2_k, p.h2_fast, p.h2_sh_in, p.h2_sh_out));
-    }
+
+    // ---- score MLP layer 2 (selector.py:331-344): per head [n x 32] . [32 x 16] -------
+    ok = ok && mma_layer([&] {
+        for (int t = 0; t < tiles; ++t)
+            for (int h = 0; h < 3; ++h)
+                tc05::mma_i8_ss(tbase + t * 48 + h * 16, tc05::smem_desc(h1_u + 2 * h * STRIP + t * 2048, STRIP, 128),
+                                tc05::smem_desc(w2t_u + h * W2_HEAD, 256, 128), id16, 0);
+    });
+    // layer-2 outputs [h][c][16] (one 16-byte row per candidate and head, over the dead
+    // local features)
+    if (ok)
+        for (int t = 0; t < tiles; ++t) {
+            const int r = t * 128 + quad * 32 + lane;
+            if (part < 3) {
+                const int h = part;
+                uint32_t v[16];
+                tc05::ld16(lane_base + t * 48 + h * 16, v);
+                tc05::wait_ld_regs(v);
+                if (r >= 1 && r < n) {
+                    const int32_t *b2 = p.b2 + h * 16;
+                    *(uint4 *)(h2s + (h * MAXC + (r - 1)) * 16) =
+                        sel_piece_any(p.tab_h2.mode, v, [&](int i) { return (int64_t)b2[i]; }, act_2);
+                }
+            }
+        }
+    tc05::fence_before();
     __syncthreads();
     if (dbg.h2)
         for (int i = tid; i < 3 * C * 16; i += THREADS) {
@@ -291,7 +435,7 @@ __global__ void __launch_bounds__(THREADS) selector_kernel(
     // the token rows come back for the compaction (their copies overlap the phases below)
     if (p.tab_h1.mode || p.tab_h2.mode) {
         for (int c = tid; c < n * 12; c += THREADS) {
-            const uint32_t dst = (uint32_t)__cvta_generic_to_shared(tok + c * 16);
+            const uint32_t dst = (uint32_t)__cvta_generic_to_shared(tok + (c % 12) * STRIP + (c / 12) * 16);
             asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(dst),
                          "l"(x + (size_t)row0 * 192 + c * 16)
                          : "memory");
@@ -392,10 +536,11 @@ __global__ void __launch_bounds__(THREADS) selector_kernel(
     const int nout = 1 + kept + (parts > 0 ? 1 : 0);
 
     // ---- write rows: CLS, kept (stable), package --------------------------------------
-    if (tid < 12) ((int4 *)out)[tid] = ((const int4 *)tok)[tid];
+    if (tid < 12) ((int4 *)out)[tid] = *(const int4 *)(tok + tid * STRIP);
     for (int idx = tid; idx < C * 12; idx += THREADS) {
         const int c = idx / 12, ch = idx - c * 12;
-        if (flags[c] & 1) ((int4 *)(out + (size_t)(1 + kidx[c]) * 192))[ch] = ((const int4 *)(tok + (1 + c) * 192))[ch];
+        if (flags[c] & 1)
+            ((int4 *)(out + (size_t)(1 + kidx[c]) * 192))[ch] = *(const int4 *)(tok + ch * STRIP + (1 + c) * 16);
     }
     if (parts > 0) {
         // Σ s·x[d] (or Σ x[d]) over the participants: thread (d, q) of 2 x 192 sums every
@@ -406,12 +551,13 @@ __global__ void __launch_bounds__(THREADS) selector_kernel(
         if (tid < 384) {
             const int q = tid / 192, d = tid - q * 192;
             int32_t num = 0;
+            const int8_t *col = strip_at(tok, 0, d);
             if (pden == 0) {
                 for (int c = q; c < C; c += 2)
-                    if (flags[c] & 2) num += tok[(1 + c) * 192 + d];
+                    if (flags[c] & 2) num += col[(1 + c) * 16];
             } else {
                 for (int c = q; c < C; c += 2)
-                    if (flags[c] & 2) num += fused[c] * (int32_t)tok[(1 + c) * 192 + d];
+                    if (flags[c] & 2) num += fused[c] * (int32_t)col[(1 + c) * 16];
             }
             ppart[tid] = num;
         }
@@ -452,6 +598,14 @@ __global__ void __launch_bounds__(THREADS) selector_kernel(
     if (dbg.global_ && tid < 96) dbg.global_[(size_t)img * 96 + tid] = glob[tid];
     if (dbg.stats)
         for (int i = tid; i < 3 * C; i += THREADS) dbg.stats[(size_t)img * MAXC * 3 + i] = stats[i];
+    // release TMEM; after a wait that gave up, first let that layer's MMAs finish (bounded)
+    if (tid == 0 && *wstat) tc05::mbar_wait(bar, (uint32_t)misc[25], SEL_WAIT);
+    tc05::fence_before();
+    __syncthreads();
+    if (tid < 32) {
+        tc05::fence_after();
+        tc05::tmem_dealloc(tbase, SEL_TMEM_COLS);
+    }
 }
 
 __global__ void __launch_bounds__(256) pack_kernel(const int8_t *__restrict__ stage,
