@@ -160,27 +160,27 @@ __device__ __forceinline__ int32_t sel_act(int64_t v, const SelAct &a) {
     if (pc == 0xFFFFu) o = a.s[t.fine + (int)((e & 0xFFFFu) << t.k) + off];
     return o;
 }
-// 16 outputs of one TMEM piece: act(acc + bias) packed as 16 int8 bytes.
+// 8 outputs of one TMEM piece: act(acc + bias) packed as 8 int8 bytes.
 template <int A, class B>
-__device__ __forceinline__ uint4 sel_piece(const uint32_t (&v)[16], B &&bias, const SelAct &a) {
-    uint32_t pk[4];
+__device__ __forceinline__ uint2 sel_piece(const uint32_t (&v)[8], B &&bias, const SelAct &a) {
+    uint32_t pk[2];
 #pragma unroll
-    for (int w = 0; w < 4; ++w) {
+    for (int w = 0; w < 2; ++w) {
         int32_t o[4];
 #pragma unroll
         for (int b = 0; b < 4; ++b) o[b] = sel_act<A>((int64_t)(int32_t)v[4 * w + b] + bias(4 * w + b), a);
         pk[w] = pack_sat8(o[0], o[1], o[2], o[3]);
     }
-    return make_uint4(pk[0], pk[1], pk[2], pk[3]);
+    return make_uint2(pk[0], pk[1]);
 }
 template <class B>
-__device__ __forceinline__ uint4 sel_piece_any(int mode, const uint32_t (&v)[16], B &&bias, const SelAct &a) {
+__device__ __forceinline__ uint2 sel_piece_any(int mode, const uint32_t (&v)[8], B &&bias, const SelAct &a) {
     if (mode == 1) return sel_piece<1>(v, bias, a);
     if (mode == 2) return sel_piece<2>(v, bias, a);
     return sel_piece<0>(v, bias, a);
 }
 
-__global__ void __launch_bounds__(THREADS) selector_kernel(
+__global__ void __launch_bounds__(THREADS, 2) selector_kernel(
     const int8_t *__restrict__ x, const int32_t *__restrict__ offsets, const uint8_t *__restrict__ pkg_in,
     SelParams p, int8_t *__restrict__ stage, int32_t *__restrict__ counts_out, uint8_t *__restrict__ pkg_out,
     hv_selector_summary *__restrict__ summary, int sum_stride, uint8_t *__restrict__ warn,
@@ -300,18 +300,18 @@ __global__ void __launch_bounds__(THREADS) selector_kernel(
                                     tc05::smem_desc(tok_u + (4 * h + 2 * k) * STRIP + t * 2048, STRIP, 128),
                                     tc05::smem_desc(lwt_u + h * LW_HEAD + 2 * k * 512, 512, 128), id32, k);
     });
-    // epilogue: thread = token row (TMEM lane), pieces of 16 columns (head pc / 2,
-    // outputs 16 (pc % 2) ..) dealt to the quadrant's four warps
+    // epilogue: thread = token row (TMEM lane); the 12 pieces of 8 columns (head
+    // pc / 4, outputs 8 (pc % 4) ..) are dealt three to each of the quadrant's warps
     if (ok)
         for (int t = 0; t < tiles; ++t) {
             const int r = t * 128 + quad * 32 + lane;
-            for (int pc = part; pc < 6; pc += 4) {
-                uint32_t v[16];
-                tc05::ld16(lane_base + t * 96 + pc * 16, v);
+            for (int pc = part; pc < 12; pc += 4) {
+                uint32_t v[8];
+                tc05::ld8(lane_base + t * 96 + pc * 8, v);
                 tc05::wait_ld_regs(v);
                 if (r >= 1 && r < n) {
-                    const int32_t *lb = p.local_b + pc * 16;  // head pc / 2, outputs 16 (pc % 2) ..
-                    *(uint4 *)(local + pc * STRIP + r * 16) =
+                    const int32_t *lb = p.local_b + pc * 8;
+                    *(uint2 *)(local + (pc >> 1) * STRIP + r * 16 + (pc & 1) * 8) =
                         sel_piece_any(p.tab_local.mode, v, [&](int i) { return (int64_t)lb[i]; }, act_l);
                 }
             }
@@ -367,9 +367,8 @@ __global__ void __launch_bounds__(THREADS) selector_kernel(
     if (tid < 96) {
         // the global half of layer 1, once per image (W1 rows read from global memory)
         const int h = tid >> 5, j = tid & 31;
-        int32_t acc = 0;
-        const int8_t *wrow = p.w1t + (h * 32 + j) * 64 + 32;
-        for (int k = 0; k < 32; ++k) acc += (int32_t)glob[h * 32 + k] * wrow[k];
+        const int4 *wrow = (const int4 *)(p.w1t + (h * 32 + j) * 64 + 32);
+        const int32_t acc = dot16<2>(glob + h * 32, (const int8_t *)wrow, 0);  // (2 x 16-byte words)
         g1[h * 32 + j] = (int64_t)acc + p.b1[h * 32 + j];
     }
     __syncthreads();
@@ -384,13 +383,13 @@ __global__ void __launch_bounds__(THREADS) selector_kernel(
     if (ok)
         for (int t = 0; t < tiles; ++t) {
             const int r = t * 128 + quad * 32 + lane;
-            for (int pc = part; pc < 6; pc += 4) {
-                uint32_t v[16];
-                tc05::ld16(lane_base + t * 96 + pc * 16, v);
+            for (int pc = part; pc < 12; pc += 4) {
+                uint32_t v[8];
+                tc05::ld8(lane_base + t * 96 + pc * 8, v);
                 tc05::wait_ld_regs(v);
                 if (r >= 1 && r < n) {
-                    const int64_t *gb = g1 + pc * 16;  // global half of layer 1 plus its bias
-                    *(uint4 *)(h1s + pc * STRIP + r * 16) =
+                    const int64_t *gb = g1 + pc * 8;  // global half of layer 1 plus its bias
+                    *(uint2 *)(h1s + (pc >> 1) * STRIP + r * 16 + (pc & 1) * 8) =
                         sel_piece_any(p.tab_h1.mode, v, [&](int i) { return gb[i]; }, act_1);
                 }
             }
@@ -411,14 +410,13 @@ __global__ void __launch_bounds__(THREADS) selector_kernel(
     if (ok)
         for (int t = 0; t < tiles; ++t) {
             const int r = t * 128 + quad * 32 + lane;
-            if (part < 3) {
-                const int h = part;
-                uint32_t v[16];
-                tc05::ld16(lane_base + t * 48 + h * 16, v);
+            for (int pc = part; pc < 6; pc += 4) {  // pieces of 8: head pc / 2, outputs 8 (pc % 2) ..
+                uint32_t v[8];
+                tc05::ld8(lane_base + t * 48 + pc * 8, v);
                 tc05::wait_ld_regs(v);
                 if (r >= 1 && r < n) {
-                    const int32_t *b2 = p.b2 + h * 16;
-                    *(uint4 *)(h2s + (h * MAXC + (r - 1)) * 16) =
+                    const int32_t *b2 = p.b2 + pc * 8;
+                    *(uint2 *)(h2s + ((pc >> 1) * MAXC + (r - 1)) * 16 + (pc & 1) * 8) =
                         sel_piece_any(p.tab_h2.mode, v, [&](int i) { return (int64_t)b2[i]; }, act_2);
                 }
             }
