@@ -367,9 +367,11 @@ def test_selector_ragged_batch_vs_oracle(cuda, oracle):
     from heatvit_b200.selector import token_selector_batch
     params = synth.config_params(synth.SEED, pruned=True)
     rng = np.random.default_rng(12)
-    counts = list(rng.integers(2, 198, 40))
+    # random counts plus the edges of the selector's 128-row tensor-core tiles (one
+    # full tile, a second tile holding one row) and the smallest selectable image
+    counts = list(rng.integers(2, 198, 40)) + [2, 3, 127, 128, 129, 130, 196, 197]
     mats = [rng.integers(-128, 128, (n, 192)) for n in counts]
-    pk = list(rng.integers(0, 2, 40))
+    pk = list(rng.integers(0, 2, len(counts)))
     for stage in range(3):
         res = token_selector_batch(mats, pk, params.selectors[stage], intermediates=True)
         for m, p, r in zip(mats, pk, res):
