@@ -408,10 +408,11 @@ __global__ void __launch_bounds__(CFG::THREADS, CFG::PER_SM) attention_tc_kernel
                                 tc05::smem_desc(tc05::smem_u32(sK) + s * 256, 128, 512), idesc, s);
             tc05::commit(bar);
         }
+        // Every thread sees the MMA complete on the mbarrier itself (the next MMA is
+        // issued only after a barrier that every thread reaches after this wait, so
+        // none can miss the phase); a wait that gave up is acted on at that barrier.
         if (tc05::mbar_wait(bar, phase, WAIT_ITERS)) phase ^= 1;
         else *abort_flag = 1;
-        __syncthreads();
-        if (*abort_flag) break;
         tc05::fence_after();
         // K and Q are consumed: the next unit's copies overlap this unit's softmax
         if (more) {
@@ -494,6 +495,7 @@ __global__ void __launch_bounds__(CFG::THREADS, CFG::PER_SM) attention_tc_kernel
         tc05::fence_proxy_async();
         tc05::fence_before();
         __syncthreads();
+        if (*abort_flag) break;
         if (tid == 0) {
             tc05::fence_after();
             const uint32_t idesc = tc05::idesc_i8(128, 64, false, true, true);
@@ -503,10 +505,8 @@ __global__ void __launch_bounds__(CFG::THREADS, CFG::PER_SM) attention_tc_kernel
                                 tc05::smem_desc(tc05::smem_u32(sV) + s * 2048, 512, 128), idesc, s);
             tc05::commit(bar);
         }
-        if (tc05::mbar_wait(bar, phase, WAIT_ITERS)) phase ^= 1;
+        if (tc05::mbar_wait(bar, phase, WAIT_ITERS)) phase ^= 1;  // (as after S = Q.K^T)
         else *abort_flag = 1;
-        __syncthreads();
-        if (*abort_flag) break;
         tc05::fence_after();
         // V is consumed: the next unit's V copies overlap the rest of this unit
         if (more) load_kv<CFG, 1>(qkv, cur, sV, tid);
