@@ -263,22 +263,24 @@ __global__ void __launch_bounds__(THREADS, 2) selector_kernel(
     uint32_t phase = 0;
     // One layer: thread 0 issues `issue` (the tensor-core work) and commits; every
     // thread learns whether it completed in time (bounded wait, then a barrier).
+    // Every thread waits on the mbarrier itself (no barrier after the wait: the next
+    // layer is issued only after a barrier that every thread reaches after this wait,
+    // so none can miss a phase).
     auto mma_layer = [&](auto &&issue) -> bool {
         if (tid == 0) {
             tc05::fence_after();
             issue();
             tc05::commit(bar);
-            const bool ok = tc05::mbar_wait(bar, phase, SEL_WAIT);
-            *wstat = ok ? 0 : 1;
-            if (!ok) {
-                misc[25] = (int)phase;  // the parity to drain before TMEM is released
-                if (p.err) atomicExch(p.err, 3);
-            }
+        }
+        const bool ok = tc05::mbar_wait(bar, phase, SEL_WAIT);
+        if (!ok) {
+            *wstat = 1;
+            misc[25] = (int)phase;  // the parity to drain before TMEM is released
+            if (p.err) atomicExch(p.err, 3);
         }
         phase ^= 1;
-        __syncthreads();
         tc05::fence_after();
-        return *wstat == 0;
+        return ok;
     };
     const uint32_t id32 = tc05::idesc_i8(128, 32, true, true), id16 = tc05::idesc_i8(128, 16, true, true);
     const uint32_t tok_u = tc05::smem_u32(tok), loc_u = tc05::smem_u32(local), lwt_u = tc05::smem_u32(lwt);
