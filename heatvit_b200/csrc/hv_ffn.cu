@@ -17,8 +17,9 @@
 // boxes would cost one copy request per row and 16-byte strip.  The tile's residual
 // rows (contiguous, 24 KB) arrive the same way, ahead of the FC2 epilogue.
 //
-// Roles (576 threads): warp 0 lane 0 issues every TMA load (A tiles, W1 and W2
-// chunks, in consumption order); warp 1 lane 0 issues the MMAs, FC1 of chunk j + 1
+// Roles (576 threads): warp 0 lane 0 issues every copy (A tiles by TMA; W1 and W2
+// chunks and residual rows by bulk copy; in consumption order); warp 1 lane 0
+// issues the MMAs, FC1 of chunk j + 1
 // ahead of FC2 of chunk j, so the GELU epilogue of chunk j overlaps the tensor
 // work; warps 2-17 run the epilogues, four per TMEM lane quadrant (thread = TMEM
 // lane; the quadrant's four warps split each chunk's 128 columns into 32-column

@@ -10,6 +10,13 @@
 // Splitting layer 1 as [local ‖ global]·W1 = local·W1[0:32] + global·W1[32:64]
 // is exact in integer arithmetic.
 //
+// The local MLP and score layers 1-2 run on tcgen05 (kind::i8, M = 128 over the
+// image's token rows, one MMA per head and K step) with the exact GELU tables in
+// their TMEM epilogues; the token rows and those layers' outputs are kept in the
+// strip layout the tensor cores read (see STRIP).  Score layer 3, the softmaxes,
+// the head statistics and head-weight MLP, the fuse and the compaction run on the
+// CUDA cores.
+//
 // The output goes to a per-image staging slot (stride 197 rows); the pack
 // kernel then prefix-sums the new counts and writes the packed ragged layout
 // that every later kernel consumes.
