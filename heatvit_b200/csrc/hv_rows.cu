@@ -165,7 +165,9 @@ __global__ void __launch_bounds__(256, 3) ln_kernel(const int8_t *x, int8_t *out
         s_bet[slot] = OUT32 ? b * (1 << p.sh_b) : b;
         int32_t *pair = (int32_t *)&s_gb[(c / 24) * 13 + (c % 24) / 2] + 2 * (c & 1);
         pair[0] = p.gamma[c];
-        pair[1] = OUT32 ? b * (1 << p.sh_b) : b;
+        // (the pairs feed only the 32-bit fast form, which also takes its rounding
+        // half here: 2^(sh_out - 1) with sh_out >= 1 there)
+        pair[1] = OUT32 ? b * (1 << p.sh_b) + (1 << (p.sh_out - 1)) : b;
     }
     __syncthreads();
     const int4 *gb = s_gb + sub * 13;
@@ -267,7 +269,7 @@ __global__ void __launch_bounds__(256, 3) ln_kernel(const int8_t *x, int8_t *out
                 // Short form with the output stage on the FMA pipe, per element:
                 //   t  = vp*ahh + (khh + 255)        (vp = v + 128, 64-bit)
                 //   nr = vp*aq + kq + hi32(t)
-                //   o  = (x + 2^(sh-1) + [x < 0]*-1) >> sh,  x = nr*gamma + beta'
+                //   o  = (x + 2^(sh-1) - [x < 0]) >> sh,  x = nr*gamma + beta'
                 // The +255 keeps hi32(t) equal to the short form's term exactly when the
                 // low word of vp*ahh + khh lies in [1, 2^32 - 256] (no carry) and then
                 // lifts it to [256, 2^32 - 1]; every other case leaves a low word below
@@ -277,7 +279,7 @@ __global__ void __launch_bounds__(256, 3) ln_kernel(const int8_t *x, int8_t *out
                 const uint32_t ahh = __shfl_sync(0xffffffffu, af.ahh, owner);
                 const uint64_t kh = (uint64_t)__shfl_sync(0xffffffffu, af.khh, owner) + 255u;
                 const int32_t kq = __shfl_sync(0xffffffffu, af.kq, owner);
-                const int32_t one = p.one, half = 1 << (p.sh_out - 1);
+                const int32_t half = 1 << (p.sh_out - 1);
                 const uint32_t words[6] = {wn[0].x, wn[0].y, wn[1].x, wn[1].y, wn[2].x, wn[2].y};
                 load_words(k + 1, wn);
                 uint32_t lo_min = 0xFFFFFFFFu, ow[6];
@@ -293,9 +295,10 @@ __global__ void __launch_bounds__(256, 3) ln_kernel(const int8_t *x, int8_t *out
                         const uint64_t t = (uint64_t)vp * ahh + kh;
                         lo_min = min(lo_min, (uint32_t)t);
                         const int32_t nr = (int32_t)(vp * aq) + kq + (int32_t)(t >> 32);
-                        const int32_t xv = nr * gg[b] + bb[b];
-                        const int32_t xh = xv * one + half;
-                        o4[b] = (__mulhi(xv, one) + xh) >> p.sh_out;
+                        // xh = x + 2^(sh-1) (the half is folded into bb): the ties-away
+                        // shift of x is (xh - [x < 0]) >> sh, and x < 0 iff xh < 2^(sh-1)
+                        const int32_t xh = nr * gg[b] + bb[b];
+                        o4[b] = (xh - (xh < half ? 1 : 0)) >> p.sh_out;
                     }
                     ow[q] = pack_sat8(o4[0], o4[1], o4[2], o4[3]);
                 }
