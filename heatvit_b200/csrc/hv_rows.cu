@@ -261,14 +261,18 @@ __global__ void __launch_bounds__(256, 3) ln_kernel(const int8_t *x, int8_t *out
             const int r = base + 4 * k + grp;
             const bool active = r < rows;
             const int owner = 4 * k + grp;
+            // the owner's statistics, for the exact per-element form only (fetched in
+            // warp-uniform branches, so the fast form skips the shuffles)
             LnStats rs;
-            rs.mean = shfl64(st.mean, owner);
-            rs.inv = (uint64_t)shfl64((int64_t)st.inv, owner);
-            rs.neg = false;
+            auto fetch_rs = [&]() {
+                rs.mean = shfl64(st.mean, owner);
+                rs.inv = (uint64_t)shfl64((int64_t)st.inv, owner);
+                rs.neg = false;
+            };
             if (OUT32 && all_safe) {
                 // Short form with the output stage on the FMA pipe, per element:
-                //   t  = vp*ahh + (khh + 255)        (vp = v + 128, 64-bit)
-                //   nr = vp*aq + kq + hi32(t)
+                //   t  = vp*ahh + (khh + 255 + kq*2^32)   (vp = v + 128, 64-bit)
+                //   nr = vp*aq + hi32(t)            (hi32(t) carries kq, mod 2^32)
                 //   o  = (x + 2^(sh-1) - [x < 0]) >> sh,  x = nr*gamma + beta'
                 // The +255 keeps hi32(t) equal to the short form's term exactly when the
                 // low word of vp*ahh + khh lies in [1, 2^32 - 256] (no carry) and then
@@ -277,8 +281,9 @@ __global__ void __launch_bounds__(256, 3) ln_kernel(const int8_t *x, int8_t *out
                 // 256 is redone with the exact per-element form.
                 const uint32_t aq = __shfl_sync(0xffffffffu, af.aq, owner);
                 const uint32_t ahh = __shfl_sync(0xffffffffu, af.ahh, owner);
-                const uint64_t kh = (uint64_t)__shfl_sync(0xffffffffu, af.khh, owner) + 255u;
                 const int32_t kq = __shfl_sync(0xffffffffu, af.kq, owner);
+                const uint64_t kh = ((uint64_t)__shfl_sync(0xffffffffu, af.khh, owner) + 255u) +
+                                    ((uint64_t)(uint32_t)kq << 32);
                 const int32_t half = 1 << (p.sh_out - 1);
                 const uint32_t words[6] = {wn[0].x, wn[0].y, wn[1].x, wn[1].y, wn[2].x, wn[2].y};
                 load_words(k + 1, wn);
@@ -294,7 +299,7 @@ __global__ void __launch_bounds__(256, 3) ln_kernel(const int8_t *x, int8_t *out
                         const uint32_t vp = __byte_perm(xb, 0u, 0x4440u + b);
                         const uint64_t t = (uint64_t)vp * ahh + kh;
                         lo_min = min(lo_min, (uint32_t)t);
-                        const int32_t nr = (int32_t)(vp * aq) + kq + (int32_t)(t >> 32);
+                        const int32_t nr = (int32_t)(vp * aq) + (int32_t)(t >> 32);
                         // xh = x + 2^(sh-1) (the half is folded into bb): the ties-away
                         // shift of x is (xh - [x < 0]) >> sh, and x < 0 iff xh < 2^(sh-1)
                         const int32_t xh = nr * gg[b] + bb[b];
@@ -304,6 +309,7 @@ __global__ void __launch_bounds__(256, 3) ln_kernel(const int8_t *x, int8_t *out
                 }
                 if (!active) lo_min = 0xFFFFFFFFu;
                 if (__any_sync(0xffffffffu, lo_min < 256u)) {
+                    fetch_rs();
                     LnAff f;
                     f.aq = aq;
                     f.ahh = ahh;
@@ -333,6 +339,7 @@ __global__ void __launch_bounds__(256, 3) ln_kernel(const int8_t *x, int8_t *out
                 }
                 continue;
             }
+            fetch_rs();
             int32_t v[24];
             ln_load24(x + (size_t)(active ? r : 0) * 192, sub, active, v);
             int32_t o[24];
