@@ -20,8 +20,10 @@
 // and P is written block-diagonal (zero outside the row's own block), so one
 // P·V over all 128 stacked V rows gives each row its own head's context.
 //
-// Per unit (CTA of 4 x SPL warps, persistent over its units; SPL = 1 for list A,
-// 4 for list B):
+// Launches: list B's shape (SPL = 4) walks list B and, for batches of at most 3
+// images per SM, list A after it in the same launch; larger batches give list A a
+// launch of its own in the SPL = 1 shape.
+// Per unit (CTA of 4 x SPL warps, persistent over its units):
 //   1. K, V and Q are staged in shared memory with 16-byte cp.async copies in the
 //      no-swizzle canonical layout (hv_tc05.cuh); K and Q are K-major operands, V is
 //      the same byte layout read as an MN-major B operand (tokens along K).  Each
@@ -37,7 +39,8 @@
 //      the exp terms go back to TMEM, then the UQ0.8 probabilities to shared memory
 //      as the A operand of the next MMA.
 //   4. ctx = P·V (unsigned A) into TMEM columns [0, 64), requantised and stored.
-// TMEM: 128 columns per CTA for list A (4 CTAs per SM), 256 for list B (2 per SM).
+// TMEM: 128 columns per CTA in the SPL = 1 shape (4 CTAs per SM), 256 in the SPL = 4
+// shape (2 per SM).
 #include <algorithm>
 
 #include "hv_internal.cuh"
@@ -336,8 +339,10 @@ template <bool FAST, class CFG>
 __global__ void __launch_bounds__(CFG::THREADS, CFG::PER_SM) attention_tc_kernel(const int8_t *__restrict__ qkv,
                                                                int8_t *__restrict__ ctx, AttnParams p,
                                                                int *__restrict__ err,
-                                                               const uint2 *__restrict__ list,
-                                                               const int32_t *__restrict__ count) {
+                                                               const uint2 *__restrict__ list1,
+                                                               const int32_t *__restrict__ count1,
+                                                               const uint2 *__restrict__ list2,
+                                                               const int32_t *__restrict__ count2) {
     extern __shared__ __align__(1024) uint8_t smem[];
     uint8_t *sP = smem + CFG::OFF_P;
     uint8_t *sQ = smem + CFG::OFF_Q;
@@ -371,7 +376,10 @@ __global__ void __launch_bounds__(CFG::THREADS, CFG::PER_SM) attention_tc_kernel
     const uint32_t tbase = *tmem_slot;
     const uint32_t lane_addr = tbase + ((uint32_t)(quad * 32) << 16);
     uint32_t phase = 0;
-    const int units = *count;
+    // one index space over one or two lists (list B's units, 6 per long image, come
+    // first when both are walked, so the longest units start first)
+    const int n1 = *count1, units = n1 + (count2 ? *count2 : 0);
+    auto entry = [&](int i) { return i < n1 ? list1[i] : list2[i - n1]; };
     const int stride = gridDim.x;
 
     // cp.async groups, oldest first: [K, Q] of a unit (issued once the previous unit's
@@ -380,9 +388,9 @@ __global__ void __launch_bounds__(CFG::THREADS, CFG::PER_SM) attention_tc_kernel
     // latency hides behind a whole unit's work.
     Unit cur;
     uint2 ahead = make_uint2(0, 0);
-    if ((int)blockIdx.x + stride < units) ahead = list[blockIdx.x + stride];
+    if ((int)blockIdx.x + stride < units) ahead = entry(blockIdx.x + stride);
     if ((int)blockIdx.x < units) {
-        cur = decode_unit(list[blockIdx.x]);
+        cur = decode_unit(entry(blockIdx.x));
         load_kv<CFG, 0>(qkv, cur, sK, tid);
         load_q<CFG>(qkv, cur, sQ, tid);
         cp_commit();
@@ -417,7 +425,7 @@ __global__ void __launch_bounds__(CFG::THREADS, CFG::PER_SM) attention_tc_kernel
         // K and Q are consumed: the next unit's copies overlap this unit's softmax
         if (more) {
             cur = decode_unit(ahead);
-            if (ui + 2 * stride < units) ahead = list[ui + 2 * stride];
+            if (ui + 2 * stride < units) ahead = entry(ui + 2 * stride);
             load_kv<CFG, 0>(qkv, cur, sK, tid);
             load_q<CFG>(qkv, cur, sQ, tid);
         }
@@ -575,30 +583,36 @@ cudaError_t launch_attn_plan(const int32_t *offsets, int images, const AttnPlan 
 }
 
 template <class CFG>
-cudaError_t launch_one(const int8_t *qkv, int8_t *ctx, const AttnParams &p, int *err,
-                       const uint2 *list, const int32_t *count, int grid, cudaStream_t st) {
+cudaError_t launch_one(const int8_t *qkv, int8_t *ctx, const AttnParams &p, int *err, const uint2 *list1,
+                       const int32_t *count1, const uint2 *list2, const int32_t *count2, int grid,
+                       cudaStream_t st) {
     auto k = p.fast ? attention_tc_kernel<true, CFG> : attention_tc_kernel<false, CFG>;
     cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, CFG::SMEM);
     if (e != cudaSuccess) return e;
-    return launch_pdl(k, dim3(grid), dim3(CFG::THREADS), CFG::SMEM, st, qkv, ctx, p, err, list, count);
+    return launch_pdl(k, dim3(grid), dim3(CFG::THREADS), CFG::SMEM, st, qkv, ctx, p, err, list1, count1, list2,
+                      count2);
 }
 
 cudaError_t launch_attention(const int8_t *qkv, const int32_t *offsets, int images, int8_t *ctx,
                              const AttnParams &p, int may_be_short, int sms, int *err, const AttnPlan &plan,
                              cudaStream_t st) {
     if (images <= 0) return cudaSuccess;
-    // List A: one warp per TMEM lane quadrant, double-buffered TMEM reads (four
-    // CTAs of 4 warps per SM); list B: four warps per quadrant splitting each row's
-    // pieces, single-buffered (two CTAs of 16 warps per SM, 64 registers).
     const uint2 *la = plan.list_a, *lb = plan.list_b;
     const int32_t *ca = plan.cnt, *cb = plan.cnt + 1;
-    if (may_be_short) {
-        const int ga = std::min(images * 3, sms * 4);
-        cudaError_t e = launch_one<AttnCfg<128, 1, true>>(qkv, ctx, p, err, la, ca, ga, st);
-        if (e != cudaSuccess) return e;
-    }
     const int gb = std::min(images * 6, sms * 2);
-    return launch_one<AttnCfg<224, 4, false>>(qkv, ctx, p, err, lb, cb, gb, st);
+    // List B: four warps per TMEM lane quadrant splitting each row's pieces,
+    // single-buffered (two CTAs of 16 warps per SM, 64 registers).  Up to 3 images
+    // per SM, one launch of that shape walks list B and then list A (one launch
+    // fewer per block); above that, list A has a launch of its own with one warp
+    // per quadrant and double-buffered TMEM reads (four CTAs of 4 warps per SM),
+    // which is faster per unit once its units fill the four CTAs per SM.
+    if (!may_be_short || images <= 3 * sms)
+        return launch_one<AttnCfg<224, 4, false>>(qkv, ctx, p, err, lb, cb, may_be_short ? la : nullptr,
+                                                  may_be_short ? ca : nullptr, gb, st);
+    cudaError_t e = launch_one<AttnCfg<128, 1, true>>(qkv, ctx, p, err, la, ca, nullptr, nullptr,
+                                                      std::min(images * 3, sms * 4), st);
+    if (e != cudaSuccess) return e;
+    return launch_one<AttnCfg<224, 4, false>>(qkv, ctx, p, err, lb, cb, nullptr, nullptr, gb, st);
 }
 
 }  // namespace hv

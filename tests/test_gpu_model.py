@@ -272,6 +272,25 @@ def test_transformer_block_fused_ragged_vs_oracle(cuda, oracle):
             np.testing.assert_array_equal(z, want)
 
 
+def test_transformer_block_ragged_two_attention_launches_vs_oracle(cuda, oracle):
+    """More than 3 images per SM with lengths on both sides of 128: the attention
+    stage then runs list A (n <= 128) and list B (n > 128) as two launches of two CTA
+    shapes instead of one launch over both lists."""
+    import torch
+    from heatvit_b200 import synth
+    from heatvit_b200.transformer import transformer_block_batch
+    params = synth.config_params(synth.SEED, pruned=True)
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    rng = np.random.default_rng(41)
+    counts = rng.integers(1, 198, 3 * sms + 37)
+    counts[:4] = [197, 128, 129, 1]
+    xs = [rng.integers(-128, 128, (int(n), 192)) for n in counts]
+    zs = transformer_block_batch(xs, params.blocks[5])
+    for x, z in zip(xs, zs):
+        want, _, _ = oracle.transformer_block(x, params.blocks[5])
+        np.testing.assert_array_equal(z, want)
+
+
 @pytest.mark.parametrize("q,k", [(-8, 9), (-5, 12), (-10, 7)])
 def test_attention_wide_scores_vs_oracle(cuda, oracle, q, k):
     """Attention rows with wide Q8.16 spreads: qkv_out_scale_exp q (score_scale 2q - 3)
