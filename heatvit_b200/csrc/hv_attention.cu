@@ -7,9 +7,10 @@
 //   ctx   = requant(prob(uint8)·V, prob_scale + q, context_out, 8)
 // written straight into the head-concatenated layout (layout.py:132-155).
 //
-// Work units.  attn_plan_kernel lists the batch's work once per token layout (after
-// the batch is set up and after every selector): a unit is one 128-row tile of query
-// rows.
+// Work units (hv_attn_units.cuh) are listed once per token layout by the kernel that
+// makes the layout: the batch set-up, the token packer after every selector, or
+// attn_plan_kernel for a layout given by the caller.  A unit is one 128-row tile of
+// query rows.
 //   * n > 128 tokens (list B): one unit per (head, 128-row half): 6 per image.
 //   * 64 < n <= 128 (list A): one unit per head.
 //   * 32 < n <= 64 (list A): heads {0, 1} packed in one tile (64 rows each), head 2
@@ -43,6 +44,7 @@
 // shape (2 per SM).
 #include <algorithm>
 
+#include "hv_attn_units.cuh"
 #include "hv_internal.cuh"
 #include "hv_tc05.cuh"
 
@@ -51,17 +53,6 @@ namespace hv {
 namespace {
 
 constexpr uint32_t WAIT_ITERS = 1u << 24;
-
-// Unit encoding: image << 7 | mtile << 6 | log2(G) << 4 | first head << 2 | heads.
-__host__ __device__ __forceinline__ uint32_t unit_code(int img, int mt, int glog, int h0, int nh) {
-    return ((uint32_t)img << 7) | ((uint32_t)mt << 6) | ((uint32_t)glog << 4) | ((uint32_t)h0 << 2) | (uint32_t)nh;
-}
-
-// Units of an image of n tokens on list A (n <= 128) and list B (n > 128).
-__device__ __forceinline__ int units_a(int n) { return n <= 0 || n > 128 ? 0 : (n <= 32 ? 1 : (n <= 64 ? 2 : 3)); }
-// (an image longer than 224 tokens has no units: the model never makes one, and the
-// kernel's buffers hold 224 rows)
-__device__ __forceinline__ int units_b(int n) { return n > 128 && n <= 224 ? 6 : 0; }
 
 // One CTA (1024 threads) lists every unit of the batch, image-major.  cnt[0], cnt[1]
 // = lengths of list A and list B.
@@ -100,17 +91,7 @@ __global__ void __launch_bounds__(1024) attn_plan_kernel(const int32_t *__restri
         }
         pa += sa - ca;  // exclusive position of this image's first unit
         pb += sb - cb;
-        // the image's first row and token count ride with every unit (row0 < 2^24)
-        const uint32_t rn = img < images ? ((uint32_t)offsets[img] << 8) | (uint32_t)n : 0u;
-        if (ca == 1) {
-            list_a[pa] = make_uint2(unit_code(img, 0, 2, 0, 3), rn);
-        } else if (ca == 2) {
-            list_a[pa] = make_uint2(unit_code(img, 0, 1, 0, 2), rn);
-            list_a[pa + 1] = make_uint2(unit_code(img, 0, 1, 2, 1), rn);
-        } else if (ca == 3) {
-            for (int h = 0; h < 3; ++h) list_a[pa + h] = make_uint2(unit_code(img, 0, 0, h, 1), rn);
-        }
-        for (int u = 0; u < cb; ++u) list_b[pb + u] = make_uint2(unit_code(img, u / 3, 0, u % 3, 1), rn);
+        if (img < images) write_image_units(list_a, list_b, pa, pb, img, offsets[img], n);
         __syncthreads();
         if (tid == 0) {
             int ta = 0, tb = 0;

@@ -160,9 +160,10 @@ cudaError_t launch_selector(const int8_t *x, const int32_t *offsets, const uint8
                             int tc_stride, int tc_col, const SelDebug *dbg, cudaStream_t st);
 
 // Pack stage[i] (count counts[i], stride 197 rows) into x at prefix-summed
-// offsets; writes offsets_out[0..images].
+// offsets; writes offsets_out[0..images] and, when plan is non-null, the attention
+// unit lists of the packed layout (so no attn_plan_kernel launch follows).
 cudaError_t launch_pack(const int8_t *stage, const int32_t *counts, int images, int8_t *x,
-                        int32_t *offsets_out, cudaStream_t st);
+                        int32_t *offsets_out, const AttnPlan *plan, cudaStream_t st);
 
 // Element-wise units (unit API).
 cudaError_t launch_gelu(const int32_t *x, int64_t n, int32_t *out, cudaStream_t st);

@@ -17,6 +17,7 @@
 #include <vector>
 #include <algorithm>
 
+#include "hv_attn_units.cuh"
 #include "hv_internal.cuh"
 
 using namespace hv;
@@ -353,7 +354,7 @@ int ensure_capacity(hv_model *m, int images, int i = 0) {
 
 // ---- small pipeline kernels ----------------------------------------------------
 __global__ void init_batch_kernel(int images, int32_t *off, uint8_t *pkg, uint8_t *warn, int32_t *tc, int tc_stride,
-                                  int8_t *x, const int8_t *cls_row) {
+                                  int8_t *x, const int8_t *cls_row, AttnPlan plan) {
     griddep_wait();  // the previous inference may still read these buffers
     griddep_launch();
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i <= images; i += gridDim.x * blockDim.x) {
@@ -361,8 +362,14 @@ __global__ void init_batch_kernel(int images, int32_t *off, uint8_t *pkg, uint8_
         if (i < images) {
             pkg[i] = 0;
             if (tc) tc[(size_t)i * tc_stride] = HV_TOKENS;
+            // the attention units of the full layout: 6 per image on list B
+            write_image_units(plan.list_a, plan.list_b, 0, 6 * i, i, i * HV_TOKENS, HV_TOKENS);
         }
         if (i < ((images + 3) & ~3)) warn[i] = 0;
+    }
+    if (blockIdx.x == 0 && threadIdx.x == 0) {
+        plan.cnt[0] = 0;
+        plan.cnt[1] = 6 * images;
     }
     // CLS rows (row 0 of every image): 12 x 16 bytes each.
     for (int c = blockIdx.x * blockDim.x + threadIdx.x; c < images * 12; c += gridDim.x * blockDim.x) {
@@ -598,7 +605,7 @@ int infer_impl(hv_model *m, const int8_t *d_images, int batch, int32_t *d_logits
     if (d_ckpt_rows) CUDA_TRY(cudaMemsetAsync(d_ckpt_rows, 0, sizeof(int32_t) * (size_t)batch * HV_CKPT_SLOTS, st));
     int cur = 0;
     CUDA_TRY(launch_pdl(init_batch_kernel, dim3(std::min(148 * 4, (batch * 12 + 255) / 256 + 1)), dim3(256), 0, st, 
-        batch, m->off[0], m->pkg[0], m->warn, d_tc, tc_stride, m->X, m->w<int8_t>(m->cls_row)));
+        batch, m->off[0], m->pkg[0], m->warn, d_tc, tc_stride, m->X, m->w<int8_t>(m->cls_row), m->plan));
     CUDA_TRY(cudaGetLastError());
     {
         Prof pr(m, HV_STAGE_PATCH, st);
@@ -610,8 +617,7 @@ int infer_impl(hv_model *m, const int8_t *d_images, int batch, int32_t *d_logits
         ckpt_copy_kernel<<<batch, 256, 0, st>>>(m->X, m->off[cur], d_ckpt, d_ckpt_rows, HV_CKPT_PATCH);
         CUDA_TRY(cudaGetLastError());
     }
-    CUDA_TRY(launch_attn_plan(m->off[cur], batch, m->plan, st));
-    int sel_no = 0;
+    int sel_no = 0;  // (init_batch_kernel wrote the attention units of the full layout)
     for (int b = 0; b < HV_BLOCKS; ++b) {
         const int si = m->sel_before[b];
         if (si >= 0) {
@@ -621,9 +627,8 @@ int infer_impl(hv_model *m, const int8_t *d_images, int batch, int32_t *d_logits
                                      d_summary ? d_summary + sel_no : nullptr, ns, m->warn, d_tc, tc_stride,
                                      sel_no + 1, nullptr, st));
             pr.end(st, m->off[cur] + batch, 0);
-            CUDA_TRY(launch_pack(m->STAGE, m->counts, batch, m->X, m->off[cur ^ 1], st));
+            CUDA_TRY(launch_pack(m->STAGE, m->counts, batch, m->X, m->off[cur ^ 1], &m->plan, st));
             cur ^= 1;
-            CUDA_TRY(launch_attn_plan(m->off[cur], batch, m->plan, st));
             ++sel_no;
             if (d_ckpt) {
                 ckpt_copy_kernel<<<batch, 256, 0, st>>>(m->X, m->off[cur], d_ckpt, d_ckpt_rows,
@@ -1868,7 +1873,7 @@ int hv_patch_embedding(hv_model *m, const int8_t *d_images, int batch, int8_t *d
     if (rc) return rc;
     cudaStream_t st = (cudaStream_t)stream;
     CUDA_TRY(launch_pdl(init_batch_kernel, dim3(std::min(148 * 4, (batch * 12 + 255) / 256 + 1)), dim3(256), 0, st, 
-        batch, m->off[0], m->pkg[0], m->warn, nullptr, 0, d_tokens, m->w<int8_t>(m->cls_row)));
+        batch, m->off[0], m->pkg[0], m->warn, nullptr, 0, d_tokens, m->w<int8_t>(m->cls_row), m->plan));
     CUDA_TRY(cudaGetLastError());
     return run_patch(m, d_images, batch, d_tokens, st);
 }
@@ -1890,7 +1895,7 @@ int hv_token_selector(hv_model *m, int selector_index, const int8_t *d_x, const 
     SelParams sp = bind_sel(m, m->sels[selector_index]);
     CUDA_TRY(launch_selector(d_x, d_offsets, d_pkg_in, images, sp, m->STAGE, m->counts, d_pkg_out, d_summary, 1,
                              m->warn, nullptr, 0, 0, &dbg, st));
-    CUDA_TRY(launch_pack(m->STAGE, m->counts, images, d_y, d_offsets_out, st));
+    CUDA_TRY(launch_pack(m->STAGE, m->counts, images, d_y, d_offsets_out, nullptr, st));
     return HV_OK;
 }
 

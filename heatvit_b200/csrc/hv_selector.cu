@@ -20,6 +20,7 @@
 // The output goes to a per-image staging slot (stride 197 rows); the pack
 // kernel then prefix-sums the new counts and writes the packed ragged layout
 // that every later kernel consumes.
+#include "hv_attn_units.cuh"
 #include "hv_internal.cuh"
 #include "hv_tc05.cuh"
 
@@ -615,26 +616,54 @@ __global__ void __launch_bounds__(THREADS, 2) selector_kernel(
     }
 }
 
+// One CTA per image: copies the image's kept rows from the staging buffer to their
+// packed place and writes its offset and, when `plan` has lists, its attention units
+// (the prefix sums over the images before it give all three positions).
 __global__ void __launch_bounds__(256) pack_kernel(const int8_t *__restrict__ stage,
                                                    const int32_t *__restrict__ counts, int images,
-                                                   int8_t *__restrict__ x, int32_t *__restrict__ offsets_out) {
+                                                   int8_t *__restrict__ x, int32_t *__restrict__ offsets_out,
+                                                   AttnPlan plan) {
     griddep_wait();
     griddep_launch();
-    __shared__ int part[8];
+    __shared__ int part[3][8];
     const int img = blockIdx.x, tid = threadIdx.x;
-    int s = 0;
-    for (int i = tid; i < img; i += 256) s += counts[i];
+    int s = 0, sa = 0, sb = 0;
+    for (int i = tid; i < img; i += 256) {
+        const int n = counts[i];
+        s += n;
+        sa += units_a(n);
+        sb += units_b(n);
+    }
 #pragma unroll
-    for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-    if ((tid & 31) == 0) part[tid >> 5] = s;
+    for (int o = 16; o; o >>= 1) {
+        s += __shfl_xor_sync(0xffffffffu, s, o);
+        sa += __shfl_xor_sync(0xffffffffu, sa, o);
+        sb += __shfl_xor_sync(0xffffffffu, sb, o);
+    }
+    if ((tid & 31) == 0) {
+        part[0][tid >> 5] = s;
+        part[1][tid >> 5] = sa;
+        part[2][tid >> 5] = sb;
+    }
     __syncthreads();
-    int off = 0;
+    int off = 0, pa = 0, pb = 0;
 #pragma unroll
-    for (int w = 0; w < 8; ++w) off += part[w];
+    for (int w = 0; w < 8; ++w) {
+        off += part[0][w];
+        pa += part[1][w];
+        pb += part[2][w];
+    }
     const int cnt = counts[img];
     if (tid == 0) {
         offsets_out[img] = off;
         if (img == images - 1) offsets_out[images] = off + cnt;
+        if (plan.cnt) {
+            write_image_units(plan.list_a, plan.list_b, pa, pb, img, off, cnt);
+            if (img == images - 1) {
+                plan.cnt[0] = pa + units_a(cnt);
+                plan.cnt[1] = pb + units_b(cnt);
+            }
+        }
     }
     const int4 *src = (const int4 *)(stage + (size_t)img * 197 * 192);
     int4 *dst = (int4 *)(x + (size_t)off * 192);
@@ -656,9 +685,10 @@ cudaError_t launch_selector(const int8_t *x, const int32_t *offsets, const uint8
 }
 
 cudaError_t launch_pack(const int8_t *stage, const int32_t *counts, int images, int8_t *x, int32_t *offsets_out,
-                        cudaStream_t st) {
+                        const AttnPlan *plan, cudaStream_t st) {
     if (images <= 0) return cudaSuccess;
-    return launch_pdl(pack_kernel, dim3(images), dim3(256), 0, st, stage, counts, images, x, offsets_out);
+    const AttnPlan pl = plan ? *plan : AttnPlan{nullptr, nullptr, nullptr};
+    return launch_pdl(pack_kernel, dim3(images), dim3(256), 0, st, stage, counts, images, x, offsets_out, pl);
 }
 
 }  // namespace hv
