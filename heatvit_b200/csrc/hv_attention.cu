@@ -241,6 +241,32 @@ __device__ __forceinline__ uint32_t piece_exp(uint32_t (&v)[16], int valid, int3
     return s8[0];
 }
 
+// Exp terms of a warp's 4 tail columns, the first `valid` of them real (the rest
+// give 0); returns their sum.  Same table / arithmetic choice as piece_exp.
+template <bool FAST>
+__device__ __forceinline__ uint32_t tail_exp(uint32_t (&v)[4], int valid, int32_t mx, int32_t cmn,
+                                             const AttnParams &p, const uint32_t *tab) {
+    uint32_t orv = 0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        uint32_t nn = negxt_of<FAST>((int32_t)v[j], mx, cmn, p);
+        if (j >= valid) nn = 0u;
+        v[j] = nn;
+        orv |= nn;
+    }
+    if (__all_sync(0xffffffffu, orv < (uint32_t)kSmallN)) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) v[j] = tab[v[j]];
+    } else {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) v[j] = softmax_exp_q16_n(v[j]);
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+        if (j >= valid) v[j] = 0u;
+    return (v[0] + v[1]) + (v[2] + v[3]);
+}
+
 // Largest of 16 values (the first `valid` when MASK), as a pairwise tree.
 template <bool MASK>
 __device__ __forceinline__ int32_t piece_max(const uint32_t (&v)[16], int valid) {
@@ -423,12 +449,28 @@ __global__ void __launch_bounds__(CFG::THREADS, CFG::PER_SM) attention_tc_kernel
         const uint32_t row_addr = lane_addr + cb;
         const int nv = (u.n + 15) >> 4, nfull = u.n >> 4;  // 16-column pieces: with a column / all full
         constexpr int SP = CFG::SPLIT;
+        // With 4 warps per quadrant the full pieces are dealt round-robin and a partial
+        // last piece is split instead, 4 columns per warp (13 pieces at 197 tokens
+        // would otherwise give one warp 4 pieces and the others 3).
+        constexpr bool TAILS = SP == 4;
+        const int npc = TAILS ? nfull : nv;                    // pieces dealt round-robin
+        const bool has_tail = TAILS && (u.n & 15);             // unit-uniform
+        const int tcol = nfull * 16 + 4 * part;                // this warp's tail columns
+        const int tval = min(4, max(0, u.n - tcol));           // real ones among them
         if (live) {
             // q16 is monotone in the accumulator: the row max is taken on raw values
             int32_t mxa = INT32_MIN;
-            for_pieces<CFG::DB>(row_addr, part, SP, nv, [&](uint32_t (&v)[16], int c) {
+            for_pieces<CFG::DB>(row_addr, part, SP, npc, [&](uint32_t (&v)[16], int c) {
                 mxa = max(mxa, c < nfull ? piece_max<false>(v, 16) : piece_max<true>(v, u.n - c * 16));
             });
+            if (has_tail) {
+                uint32_t w[4];
+                tc05::ld4(row_addr + tcol, w);
+                tc05::wait_ld_regs(w);
+#pragma unroll
+                for (int j = 0; j < 4; ++j)
+                    if (j < tval) mxa = max(mxa, (int32_t)w[j]);
+            }
             if (SP > 1) {
                 sred[part * 128 + lrow] = mxa;
                 quad_sync<CFG>(quad);
@@ -439,11 +481,18 @@ __global__ void __launch_bounds__(CFG::THREADS, CFG::PER_SM) attention_tc_kernel
             const int32_t cmn =
                 (int32_t)(((int64_t)1 << p.fast_shift) - 1 - p.fast_half + ((int64_t)mx << p.fast_shift));
             uint32_t sum = 0;
-            for_pieces<CFG::DB>(row_addr, part, SP, nv, [&](uint32_t (&v)[16], int c) {
+            for_pieces<CFG::DB>(row_addr, part, SP, npc, [&](uint32_t (&v)[16], int c) {
                 if (c < nfull) sum += piece_exp<FAST, false>(v, 16, mx, cmn, p, stab);
                 else sum += piece_exp<FAST, true>(v, u.n - c * 16, mx, cmn, p, stab);
                 tc05::st16(row_addr + c * 16, v);
             });
+            if (has_tail) {
+                uint32_t w[4];
+                tc05::ld4(row_addr + tcol, w);
+                tc05::wait_ld_regs(w);
+                sum += tail_exp<FAST>(w, tval, mx, cmn, p, stab);
+                tc05::st4(row_addr + tcol, w);
+            }
             tc05::wait_st();
             if (SP > 1) {
                 sred[(SP + part) * 128 + lrow] = (int32_t)sum;
@@ -457,7 +506,7 @@ __global__ void __launch_bounds__(CFG::THREADS, CFG::PER_SM) attention_tc_kernel
             const uint32_t rc = softmax_recip32(sum);
             // P row: the own block's probabilities, zeros in every other column
             const int cb16 = cb >> 4;
-            for_pieces<CFG::DB>(row_addr, part, SP, nv, [&](uint32_t (&v)[16], int c) {
+            for_pieces<CFG::DB>(row_addr, part, SP, npc, [&](uint32_t (&v)[16], int c) {
                 uint32_t pk[4];
 #pragma unroll
                 for (int w = 0; w < 4; ++w) {
@@ -474,6 +523,17 @@ __global__ void __launch_bounds__(CFG::THREADS, CFG::PER_SM) attention_tc_kernel
                 *(uint4 *)(sP + tc05::kmajor_offset(lrow, (cb16 + c) * 16, scols)) =
                     make_uint4(pk[0], pk[1], pk[2], pk[3]);
             });
+            if (has_tail) {  // this warp's 4 bytes of the partial piece (zeros past the row)
+                uint32_t w[4];
+                tc05::ld4(row_addr + tcol, w);
+                tc05::wait_ld_regs(w);
+                int32_t pr[4];
+#pragma unroll
+                for (int b = 0; b < 4; ++b)
+                    pr[b] = (int32_t)(((uint64_t)w[b] * rc + (32768u + (1u << 23))) >> 24);
+                *(uint32_t *)(sP + tc05::kmajor_offset(lrow, (cb16 + nfull) * 16, scols) + 4 * part) =
+                    pack_satu8(pr[0], pr[1], pr[2], pr[3]);
+            }
             for (int c = part; c < scols / 16; c += SP)
                 if (c < cb16 || c >= cb16 + nv)
                     *(uint4 *)(sP + tc05::kmajor_offset(lrow, c * 16, scols)) = make_uint4(0, 0, 0, 0);
