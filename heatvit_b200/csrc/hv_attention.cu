@@ -560,7 +560,26 @@ __global__ void __launch_bounds__(CFG::THREADS, CFG::PER_SM) attention_tc_kernel
         // V is consumed: the next unit's V copies overlap the rest of this unit
         if (more) load_kv<CFG, 1>(qkv, cur, sV, tid);
         cp_commit();
-        if (live) {
+        if (live && SP == 4) {
+            // one 16-column quarter of the row's 64 context columns per warp
+            const int h = u.h0 + j;
+            uint32_t o[16];
+            tc05::ld16(lane_addr + part * 16, o);
+            tc05::wait_ld_regs(o);
+            uint32_t pk[4];
+#pragma unroll
+            for (int w = 0; w < 4; ++w) {
+                int32_t q[4];
+#pragma unroll
+                for (int b = 0; b < 4; ++b) {
+                    const int32_t a = (int32_t)o[w * 4 + b];
+                    q[b] = p.ctx_fast ? rsa32(a, p.ctx_shift) : (int32_t)requant64(a, p.ctx_shift, 8);
+                }
+                pk[w] = pack_sat8(q[0], q[1], q[2], q[3]);
+            }
+            if (t < u.n)
+                *(uint4 *)(ctx + (size_t)(u.row0 + t) * 192 + h * 64 + part * 16) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+        } else if (live) {
             const int h = u.h0 + j;
             for (int half = part; half < 2; half += CFG::SPLIT) {
                 uint32_t o[32];
