@@ -49,7 +49,7 @@ GEMM_SHAPES = {"qkv": (192, 576, 0), "proj": (192, 192, 192), "fc1": (192, 768, 
 # (profiles/): block 1 of a 1024-image step, 201,728 rows (dram__bytes_read.sum +
 # dram__bytes_write.sum).  Traffic grows with the rows of a launch.
 STAGE_TRAFFIC_PER_ROW = {"ffn": (77_869_824 + 11_407_360) / 201_728,
-                         "attn": (116_340_992 + 20_178_688) / 201_728,
+                         "attn": (116_336_896 + 17_401_088) / 201_728,
                          "ln1": (38_799_616 + 1_387_776) / 201_728}
 
 
