@@ -204,20 +204,24 @@ __global__ void __launch_bounds__(256, 3) ln_kernel(const int8_t *x, int8_t *out
         };
         uint2 wn[3];
         load_words(0, wn);
-#pragma unroll 1
+        // (unrolled by two: the shuffle reductions of consecutive sub-passes overlap)
+#pragma unroll 2
         for (int k = 0; k < g; ++k) {
             const int r = base + 4 * k + grp;
             const uint2 w[3] = {wn[0], wn[1], wn[2]};
             load_words(k + 1, wn);
-            // Σx and Σx² of the 24 bytes with 4-way byte dot products (|Σx²| < 2^21)
-            int32_t s = 0, q = 0;
+            // Σx and Σx² of the 24 bytes with 4-way byte dot products (|Σx²| < 2^21),
+            // two independent chains each
+            int32_t s = 0, q = 0, s1 = 0, q1 = 0;
 #pragma unroll
             for (int i = 0; i < 3; ++i) {
                 s = __dp4a((int)w[i].x, 0x01010101, s);
-                s = __dp4a((int)w[i].y, 0x01010101, s);
+                s1 = __dp4a((int)w[i].y, 0x01010101, s1);
                 q = __dp4a((int)w[i].x, (int)w[i].x, q);
-                q = __dp4a((int)w[i].y, (int)w[i].y, q);
+                q1 = __dp4a((int)w[i].y, (int)w[i].y, q1);
             }
+            s += s1;
+            q += q1;
             int64_t s2;
             if (p.sq_shift >= 0) {
 #pragma unroll
