@@ -67,7 +67,7 @@ constexpr int SZ_FLAGS = MAXC;  // bit0 keep, bit1 participant
 constexpr int OFF_STATS = (OFF_FLAGS + SZ_FLAGS + 15) & ~15;
 constexpr int SZ_STATS = MAXC * 3;
 constexpr int OFF_MISC = (OFF_STATS + SZ_STATS + 15) & ~15;
-constexpr int SZ_MISC = 128;  // [0] warn, [1] kept, [2] participants, [4..4+THREADS/32) scan,
+constexpr int SZ_MISC = 128;  // [0] warn, [4..4+THREADS/32) scan,
                               // [24] wait status, byte 112: mbarrier, byte 120: TMEM base
 constexpr int OFF_H1 = OFF_MISC + SZ_MISC;  // score layer-1 outputs [6 strips][197][16]
 constexpr int SZ_H1 = 6 * STRIP;
@@ -82,7 +82,8 @@ constexpr int OFF_TAB1 = OFF_TOK;
 constexpr int OFF_TAB2 = OFF_TOK + kSelTabH1Bytes;
 static_assert(kSelTabH1Bytes + kSelTabH2Bytes <= SZ_TOK, "score-layer tables fit the token rows");
 static_assert(OFF_TABL % 16 == 0 && OFF_TAB2 % 16 == 0, "16-byte table staging");
-static_assert(2 * (SMEM_BYTES + 1024) <= 228 * 1024, "two selector CTAs per SM");
+// (plus 128 bytes of static shared memory: the per-warp package sums)
+static_assert(2 * (SMEM_BYTES + 128 + 1024) <= 228 * 1024, "two selector CTAs per SM");
 static_assert(OFF_LOCAL % 16 == 0 && OFF_LWT % 16 == 0 && OFF_W1T % 16 == 0 && OFF_W2T % 16 == 0 &&
                   OFF_H1 % 16 == 0 && OFF_MISC % 16 == 0,
               "16-byte aligned tensor-core operands");
@@ -340,19 +341,28 @@ __global__ void __launch_bounds__(THREADS, 2) selector_kernel(
     // ---- global mean (selector.py:273-289) and head stats (358-367), the last reads
     // of the token rows before the score-layer tables take their place ----------------
     {
-        // four threads per (head, lane) sum interleaved candidates, then one of them adds
-        // the four partial sums (shorter dependent chains than one thread over C)
-        int32_t *gpart = hs;  // head-score rows are free until the score MLP
-        if (tid < 384) {
-            const int q = tid / 96, hj = tid - q * 96;
-            int32_t t = 0;
-            const int8_t *col = strip_at(local, 0, hj);
-            for (int c = q; c < C; c += 4) t += col[(1 + c) * 16];
-            gpart[q * 96 + hj] = t;
+        // thread (j, q) of 24 x 20 sums the 4 features of word j of the local rows (one
+        // 32-bit word of a strip row) over every twentieth candidate; the 20 partials
+        // of a feature meet in shared memory (the score layer-1 rows, not yet written)
+        constexpr int GQ = 20;
+        int32_t *gpart = (int32_t *)(smem + OFF_H1);
+        if (tid < 24 * GQ) {
+            const int q = tid / 24, j = tid - q * 24;
+            const int8_t *col = local + (j >> 2) * STRIP + (j & 3) * 4;
+            int32_t t[4] = {0, 0, 0, 0};
+            for (int c = q; c < C; c += GQ) {
+                const uint32_t wv = *(const uint32_t *)(col + (1 + c) * 16);
+#pragma unroll
+                for (int k = 0; k < 4; ++k) t[k] += (int32_t)(int8_t)(wv >> (8 * k));
+            }
+#pragma unroll
+            for (int k = 0; k < 4; ++k) gpart[q * 96 + 4 * j + k] = t[k];
         }
         __syncthreads();
         if (tid < 96) {
-            const int32_t t = gpart[tid] + gpart[96 + tid] + gpart[192 + tid] + gpart[288 + tid];
+            int32_t t = 0;
+#pragma unroll
+            for (int q = 0; q < GQ; ++q) t += gpart[q * 96 + tid];
             glob[tid] = (int8_t)sat8((int32_t)round_div64(t, C));
         }
     }
@@ -509,38 +519,36 @@ __global__ void __launch_bounds__(THREADS, 2) selector_kernel(
     asm volatile("cp.async.wait_all;\n" ::: "memory");  // the token rows are back
     __syncthreads();
 
-    // ---- stable compaction index: exclusive scan of keep flags (C <= 196 < 256) -----
+    // ---- stable compaction index: exclusive scan of keep flags (C <= 196 < 256), and
+    // the participants of the package (pruned normals plus the incoming package,
+    // always) with the sum of their fused scores: per-warp ballots and reductions,
+    // combined after one barrier (each fused score <= 65536, so the sums fit int32)
+    __shared__ int wpart[THREADS / 32], wden[THREADS / 32];
+    int kept = 0, parts = 0;
+    long long pden = 0;
     {
         const int lane = tid & 31, warp = tid >> 5;
-        const int kf = tid < C ? (flags[tid] & 1) : 0;
-        const unsigned bal = __ballot_sync(0xffffffffu, kf);
-        if (lane == 0) misc[4 + warp] = __popc(bal);
+        const int fl = tid < C ? flags[tid] : 0;
+        const unsigned bal = __ballot_sync(0xffffffffu, fl & 1);
+        const unsigned pbal = __ballot_sync(0xffffffffu, fl & 2);
+        const int dsum = __reduce_add_sync(0xffffffffu, (fl & 2) ? fused[tid] : 0);
+        if (lane == 0) {
+            misc[4 + warp] = __popc(bal);
+            wpart[warp] = __popc(pbal);
+            wden[warp] = dsum;
+        }
         __syncthreads();
         int base = 0;
         for (int w = 0; w < warp; ++w) base += misc[4 + w];
         if (tid < C) kidx[tid] = base + __popc(bal & ((1u << lane) - 1u));
-        if (tid == THREADS - 1) {
-            int tot = 0;
-            for (int w = 0; w < THREADS / 32; ++w) tot += misc[4 + w];
-            misc[1] = tot;
+#pragma unroll
+        for (int w = 0; w < THREADS / 32; ++w) {
+            kept += misc[4 + w];
+            parts += wpart[w];
+            pden += wden[w];
         }
     }
-    // participants: pruned normals plus the incoming package (always).
-    __shared__ long long den_sh;
-    if (tid == 0) den_sh = 0;
-    __syncthreads();
-    {
-        long long d = 0;
-        int cnt = 0;
-        for (int c = tid; c < C; c += THREADS)
-            if (flags[c] & 2) { d += fused[c]; ++cnt; }
-        if (d) atomicAdd((unsigned long long *)&den_sh, (unsigned long long)d);
-        if (cnt) atomicAdd(&misc[2], cnt);
-    }
-    __syncthreads();
-    const int kept = misc[1];
-    const int parts = misc[2];
-    const long long pden = den_sh;
+    __syncthreads();  // kidx
     const int nout = 1 + kept + (parts > 0 ? 1 : 0);
 
     // ---- write rows: CLS, kept (stable), package --------------------------------------
@@ -551,27 +559,33 @@ __global__ void __launch_bounds__(THREADS, 2) selector_kernel(
             ((int4 *)(out + (size_t)(1 + kidx[c]) * 192))[ch] = *(const int4 *)(tok + ch * STRIP + (1 + c) * 16);
     }
     if (parts > 0) {
-        // Σ s·x[d] (or Σ x[d]) over the participants: thread (d, q) of 2 x 192 sums every
-        // other candidate (s <= 65536, |x| <= 128, at most 98 terms: int32 is exact), the
-        // two halves meet in shared memory (over the score layer-1 rows, dead by now)
+        // Σ s·x[d] (or Σ x[d]) over the participants: thread (j, q) of 48 x 10 sums
+        // columns 4j..4j+3 (one 32-bit word of a token strip row) over every tenth
+        // candidate (s <= 65536, |x| <= 128, at most 20 terms per thread: int32 is
+        // exact); the ten partials of a column meet in shared memory (over the score
+        // layer-1 rows, dead by now)
         int8_t *prow = out + (size_t)(1 + kept) * 192;
         int32_t *ppart = (int32_t *)(smem + OFF_H1);
-        if (tid < 384) {
-            const int q = tid / 192, d = tid - q * 192;
-            int32_t num = 0;
-            const int8_t *col = strip_at(tok, 0, d);
-            if (pden == 0) {
-                for (int c = q; c < C; c += 2)
-                    if (flags[c] & 2) num += col[(1 + c) * 16];
-            } else {
-                for (int c = q; c < C; c += 2)
-                    if (flags[c] & 2) num += fused[c] * (int32_t)col[(1 + c) * 16];
-            }
-            ppart[tid] = num;
+        constexpr int PQ = 10;
+        if (tid < 48 * PQ) {
+            const int q = tid / 48, j = tid - q * 48;
+            const int8_t *col = tok + (j >> 2) * STRIP + (j & 3) * 4;
+            int32_t num[4] = {0, 0, 0, 0};
+            for (int c = q; c < C; c += PQ)
+                if (flags[c] & 2) {
+                    const int32_t s = pden == 0 ? 1 : fused[c];
+                    const uint32_t wv = *(const uint32_t *)(col + (1 + c) * 16);
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) num[k] += s * (int32_t)(int8_t)(wv >> (8 * k));
+                }
+#pragma unroll
+            for (int k = 0; k < 4; ++k) ppart[q * 192 + 4 * j + k] = num[k];
         }
         __syncthreads();
         if (tid < 192) {
-            const long long num = (long long)ppart[tid] + ppart[192 + tid];
+            long long num = 0;
+#pragma unroll
+            for (int q = 0; q < PQ; ++q) num += ppart[q * 192 + tid];
             prow[tid] = (int8_t)sat8((int32_t)round_div64(num, pden == 0 ? parts : pden));
         }
     }
