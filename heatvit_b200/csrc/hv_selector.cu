@@ -104,9 +104,18 @@ __device__ __forceinline__ int8_t *strip_at(int8_t *base, int r, int k) {
 __device__ __forceinline__ int32_t sat_q016(int64_t v) { return (int32_t)(v < 0 ? 0 : (v > 65536 ? 65536 : v)); }
 
 // Copy a GELU table (t.bytes, a multiple of 16) into shared memory.
+// 16 bytes global -> shared by cp.async (both 16-byte aligned); the caller waits
+// (cp.async.wait_all) before the barrier after which the bytes are read.
+__device__ __forceinline__ void cp16(void *dst, const void *src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"((uint32_t)__cvta_generic_to_shared(dst)),
+                 "l"(src)
+                 : "memory");
+}
+
+// A GELU table into shared memory by cp.async (see cp16).
 __device__ __forceinline__ void stage_tab(const GeluTab &t, int8_t *dst, int tid) {
     if (!t.mode) return;
-    for (int i = tid; i < t.bytes / 16; i += THREADS) ((int4 *)dst)[i] = ((const int4 *)t.tab)[i];
+    for (int i = tid; i < t.bytes / 16; i += THREADS) cp16(dst + 16 * i, (const int8_t *)t.tab + 16 * i);
 }
 
 // acc + a · b over W 16-byte words of packed int8 (shared memory, 16-byte aligned).
@@ -234,22 +243,24 @@ __global__ void __launch_bounds__(THREADS, 2) selector_kernel(
     }
 
     // ---- load tokens (strip layout) and weights (per-head B operands) --------------
+    // (all by cp.async, so every thread's copies are in flight at once)
     for (int c = tid; c < n * 12; c += THREADS)
-        *(int4 *)(tok + (c % 12) * STRIP + (c / 12) * 16) = ((const int4 *)(x + (size_t)row0 * 192))[c];
+        cp16(tok + (c % 12) * STRIP + (c / 12) * 16, x + (size_t)row0 * 192 + 16 * c);
     for (int c = tid; c < 3 * 32 * 4; c += THREADS) {  // local_wt [h][j][64]: 4 chunks per row
         const int hj = c >> 2, k4 = c & 3, h = hj >> 5, j = hj & 31;
-        *(int4 *)(lwt + h * LW_HEAD + k4 * 512 + j * 16) = ((const int4 *)p.local_wt)[c];
+        cp16(lwt + h * LW_HEAD + k4 * 512 + j * 16, p.local_wt + 16 * c);
     }
     for (int c = tid; c < 3 * 32 * 2; c += THREADS) {  // w1t [h][j][0..31]: the local half
         const int hj = c >> 1, k2 = c & 1, h = hj >> 5, j = hj & 31;
-        *(int4 *)(w1t + h * W1_HEAD + k2 * 512 + j * 16) = ((const int4 *)p.w1t)[hj * 4 + k2];
+        cp16(w1t + h * W1_HEAD + k2 * 512 + j * 16, p.w1t + 16 * (hj * 4 + k2));
     }
     for (int c = tid; c < 3 * 16 * 2; c += THREADS) {  // w2t [h][m][32]
         const int hm = c >> 1, k2 = c & 1, h = hm >> 4, m = hm & 15;
-        *(int4 *)(w2t + h * W2_HEAD + k2 * 256 + m * 16) = ((const int4 *)p.w2t)[c];
+        cp16(w2t + h * W2_HEAD + k2 * 256 + m * 16, p.w2t + 16 * c);
     }
     if (tid < 24) ((int32_t *)w3t)[tid] = ((const int32_t *)p.w3t)[tid];
     stage_tab(p.tab_local, tabl, tid);
+    asm volatile("cp.async.wait_all;\n" ::: "memory");
     uint64_t *bar = (uint64_t *)((uint8_t *)misc + 112);
     uint32_t *tslot = (uint32_t *)((uint8_t *)misc + 120);
     volatile int *wstat = (volatile int *)(misc + 24);
@@ -382,7 +393,7 @@ __global__ void __launch_bounds__(THREADS, 2) selector_kernel(
         }
     }
     __syncthreads();
-    stage_tab(p.tab_h1, tab1, tid);
+    stage_tab(p.tab_h1, tab1, tid);  // (their copies overlap the global half below)
     stage_tab(p.tab_h2, tab2, tid);
     if (tid < 96) {
         // the global half of layer 1, once per image (W1 rows read from global memory)
@@ -391,6 +402,7 @@ __global__ void __launch_bounds__(THREADS, 2) selector_kernel(
         const int32_t acc = dot16<2>(glob + h * 32, (const int8_t *)wrow, 0);  // (2 x 16-byte words)
         g1[h * 32 + j] = (int64_t)acc + p.b1[h * 32 + j];
     }
+    asm volatile("cp.async.wait_all;\n" ::: "memory");  // the score-layer tables
     __syncthreads();
 
     // ---- score MLP layer 1 (selector.py:307-330): per head [n x 32] . [32 x 32] -------
