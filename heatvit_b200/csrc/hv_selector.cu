@@ -223,7 +223,7 @@ __global__ void __launch_bounds__(THREADS, 2) selector_kernel(
     int32_t *kidx = (int32_t *)(smem + OFF_KIDX);
     uint8_t *flags = (uint8_t *)(smem + OFF_FLAGS);
     int8_t *stats = (int8_t *)(smem + OFF_STATS);
-    int32_t *misc = (int32_t *)(smem + OFF_MISC);  // [0] warn, [1] kept, [2] participants, [4..] scan
+    int32_t *misc = (int32_t *)(smem + OFF_MISC);  // [0] warn, [4..] scan
 
     const int img = blockIdx.x, tid = threadIdx.x;
     const int row0 = offsets[img];
@@ -472,22 +472,27 @@ __global__ void __launch_bounds__(THREADS, 2) selector_kernel(
         }
         asm volatile("cp.async.commit_group;\n" ::: "memory");
     }
-    for (int it = tid; it < 3 * C; it += THREADS) {
-        int h, c;
-        split_hc(it, C, h, c);
-        const int8_t *hrow = h2s + (h * MAXC + c) * 16;
-        int32_t q[2];
+    // Layer 3 (3C items) and the head-weight MLP (C items, each costlier) are
+    // independent: the last C threads take the head-weight MLP, one candidate each,
+    // while the others run layer 3.
+    const int nl3 = THREADS - C;  // >= THREADS - MAXC
+    if (tid < nl3) {
+        for (int it = tid; it < 3 * C; it += nl3) {
+            int h, c;
+            split_hc(it, C, h, c);
+            const int8_t *hrow = h2s + (h * MAXC + c) * 16;
+            int32_t q[2];
 #pragma unroll
-        for (int o = 0; o < 2; ++o) {
-            const int32_t acc = dot16<1>(hrow, w3t + (h * 2 + o) * 16, 0);
-            const int32_t logit = (int32_t)requant64((int64_t)acc + p.b3[h * 2 + o], p.logit_shift, 8);
-            q[o] = (int32_t)requant64(logit, p.logit_q16_shift, 24);
+            for (int o = 0; o < 2; ++o) {
+                const int32_t acc = dot16<1>(hrow, w3t + (h * 2 + o) * 16, 0);
+                const int32_t logit = (int32_t)requant64((int64_t)acc + p.b3[h * 2 + o], p.logit_shift, 8);
+                q[o] = (int32_t)requant64(logit, p.logit_q16_shift, 24);
+            }
+            hs[h * MAXC + c] = keep_score(q[0], q[1]);
         }
-        hs[h * MAXC + c] = keep_score(q[0], q[1]);
-    }
-
-    // ---- head-weight MLP per candidate (selector.py:370-389) -------------------------
-    for (int c = tid; c < C; c += THREADS) {
+    } else {
+        // ---- head-weight MLP per candidate (selector.py:370-389) ---------------------
+        const int c = tid - nl3;
         int32_t st[3];
 #pragma unroll
         for (int h = 0; h < 3; ++h) st[h] = stats[c * 3 + h];
